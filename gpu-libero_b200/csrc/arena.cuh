@@ -1,0 +1,112 @@
+// Per-world shared-memory arena of the fused control-step kernel.
+//
+// One CTA owns one world for a whole control step; every array the substep
+// touches lives here, so HBM is read once (state in) and written once (state
+// and outputs out) per control step.  The layout is computed identically on
+// the host (to size the dynamic shared memory) and on the device.
+#pragma once
+#include <cstddef>
+#include "b200phys.h"
+
+namespace b200 {
+
+// Per-contact record, in reals.
+enum ContactField {
+  kCDist = 0, kCPos = 1, kCFrame = 4, kCMargin = 13, kCFriction = 14,
+  kCSolref = 19, kCSolrefFriction = 21, kCSolimp = 23, kCWidth = 28
+};
+
+struct Carve {
+  size_t at = 0;
+  template <class T> __host__ __device__ size_t take(size_t count) {
+    at = (at + 15) & ~size_t(15);
+    size_t offset = at;
+    at += count * sizeof(T);
+    return offset;
+  }
+};
+
+template <class R> struct Arena {
+  // state
+  R *qpos, *qvel, *warm, *ctrl, *goal_pos, *goal_rot, *gripper, *action;
+  // position stage
+  R *xpos, *xquat, *xmat, *xipos, *ximat, *anchor, *axis, *gxpos, *gxmat, *sxpos, *sxmat;
+  R *com, *cinert, *crb, *cdof, *M, *L;
+  // velocity stage
+  R *cvel, *cacc, *cfrc, *cdof_dot, *act_length, *act_moment;
+  // dof vectors
+  R *qfrc_bias, *qfrc_passive, *qfrc_actuator, *qfrc_smooth, *qacc_smooth, *qacc, *Ma, *Mv;
+  R *grad, *search, *qfrc_constraint, *ee_vel;
+  // contacts and rows
+  R *con;
+  int *con_dim, *con_g1, *con_g2, *con_key, *con_order, *con_adr;
+  R *J, *efc_D, *efc_aref, *efc_floss, *efc_force, *efc_jaref, *efc_jv, *efc_quad;
+  int *efc_type, *efc_id, *efc_state;
+  // Newton Hessian, reused as OSC scratch (double) before the solve
+  R *H;
+  double *osc;
+  // scalars and reduction scratch
+  R *scal;   // [0] alpha [1] improvement [2] search_dot [3] grad_dot [4] decrement [5] time
+  int *iscal;  // [0] ncon [1] nefc [2] nf [3] overflow [4] niter [5] done [6] error [7] ls evals [8] raw count
+  R *red;    // reduction scratch (one real per warp, times 4)
+
+  static constexpr int kOscDoubles = 600;
+
+  __host__ __device__ static size_t layout(const B200Model &m, int threads, Arena *a, unsigned char *base) {
+    Carve c;
+    const int nq = m.nq, nv = m.nv, nu = m.nu, nb = m.nbody, nj = m.njnt, ng = m.ngeom, ns = m.nsite;
+    const int nc = m.ncon_max, ne = m.nefc_max, nvs = m.nvs;
+    size_t o[80];
+    int k = 0;
+    o[k++] = c.take<R>(nq); o[k++] = c.take<R>(nv); o[k++] = c.take<R>(nv); o[k++] = c.take<R>(nu);
+    o[k++] = c.take<R>(3); o[k++] = c.take<R>(9); o[k++] = c.take<R>(2); o[k++] = c.take<R>(7);
+    o[k++] = c.take<R>(nb * 3); o[k++] = c.take<R>(nb * 4); o[k++] = c.take<R>(nb * 9);
+    o[k++] = c.take<R>(nb * 3); o[k++] = c.take<R>(nb * 9); o[k++] = c.take<R>(nj * 3);
+    o[k++] = c.take<R>(nj * 3); o[k++] = c.take<R>(ng * 3); o[k++] = c.take<R>(ng * 9);
+    o[k++] = c.take<R>(ns * 3); o[k++] = c.take<R>(ns * 9);
+    o[k++] = c.take<R>(nb * 3); o[k++] = c.take<R>(nb * 10); o[k++] = c.take<R>(nb * 10);
+    o[k++] = c.take<R>(nv * 6); o[k++] = c.take<R>(m.nM); o[k++] = c.take<R>(m.nM);
+    o[k++] = c.take<R>(nb * 6); o[k++] = c.take<R>(nb * 6); o[k++] = c.take<R>(nb * 6);
+    o[k++] = c.take<R>(nv * 6); o[k++] = c.take<R>(nu); o[k++] = c.take<R>(nu);
+    for (int i = 0; i < 11; ++i) o[k++] = c.take<R>(nv);
+    o[k++] = c.take<R>(6);
+    o[k++] = c.take<R>((size_t)nc * kCWidth);
+    for (int i = 0; i < 6; ++i) o[k++] = c.take<int>(nc);
+    o[k++] = c.take<R>((size_t)ne * nvs);
+    for (int i = 0; i < 6; ++i) o[k++] = c.take<R>(ne);
+    o[k++] = c.take<R>((size_t)ne * 3);
+    for (int i = 0; i < 3; ++i) o[k++] = c.take<int>(ne);
+    size_t hbytes = (size_t)nv * nvs * sizeof(R), obytes = (size_t)kOscDoubles * sizeof(double);
+    o[k++] = c.take<unsigned char>(hbytes > obytes ? hbytes : obytes);
+    o[k++] = c.take<R>(8); o[k++] = c.take<int>(12); o[k++] = c.take<R>(4 * ((threads + 31) / 32));
+    size_t total = (c.at + 15) & ~size_t(15);
+    if (a) {
+      int i = 0;
+#define B200_P(field, T) a->field = (T *)(base + o[i++])
+      B200_P(qpos, R); B200_P(qvel, R); B200_P(warm, R); B200_P(ctrl, R);
+      B200_P(goal_pos, R); B200_P(goal_rot, R); B200_P(gripper, R); B200_P(action, R);
+      B200_P(xpos, R); B200_P(xquat, R); B200_P(xmat, R); B200_P(xipos, R); B200_P(ximat, R);
+      B200_P(anchor, R); B200_P(axis, R); B200_P(gxpos, R); B200_P(gxmat, R); B200_P(sxpos, R); B200_P(sxmat, R);
+      B200_P(com, R); B200_P(cinert, R); B200_P(crb, R); B200_P(cdof, R); B200_P(M, R); B200_P(L, R);
+      B200_P(cvel, R); B200_P(cacc, R); B200_P(cfrc, R); B200_P(cdof_dot, R); B200_P(act_length, R); B200_P(act_moment, R);
+      B200_P(qfrc_bias, R); B200_P(qfrc_passive, R); B200_P(qfrc_actuator, R); B200_P(qfrc_smooth, R);
+      B200_P(qacc_smooth, R); B200_P(qacc, R); B200_P(Ma, R); B200_P(Mv, R); B200_P(grad, R); B200_P(search, R);
+      B200_P(qfrc_constraint, R);
+      B200_P(ee_vel, R);
+      B200_P(con, R);
+      B200_P(con_dim, int); B200_P(con_g1, int); B200_P(con_g2, int); B200_P(con_key, int); B200_P(con_order, int);
+      B200_P(con_adr, int);
+      B200_P(J, R); B200_P(efc_D, R); B200_P(efc_aref, R); B200_P(efc_floss, R); B200_P(efc_force, R);
+      B200_P(efc_jaref, R); B200_P(efc_jv, R); B200_P(efc_quad, R);
+      B200_P(efc_type, int); B200_P(efc_id, int); B200_P(efc_state, int);
+      a->H = (R *)(base + o[i]);
+      a->osc = (double *)(base + o[i]);
+      ++i;
+      B200_P(scal, R); B200_P(iscal, int); B200_P(red, R);
+#undef B200_P
+    }
+    return total;
+  }
+};
+
+}  // namespace b200

@@ -1,0 +1,1650 @@
+// B200-native batched rigid-body physics step (sm_100a).
+//
+// One CTA owns one world for a whole control step.  The world's state is
+// loaded from HBM once, every substep of the control step runs out of shared
+// memory (forward kinematics, composite-rigid-body mass matrix and factor,
+// collision, constraint rows, RNE, FP64 OSC, actuation, Newton with exact line
+// search, implicit-damping Euler), and state plus outputs are written back
+// once.  This fuses the reference's ~40-node-per-substep CUDA graph
+// (libero/libero/gpu/host/backends/cuda_fp32/runtime.py:40-56) into one launch
+// per control step.  Reductions run in a fixed order, so a world's trajectory
+// is bit-reproducible run to run (the reference's pooled atomics are not).
+//
+// Build: nvcc -gencode arch=compute_100a,code=sm_100a --fmad=true
+//        --prec-div=true --prec-sqrt=true --ftz=false (the reference's
+//        FP32 flags, libero/libero/gpu/cmake/MjwarpBox.cmake:15).
+#include <cuda_runtime.h>
+#include <cfloat>
+#include <cstdint>
+#include "b200phys.h"
+#include "arena.cuh"
+#include "math.cuh"
+#include "collide.cuh"
+
+#ifndef B200PHYS_SOURCE_ID
+#define B200PHYS_SOURCE_ID "b200phys-dev"
+#endif
+
+namespace b200 {
+
+constexpr int kSatisfied = 0, kQuadratic = 1, kLinearNeg = 2, kLinearPos = 3, kCone = 4;
+
+#define FOR(i, n) for (int i = threadIdx.x; i < (n); i += T)
+#define SYNC() __syncthreads()
+
+template <class R, int T> __device__ R block_sum(R v, R *red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  R s = 0;
+  for (int k = 0; k < T / 32; ++k) s += red[k];
+  __syncthreads();
+  return s;
+}
+
+template <class R> __device__ __forceinline__ R warp_sum(R v) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// M[i][j] from the per-tree dense blocks (0 across trees)
+template <class R> __device__ __forceinline__ R mass_at(const Mdl<R> &M, const R *Mb, int i, int j) {
+  const int t = IF(dof_treeid)[i];
+  if (t != IF(dof_treeid)[j]) return R(0);
+  const int a = IF(tree_dofadr)[t], n = IF(tree_dofnum)[t];
+  return Mb[IF(tree_madr)[t] + (i - a) * n + (j - a)];
+}
+
+template <class R> __device__ __forceinline__ bool dof_ancestor(const Mdl<R> &M, int body, int dof) {
+  return (((unsigned)IF(body_dofmask)[4 * body + (dof >> 5)]) >> (dof & 31)) & 1u;
+}
+
+// ============================================================ position stage
+// forward kinematics, level by level (mjwarp_kinematics.cu:95-212 semantics)
+template <class R, int T> __device__ void kinematics(const Mdl<R> &M, Arena<R> &A) {
+  const B200Model &m = M.m;
+  if (threadIdx.x == 0) {
+    A.xpos[0] = A.xpos[1] = A.xpos[2] = 0;
+    A.xquat[0] = 1; A.xquat[1] = A.xquat[2] = A.xquat[3] = 0;
+  }
+  SYNC();
+  const int *order = IF(body_order), *lstart = IF(level_start);
+  for (int level = 1; level < m.nlevel; ++level) {
+    const int a = lstart[level], n = lstart[level + 1] - a;
+    FOR(k, n) {
+      const int b = order[a + k];
+      const int first = IF(body_jntadr)[b], count = IF(body_jntnum)[b], p = IF(body_parentid)[b];
+      V3<R> pos;
+      Q4<R> quat;
+      if (count == 1 && IF(jnt_type)[first] == B200_JNT_FREE) {
+        const R *q = A.qpos + IF(jnt_qposadr)[first];
+        pos = v3<R>(q[0], q[1], q[2]);
+        quat = qnormalize(Q4<R>{q[3], q[4], q[5], q[6]});
+        st3(A.anchor + 3 * first, pos);
+        st3(A.axis + 3 * first, ld3(RF(jnt_axis) + 3 * first));
+      } else {
+        const Q4<R> pq = ldq(A.xquat + 4 * p);
+        pos = qrot(ld3(RF(body_pos) + 3 * b), pq) + ld3(A.xpos + 3 * p);
+        quat = qmul(pq, ldq(RF(body_quat) + 4 * b));
+        for (int j = first; j < first + count; ++j) {
+          const int kind = IF(jnt_type)[j], qa = IF(jnt_qposadr)[j];
+          const V3<R> lpos = ld3(RF(jnt_pos) + 3 * j), lax = ld3(RF(jnt_axis) + 3 * j);
+          const V3<R> anchor = qrot(lpos, quat) + pos, axis = qrot(lax, quat);
+          if (kind == B200_JNT_BALL) {
+            quat = qmul(quat, qnormalize(ldq(A.qpos + qa)));
+            pos = anchor - qrot(lpos, quat);
+          } else if (kind == B200_JNT_SLIDE) {
+            pos = pos + axis * (A.qpos[qa] - RF(qpos0)[qa]);
+          } else if (kind == B200_JNT_HINGE) {
+            const R angle = (A.qpos[qa] - RF(qpos0)[qa]) * R(0.5);
+            const R s = msin(angle), c = mcos(angle);
+            quat = qmul(quat, Q4<R>{c, lax.x * s, lax.y * s, lax.z * s});
+            pos = anchor - qrot(lpos, quat);
+          }
+          st3(A.anchor + 3 * j, anchor);
+          st3(A.axis + 3 * j, axis);
+        }
+        quat = qnormalize(quat);
+      }
+      st3(A.xpos + 3 * b, pos);
+      stq(A.xquat + 4 * b, quat);
+    }
+    SYNC();
+  }
+  FOR(b, m.nbody) {
+    const Q4<R> q = ldq(A.xquat + 4 * b);
+    qmat(A.xmat + 9 * b, q);
+    st3(A.xipos + 3 * b, ld3(A.xpos + 3 * b) + qrot(ld3(RF(body_ipos) + 3 * b), q));
+    qmat(A.ximat + 9 * b, qmul(q, ldq(RF(body_iquat) + 4 * b)));
+  }
+  FOR(g, m.ngeom) {
+    const int b = IF(geom_bodyid)[g];
+    const Q4<R> q = ldq(A.xquat + 4 * b);
+    st3(A.gxpos + 3 * g, ld3(A.xpos + 3 * b) + qrot(ld3(RF(geom_pos) + 3 * g), q));
+    qmat(A.gxmat + 9 * g, qmul(q, ldq(RF(geom_quat) + 4 * g)));
+  }
+  FOR(s, m.nsite) {
+    const int b = IF(site_bodyid)[s];
+    const Q4<R> q = ldq(A.xquat + 4 * b);
+    st3(A.sxpos + 3 * s, ld3(A.xpos + 3 * b) + qrot(ld3(RF(site_pos) + 3 * s), q));
+    qmat(A.sxmat + 9 * s, qmul(q, ldq(RF(site_quat) + 4 * s)));
+  }
+  SYNC();
+}
+
+// subtree com, centred inertia, motion axes, CRB and the mass matrix
+// (mjwarp_com_pos.cu:7-88, mjwarp_mass_matrix.cu:52-104).  Subtrees are
+// contiguous body intervals, so each sum has one owner and no barrier chain.
+template <class R, int T> __device__ void com_crb_mass(const Mdl<R> &M, Arena<R> &A) {
+  const B200Model &m = M.m;
+  const int nb = m.nbody;
+  const R *mass = RF(body_mass);
+  FOR(w, 3 * nb) {
+    const int b = w / 3, c = w % 3;
+    R s = A.xipos[3 * b + c] * mass[b];
+    for (int k = b + 1; k < IF(body_subtree_end)[b]; ++k) s += A.xipos[3 * k + c] * mass[k];
+    const R sm = RF(body_subtreemass)[b];
+    A.com[3 * b + c] = sm != R(0) ? s / sm : s;
+  }
+  SYNC();
+  FOR(b, nb) {
+    const R *r = A.ximat + 9 * b, *in = RF(body_inertia) + 3 * b, *com = A.com + 3 * IF(body_rootid)[b];
+    const R dx = A.xipos[3 * b] - com[0], dy = A.xipos[3 * b + 1] - com[1], dz = A.xipos[3 * b + 2] - com[2];
+    R sc[9];
+    for (int i = 0; i < 3; ++i)
+      for (int j = 0; j < 3; ++j) sc[3 * i + j] = r[3 * i + j] * in[j];
+    const int rows[6] = {0, 1, 2, 0, 0, 1}, cols[6] = {0, 1, 2, 1, 2, 2};
+    R *o = A.cinert + 10 * b;
+    const R ms = mass[b];
+    for (int i = 0; i < 6; ++i) {
+      const int a = 3 * rows[i], c = 3 * cols[i];
+      o[i] = sc[a] * r[c] + sc[a + 1] * r[c + 1] + sc[a + 2] * r[c + 2];
+    }
+    o[0] += ms * (dy * dy + dz * dz); o[1] += ms * (dx * dx + dz * dz); o[2] += ms * (dx * dx + dy * dy);
+    o[3] -= ms * dx * dy; o[4] -= ms * dx * dz; o[5] -= ms * dy * dz;
+    o[6] = ms * dx; o[7] = ms * dy; o[8] = ms * dz; o[9] = ms;
+  }
+  FOR(j, m.njnt) {
+    const int b = IF(jnt_bodyid)[j], kind = IF(jnt_type)[j];
+    R *out = A.cdof + 6 * IF(jnt_dofadr)[j];
+    const R *com = A.com + 3 * IF(body_rootid)[b];
+    const R dx = com[0] - A.anchor[3 * j], dy = com[1] - A.anchor[3 * j + 1], dz = com[2] - A.anchor[3 * j + 2];
+    if (kind == B200_JNT_FREE) {
+      for (int a = 0; a < 3; ++a)
+        for (int c = 0; c < 6; ++c) out[6 * a + c] = R(c == a + 3);
+      out += 18;
+    }
+    if (kind == B200_JNT_FREE || kind == B200_JNT_BALL) {
+      const R *r = A.xmat + 9 * b;
+      for (int a = 0; a < 3; ++a) {
+        const R x = r[a], y = r[3 + a], z = r[6 + a];
+        R *o = out + 6 * a;
+        o[0] = x; o[1] = y; o[2] = z;
+        o[3] = y * dz - z * dy; o[4] = z * dx - x * dz; o[5] = x * dy - y * dx;
+      }
+    } else if (kind == B200_JNT_SLIDE) {
+      for (int c = 0; c < 3; ++c) { out[c] = 0; out[c + 3] = A.axis[3 * j + c]; }
+    } else {
+      const R x = A.axis[3 * j], y = A.axis[3 * j + 1], z = A.axis[3 * j + 2];
+      out[0] = x; out[1] = y; out[2] = z;
+      out[3] = y * dz - z * dy; out[4] = z * dx - x * dz; out[5] = x * dy - y * dx;
+    }
+  }
+  SYNC();
+  FOR(w, 10 * nb) {
+    const int b = w / 10, c = w % 10;
+    R s = A.cinert[w];
+    if (b > 0)
+      for (int k = b + 1; k < IF(body_subtree_end)[b]; ++k) s += A.cinert[10 * k + c];
+    A.crb[w] = s;
+  }
+  FOR(k, m.nM) A.M[k] = 0;
+  SYNC();
+  FOR(i, m.nv) {
+    R f[6];
+    inert_mul(A.crb + 10 * IF(dof_bodyid)[i], A.cdof + 6 * i, f);
+    const int t = IF(dof_treeid)[i], a = IF(tree_dofadr)[t], n = IF(tree_dofnum)[t], base = IF(tree_madr)[t];
+    for (int j = i; j >= 0; j = IF(dof_parentid)[j]) {
+      R v = 0;
+      for (int c = 0; c < 6; ++c) v += A.cdof[6 * j + c] * f[c];
+      if (j == i) v = RF(dof_armature)[i] + v;
+      A.M[base + (i - a) * n + (j - a)] = v;
+      A.M[base + (j - a) * n + (i - a)] = v;
+    }
+  }
+  SYNC();
+}
+
+// dense upper Cholesky (U^T U = A) of one tree block, one thread per tree
+// (the per-tree factor of mjwarp_mass_factor.cu:19-61)
+template <class R> __device__ void chol_tree(const R *Ab, R *U, int n) {
+  for (int i = 0; i < n; ++i) {
+    R v = Ab[i * n + i];
+    for (int k = 0; k < i; ++k) v -= U[k * n + i] * U[k * n + i];
+    const R d = msqrt(v);
+    U[i * n + i] = d;
+    const R inv = R(1) / d;
+    for (int j = i + 1; j < n; ++j) {
+      R e = Ab[j * n + i];
+      for (int k = 0; k < i; ++k) e -= U[k * n + i] * U[k * n + j];
+      U[i * n + j] = e * inv;
+    }
+    for (int j = 0; j < i; ++j) U[i * n + j] = 0;
+  }
+}
+template <class R> __device__ void chol_tree_solve(const R *U, R *x, int n) {
+  for (int i = 0; i < n; ++i) {
+    R v = x[i];
+    for (int k = 0; k < i; ++k) v -= U[k * n + i] * x[k];
+    x[i] = v / U[i * n + i];
+  }
+  for (int i = n - 1; i >= 0; --i) {
+    R v = x[i];
+    for (int k = i + 1; k < n; ++k) v -= U[i * n + k] * x[k];
+    x[i] = v / U[i * n + i];
+  }
+}
+
+// y = M x with the dense tree blocks (one thread per dof)
+template <class R, int T> __device__ void mass_mul(const Mdl<R> &M, const R *Mb, const R *x, R *y) {
+  FOR(i, M.m.nv) {
+    const int t = IF(dof_treeid)[i], a = IF(tree_dofadr)[t], n = IF(tree_dofnum)[t];
+    const R *row = Mb + IF(tree_madr)[t] + (i - a) * n;
+    R s = 0;
+    for (int j = 0; j < n; ++j) s += row[j] * x[a + j];
+    y[i] = s;
+  }
+}
+
+// ============================================================ collision
+template <class R, int T> __device__ void collision(const Mdl<R> &M, Arena<R> &A) {
+  const B200Model &m = M.m;
+  if (threadIdx.x == 0) A.iscal[8] = 0;
+  SYNC();
+  if (!(m.disable_flags & (B200_DSBL_CONSTRAINT | B200_DSBL_CONTACT))) {
+    FOR(p, m.npair) collide_pair(M, A, p);
+  }
+  SYNC();
+  const int n = mmin(A.iscal[8], m.ncon_max);
+  // deterministic order: rank of each contact's (pair, id) key
+  FOR(c, n) {
+    const int key = A.con_key[c];
+    int rank = 0;
+    for (int k = 0; k < n; ++k) rank += A.con_key[k] < key;
+    A.con_order[rank] = c;
+  }
+  if (threadIdx.x == 0) A.iscal[0] = n;
+  SYNC();
+}
+
+// ============================================================ constraints
+// mjwarp_constraint_build.cu:24-196
+template <class R> struct KBI { R k, b, imp; };
+template <class R> __device__ KBI<R> impedance(const B200Model &m, const R *ref, const R *imp, R position) {
+  const R minval = R(1e-15), minimp = R(0.0001), maximp = R(0.9999);
+  const bool refsafe = !(m.disable_flags & B200_DSBL_REFSAFE);
+  const R ts = R(m.timestep);
+  const R time = refsafe ? mmax(ref[0], R(2) * ts) : ref[0];
+  const R lo = mclamp(imp[0], minimp, maximp), hi = mclamp(imp[1], minimp, maximp);
+  const R width = mmax(minval, imp[2]), mid = mclamp(imp[3], minimp, maximp), power = mmax(R(1), imp[4]);
+  KBI<R> o;
+  o.k = ref[0] <= R(0) ? -ref[0] / mmax(minval, hi * hi) : R(1) / mmax(minval, hi * hi * time * time * ref[1] * ref[1]);
+  o.b = ref[1] <= R(0) ? -ref[1] / mmax(minval, hi) : R(2) / mmax(minval, hi * time);
+  const R x = mabs(position) / width;
+  if (lo == hi || imp[2] <= minval) o.imp = R(0.5) * (lo + hi);
+  else if (x <= R(0)) o.imp = lo;
+  else if (x >= R(1)) o.imp = hi;
+  else if (power == R(1)) o.imp = lo + x * (hi - lo);
+  else if (x <= mid) o.imp = mclamp(lo + (R(1) / mpow(mid, power - R(1))) * mpow(x, power) * (hi - lo), lo, hi);
+  else o.imp = mclamp(lo + (R(1) - (R(1) / mpow(R(1) - mid, power - R(1))) * mpow(R(1) - x, power)) * (hi - lo), lo, hi);
+  return o;
+}
+
+template <class R>
+__device__ void row_params(const B200Model &m, Arena<R> &A, int r, R pos, R imp_pos, R weight, const R *ref,
+                           const R *imp, R velocity, R friction, int type, int id) {
+  const KBI<R> kbi = impedance(m, ref, imp, imp_pos);
+  const R k = type == 1 ? R(0) : kbi.k;
+  A.efc_D[r] = R(1) / mmax(weight * (R(1) - kbi.imp) / kbi.imp, R(1e-15));
+  A.efc_aref[r] = -k * kbi.imp * pos - kbi.b * velocity;
+  A.efc_floss[r] = friction;
+  A.efc_type[r] = type;
+  A.efc_id[r] = id;
+}
+
+template <class R, int T> __device__ void constraints(const Mdl<R> &M, Arena<R> &A) {
+  const B200Model &m = M.m;
+  const int nv = m.nv, nvs = m.nvs, cap = m.nefc_max;
+  const bool off = m.disable_flags & B200_DSBL_CONSTRAINT;
+  const bool elliptic = m.cone == 1;
+  // row allocation is serial bookkeeping over a few dozen items (thread 0)
+  if (threadIdx.x == 0) {
+    int nefc = 0, nf = 0, of = 0;
+    if (!off && !(m.disable_flags & B200_DSBL_FRICTIONLOSS))
+      for (int k = 0; k < m.nfric; ++k) {
+        if (nefc >= cap) { of |= B200_OVERFLOW_NEFC; continue; }
+        A.efc_type[nefc] = 1;
+        A.efc_id[nefc] = IF(fric_dof)[k];
+        ++nefc; ++nf;
+      }
+    if (!off && !(m.disable_flags & B200_DSBL_LIMIT))
+      for (int k = 0; k < m.nlimited; ++k) {
+        const int j = IF(limited_jnt)[k];
+        const R *range = RF(jnt_range) + 2 * j;
+        const R q = A.qpos[IF(jnt_qposadr)[j]];
+        const R pos = mmin(q - range[0], range[1] - q) - RF(jnt_margin)[j];
+        if (!(pos < R(0))) continue;
+        if (nefc >= cap) { of |= B200_OVERFLOW_NEFC; continue; }
+        A.efc_type[nefc] = 3;
+        A.efc_id[nefc] = j;
+        ++nefc;
+      }
+    const int ncon = A.iscal[0];
+    for (int k = 0; k < ncon; ++k) {
+      const int c = A.con_order[k];
+      A.con_adr[c] = -1;
+      if (off || (m.disable_flags & B200_DSBL_CONTACT)) continue;
+      const R *cr = A.con + (size_t)c * kCWidth;
+      if (!(cr[kCDist] - cr[kCMargin] < R(0))) continue;
+      const int dim = A.con_dim[c], count = elliptic || dim == 1 ? dim : 2 * (dim - 1);
+      if (nefc + count > cap) { of |= B200_OVERFLOW_NEFC; continue; }
+      A.con_adr[c] = nefc;
+      const int type = dim == 1 ? 5 : (elliptic ? 7 : 6);
+      for (int i = 0; i < count; ++i) { A.efc_type[nefc + i] = type; A.efc_id[nefc + i] = c; }
+      nefc += count;
+    }
+    A.iscal[1] = nefc;
+    A.iscal[2] = nf;
+    A.iscal[3] |= of;
+  }
+  SYNC();
+  const int nefc = A.iscal[1];
+  // Jacobian rows, one (row, dof) per thread
+  FOR(w, nefc * nv) {
+    const int r = w / nv, d = w % nv, type = A.efc_type[r];
+    R v = 0;
+    if (type == 1) v = R(d == A.efc_id[r]);
+    else if (type == 3) {
+      const int j = A.efc_id[r];
+      if (d == IF(jnt_dofadr)[j]) {
+        const R *range = RF(jnt_range) + 2 * j;
+        const R q = A.qpos[IF(jnt_qposadr)[j]];
+        v = R((q - range[0]) < (range[1] - q)) * R(2) - R(1);
+      }
+    } else {
+      const int c = A.efc_id[r], comp = r - A.con_adr[c];
+      const R *cr = A.con + (size_t)c * kCWidth;
+      const int b1 = IF(geom_bodyid)[A.con_g1[c]], b2 = IF(geom_bodyid)[A.con_g2[c]];
+      const bool in1 = dof_ancestor(M, b1, d), in2 = dof_ancestor(M, b2, d);
+      if (in1 || in2) {
+        const V3<R> point = ld3(cr + kCPos);
+        const R *mo = A.cdof + 6 * d;
+        const V3<R> ang = v3<R>(mo[0], mo[1], mo[2]), lin = v3<R>(mo[3], mo[4], mo[5]);
+        V3<R> l = v3<R>(0, 0, 0), a = v3<R>(0, 0, 0);
+        if (in2) {
+          l = lin + cross(ang, point - ld3(A.com + 3 * IF(body_rootid)[b2]));
+          a = ang;
+        }
+        if (in1) {
+          l = l - (lin + cross(ang, point - ld3(A.com + 3 * IF(body_rootid)[b1])));
+          a = a - ang;
+        }
+        const int dim = A.con_dim[c];
+        if (elliptic) v = dot(comp < 3 ? l : a, ld3(cr + kCFrame + 3 * (comp % 3)));
+        else {
+          v = dot(l, ld3(cr + kCFrame));
+          if (dim > 1) {
+            const int dir = comp / 2 + 1;
+            const R fr = cr[kCFriction + dir - 1] * (R(1) - R(2) * R(comp & 1));
+            v += dot(dir < 3 ? l : a, ld3(cr + kCFrame + 3 * (dir % 3))) * fr;
+          }
+        }
+      }
+    }
+    A.J[(size_t)r * nvs + d] = v;
+  }
+  SYNC();
+  // row parameters (impedance, D, aref)
+  FOR(r, nefc) {
+    const int type = A.efc_type[r];
+    R jqv = 0;
+    for (int d = 0; d < nv; ++d) jqv += A.J[(size_t)r * nvs + d] * A.qvel[d];
+    if (type == 1) {
+      const int d = A.efc_id[r];
+      row_params(m, A, r, R(0), R(0), RF(dof_invweight0)[d], RF(dof_solref) + 2 * d, RF(dof_solimp) + 5 * d,
+                 A.qvel[d], RF(dof_frictionloss)[d], 1, d);
+    } else if (type == 3) {
+      const int j = A.efc_id[r], d = IF(jnt_dofadr)[j];
+      const R *range = RF(jnt_range) + 2 * j;
+      const R q = A.qpos[IF(jnt_qposadr)[j]];
+      const R pos = mmin(q - range[0], range[1] - q) - RF(jnt_margin)[j];
+      const R sign = R((q - range[0]) < (range[1] - q)) * R(2) - R(1);
+      row_params(m, A, r, pos, pos, RF(dof_invweight0)[d], RF(jnt_solref) + 2 * j, RF(jnt_solimp) + 5 * j,
+                 sign * A.qvel[d], R(0), 3, j);
+    } else {
+      const int c = A.efc_id[r], comp = r - A.con_adr[c], dim = A.con_dim[c];
+      const R *cr = A.con + (size_t)c * kCWidth;
+      const int b1 = IF(geom_bodyid)[A.con_g1[c]], b2 = IF(geom_bodyid)[A.con_g2[c]];
+      R weight = RF(body_invweight0)[2 * b1] + RF(body_invweight0)[2 * b2];
+      const R ratio = R(m.impratio_invsqrt), position = cr[kCDist] - cr[kCMargin];
+      const R *fr = cr + kCFriction;
+      R scale = 1, pos_aref = position;
+      if (elliptic && comp > 0) {
+        scale = ratio * ratio;
+        if (comp > 1) scale *= fr[0] * fr[0] / (fr[comp - 1] * fr[comp - 1]);
+        pos_aref = 0;
+      } else if (!elliptic && dim > 1) {
+        weight = weight + fr[0] * fr[0] * weight;
+        weight = weight * R(2) * fr[0] * fr[0] * ratio * ratio;
+      }
+      row_params(m, A, r, pos_aref, position, weight, cr + kCSolref, cr + kCSolimp, jqv, R(0), type, c);
+      if (elliptic && comp > 0) {
+        A.efc_D[r] /= scale;
+        const R *ref = cr + kCSolref;
+        if (cr[kCSolrefFriction] != R(0) || cr[kCSolrefFriction + 1] != R(0)) ref = cr + kCSolrefFriction;
+        A.efc_aref[r] = -impedance(m, ref, cr + kCSolimp, position).b * jqv;
+      }
+    }
+  }
+  SYNC();
+}
+
+// ============================================================ velocity stage
+// fused_motion.cu (cvel, cdof_dot, RNE bias), mjwarp_passive.cu, transmission
+template <class R> __device__ __forceinline__ void motion_cross(const R *v, const R *u, R *o) {
+  o[0] = -v[2] * u[1] + v[1] * u[2];
+  o[1] = v[2] * u[0] - v[0] * u[2];
+  o[2] = -v[1] * u[0] + v[0] * u[1];
+  o[3] = -v[2] * u[4] + v[1] * u[5] - v[5] * u[1] + v[4] * u[2];
+  o[4] = v[2] * u[3] - v[0] * u[5] + v[5] * u[0] - v[3] * u[2];
+  o[5] = -v[1] * u[3] + v[0] * u[4] - v[4] * u[0] + v[3] * u[1];
+}
+template <class R> __device__ __forceinline__ void force_cross(const R *v, const R *f, R *o) {
+  o[0] = -v[2] * f[1] + v[1] * f[2] - v[5] * f[4] + v[4] * f[5];
+  o[1] = v[2] * f[0] - v[0] * f[2] + v[5] * f[3] - v[3] * f[5];
+  o[2] = -v[1] * f[0] + v[0] * f[1] - v[4] * f[3] + v[3] * f[4];
+  o[3] = -v[2] * f[4] + v[1] * f[5];
+  o[4] = v[2] * f[3] - v[0] * f[5];
+  o[5] = -v[1] * f[3] + v[0] * f[4];
+}
+
+template <class R, int T> __device__ void velocity(const Mdl<R> &M, Arena<R> &A) {
+  const B200Model &m = M.m;
+  if (threadIdx.x < 6) {
+    const int c = threadIdx.x;
+    A.cvel[c] = 0;
+    R g = 0;
+    if (c >= 3 && !(m.disable_flags & B200_DSBL_GRAVITY))
+      g = -R(c == 3 ? m.gravity_x : c == 4 ? m.gravity_y : m.gravity_z);
+    A.cacc[c] = g;
+  }
+  SYNC();
+  const int *order = IF(body_order), *lstart = IF(level_start);
+  for (int level = 1; level < m.nlevel; ++level) {
+    const int a = lstart[level], n = lstart[level + 1] - a;
+    FOR(k, n) {
+      const int b = order[a + k], p = IF(body_parentid)[b];
+      R vel[6], acc[6];
+      for (int c = 0; c < 6; ++c) { vel[c] = A.cvel[6 * p + c]; acc[c] = A.cacc[6 * p + c]; }
+      int dof = IF(body_dofadr)[b];
+      const int j0 = IF(body_jntadr)[b], j1 = j0 + IF(body_jntnum)[b];
+      for (int j = j0; j < j1; ++j) {
+        const int type = IF(jnt_type)[j];
+        if (type == B200_JNT_FREE) {
+          for (int i = 0; i < 3; ++i) {
+            for (int c = 0; c < 6; ++c) vel[c] += A.cdof[6 * (dof + i) + c] * A.qvel[dof + i];
+            for (int c = 0; c < 6; ++c) A.cdof_dot[6 * (dof + i) + c] = 0;
+          }
+          dof += 3;
+        }
+        const int width = type == B200_JNT_FREE || type == B200_JNT_BALL ? 3 : 1;
+        for (int i = 0; i < width; ++i) {
+          R dd[6];
+          motion_cross(vel, A.cdof + 6 * (dof + i), dd);
+          for (int c = 0; c < 6; ++c) {
+            A.cdof_dot[6 * (dof + i) + c] = dd[c];
+            acc[c] += dd[c] * A.qvel[dof + i];
+          }
+        }
+        for (int i = 0; i < width; ++i)
+          for (int c = 0; c < 6; ++c) vel[c] += A.cdof[6 * (dof + i) + c] * A.qvel[dof + i];
+        dof += width;
+      }
+      for (int c = 0; c < 6; ++c) { A.cvel[6 * b + c] = vel[c]; A.cacc[6 * b + c] = acc[c]; }
+    }
+    SYNC();
+  }
+  // raw body forces (into cfrc), then subtree sums
+  FOR(b, m.nbody) {
+    R f[6], mom[6], corr[6];
+    if (b == 0) {
+      for (int c = 0; c < 6; ++c) A.cfrc[c] = 0;
+    } else {
+      inert_mul(A.cinert + 10 * b, A.cacc + 6 * b, f);
+      inert_mul(A.cinert + 10 * b, A.cvel + 6 * b, mom);
+      force_cross(A.cvel + 6 * b, mom, corr);
+      for (int c = 0; c < 6; ++c) A.cfrc[6 * b + c] = f[c] + corr[c];
+    }
+  }
+  SYNC();
+  // subtree composite into cacc (acceleration is no longer needed)
+  FOR(w, 6 * m.nbody) {
+    const int b = w / 6, c = w % 6;
+    R s = A.cfrc[w];
+    for (int k = b + 1; k < IF(body_subtree_end)[b]; ++k) s += A.cfrc[6 * k + c];
+    A.cacc[w] = s;
+  }
+  SYNC();
+  FOR(d, m.nv) {
+    const R *f = A.cacc + 6 * IF(dof_bodyid)[d];
+    R v = 0;
+    for (int c = 0; c < 6; ++c) v += A.cdof[6 * d + c] * f[c];
+    A.qfrc_bias[d] = v;
+    const R damping = RF(dof_damping)[d];
+    R force = 0;
+    if (!(m.disable_flags & B200_DSBL_DAMPER) && damping != R(0)) force = -A.qvel[d] * damping;
+    const int j = IF(dof_jntid)[d], kind = IF(jnt_type)[j];
+    const R stiff = RF(jnt_stiffness)[j];
+    if (!(m.disable_flags & B200_DSBL_SPRING) && stiff != R(0) && (kind == B200_JNT_SLIDE || kind == B200_JNT_HINGE)) {
+      const int p = IF(jnt_qposadr)[j];
+      force += -(A.qpos[p] - RF(qpos_spring)[p]) * stiff;
+    }
+    A.qfrc_passive[d] = force;
+  }
+  FOR(u, m.nu) {
+    const int j = IF(actuator_trnid)[u];
+    const R gear = RF(actuator_gear)[u];
+    A.act_length[u] = gear * A.qpos[IF(jnt_qposadr)[j]];
+    A.act_moment[u] = gear;
+  }
+  SYNC();
+}
+
+// ============================================================ OSC (FP64)
+// robosuite OSC_POSE as computed by the reference (fused_control_drive.cu:35-111,
+// osc_solver.cu:309-676).  Warp 0 computes; shared scratch aliases H.
+namespace osc {
+enum { kM = 0, kMi = 49, kN = 98, kJ = 147, kJT = 189, kMJT = 231, kJbar = 273, kA = 315, kLf = 351, kAp = 387,
+       kLp = 423, kAr = 459, kLr = 495, kMisc = 531 };
+}
+
+// one-sided Jacobi pseudoinverse of an n x n block (6-stride), one lane group
+// of 8 lanes, lane r owning row r (osc_solver.cu:120-253 pinv_group)
+__device__ void pinv_group(const double *in, double *out, int n, int lane8, unsigned mask, int *ok) {
+  double scale = 0;
+  if (lane8 < n)
+    for (int c = 0; c < n; ++c) scale = fmax(scale, fabs(in[lane8 * 6 + c]));
+  for (int o = 4; o > 0; o >>= 1) scale = fmax(scale, __shfl_xor_sync(mask, scale, o, 8));
+  for (int z = lane8; z < 36; z += 8) out[z] = 0;
+  if (!(scale > 0)) { *ok = 0; return; }
+  double b[6], v[6];
+  for (int c = 0; c < 6; ++c) {
+    b[c] = lane8 < n && c < n ? in[lane8 * 6 + c] / scale : 0.0;
+    v[c] = lane8 < n && c == lane8 ? 1.0 : 0.0;
+  }
+  bool converged = false;
+  for (int sweep = 0; sweep < 64; ++sweep) {
+    int rotations = 0;
+    for (int p = 0; p < n - 1; ++p)
+      for (int q = p + 1; q < n; ++q) {
+        double bp = 0, bq = 0, vp = 0, vq = 0;
+#pragma unroll
+        for (int c = 0; c < 6; ++c) {
+          if (c == p) { bp = b[c]; vp = v[c]; }
+          if (c == q) { bq = b[c]; vq = v[c]; }
+        }
+        double alpha = bp * bp, beta = bq * bq, gamma = bp * bq;
+        for (int o = 4; o > 0; o >>= 1) {
+          alpha += __shfl_xor_sync(mask, alpha, o, 8);
+          beta += __shfl_xor_sync(mask, beta, o, 8);
+          gamma += __shfl_xor_sync(mask, gamma, o, 8);
+        }
+        if (fabs(gamma) > DBL_EPSILON * sqrt(alpha) * sqrt(beta)) {
+          const double zeta = (beta - alpha) / (2 * gamma);
+          const double t = (zeta < 0 ? -1.0 : 1.0) / (fabs(zeta) + sqrt(1 + zeta * zeta));
+          const double c = 1 / sqrt(1 + t * t), s = c * t;
+          const double nbp = c * bp - s * bq, nbq = s * bp + c * bq, nvp = c * vp - s * vq, nvq = s * vp + c * vq;
+#pragma unroll
+          for (int k = 0; k < 6; ++k) {
+            if (k == p) { b[k] = nbp; v[k] = nvp; }
+            if (k == q) { b[k] = nbq; v[k] = nvq; }
+          }
+          ++rotations;
+        }
+      }
+    if (rotations == 0) { converged = true; break; }
+  }
+  double norms[6], sing[6], maxn = 0;
+  for (int p = 0; p < 6; ++p) {
+    double s = b[p] * b[p];
+    for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(mask, s, o, 8);
+    norms[p] = s;
+    sing[p] = sqrt(s);
+    if (p < n) maxn = fmax(maxn, sing[p]);
+  }
+  double maxcorr = 0;
+  for (int p = 0; p < n; ++p)
+    for (int q = p + 1; q < n; ++q) {
+      double g = b[p] * b[q];
+      for (int o = 4; o > 0; o >>= 1) g += __shfl_xor_sync(mask, g, o, 8);
+      if (sing[p] > 1e-15 * maxn && sing[q] > 1e-15 * maxn) maxcorr = fmax(maxcorr, fabs(g) / (sing[p] * sing[q]));
+    }
+  if (maxcorr < 2e-15) converged = true;
+  // out[row][col] = sum_k V[row][k] B[col][k] / (norm_k * scale); lane owns row
+  for (int c = 0; c < n; ++c) {
+    double val = 0;
+    for (int k = 0; k < n; ++k) {
+      const double bck = __shfl_sync(mask, b[k], c, 8);
+      if (sing[k] > 1e-15 * maxn) val += v[k] * bck * ((1 / norms[k]) / scale);
+    }
+    if (lane8 < n) out[lane8 * 6 + c] = val;
+  }
+  if (!converged) *ok = 0;
+}
+
+template <class R> __device__ R action_component(const Mdl<R> &M, R action, int axis) {
+  const R *p = RF(osc_action_config);
+  const R scale = mabs(p[18 + axis] - p[12 + axis]) / mabs(p[6 + axis] - p[axis]);
+  const R a = action != action ? action : mmin(p[6 + axis], mmax(p[axis], action));
+  return (a - (p[6 + axis] + p[axis]) * R(0.5)) * scale + (p[18 + axis] + p[12 + axis]) * R(0.5);
+}
+
+template <class R> __device__ void rotation_delta(R x, R y, R z, double *r) {
+  const R angle = msqrt(x * x + y * y + z * z);
+  const R f = angle == R(0) ? R(0) : msin(angle * R(0.5)) / angle;
+  const R raw[4] = {x * f, y * f, z * f, angle == R(0) ? R(1) : mcos(angle * R(0.5))};
+  float q[4] = {(float)raw[3], (float)raw[0], (float)raw[1], (float)raw[2]};
+  R acc = 0;
+  for (int i = 0; i < 4; ++i) acc += (R)(q[i] * q[i]);
+  const float norm = (float)acc;
+  const R factor = msqrt(R(2) / (R)norm);
+  for (int i = 0; i < 4; ++i) q[i] = (float)((R)q[i] * factor);
+  r[0] = (double)(R(1) - (R)(q[2] * q[2]) - (R)(q[3] * q[3]));
+  r[4] = (double)(R(1) - (R)(q[1] * q[1]) - (R)(q[3] * q[3]));
+  r[8] = (double)(R(1) - (R)(q[1] * q[1]) - (R)(q[2] * q[2]));
+  r[1] = (double)(R)(q[1] * q[2] - q[3] * q[0]);
+  r[2] = (double)(R)(q[1] * q[3] + q[2] * q[0]);
+  r[3] = (double)(R)(q[1] * q[2] + q[3] * q[0]);
+  r[5] = (double)(R)(q[2] * q[3] - q[1] * q[0]);
+  r[6] = (double)(R)(q[1] * q[3] - q[2] * q[0]);
+  r[7] = (double)(R)(q[2] * q[3] + q[1] * q[0]);
+}
+
+template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> &A, bool policy) {
+  const B200Model &m = M.m;
+  const int nv = m.nv, site = m.ee_site, body = IF(site_bodyid)[site];
+  const int *vi = IF(osc_dofadr), *qi = IF(osc_qposadr), *ids = IF(osc_actuator);
+  double *S = A.osc;
+  const int lane = threadIdx.x;
+  // ee velocity over all dofs (non-ancestors have zero Jacobian columns)
+  if (lane < 64) {  // two full warps: 8-lane groups, groups 6 and 7 idle
+    const int ax = lane / 8, l8 = lane & 7;
+    R v = 0;
+    const V3<R> point = ld3(A.sxpos + 3 * site), com = ld3(A.com + 3 * IF(body_rootid)[body]);
+    for (int d = l8; d < nv && ax < 6; d += 8) {
+      if (!dof_ancestor(M, body, d)) continue;
+      const R *mo = A.cdof + 6 * d;
+      R jv;
+      if (ax < 3) {
+        const V3<R> ang = v3<R>(mo[0], mo[1], mo[2]);
+        jv = mo[3 + ax] + cross(ang, point - com)[ax];
+      } else jv = mo[ax - 3];
+      v += jv * A.qvel[d];
+    }
+    for (int o = 4; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o, 8);
+    if (l8 == 0 && ax < 6) A.ee_vel[ax] = v;
+  }
+  // gathers: arm mass block, 6x7 Jacobian (and its transpose)
+  for (int z = lane; z < 49; z += T) S[osc::kM + z] = (double)mass_at(M, A.M, vi[z / 7], vi[z % 7]);
+  for (int z = lane; z < 42; z += T) {
+    const int ax = z / 7, d = vi[z % 7];
+    double jv = 0;
+    if (dof_ancestor(M, body, d)) {
+      const R *mo = A.cdof + 6 * d;
+      if (ax < 3) {
+        const V3<R> ang = v3<R>(mo[0], mo[1], mo[2]);
+        const V3<R> off = ld3(A.sxpos + 3 * site) - ld3(A.com + 3 * IF(body_rootid)[body]);
+        jv = (double)(mo[3 + ax] + cross(ang, off)[ax]);
+      } else jv = (double)mo[ax - 3];
+    }
+    S[osc::kJ + z] = jv;
+    S[osc::kJT + (z % 7) * 6 + ax] = jv;
+  }
+  SYNC();
+  int *err = &A.iscal[6];
+  if (*err) return;  // block-uniform
+  if (threadIdx.x < 32) {
+    // 7x7 inverse by Gauss-Jordan with partial pivoting, lane r owns row r of [M | I]
+    double row[14];
+    const int r = lane;
+    for (int c = 0; c < 7; ++c) row[c] = r < 7 ? S[osc::kM + r * 7 + c] : 0.0;
+    for (int c = 0; c < 7; ++c) row[7 + c] = r < 7 && c == r ? 1.0 : 0.0;
+    bool singular = false;
+    for (int c = 0; c < 7; ++c) {
+      double cand = r >= c && r < 7 ? fabs(row[c]) : -1.0;
+      int who = r;
+      for (int o = 16; o > 0; o >>= 1) {
+        const double oc = __shfl_xor_sync(0xffffffffu, cand, o);
+        const int ow = __shfl_xor_sync(0xffffffffu, who, o);
+        if (oc > cand || (oc == cand && ow < who)) { cand = oc; who = ow; }
+      }
+      if (cand == 0.0) singular = true;
+      // swap rows c and who
+      for (int k = 0; k < 14; ++k) {
+        const double mine = row[k];
+        const double atc = __shfl_sync(0xffffffffu, mine, c);
+        const double atw = __shfl_sync(0xffffffffu, mine, who);
+        if (r == c) row[k] = atw;
+        else if (r == who) row[k] = atc;
+      }
+      const double piv = __shfl_sync(0xffffffffu, row[c], c);
+      double prow[14];
+      for (int k = 0; k < 14; ++k) prow[k] = __shfl_sync(0xffffffffu, row[k], c) / piv;
+      if (r == c) for (int k = 0; k < 14; ++k) row[k] = prow[k];
+      else if (r < 7) {
+        const double f = row[c];
+        for (int k = 0; k < 14; ++k) row[k] -= f * prow[k];
+      }
+    }
+    if (r < 7) for (int c = 0; c < 7; ++c) S[osc::kMi + r * 7 + c] = row[7 + c];
+    if (lane == 0 && singular) *err = 2;
+  }
+  SYNC();
+  if (*err) return;
+  for (int z = lane; z < 42; z += T) {  // MJT = Mi JT (7x6)
+    const int r = z / 6, c = z % 6;
+    double v = 0;
+    for (int k = 0; k < 7; ++k) v += S[osc::kMi + r * 7 + k] * S[osc::kJT + k * 6 + c];
+    S[osc::kMJT + z] = v;
+  }
+  SYNC();
+  for (int z = lane; z < 36; z += T) {  // A = J MJT (6x6)
+    const int r = z / 6, c = z % 6;
+    double v = 0;
+    for (int k = 0; k < 7; ++k) v += S[osc::kJ + r * 7 + k] * S[osc::kMJT + k * 6 + c];
+    S[osc::kA + z] = v;
+  }
+  SYNC();
+  for (int z = lane; z < 36; z += T) {
+    const int r = z / 6, c = z % 6;
+    S[osc::kAp + z] = r < 3 && c < 3 ? S[osc::kA + z] : 0.0;
+    S[osc::kAr + z] = r < 3 && c < 3 ? S[osc::kA + (r + 3) * 6 + c + 3] : 0.0;
+  }
+  SYNC();
+  if (threadIdx.x < 32) {
+    __shared__ int ok_flags[3];
+    const int group = lane >> 3, l8 = lane & 7;
+    const unsigned mask = 0xffu << (lane & 24);
+    if (l8 == 0 && group < 3) ok_flags[group] = 1;
+    __syncwarp();
+    if (group == 0) pinv_group(S + osc::kA, S + osc::kLf, 6, l8, mask, &ok_flags[0]);
+    else if (group == 1) pinv_group(S + osc::kAp, S + osc::kLp, 3, l8, mask, &ok_flags[1]);
+    else if (group == 2) pinv_group(S + osc::kAr, S + osc::kLr, 3, l8, mask, &ok_flags[2]);
+    __syncwarp();
+    if (lane == 0 && !(ok_flags[0] && ok_flags[1] && ok_flags[2])) *err = 4;
+  }
+  SYNC();
+  if (*err) return;
+  for (int z = lane; z < 42; z += T) {  // Jbar = MJT Lf (7x6)
+    const int r = z / 6, c = z % 6;
+    double v = 0;
+    for (int k = 0; k < 6; ++k) v += S[osc::kMJT + r * 6 + k] * S[osc::kLf + k * 6 + c];
+    S[osc::kJbar + z] = v;
+  }
+  double *gp = S + osc::kMisc, *gr = gp + 3, *cur = gr + 9, *desired = cur + 9, *op = desired + 6, *opm = op + 6;
+  double *pd = opm + 7;
+  if (lane == 0) {
+    for (int r = 0; r < 3; ++r) gp[r] = (double)A.goal_pos[r];
+    for (int i = 0; i < 9; ++i) { gr[i] = (double)A.goal_rot[i]; cur[i] = (double)A.sxmat[9 * site + i]; }
+    if (policy) {
+      for (int r = 0; r < 3; ++r) gp[r] = (double)(R)(A.sxpos[3 * site + r] + action_component(M, A.action[r], r));
+      const R x = action_component(M, A.action[3], 3), y = action_component(M, A.action[4], 4),
+              z = action_component(M, A.action[5], 5);
+      if (x != R(0) || y != R(0) || z != R(0)) {
+        double d[9];
+        rotation_delta(x, y, z, d);
+        double g2[9];
+        for (int r = 0; r < 3; ++r)
+          for (int c = 0; c < 3; ++c) {
+            double v = 0;
+            for (int k = 0; k < 3; ++k) v += d[r * 3 + k] * cur[k * 3 + c];
+            g2[r * 3 + c] = v;
+          }
+        for (int i = 0; i < 9; ++i) gr[i] = sizeof(R) == 4 ? (double)(float)g2[i] : g2[i];
+      }
+    }
+  }
+  SYNC();
+  for (int z = lane; z < 49; z += T) {  // N = I - Jbar J (7x7)
+    const int r = z / 7, c = z % 7;
+    double v = 0;
+    for (int k = 0; k < 6; ++k) v += S[osc::kJbar + r * 6 + k] * S[osc::kJ + k * 7 + c];
+    S[osc::kN + z] = (r == c ? 1.0 : 0.0) - v;
+  }
+  const R *gains = RF(osc_gains), *q0 = RF(osc_q0), *nul = RF(osc_null);
+  if (lane < 3) {
+    const int r = lane, nx = (r + 1) % 3, ls = (r + 2) % 3;
+    double er = 0;
+    for (int c = 0; c < 3; ++c) er += 0.5 * (cur[nx * 3 + c] * gr[ls * 3 + c] - cur[ls * 3 + c] * gr[nx * 3 + c]);
+    const double ep = gp[r] - (double)A.sxpos[3 * site + r];
+    desired[r] = (double)gains[r] * ep - (double)gains[r + 6] * (double)A.ee_vel[r];
+    desired[r + 3] = (double)gains[r + 3] * er - (double)gains[r + 9] * (double)A.ee_vel[r + 3];
+  }
+  if (lane < 7)
+    pd[lane] = (double)nul[0] * ((double)q0[lane] - (double)A.qpos[qi[lane]]) - (double)nul[1] * (double)A.qvel[vi[lane]];
+  SYNC();
+  if (lane < 6) {
+    double v = 0;
+    if (m.osc_uncouple) {
+      const int row = lane % 3, offs = lane < 3 ? 0 : 3;
+      const double *lam = S + (lane < 3 ? osc::kLp : osc::kLr);
+      for (int k = 0; k < 3; ++k) v += lam[row * 6 + k] * desired[offs + k];
+    } else
+      for (int k = 0; k < 6; ++k) v += S[osc::kLf + lane * 6 + k] * desired[k];
+    op[lane] = v;
+  } else if (lane >= 32 && lane < 39) {
+    const int r = lane - 32;
+    double v = 0;
+    for (int k = 0; k < 7; ++k) v += S[osc::kM + r * 7 + k] * pd[k];
+    opm[r] = v;
+  }
+  SYNC();
+  if (lane < 7) {
+    const int i = lane;
+    double task = 0, post = 0;
+    for (int k = 0; k < 6; ++k) task += S[osc::kJT + i * 6 + k] * op[k];
+    for (int k = 0; k < 7; ++k) post += S[osc::kN + k * 7 + i] * opm[k];
+    const double t = task + (double)A.qfrc_bias[vi[i]] + post;
+    const R *rg = RF(actuator_ctrlrange) + 2 * ids[i];
+    const double lim = t != t ? t : fmin((double)rg[1], fmax((double)rg[0], t));
+    A.ctrl[ids[i]] = (R)lim;
+  }
+  FOR(i, 3) A.goal_pos[i] = (R)gp[i];
+  FOR(i, 9) A.goal_rot[i] = (R)gr[i];
+  if (lane == T - 1) {
+    const R a6 = A.action[6];
+    const R sgn = a6 != a6 ? a6 : (a6 > R(0) ? R(1) : (a6 < R(0) ? R(-1) : R(0)));
+    const R speed = RF(osc_action_config)[24];
+    for (int i = 0; i < 2; ++i) {
+      R v = A.gripper[i] + speed * (i == 0 ? R(-1) : R(1)) * sgn;
+      v = v != v ? v : mmin(R(1), mmax(R(-1), v));
+      A.gripper[i] = v;
+      const R *rg = RF(actuator_ctrlrange) + 2 * ids[7 + i];
+      A.ctrl[ids[7 + i]] = (rg[1] + rg[0]) * R(0.5) + (rg[1] - rg[0]) * R(0.5) * v;
+    }
+  }
+  SYNC();
+}
+
+// ============================================================ actuation
+template <class R, int T> __device__ void actuation(const Mdl<R> &M, Arena<R> &A) {
+  const B200Model &m = M.m;
+  FOR(d, m.nv) {
+    R f = 0;
+    for (int u = 0; u < m.nu; ++u) {
+      const int j = IF(actuator_trnid)[u];
+      if (IF(jnt_dofadr)[j] != d) continue;
+      R c = A.ctrl[u];
+      if (IF(actuator_ctrllimited)[u] && !(m.disable_flags & B200_DSBL_CLAMPCTRL)) {
+        const R *rg = RF(actuator_ctrlrange) + 2 * u;
+        c = mmin(mmax(rg[0], c), rg[1]);
+      }
+      const R *gp = RF(actuator_gainprm) + 3 * u, *bp = RF(actuator_biasprm) + 3 * u;
+      const R vel = A.act_moment[u] * A.qvel[d];
+      R gain = gp[0];
+      if (IF(actuator_gaintype)[u] == 1) gain = gp[0] + gp[1] * A.act_length[u] + gp[2] * vel;
+      R bias = 0;
+      if (IF(actuator_biastype)[u] == 1) bias = bp[0] + bp[1] * A.act_length[u] + bp[2] * vel;
+      R force = gain * c + bias;
+      if (IF(actuator_forcelimited)[u]) {
+        const R *fr = RF(actuator_forcerange) + 2 * u;
+        force = mmin(mmax(fr[0], force), fr[1]);
+      }
+      f += A.act_moment[u] * force;
+    }
+    A.qfrc_actuator[d] = f;
+    A.qfrc_smooth[d] = A.qfrc_passive[d] - A.qfrc_bias[d] + f;
+    A.qacc_smooth[d] = A.qfrc_smooth[d];
+  }
+  SYNC();
+  FOR(t, m.ntree) {
+    const int a = IF(tree_dofadr)[t], n = IF(tree_dofnum)[t], base = IF(tree_madr)[t];
+    chol_tree_solve(A.L + base, A.qacc_smooth + a, n);
+  }
+  SYNC();
+}
+
+// ============================================================ Newton
+// mjwarp_solver_state.cu, mjwarp_constraint.cu, mjwarp_hessian.cu,
+// mjwarp_direction.cu, mjwarp_linesearch.cu
+template <class R, int T> __device__ void eval_gradient(const Mdl<R> &M, Arena<R> &A) {
+  const B200Model &m = M.m;
+  const int nefc = A.iscal[1], nf = A.iscal[2], nv = m.nv, nvs = m.nvs;
+  const R impratio = R(m.impratio_invsqrt);
+  FOR(r, nefc) {
+    const R d = A.efc_D[r], res = A.efc_jaref[r];
+    R force;
+    int state;
+    if (r < nf) {
+      const R loss = A.efc_floss[r], radius = safe_div(loss, d);
+      if (res <= -radius) { force = loss; state = kLinearNeg; }
+      else if (res >= radius) { force = -loss; state = kLinearPos; }
+      else { force = -d * res; state = kQuadratic; }
+    } else if (A.efc_type[r] == 7) {
+      const int c = A.efc_id[r], head = A.con_adr[c], dim = A.con_dim[c];
+      const R *fr = A.con + (size_t)c * kCWidth + kCFriction;
+      const R mu = fr[0] * impratio, normal = A.efc_jaref[head], d0 = A.efc_D[head];
+      R tt = 0, tscale = 0;
+      for (int j = 1; j < dim; ++j) {
+        const R u = A.efc_jaref[head + j] * fr[j - 1];
+        tt += u * u;
+        if (r == head + j) tscale = u * fr[j - 1];
+      }
+      const R n = normal * mu, t = tt <= R(0) ? R(0) : msqrt(tt);
+      if (n >= mu * t || (t <= R(0) && n >= R(0))) { force = 0; state = kSatisfied; }
+      else if (mu * n + t <= R(0) || (t <= R(0) && n < R(0))) { force = -d * res; state = kQuadratic; }
+      else {
+        const R dm = safe_div(d0, mu * mu * (R(1) + mu * mu));
+        const R fn = -dm * (n - mu * t) * mu;
+        force = r == head ? fn : -safe_div(fn, t) * tscale;
+        state = kCone;
+      }
+    } else if (res >= R(0)) { force = 0; state = kSatisfied; }
+    else { force = -d * res; state = kQuadratic; }
+    A.efc_force[r] = force;
+    A.efc_state[r] = state;
+  }
+  SYNC();
+  R gd = 0;
+  FOR(i, nv) {
+    R tot = 0;
+    for (int r = 0; r < nefc; ++r) tot += A.J[(size_t)r * nvs + i] * A.efc_force[r];
+    A.qfrc_constraint[i] = tot;
+    const R g = A.Ma[i] - A.qfrc_smooth[i] - tot;
+    A.grad[i] = g;
+    gd += g * g;
+  }
+  gd = block_sum<R, T>(gd, A.red);
+  if (threadIdx.x == 0) A.scal[3] = gd;
+}
+
+template <class R, int T> __device__ void hessian(const Mdl<R> &M, Arena<R> &A) {
+  const B200Model &m = M.m;
+  const int nefc = A.iscal[1], nv = m.nv, nvs = m.nvs;
+  R *H = A.H;
+  // lower triangle H[i][j], j <= i
+  const int ntri = nv * (nv + 1) / 2;
+  const R impratio = R(m.impratio_invsqrt);
+  const int ncon = A.iscal[0];
+  FOR(e, ntri) {
+    int i = (int)((msqrt(8.0f * e + 1.0f) - 1.0f) * 0.5f);
+    while (i * (i + 1) / 2 > e) --i;
+    while ((i + 1) * (i + 2) / 2 <= e) ++i;
+    const int j = e - i * (i + 1) / 2;
+    R v = mass_at(M, A.M, i, j);
+    for (int r = 0; r < nefc; ++r)
+      if (A.efc_state[r] == kQuadratic) v += A.J[(size_t)r * nvs + i] * A.efc_D[r] * A.J[(size_t)r * nvs + j];
+    if (m.cone == 1)
+      for (int k = 0; k < ncon; ++k) {
+        const int c = A.con_order[k], head = A.con_adr[c], dim = A.con_dim[c];
+        if (head < 0 || dim == 1 || A.efc_state[head] != kCone) continue;
+        const R *fr = A.con + (size_t)c * kCWidth + kCFriction;
+        const R mu = fr[0] * impratio, mu2 = mu * mu, den = mu2 * (R(1) + mu2);
+        const R dm = A.efc_D[head] / (den != R(0) ? den : R(1e-15));
+        if (dm == R(0)) continue;
+        const R n = A.efc_jaref[head] * mu;
+        R tt = 0, p1 = 0, p2 = 0, td = 0;
+        for (int d = 1; d < dim; ++d) {
+          const R s = fr[d - 1], u = A.efc_jaref[head + d] * s;
+          const R z1 = s * A.J[(size_t)(head + d) * nvs + i], z2 = s * A.J[(size_t)(head + d) * nvs + j];
+          tt += u * u; p1 += u * z1; p2 += u * z2; td += z1 * z2;
+        }
+        const R t = mmax(msqrt(tt), R(1e-15)), it = R(1) / t, mnt = mu * n * it;
+        p1 *= it; p2 *= it;
+        const R z01 = mu * A.J[(size_t)head * nvs + i], z02 = mu * A.J[(size_t)head * nvs + j];
+        v += dm * (z01 * z02 - mu * (z01 * p2 + z02 * p1) + mnt * p1 * p2 + (mu2 - mnt) * td);
+      }
+    H[i * nvs + j] = v;
+  }
+  SYNC();
+}
+
+// Cholesky (lower, in place on H's lower triangle), then solve H x = grad;
+// search = -x (mjwarp_direction.cu:80-160)
+template <class R, int T> __device__ void direction(const Mdl<R> &M, Arena<R> &A) {
+  const int nv = M.m.nv, nvs = M.m.nvs;
+  R *H = A.H, *diag = A.Mv;  // Mv is free between line searches
+  for (int k = 0; k < nv; ++k) {
+    const R d = msqrt(H[k * nvs + k]);
+    const R inv = R(1) / d;
+    FOR(i, nv - k) {
+      if (i == 0) diag[k] = d;
+      else H[(k + i) * nvs + k] *= inv;
+    }
+    SYNC();
+    const int rest = nv - k - 1, cnt = rest * (rest + 1) / 2;
+    FOR(e, cnt) {
+      int ii = (int)((msqrt(8.0f * e + 1.0f) - 1.0f) * 0.5f);
+      while (ii * (ii + 1) / 2 > e) --ii;
+      while ((ii + 1) * (ii + 2) / 2 <= e) ++ii;
+      const int jj = e - ii * (ii + 1) / 2;
+      const int i = k + 1 + ii, j = k + 1 + jj;
+      H[i * nvs + j] -= H[i * nvs + k] * H[j * nvs + k];
+    }
+    SYNC();
+  }
+  // triangular solves in warp 0: lane i owns x[i], x[i+32], ...
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    R x[4];
+    for (int s = 0; s < 4; ++s) {
+      const int i = lane + 32 * s;
+      x[s] = i < nv ? A.grad[i] : R(0);
+    }
+    for (int k = 0; k < nv; ++k) {
+      const int owner = k & 31, slot = k >> 5;
+      R xk = 0;
+      for (int s = 0; s < 4; ++s)
+        if (s == slot) xk = x[s];
+      xk = __shfl_sync(0xffffffffu, xk, owner) / diag[k];
+      for (int s = 0; s < 4; ++s) {
+        const int i = lane + 32 * s;
+        if (i == k) x[s] = xk;
+        else if (i > k && i < nv) x[s] -= H[i * nvs + k] * xk;
+      }
+    }
+    for (int k = nv - 1; k >= 0; --k) {
+      const int owner = k & 31, slot = k >> 5;
+      R xk = 0;
+      for (int s = 0; s < 4; ++s)
+        if (s == slot) xk = x[s];
+      xk = __shfl_sync(0xffffffffu, xk, owner) / diag[k];
+      for (int s = 0; s < 4; ++s) {
+        const int i = lane + 32 * s;
+        if (i == k) x[s] = xk;
+        else if (i < k) x[s] -= H[k * nvs + i] * xk;
+      }
+    }
+    R sq = 0, dec = 0;
+    for (int s = 0; s < 4; ++s) {
+      const int i = lane + 32 * s;
+      if (i < nv) {
+        A.search[i] = -x[s];
+        sq += x[s] * x[s];
+        dec += A.grad[i] * x[s];
+      }
+    }
+    sq = warp_sum(sq);
+    dec = warp_sum(dec);
+    if (lane == 0) { A.scal[2] = sq; A.scal[4] = dec; }
+  }
+  SYNC();
+}
+
+// ---- exact line search (mjwarp_linesearch.cu:80-365), warp 0
+template <class R> struct Pt { R cost, slope, curv; };
+template <class R> __device__ __forceinline__ Pt<R> padd(Pt<R> a, Pt<R> b) {
+  return {a.cost + b.cost, a.slope + b.slope, a.curv + b.curv};
+}
+template <class R> __device__ __forceinline__ Pt<R> quadratic(R q1, R q2, R alpha) {
+  const R aq2 = alpha * q2;
+  return {alpha * aq2 + alpha * q1, R(2) * aq2 + q1, R(2) * q2};
+}
+template <class R> __device__ __forceinline__ bool in_bracket(Pt<R> x, Pt<R> y) {
+  return (x.slope < y.slope && y.slope < R(0)) || (x.slope > y.slope && y.slope > R(0));
+}
+template <class R> struct LsRow {
+  int kind, state0;
+  R x, v, d, loss, q0, q1, q2, u0, v0, uu, uv, vv, dm, mu, cost0, t0, r0;
+};
+template <class R> __device__ LsRow<R> load_row(const Mdl<R> &M, const Arena<R> &A, int r, int nf) {
+  LsRow<R> o;
+  o.kind = 0; o.state0 = 0;
+  o.x = o.v = o.d = o.loss = o.q0 = o.q1 = o.q2 = o.u0 = o.v0 = o.uu = o.uv = o.vv = o.dm = o.mu = o.cost0 = o.t0 = o.r0 = 0;
+  if (r < nf) o.kind = 1;
+  else if (A.efc_type[r] != 7) o.kind = 2;
+  else {
+    const int c = A.efc_id[r], head = A.con_adr[c];
+    if (r != head) { o.kind = 4; return o; }
+    o.kind = 3;
+    const R *qa = A.efc_quad + 3 * r, *qb = A.efc_quad + 3 * (head + 1), *qc = A.efc_quad + 3 * (head + 2);
+    o.q0 = qa[0]; o.q1 = qa[1]; o.q2 = qa[2];
+    o.u0 = qb[0]; o.v0 = qb[1]; o.uu = qb[2];
+    o.uv = qc[0]; o.vv = qc[1]; o.dm = qc[2];
+    o.mu = A.con[(size_t)c * kCWidth + kCFriction] * R(M.m.impratio_invsqrt);
+    if (o.uu <= R(0)) {
+      o.state0 = o.u0 < R(0) ? 1 : 0;
+      o.cost0 = o.state0 == 1 ? o.q0 : R(0);
+    } else {
+      o.t0 = msqrt(o.uu);
+      if (o.u0 >= o.mu * o.t0) o.state0 = 0;
+      else if (o.mu * o.u0 + o.t0 <= R(0)) { o.state0 = 1; o.cost0 = o.q0; }
+      else { o.state0 = 4; o.r0 = o.u0 - o.mu * o.t0; o.cost0 = R(0.5) * o.dm * o.r0 * o.r0; }
+    }
+    return o;
+  }
+  o.x = A.efc_jaref[r]; o.v = A.efc_jv[r]; o.d = A.efc_D[r];
+  if (o.kind == 1) o.loss = A.efc_floss[r];
+  return o;
+}
+template <class R> __device__ Pt<R> friction_point(const LsRow<R> &r, R x) {
+  const R rf = safe_div(r.loss, r.d);
+  if (-rf < x && x < rf) {
+    const R vd = r.v * r.d;
+    return {R(0.5) * r.d * x * x, vd * x, r.v * vd};
+  }
+  if (x <= -rf) return {r.loss * (R(-0.5) * rf - x), -r.loss * r.v, R(0)};
+  return {r.loss * (R(-0.5) * rf + x), r.loss * r.v, R(0)};
+}
+template <class R> __device__ Pt<R> eval_zero(const LsRow<R> &r) {
+  if (r.kind == 4) return {0, 0, 0};
+  if (r.kind == 3) {
+    if (r.state0 == 1) return {r.q0, r.q1, R(2) * r.q2};
+    if (r.state0 == 4) {
+      const R ti = R(1) / r.t0, t1 = r.uv * ti, t2 = (r.vv - t1 * t1) * ti, r1 = r.v0 - r.mu * t1;
+      return {r.cost0, r.dm * r.r0 * r1, r.dm * (r1 * r1 - r.mu * r.r0 * t2)};
+    }
+    return {0, 0, 0};
+  }
+  if (r.kind == 1) return friction_point(r, r.x);
+  if (r.kind == 2 && r.x >= R(0)) return {0, 0, 0};
+  const R vd = r.v * r.d;
+  return {R(0.5) * r.d * r.x * r.x, vd * r.x, r.v * vd};
+}
+template <class R> __device__ Pt<R> cone_quad_shift(const LsRow<R> &r, R alpha, R n, R tsqr) {
+  const R aq2 = alpha * r.q2;
+  R cost = alpha * (aq2 + r.q1);
+  if (r.state0 == 4) {
+    const R bd = r.mu * r.u0 + r.t0;
+    cost += R(0.5) * r.dm * bd * bd;
+  } else if (r.state0 == 0) cost = R(0.5) * r.dm * (R(1) + r.mu * r.mu) * (n * n + mmax(tsqr, R(0)));
+  return {cost, R(2) * aq2 + r.q1, R(2) * r.q2};
+}
+template <class R> __device__ Pt<R> eval_shift(const LsRow<R> &r, R alpha) {
+  if (r.kind == 4) return {0, 0, 0};
+  if (r.kind == 3) {
+    const R n = r.u0 + alpha * r.v0, tsd = alpha * (R(2) * r.uv + alpha * r.vv), tsqr = r.uu + tsd;
+    if (tsqr <= R(0)) {
+      if (n < R(0)) return cone_quad_shift(r, alpha, n, tsqr);
+    } else {
+      const R t = msqrt(tsqr);
+      if (n >= r.mu * t) {
+      } else if (r.mu * n + t <= R(0)) return cone_quad_shift(r, alpha, n, tsqr);
+      else {
+        const R ti = R(1) / t, t1 = (r.uv + alpha * r.vv) * ti, t2 = (r.vv - t1 * t1) * ti;
+        const R res = n - r.mu * t, r1 = r.v0 - r.mu * t1;
+        R cost;
+        if (r.state0 == 4) {
+          const R tdelta = tsd / (t + r.t0), rdelta = alpha * r.v0 - r.mu * tdelta;
+          cost = R(0.5) * r.dm * rdelta * (R(2) * r.r0 + rdelta);
+        } else if (r.state0 == 1) {
+          const R aq2 = alpha * r.q2, bd = r.mu * n + t;
+          cost = alpha * (aq2 + r.q1) - R(0.5) * r.dm * bd * bd;
+        } else cost = R(0.5) * r.dm * res * res;
+        return {cost, r.dm * res * r1, r.dm * (r1 * r1 + res * (-r.mu * t2))};
+      }
+    }
+    return {-r.cost0, 0, 0};
+  }
+  if (r.kind == 1) {
+    Pt<R> pt = friction_point(r, r.x + alpha * r.v);
+    pt.cost -= friction_point(r, r.x).cost;
+    return pt;
+  }
+  const R quad0 = R(0.5) * r.d * r.x * r.x;
+  const R cost0 = r.kind == 2 && r.x >= R(0) ? R(0) : quad0;
+  if (r.kind == 2 && r.x + alpha * r.v >= R(0)) return {-cost0, 0, 0};
+  const R vd = r.v * r.d, h = r.v * vd, ah = alpha * h;
+  return {alpha * (vd * r.x + R(0.5) * ah) + (quad0 - cost0), vd * r.x + ah, h};
+}
+template <class R> __device__ __forceinline__ Pt<R> warp_pt(Pt<R> p) {
+  return {warp_sum(p.cost), warp_sum(p.slope), warp_sum(p.curv)};
+}
+
+template <class R, int T> __device__ void linesearch(const Mdl<R> &M, Arena<R> &A) {
+  const B200Model &m = M.m;
+  const int nv = m.nv, nvs = m.nvs, nefc = A.iscal[1], nf = A.iscal[2];
+  mass_mul<R, T>(M, A.M, A.search, A.Mv);
+  FOR(r, nefc) {
+    R s = 0;
+    for (int i = 0; i < nv; ++i) s += A.J[(size_t)r * nvs + i] * A.search[i];
+    A.efc_jv[r] = s;
+  }
+  SYNC();
+  const R impratio = R(m.impratio_invsqrt);
+  FOR(r, nefc) {
+    if (A.efc_type[r] != 7) continue;
+    const int c = A.efc_id[r];
+    if (r != A.con_adr[c]) continue;
+    const R *fr = A.con + (size_t)c * kCWidth + kCFriction;
+    const R x = A.efc_jaref[r], v = A.efc_jv[r], d = A.efc_D[r], vd = v * d;
+    R q0 = R(0.5) * x * x * d, q1 = vd * x, q2 = R(0.5) * v * vd;
+    const R mu = fr[0] * impratio, u0 = x * mu, v0 = v * mu;
+    R uu = 0, uv = 0, vv = 0;
+    for (int j = 1; j < A.con_dim[c]; ++j) {
+      const int t = r + j;
+      const R jv = A.efc_jv[t], ja = A.efc_jaref[t], dj = A.efc_D[t], djx = dj * ja;
+      q0 += R(0.5) * ja * djx; q1 += jv * djx; q2 += R(0.5) * jv * dj * jv;
+      const R uj = ja * fr[j - 1], vj = jv * fr[j - 1];
+      uu += uj * uj; uv += uj * vj; vv += vj * vj;
+    }
+    R *q = A.efc_quad + 3 * r;
+    q[0] = q0; q[1] = q1; q[2] = q2;
+    q[3] = u0; q[4] = v0; q[5] = uu;
+    q[6] = uv; q[7] = vv;
+    const R mu2 = mu * mu;
+    q[8] = d / (mu2 * (R(1) + mu2));
+  }
+  SYNC();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const R tol = R(m.tolerance), lstol = R(m.ls_tolerance), scale = R(m.meaninertia) * R(nv);
+    const R gtol = mmax(tol * lstol * msqrt(A.scal[2]) * scale, R(1e-6));
+    R g1 = 0, g2 = 0;
+    for (int i = lane; i < nv; i += 32) {
+      g1 += A.search[i] * (A.Ma[i] - A.qfrc_smooth[i]);
+      g2 += R(0.5) * A.search[i] * A.Mv[i];
+    }
+    g1 = warp_sum(g1);
+    g2 = warp_sum(g2);
+    Pt<R> loc = {0, 0, 0};
+    for (int r = lane; r < nefc; r += 32) loc = padd(loc, eval_zero(load_row(M, A, r, nf)));
+    const Pt<R> rows = warp_pt(loc);
+    int evals = 1;
+    const Pt<R> p0 = {rows.cost, g1 + rows.slope, R(2) * g2 + rows.curv};
+    const Pt<R> delta = {0, p0.slope, p0.curv};
+    const R noise = R(8) * R(FLT_EPSILON);
+    const R q1abs = msqrt(R(2) * mmax(rows.cost, R(0)) * mmax(rows.curv, R(0))) + mabs(g1);
+    const R gacc = mmax(gtol, noise * q1abs);
+    R alpha = 0, improvement = 0;
+    bool converged = mabs(p0.slope) < noise * q1abs;
+    const R a0 = -safe_div(p0.slope, p0.curv);
+    Pt<R> init = {0, 0, 0};
+    if (!converged) {
+      loc = {0, 0, 0};
+      for (int r = lane; r < nefc; r += 32) loc = padd(loc, eval_shift(load_row(M, A, r, nf), a0));
+      init = padd(quadratic(g1, g2, a0), warp_pt(loc));
+      ++evals;
+      if (mabs(init.slope) < gacc && init.cost < R(0)) { converged = true; alpha = a0; improvement = -init.cost; }
+    }
+    if (!converged) {
+      const bool less = init.slope < p0.slope;
+      Pt<R> lo = less ? init : delta, hi = less ? delta : init;
+      R la = less ? a0 : R(0), ha = less ? R(0) : a0;
+      for (int it = 0; it < m.ls_iterations; ++it) {
+        const R ln = la - safe_div(lo.slope, lo.curv), hn = ha - safe_div(hi.slope, hi.curv), ma = R(0.5) * (la + ha);
+        Pt<R> sl = {0, 0, 0}, sh = {0, 0, 0}, sm = {0, 0, 0};
+        for (int r = lane; r < nefc; r += 32) {
+          const LsRow<R> row = load_row(M, A, r, nf);
+          sl = padd(sl, eval_shift(row, ln));
+          sh = padd(sh, eval_shift(row, hn));
+          sm = padd(sm, eval_shift(row, ma));
+        }
+        const Pt<R> nl = padd(quadratic(g1, g2, ln), warp_pt(sl));
+        const Pt<R> nh = padd(quadratic(g1, g2, hn), warp_pt(sh));
+        const Pt<R> mid = padd(quadratic(g1, g2, ma), warp_pt(sm));
+        evals += 3;
+        const bool cl = mabs(nl.slope) < gacc && nl.cost < R(0), ch = mabs(nh.slope) < gacc && nh.cost < R(0);
+        const bool cm = mabs(mid.slope) < gacc && mid.cost < R(0);
+        const bool any = cl || ch || cm;
+        bool slo = false, shi = false;
+        if (any) {
+          Pt<R> best = {R(1e10), 0, 0};
+          R ba = 0;
+          if (cl && nl.cost < best.cost) { best = nl; ba = ln; }
+          if (ch && nh.cost < best.cost) { best = nh; ba = hn; }
+          if (cm && mid.cost < best.cost) { best = mid; ba = ma; }
+          lo = hi = best;
+          la = ha = ba;
+        } else {
+          bool s;
+          s = in_bracket(lo, nl); if (s) { lo = nl; la = ln; } slo |= s;
+          s = in_bracket(lo, mid); if (s) { lo = mid; la = ma; } slo |= s;
+          s = in_bracket(lo, nh); if (s) { lo = nh; la = hn; } slo |= s;
+          s = in_bracket(hi, nh) || (hi.slope < R(0) && nh.slope > R(0)); if (s) { hi = nh; ha = hn; } shi |= s;
+          s = in_bracket(hi, mid); if (s) { hi = mid; ha = ma; } shi |= s;
+          s = in_bracket(hi, nl); if (s) { hi = nl; ha = ln; } shi |= s;
+        }
+        const bool done = any || (!slo && !shi) || (lo.cost < R(0) && lo.slope < R(0) && lo.slope > -gtol) ||
+                          (hi.cost < R(0) && hi.slope > R(0) && hi.slope < gtol);
+        if (lo.cost < R(0) || hi.cost < R(0)) {
+          const bool bl = lo.cost < hi.cost;
+          alpha = bl ? la : ha;
+          improvement = -(bl ? lo.cost : hi.cost);
+        }
+        if (done) { converged = true; break; }
+      }
+    }
+    if (lane == 0) {
+      A.scal[0] = alpha;
+      A.scal[1] = improvement;
+      A.iscal[7] += evals;
+      if (!converged) A.iscal[3] |= B200_OVERFLOW_LS_ITERATIONS;
+    }
+  }
+  SYNC();
+  const R alpha = A.scal[0];
+  FOR(i, nv) {
+    A.qacc[i] += alpha * A.search[i];
+    A.Ma[i] += alpha * A.Mv[i];
+  }
+  FOR(r, nefc) A.efc_jaref[r] += alpha * A.efc_jv[r];
+  SYNC();
+}
+
+template <class R, int T> __device__ void newton(const Mdl<R> &M, Arena<R> &A) {
+  const B200Model &m = M.m;
+  const int nv = m.nv, nvs = m.nvs, nefc = A.iscal[1];
+  const bool warm = !(m.disable_flags & B200_DSBL_WARMSTART);
+  FOR(i, nv) A.qacc[i] = warm && nefc > 0 ? A.warm[i] : A.qacc_smooth[i];
+  SYNC();
+  mass_mul<R, T>(M, A.M, A.qacc, A.Ma);
+  FOR(r, nefc) {
+    R s = 0;
+    for (int i = 0; i < nv; ++i) s += A.J[(size_t)r * nvs + i] * A.qacc[i];
+    A.efc_jaref[r] = s - A.efc_aref[r];
+  }
+  if (threadIdx.x == 0) { A.iscal[4] = 0; A.iscal[5] = 0; }
+  SYNC();
+  eval_gradient<R, T>(M, A);
+  hessian<R, T>(M, A);
+  direction<R, T>(M, A);
+  if (m.iterations == 0) return;
+  const R tol = R(m.tolerance), scale = R(m.meaninertia) * R(nv);
+  for (;;) {
+    linesearch<R, T>(M, A);
+    eval_gradient<R, T>(M, A);
+    hessian<R, T>(M, A);
+    direction<R, T>(M, A);
+    if (threadIdx.x == 0) {
+      const int it = ++A.iscal[4];
+      const R imp = A.scal[1] / scale, grad = msqrt(A.scal[3]) / scale, model = (R(0.5) * A.scal[4]) / scale;
+      const bool done = A.scal[0] == R(0) || (imp > R(0) && imp < tol) || grad < tol || model < tol;
+      if (done || it >= m.iterations) {
+        if (!done) A.iscal[3] |= B200_OVERFLOW_ITERATIONS;
+        A.iscal[5] = 1;
+      }
+    }
+    SYNC();
+    if (A.iscal[5]) break;
+  }
+}
+
+// ============================================================ Euler
+template <class R, int T> __device__ void euler(const Mdl<R> &M, Arena<R> &A) {
+  const B200Model &m = M.m;
+  const int nv = m.nv;
+  const R dt = R(m.timestep);
+  const bool damped = !(m.disable_flags & (B200_DSBL_EULERDAMP | B200_DSBL_DAMPER));
+  // the mass factor is dead after the smooth solve: reuse it for M + dt*D
+  R *acc = A.Mv;
+  if (damped) {
+    FOR(k, m.nM) A.H[k] = A.M[k];
+    SYNC();
+    FOR(d, nv) {
+      const int t = IF(dof_treeid)[d], a = IF(tree_dofadr)[t], n = IF(tree_dofnum)[t];
+      A.H[IF(tree_madr)[t] + (d - a) * n + (d - a)] += dt * RF(dof_damping)[d];
+      acc[d] = A.Ma[d];
+    }
+    SYNC();
+    FOR(t, m.ntree) {
+      const int a = IF(tree_dofadr)[t], n = IF(tree_dofnum)[t], base = IF(tree_madr)[t];
+      chol_tree(A.H + base, A.L + base, n);
+      chol_tree_solve(A.L + base, acc + a, n);
+    }
+  } else
+    FOR(d, nv) acc[d] = A.qacc[d];
+  SYNC();
+  FOR(d, nv) {
+    A.warm[d] = A.qacc[d];
+    A.qvel[d] = A.qvel[d] + acc[d] * dt;
+  }
+  SYNC();
+  FOR(j, m.njnt) {
+    const int kind = IF(jnt_type)[j];
+    R *q = A.qpos + IF(jnt_qposadr)[j];
+    const R *v = A.qvel + IF(jnt_dofadr)[j];
+    if (kind == B200_JNT_FREE) {
+      q[0] += dt * v[0]; q[1] += dt * v[1]; q[2] += dt * v[2];
+      q += 3; v += 3;
+    }
+    if (kind == B200_JNT_FREE || kind == B200_JNT_BALL) {
+      const R len = msqrt(v[0] * v[0] + v[1] * v[1] + v[2] * v[2]);
+      R x = 0, y = 0, z = 0;
+      if (len > R(0)) { x = v[0] / len; y = v[1] / len; z = v[2] / len; }
+      const R ang = dt * len, s = msin(ang * R(0.5)), c = mcos(ang * R(0.5));
+      const Q4<R> r = qnormalize(qmul(qnormalize(ldq(q)), Q4<R>{c, x * s, y * s, z * s}));
+      stq(q, r);
+    } else q[0] += dt * v[0];
+  }
+  if (threadIdx.x == 0) A.scal[5] += dt;
+  SYNC();
+}
+
+// ============================================================ driver
+template <class R> __device__ __forceinline__ R *row_of(void *p, int w, int width) {
+  return p ? (R *)p + (size_t)w * width : nullptr;
+}
+__device__ __forceinline__ int *irow_of(int *p, int w, int width) {
+  return p ? p + (size_t)w * width : nullptr;
+}
+
+template <class R, int T> __device__ void load_world(const B200Model &m, const B200Data &d, Arena<R> &A, int w) {
+  const R *src;
+  src = row_of<R>(d.qpos, w, m.nq); FOR(i, m.nq) A.qpos[i] = src[i];
+  src = row_of<R>(d.qvel, w, m.nv); FOR(i, m.nv) A.qvel[i] = src[i];
+  src = row_of<R>(d.qacc_warmstart, w, m.nv); FOR(i, m.nv) A.warm[i] = src[i];
+  src = row_of<R>(d.ctrl, w, m.nu); FOR(i, m.nu) A.ctrl[i] = src[i];
+  src = row_of<R>(d.goal_pos, w, 3); FOR(i, 3) A.goal_pos[i] = src[i];
+  src = row_of<R>(d.goal_rot, w, 9); FOR(i, 9) A.goal_rot[i] = src[i];
+  src = row_of<R>(d.gripper, w, 2); FOR(i, 2) A.gripper[i] = src[i];
+  if (d.action) { src = row_of<R>(d.action, w, 7); FOR(i, 7) A.action[i] = src[i]; }
+  else FOR(i, 7) A.action[i] = 0;
+  if (threadIdx.x == 0) {
+    A.scal[5] = row_of<R>(d.time, w, 1)[0];
+    for (int k = 0; k < 12; ++k) A.iscal[k] = 0;
+    A.iscal[3] = irow_of(d.overflow, w, 1)[0];
+    A.iscal[6] = irow_of(d.error, w, 1)[0];
+  }
+  SYNC();
+}
+
+template <class R, int T> __device__ void store_state(const B200Model &m, const B200Data &d, Arena<R> &A, int w) {
+  R *dst;
+  dst = row_of<R>(d.qpos, w, m.nq); FOR(i, m.nq) dst[i] = A.qpos[i];
+  dst = row_of<R>(d.qvel, w, m.nv); FOR(i, m.nv) dst[i] = A.qvel[i];
+  dst = row_of<R>(d.qacc_warmstart, w, m.nv); FOR(i, m.nv) dst[i] = A.warm[i];
+  dst = row_of<R>(d.ctrl, w, m.nu); FOR(i, m.nu) dst[i] = A.ctrl[i];
+  dst = row_of<R>(d.goal_pos, w, 3); FOR(i, 3) dst[i] = A.goal_pos[i];
+  dst = row_of<R>(d.goal_rot, w, 9); FOR(i, 9) dst[i] = A.goal_rot[i];
+  dst = row_of<R>(d.gripper, w, 2); FOR(i, 2) dst[i] = A.gripper[i];
+  if ((dst = row_of<R>(d.qacc, w, m.nv))) FOR(i, m.nv) dst[i] = A.qacc[i];
+  if (threadIdx.x == 0) {
+    row_of<R>(d.time, w, 1)[0] = A.scal[5];
+    irow_of(d.overflow, w, 1)[0] = A.iscal[3];
+    irow_of(d.error, w, 1)[0] = A.iscal[6];
+  }
+}
+
+// derived outputs of the last substep (pre-integration, as MuJoCo publishes)
+template <class R, int T> __device__ void store_outputs(const B200Model &m, const B200Data &d, Arena<R> &A, int w) {
+  R *dst;
+  const int nb = m.nbody, ng = m.ngeom, ns = m.nsite, nv = m.nv, nc = m.ncon_max;
+  if ((dst = row_of<R>(d.xpos, w, nb * 3))) FOR(i, nb * 3) dst[i] = A.xpos[i];
+  if ((dst = row_of<R>(d.xquat, w, nb * 4))) FOR(i, nb * 4) dst[i] = A.xquat[i];
+  if ((dst = row_of<R>(d.xmat, w, nb * 9))) FOR(i, nb * 9) dst[i] = A.xmat[i];
+  if ((dst = row_of<R>(d.geom_xpos, w, ng * 3))) FOR(i, ng * 3) dst[i] = A.gxpos[i];
+  if ((dst = row_of<R>(d.geom_xmat, w, ng * 9))) FOR(i, ng * 9) dst[i] = A.gxmat[i];
+  if ((dst = row_of<R>(d.site_xpos, w, ns * 3))) FOR(i, ns * 3) dst[i] = A.sxpos[i];
+  if ((dst = row_of<R>(d.site_xmat, w, ns * 9))) FOR(i, ns * 9) dst[i] = A.sxmat[i];
+  if ((dst = row_of<R>(d.subtree_com, w, nb * 3))) FOR(i, nb * 3) dst[i] = A.com[i];
+  if ((dst = row_of<R>(d.qfrc_bias, w, nv))) FOR(i, nv) dst[i] = A.qfrc_bias[i];
+  if ((dst = row_of<R>(d.qfrc_actuator, w, nv))) FOR(i, nv) dst[i] = A.qfrc_actuator[i];
+  if ((dst = row_of<R>(d.qfrc_constraint, w, nv))) FOR(i, nv) dst[i] = A.qfrc_constraint[i];
+  if ((dst = row_of<R>(d.qacc_smooth, w, nv))) FOR(i, nv) dst[i] = A.qacc_smooth[i];
+  const int ncon = A.iscal[0], nefc = A.iscal[1];
+  if ((dst = row_of<R>(d.con_dist, w, nc))) FOR(k, ncon) dst[k] = A.con[(size_t)A.con_order[k] * kCWidth + kCDist];
+  if ((dst = row_of<R>(d.con_pos, w, nc * 3)))
+    FOR(e, ncon * 3) dst[e] = A.con[(size_t)A.con_order[e / 3] * kCWidth + kCPos + e % 3];
+  if ((dst = row_of<R>(d.con_frame, w, nc * 9)))
+    FOR(e, ncon * 9) dst[e] = A.con[(size_t)A.con_order[e / 9] * kCWidth + kCFrame + e % 9];
+  if ((dst = row_of<R>(d.efc_force, w, m.nefc_max))) FOR(r, nefc) dst[r] = A.efc_force[r];
+  int *idst;
+  if ((idst = irow_of(d.con_geom, w, nc * 2)))
+    FOR(e, ncon * 2) idst[e] = e & 1 ? A.con_g2[A.con_order[e >> 1]] : A.con_g1[A.con_order[e >> 1]];
+  if (threadIdx.x == 0) {
+    if (d.ncon) irow_of(d.ncon, w, 1)[0] = ncon;
+    if (d.nefc) irow_of(d.nefc, w, 1)[0] = nefc;
+  }
+}
+
+template <class R, int T> __device__ void step1(const Mdl<R> &M, Arena<R> &A) {
+  kinematics<R, T>(M, A);
+  com_crb_mass<R, T>(M, A);
+  FOR(t, M.m.ntree) {
+    const int base = IF(tree_madr)[t];
+    chol_tree(A.M + base, A.L + base, IF(tree_dofnum)[t]);
+  }
+  collision<R, T>(M, A);
+  constraints<R, T>(M, A);
+  velocity<R, T>(M, A);
+}
+
+template <class R, int T>
+__global__ void __launch_bounds__(T) control_step(const B200Model m, const B200Data d, int substeps, int policy) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int w = blockIdx.x;
+  if (w >= d.nworld) return;
+  Arena<R> A;
+  Arena<R>::layout(m, T, &A, smem);
+  const Mdl<R> M(m);
+  load_world<R, T>(m, d, A, w);
+  for (int s = 0; s < substeps; ++s) {
+    step1<R, T>(M, A);
+    osc_control<R, T>(M, A, policy && s == 0);
+    actuation<R, T>(M, A);
+    newton<R, T>(M, A);
+    if (threadIdx.x == 0) {
+      if (d.niter) irow_of(d.niter, w, 1)[0] = A.iscal[4];
+      if (d.newton_total) irow_of(d.newton_total, w, 1)[0] += A.iscal[4];
+    }
+    if (s == substeps - 1) store_outputs<R, T>(m, d, A, w);
+    euler<R, T>(M, A);
+  }
+  if (threadIdx.x == 0) {
+    if (d.ls_total) irow_of(d.ls_total, w, 1)[0] += A.iscal[7];
+    if (d.integration_count) irow_of(d.integration_count, w, 1)[0] += substeps;
+  }
+  store_state<R, T>(m, d, A, w);
+}
+
+template <class R, int T>
+__global__ void __launch_bounds__(T) forward_step(const B200Model m, const B200Data d, int bootstrap, const int *mask) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int w = blockIdx.x;
+  if (w >= d.nworld || (mask && !mask[w])) return;
+  Arena<R> A;
+  Arena<R>::layout(m, T, &A, smem);
+  const Mdl<R> M(m);
+  load_world<R, T>(m, d, A, w);
+  step1<R, T>(M, A);
+  if (bootstrap) {
+    FOR(i, 3) A.goal_pos[i] = A.sxpos[3 * m.ee_site + i];
+    FOR(i, 9) A.goal_rot[i] = A.sxmat[9 * m.ee_site + i];
+    FOR(i, 2) A.gripper[i] = 0;
+    if (threadIdx.x == 0) A.iscal[6] = 0;
+    SYNC();
+  }
+  actuation<R, T>(M, A);
+  newton<R, T>(M, A);
+  store_outputs<R, T>(m, d, A, w);
+  store_state<R, T>(m, d, A, w);
+}
+
+}  // namespace b200
+
+// ============================================================ C ABI
+namespace {
+constexpr int kThreads = 128;
+
+bool model_ok(const B200Model *m) {
+  return m && m->real && m->ints && (m->real_bytes == 4 || m->real_bytes == 8) && m->nv >= 1 && m->nv <= 128 &&
+         m->nbody >= 2 && m->ncon_max >= 1 && m->nefc_max >= 1 && m->nvs >= m->nv && m->nsite > m->ee_site &&
+         m->nu >= 9;
+}
+bool data_ok(const B200Data *d) {
+  return d && d->nworld >= 0 && d->qpos && d->qvel && d->qacc_warmstart && d->ctrl && d->time && d->goal_pos &&
+         d->goal_rot && d->gripper && d->overflow && d->error;
+}
+size_t smem_for(const B200Model *m) {
+  return m->real_bytes == 4 ? b200::Arena<float>::layout(*m, kThreads, nullptr, nullptr)
+                            : b200::Arena<double>::layout(*m, kThreads, nullptr, nullptr);
+}
+template <class K> int configure(K kernel, size_t smem) {
+  static int max_optin = -1;
+  if (max_optin < 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  }
+  if ((int)smem > max_optin) return (int)cudaErrorInvalidValue;
+  return (int)cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+}  // namespace
+
+extern "C" {
+const char *b200phys_source_id(void) { return B200PHYS_SOURCE_ID; }
+int b200phys_arch(void) { return 100; }
+size_t b200phys_model_bytes(void) { return sizeof(B200Model); }
+size_t b200phys_data_bytes(void) { return sizeof(B200Data); }
+size_t b200phys_world_smem_bytes(const B200Model *m) { return model_ok(m) ? smem_for(m) : 0; }
+
+int b200phys_prepare(const B200Model *m) {
+  if (!model_ok(m)) return (int)cudaErrorInvalidValue;
+  const size_t smem = smem_for(m);
+  int rc;
+  if (m->real_bytes == 4) {
+    if ((rc = configure(b200::control_step<float, kThreads>, smem))) return rc;
+    return configure(b200::forward_step<float, kThreads>, smem);
+  }
+  if ((rc = configure(b200::control_step<double, kThreads>, smem))) return rc;
+  return configure(b200::forward_step<double, kThreads>, smem);
+}
+
+int b200phys_step_launch(const B200Model *m, const B200Data *d, int substeps, int policy, void *stream) {
+  if (!model_ok(m) || !data_ok(d) || substeps < 0) return (int)cudaErrorInvalidValue;
+  if (d->nworld == 0 || substeps == 0) return 0;
+  const size_t smem = smem_for(m);
+  cudaStream_t s = (cudaStream_t)stream;
+  int rc;
+  if (m->real_bytes == 4) {
+    auto k = b200::control_step<float, kThreads>;
+    if ((rc = configure(k, smem))) return rc;
+    k<<<d->nworld, kThreads, smem, s>>>(*m, *d, substeps, policy);
+  } else {
+    auto k = b200::control_step<double, kThreads>;
+    if ((rc = configure(k, smem))) return rc;
+    k<<<d->nworld, kThreads, smem, s>>>(*m, *d, substeps, policy);
+  }
+  return (int)cudaGetLastError();
+}
+
+int b200phys_forward_launch(const B200Model *m, const B200Data *d, int bootstrap, const int *mask, void *stream) {
+  if (!model_ok(m) || !data_ok(d)) return (int)cudaErrorInvalidValue;
+  if (d->nworld == 0) return 0;
+  const size_t smem = smem_for(m);
+  cudaStream_t s = (cudaStream_t)stream;
+  int rc;
+  if (m->real_bytes == 4) {
+    auto k = b200::forward_step<float, kThreads>;
+    if ((rc = configure(k, smem))) return rc;
+    k<<<d->nworld, kThreads, smem, s>>>(*m, *d, bootstrap, mask);
+  } else {
+    auto k = b200::forward_step<double, kThreads>;
+    if ((rc = configure(k, smem))) return rc;
+    k<<<d->nworld, kThreads, smem, s>>>(*m, *d, bootstrap, mask);
+  }
+  return (int)cudaGetLastError();
+}
+}

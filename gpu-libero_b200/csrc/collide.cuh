@@ -1,0 +1,523 @@
+// Per-pair collision for one world: broadphase filters and primitive
+// narrowphase.  One thread owns one candidate pair; contacts are appended to
+// the world's shared-memory contact table and later ordered by
+// (pair index, collision id), which makes the per-world contact list
+// deterministic (the reference appends to a global pool with atomics:
+// libero/libero/gpu/cuda/collision/mjwarp_broadphase.cu:110,
+// mjwarp_contact.cuh:107).
+//
+// The decision steps are those of the reference colliders, because contact
+// lists must agree exactly:
+//   filters   mjwarp_broadphase.cu:21-96 (plane / bounding sphere / 6-axis OBB)
+//   plane     mjwarp_plane.cu:18-60 (sphere, capsule, box)
+//   box       mjwarp_box.cu:14-176 (sphere-box, capsule-box, box-box SAT+clip)
+//   material  mjwarp_contact.cuh:60-98
+#pragma once
+#include "arena.cuh"
+#include "math.cuh"
+
+namespace b200 {
+
+template <class R> struct Mdl {
+  const B200Model &m;
+  const R *f;
+  const int *i;
+  __device__ Mdl(const B200Model &m_) : m(m_), f((const R *)m_.real), i(m_.ints) {}
+};
+#define RF(name) (M.f + M.m.off_##name)
+#define IF(name) (M.i + M.m.off_##name)
+
+template <class R> struct Material {
+  int dim;
+  R margin, gap, friction[5], solref[2], solreffriction[2], solimp[5];
+};
+
+template <class R> __device__ Material<R> material(const Mdl<R> &M, int g1, int g2) {
+  Material<R> p;
+  p.margin = RF(geom_margin)[g1] + RF(geom_margin)[g2];
+  p.gap = RF(geom_gap)[g1] + RF(geom_gap)[g2];
+  R m1 = RF(geom_solmix)[g1], m2 = RF(geom_solmix)[g2], mix;
+  const R *f1 = RF(geom_friction) + 3 * g1, *f2 = RF(geom_friction) + 3 * g2;
+  R f[3];
+  const int p1 = IF(geom_priority)[g1], p2 = IF(geom_priority)[g2];
+  const int c1 = IF(geom_condim)[g1], c2 = IF(geom_condim)[g2];
+  if (p1 > p2) {
+    mix = 1; p.dim = c1;
+    for (int c = 0; c < 3; ++c) f[c] = f1[c];
+  } else if (p2 > p1) {
+    mix = 0; p.dim = c2;
+    for (int c = 0; c < 3; ++c) f[c] = f2[c];
+  } else {
+    mix = m1 + m2 != R(0) ? m1 / (m1 + m2) : R(0);
+    if (m1 < R(1e-15) && m2 < R(1e-15)) mix = R(0.5);
+    if (m1 < R(1e-15) && m2 >= R(1e-15)) mix = 0;
+    if (m1 >= R(1e-15) && m2 < R(1e-15)) mix = 1;
+    p.dim = c1 > c2 ? c1 : c2;
+    for (int c = 0; c < 3; ++c) f[c] = mmax(f1[c], f2[c]);
+  }
+  p.friction[0] = f[0]; p.friction[1] = f[0]; p.friction[2] = f[1]; p.friction[3] = f[2]; p.friction[4] = f[2];
+  const R *r1 = RF(geom_solref) + 2 * g1, *r2 = RF(geom_solref) + 2 * g2;
+  const R *i1 = RF(geom_solimp) + 5 * g1, *i2 = RF(geom_solimp) + 5 * g2;
+  for (int c = 0; c < 2; ++c) {
+    p.solref[c] = r1[0] > R(0) && r2[0] > R(0) ? mix * r1[c] + (R(1) - mix) * r2[c] : mmin(r1[c], r2[c]);
+    p.solreffriction[c] = 0;
+  }
+  for (int c = 0; c < 5; ++c) p.solimp[c] = mix * i1[c] + (R(1) - mix) * i2[c];
+  for (int c = 0; c < 5; ++c) p.friction[c] = mmax(R(1e-5), p.friction[c]);
+  return p;
+}
+
+template <class R> __device__ void frame_from_normal(V3<R> a, V3<R> *f) {
+  a = normalize(a);
+  V3<R> b = (R(-0.5) < a.y && a.y < R(0.5)) ? v3<R>(0, 1, 0) : v3<R>(0, 0, 1);
+  b = normalize(b - a * dot(a, b));
+  if (msqrt(dot(a, a)) == R(0)) b = v3<R>(0, 0, 0);
+  f[0] = a; f[1] = b; f[2] = cross(a, b);
+}
+
+// Append one contact if it is within margin+gap. Returns nothing; capacity
+// overflow sets the world's narrowphase overflow bit.
+template <class R>
+__device__ void emit(const Mdl<R> &M, Arena<R> &A, const Material<R> &p, int pair, int id, int g1, int g2, R dist,
+                     V3<R> pos, const V3<R> *frame) {
+  if (!(dist < p.margin + p.gap)) return;
+  int slot = atomicAdd(&A.iscal[8], 1);
+  if (slot >= M.m.ncon_max) {
+    atomicOr(&A.iscal[3], B200_OVERFLOW_NARROWPHASE);
+    return;
+  }
+  R *c = A.con + (size_t)slot * kCWidth;
+  c[kCDist] = dist;
+  st3(c + kCPos, pos);
+  st3(c + kCFrame, frame[0]); st3(c + kCFrame + 3, frame[1]); st3(c + kCFrame + 6, frame[2]);
+  c[kCMargin] = p.margin;
+  for (int k = 0; k < 5; ++k) { c[kCFriction + k] = p.friction[k]; c[kCSolimp + k] = p.solimp[k]; }
+  for (int k = 0; k < 2; ++k) { c[kCSolref + k] = p.solref[k]; c[kCSolrefFriction + k] = p.solreffriction[k]; }
+  A.con_dim[slot] = p.dim;
+  A.con_g1[slot] = g1;
+  A.con_g2[slot] = g2;
+  A.con_key[slot] = pair * 16 + id;
+}
+
+// ---------------------------------------------------------------- filters
+template <class R> __device__ bool obb_overlap(V3<R> c1, V3<R> c2, V3<R> s1, V3<R> s2, R margin, V3<R> p1, V3<R> p2,
+                                               const R *R1, const R *R2) {
+  V3<R> cen[2] = {rot(R1, c1) + p1, rot(R2, c2) + p2};
+  V3<R> nrm[6] = {col(R1, 0), col(R1, 1), col(R1, 2), col(R2, 0), col(R2, 1), col(R2, 2)};
+  V3<R> siz[2] = {s1, s2};
+  for (int j = 0; j < 2; ++j)
+    for (int a = 0; a < 3; ++a) {
+      const V3<R> axis = nrm[3 * j + a];
+      R proj[2], rad[2];
+      for (int i = 0; i < 2; ++i) {
+        proj[i] = dot(cen[i], axis);
+        rad[i] = mabs(siz[i].x * dot(nrm[3 * i], axis)) + mabs(siz[i].y * dot(nrm[3 * i + 1], axis)) +
+                 mabs(siz[i].z * dot(nrm[3 * i + 2], axis));
+      }
+      if (rad[0] + rad[1] + margin < mabs(proj[1] - proj[0])) return false;
+    }
+  return true;
+}
+
+template <class R> __device__ bool candidate(const Mdl<R> &M, const Arena<R> &A, int g1, int g2) {
+  const R *aabb = RF(geom_aabb);
+  const R r1 = RF(geom_rbound)[g1], r2 = RF(geom_rbound)[g2];
+  const R m1 = RF(geom_margin)[g1] + RF(geom_gap)[g1], m2 = RF(geom_margin)[g2] + RF(geom_gap)[g2];
+  const V3<R> p1 = ld3(A.gxpos + 3 * g1), p2 = ld3(A.gxpos + 3 * g2);
+  const R *R1 = A.gxmat + 9 * g1, *R2 = A.gxmat + 9 * g2;
+  if (r1 == R(0)) return dot(p2 - p1, col(R1, 2)) <= r2 + m1 + m2;
+  if (r2 == R(0)) return dot(p1 - p2, col(R2, 2)) <= r1 + m1 + m2;
+  const R bound = r1 + r2 + m1 + m2;
+  const V3<R> d = p2 - p1;
+  if (!(dot(d, d) <= bound * bound)) return false;
+  return obb_overlap(ld3(aabb + 6 * g1), ld3(aabb + 6 * g2), ld3(aabb + 6 * g1 + 3), ld3(aabb + 6 * g2 + 3), m1 + m2,
+                     p1, p2, R1, R2);
+}
+
+// ---------------------------------------------------------------- plane
+template <class R>
+__device__ void plane_pair(const Mdl<R> &M, Arena<R> &A, int pair, int g1, int g2) {
+  const Material<R> p = material(M, g1, g2);
+  const V3<R> o = ld3(A.gxpos + 3 * g1), c = ld3(A.gxpos + 3 * g2), n = col(A.gxmat + 9 * g1, 2);
+  const R *Rg = A.gxmat + 9 * g2;
+  const V3<R> size = ld3(RF(geom_size) + 3 * g2);
+  const int type = IF(geom_type)[g2];
+  V3<R> fr[3];
+  if (type == B200_GEOM_SPHERE) {
+    frame_from_normal(n, fr);
+    const R d = dot(c - o, n) - size.x;
+    emit(M, A, p, pair, 0, g1, g2, d, c - n * (size.x + R(0.5) * d), fr);
+  } else if (type == B200_GEOM_CAPSULE) {
+    const V3<R> ax = col(Rg, 2);
+    const V3<R> t = ax - n * dot(n, ax);
+    const R len = msqrt(dot(t, t));
+    V3<R> b = len == R(0) ? t : t * (R(1) / len);
+    if (len < R(0.5)) b = (R(-0.5) < n.y && n.y < R(0.5)) ? v3<R>(0, 1, 0) : v3<R>(0, 0, 1);
+    fr[0] = n; fr[1] = b; fr[2] = cross(n, b);
+    for (int e = 0; e < 2; ++e) {
+      const V3<R> end = e == 0 ? c + ax * size.y : c - ax * size.y;
+      const R d = dot(end - o, n) - size.x;
+      emit(M, A, p, pair, e, g1, g2, d, end - n * (size.x + R(0.5) * d), fr);
+    }
+  } else if (type == B200_GEOM_BOX) {
+    frame_from_normal(n, fr);
+    const R cd = dot(c - o, n);
+    for (int i = 0; i < 8; ++i) {
+      const V3<R> corner = rot(Rg, v3<R>(i & 1 ? size.x : -size.x, i & 2 ? size.y : -size.y, i & 4 ? size.z : -size.z));
+      const R d = cd + dot(n, corner);
+      emit(M, A, p, pair, i, g1, g2, d, corner + c - n * (R(0.5) * d), fr);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- box family
+template <class R> struct BoxHits {
+  int count;
+  R dist[8];
+  V3<R> pos[8], normal[8];
+};
+
+template <class R>
+__device__ void sphere_box(BoxHits<R> &o, int id, V3<R> sphere, R radius, V3<R> center, const R *Rb, V3<R> size) {
+  const V3<R> local = rotT(Rb, sphere - center);
+  V3<R> clamped;
+  for (int c = 0; c < 3; ++c) clamped[c] = mclamp(local[c], -size[c], size[c]);
+  V3<R> dir = clamped - local;
+  const R dist = msqrt(dot(dir, dir));
+  dir = dist == R(0) ? dir : dir * (R(1) / dist);
+  V3<R> pos, normal;
+  if (dist <= R(1e-15)) {
+    R closest = R(2) * (size.x + size.y + size.z);
+    int face = 0;
+    for (int i = 0; i < 6; ++i) {
+      const R d = mabs((i % 2 ? R(1) : R(-1)) * size[i / 2] - local[i / 2]);
+      if (closest > d) { closest = d; face = i; }
+    }
+    V3<R> nearest = v3<R>(0, 0, 0);
+    nearest[face / 2] = face % 2 ? R(-1) : R(1);
+    pos = local + nearest * ((radius - closest) * R(0.5));
+    normal = rot(Rb, nearest);
+    o.dist[id] = -closest - radius;
+  } else {
+    const V3<R> deepest = local + dir * radius;
+    pos = (clamped + deepest) * R(0.5);
+    normal = rot(Rb, dir);
+    o.dist[id] = dist - radius;
+  }
+  o.pos[id] = center + rot(Rb, pos);
+  o.normal[id] = normal;
+}
+
+template <class R>
+__device__ void capsule_box(BoxHits<R> &o, V3<R> center, V3<R> axis, R radius, R hl, V3<R> bc, const R *Rb, V3<R> size) {
+  o.count = 2;
+  const V3<R> pos = rotT(Rb, center - bc);
+  axis = rotT(Rb, axis);
+  const V3<R> ha = axis * hl;
+  const int axisdir = int(ha.x > R(0)) + 2 * int(ha.y > R(0)) + 4 * int(ha.z > R(0));
+  R bestdist = R(1e32), bestseg = R(-12), bestbox = 0;
+  int type = -4, face = -12, corner = -123, edge = -123;
+  for (int i = -1; i <= 1; i += 2) {
+    const V3<R> tip = pos + ha * R(i);
+    V3<R> point = tip;
+    int outside = 0, ax = -1;
+    for (int j = 0; j < 3; ++j) {
+      if (point[j] < -size[j]) { ++outside; ax = j; point[j] = -size[j]; }
+      else if (point[j] > size[j]) { ++outside; ax = j; point[j] = size[j]; }
+    }
+    if (outside > 1) continue;
+    const V3<R> dif = point - tip;
+    const R d = dot(dif, dif);
+    if (d < bestdist) { bestdist = d; bestseg = R(i); type = -2 + i; face = ax; }
+  }
+  for (int i = 0; i < 8; ++i)
+    for (int j = 0; j < 3; ++j) {
+      if (i & (1 << j)) continue;
+      V3<R> point = v3<R>((i & 1 ? R(1) : R(-1)) * size.x, (i & 2 ? R(1) : R(-1)) * size.y, (i & 4 ? R(1) : R(-1)) * size.z);
+      point[j] = 0;
+      V3<R> dif = point - pos;
+      const R u = -size[j] * dif[j], v = dot(ha, dif), ma = size[j] * size[j], mb = -size[j] * ha[j], mc = hl * hl;
+      const R det = ma * mc - mb * mb;
+      if (mabs(det) < R(1e-15)) continue;
+      const R inv = R(1) / det;
+      R x1 = (mc * u - mb * v) * inv, x2 = (ma * v - mb * u) * inv;
+      int s1 = 1, s2 = 1;
+      if (x1 > R(1)) { x1 = 1; s1 = 2; x2 = safe_div(v - mb, mc); }
+      else if (x1 < R(-1)) { x1 = -1; s1 = 0; x2 = safe_div(v + mb, mc); }
+      const bool over = x2 > R(1);
+      if (over || x2 < R(-1)) {
+        if (over) { x2 = 1; s2 = 2; x1 = safe_div(u - mb, ma); }
+        else { x2 = -1; s2 = 0; x1 = safe_div(u + mb, ma); }
+        if (x1 > R(1)) { x1 = 1; s1 = 2; } else if (x1 < R(-1)) { x1 = -1; s1 = 0; }
+      }
+      dif = dif - ha * x2;
+      dif[j] += size[j] * x1;
+      const R d = dot(dif, dif);
+      const int config = s1 * 3 + s2;
+      if (d < bestdist - R(1e-15)) {
+        bestdist = d; bestseg = x2; bestbox = x1; corner = i + (1 << j) * (config / 6); edge = j; type = config;
+      }
+    }
+  if (type == -4) { o.count = 0; return; }
+  R second = -4;
+  if (type >= 0 && type / 3 != 1) {
+    int config = axisdir ^ corner;
+    if (config != 0 && config != 7) {
+      int mul;
+      if (config == 1 || config == 2 || config == 4) mul = 1;
+      else { mul = -1; config = 7 - config; }
+      const int ax = config == 1 ? 0 : config == 2 ? 1 : 2, ax1 = (ax + 1) % 3, ax2 = (ax + 2) % 3;
+      if (axis[ax] * axis[ax] > R(0.5)) {
+        const R mm = R(2) * safe_div(size[ax], mabs(ha[ax]));
+        second = mmin(R(1) - R(mul) * bestseg, mm);
+      } else {
+        const R mm = R(2) * mmin(safe_div(size[ax1], mabs(ha[ax1])), safe_div(size[ax2], mabs(ha[ax2])));
+        second = -mmin(R(1) + R(mul) * bestseg, mm);
+      }
+      second *= R(mul);
+    }
+  } else if (type >= 0 && type / 3 == 1) {
+    const int config = (axisdir ^ corner) & (7 - (1 << edge));
+    if (config == 1 || config == 2 || config == 4) {
+      const int ax = edge;
+      int ax1 = (edge + 1) % 3, ax2 = (edge + 2) % 3;
+      if (mabs(axis[ax1]) > mabs(axis[ax2])) ax1 = ax2;
+      ax2 = 3 - ax - ax1;
+      int mul;
+      if (config & (1 << ax2)) { mul = 1; second = R(1) - bestseg; }
+      else { mul = -1; second = R(1) + bestseg; }
+      R e1 = R(2) * safe_div(size[ax2], mabs(ha[ax2]));
+      second = mmin(e1, second);
+      const R e2 = bool(axisdir & (1 << ax)) == bool(config & (1 << ax2)) ? R(1) - bestbox : R(1) + bestbox;
+      e1 = size[ax] * safe_div(e2, mabs(ha[ax]));
+      second = mmin(e1, second);
+      second *= R(mul);
+    }
+  } else if (type < 0 && face != -1) {
+    const int mul = type == -3 ? 1 : -1;
+    second = 2;
+    const V3<R> tmp = pos - ha * R(mul);
+    for (int i = 0; i < 3; ++i)
+      if (i != face) {
+        const R inv = safe_div(R(mul), ha[i]);
+        R e1 = (size[i] - tmp[i]) * inv;
+        if (R(0) < e1 && e1 < second) second = e1;
+        e1 = (-size[i] - tmp[i]) * inv;
+        if (R(0) < e1 && e1 < second) second = e1;
+      }
+    second *= R(mul);
+  }
+  sphere_box(o, 0, rot(Rb, pos + ha * bestseg) + bc, radius, bc, Rb, size);
+  if (second > R(-3)) sphere_box(o, 1, rot(Rb, pos + ha * (second + bestseg)) + bc, radius, bc, Rb, size);
+  else o.dist[1] = R(1e10);
+}
+
+template <class R> __device__ int clip_poly(int count, V3<R> *poly, int coord, R sign, R limit) {
+  R d[8];
+  bool inside = true;
+  for (int i = 0; i < count; ++i) {
+    d[i] = sign * poly[i][coord] - limit;
+    if (!(d[i] <= R(0))) inside = false;
+  }
+  if (inside) return count;
+  V3<R> out[8];
+  for (int i = 0; i < 8; ++i) out[i] = v3<R>(0, 0, 0);
+  int n = 0;
+  for (int i = 0; i < count; ++i) {
+    const int nx = i + 1 == count ? 0 : i + 1;
+    const R dp = d[i], dq = d[nx];
+    if (dp <= R(0) && n < 8) out[n++] = poly[i];
+    if (((dp < R(0) && dq > R(0)) || (dp > R(0) && dq < R(0))) && n < 8) {
+      const R t = dp / (dp - dq);
+      out[n++] = poly[i] + (poly[nx] - poly[i]) * t;
+    }
+  }
+  for (int i = 0; i < 8; ++i) poly[i] = out[i];
+  return n;
+}
+
+template <class R>
+__device__ void box_box(BoxHits<R> &o, V3<R> p1, const R *R1, V3<R> s1, V3<R> p2, const R *R2, V3<R> s2, R margin) {
+  o.count = 0;
+  const V3<R> pos21 = rotT(R1, p2 - p1), pos12 = rotT(R2, p1 - p2);
+  R rm[9], ab[9];
+  for (int i = 0; i < 3; ++i)
+    for (int j = 0; j < 3; ++j) {
+      rm[3 * i + j] = dot(col(R1, i), col(R2, j));
+      ab[3 * i + j] = mabs(rm[3 * i + j]);
+    }
+  const R septol = margin + R(1e-6) * (s1.x + s1.y + s1.z + s2.x + s2.y + s2.z);
+  R best = R(-1e10);
+  int code = -1;
+  for (int i = 0; i < 3; ++i) {
+    const R rad = ab[3 * i] * s2.x + ab[3 * i + 1] * s2.y + ab[3 * i + 2] * s2.z;
+    const R sep = mabs(pos21[i]) - s1[i] - rad;
+    if (sep > septol) return;
+    if (sep > best) { best = sep; code = i; }
+  }
+  for (int j = 0; j < 3; ++j) {
+    const R rad = ab[j] * s1.x + ab[3 + j] * s1.y + ab[6 + j] * s1.z;
+    const R sep = mabs(pos12[j]) - s2[j] - rad;
+    if (sep > septol) return;
+    if (sep > best) { best = sep; code = 3 + j; }
+  }
+  const R face_best = best;
+  const int face_code = code;
+  for (int i = 0; i < 3; ++i)
+    for (int j = 0; j < 3; ++j) {
+      const int i1 = (i + 1) % 3, i2 = (i + 2) % 3;
+      R x = -rm[3 * i2 + j], y = rm[3 * i1 + j];
+      const R n2 = x * x + y * y;
+      if (n2 < R(1e-7)) continue;
+      const R inv = R(1) / msqrt(n2);
+      x *= inv; y *= inv;
+      const R rad1 = s1[i1] * mabs(x) + s1[i2] * mabs(y);
+      const int j1 = (j + 1) % 3, j2 = (j + 2) % 3;
+      const R a1 = x * rm[3 * i1 + j1] + y * rm[3 * i2 + j1], a2 = x * rm[3 * i1 + j2] + y * rm[3 * i2 + j2];
+      const R rad2 = s2[j1] * mabs(a1) + s2[j2] * mabs(a2);
+      const R sep = mabs(x * pos21[i1] + y * pos21[i2]) - rad1 - rad2;
+      if (sep > septol) return;
+      if (sep - R(1e-6) * mabs(sep) > best && sep > face_best) { best = sep; code = 6 + 3 * i + j; }
+    }
+  if (code < 0) return;
+  int ei = 0, ej = 0, i1 = 0, i2 = 0;
+  V3<R> axis = v3<R>(0, 0, 0);
+  if (code >= 6) {
+    ei = (code - 6) / 3; ej = (code - 6) % 3; i1 = (ei + 1) % 3; i2 = (ei + 2) % 3;
+    axis[i1] = -rm[3 * i2 + ej];
+    axis[i2] = rm[3 * i1 + ej];
+    axis = normalize(axis);
+    const R align = face_code < 3 ? mabs(axis[face_code]) : mabs(dot(axis, col(rm, face_code - 3)));
+    if (align > R(0.99) && best < face_best + R(0.05) * mabs(face_best) + R(1e-15)) { code = face_code; best = face_best; }
+  }
+  if (code >= 6) {
+    const int j1 = (ej + 1) % 3, j2 = (ej + 2) % 3;
+    if (dot(axis, pos21) < R(0)) axis = -axis;
+    const V3<R> a2 = rotT(rm, axis);
+    int amb1 = -1, amb2 = -1;
+    if (mabs(axis[i1]) < R(1e-5)) amb1 = i1; else if (mabs(axis[i2]) < R(1e-5)) amb1 = i2;
+    if (mabs(a2[j1]) < R(1e-5)) amb2 = j1; else if (mabs(a2[j2]) < R(1e-5)) amb2 = j2;
+    const V3<R> d2 = col(rm, ej);
+    const R b = d2[ei], denom = R(1) - b * b;
+    R best_dist = R(1e10);
+    V3<R> w1 = v3<R>(0, 0, 0), w2 = v3<R>(0, 0, 0);
+    for (int u1 = 0; u1 < (amb1 >= 0 ? 2 : 1); ++u1)
+      for (int u2 = 0; u2 < (amb2 >= 0 ? 2 : 1); ++u2) {
+        V3<R> c1 = v3<R>(0, 0, 0);
+        c1[i1] = axis[i1] >= R(0) ? s1[i1] : -s1[i1];
+        c1[i2] = axis[i2] >= R(0) ? s1[i2] : -s1[i2];
+        if (amb1 >= 0 && u1) c1[amb1] = -c1[amb1];
+        V3<R> cr = v3<R>(0, 0, 0);
+        cr[j1] = a2[j1] >= R(0) ? -s2[j1] : s2[j1];
+        cr[j2] = a2[j2] >= R(0) ? -s2[j2] : s2[j2];
+        if (amb2 >= 0 && u2) cr[amb2] = -cr[amb2];
+        const V3<R> c2 = rot(rm, cr) + pos21, e = c2 - c1;
+        const R d1e = e[ei], d2e = dot(d2, e);
+        R s = denom >= R(1e-15) ? (d1e - b * d2e) / denom : R(0);
+        s = mclamp(s, -s1[ei], s1[ei]);
+        const R t = mclamp(b * s - d2e, -s2[ej], s2[ej]);
+        s = mclamp(d1e + b * t, -s1[ei], s1[ei]);
+        V3<R> q1 = c1;
+        q1[ei] = s;
+        const V3<R> q2 = c2 + d2 * t, gap = q2 - q1;
+        const R dd = dot(gap, gap);
+        if (dd < best_dist) { best_dist = dd; w1 = q1; w2 = q2; }
+      }
+    const R dist = dot(w2 - w1, axis);
+    if (dist > septol) return;
+    o.count = 1;
+    o.dist[0] = dist;
+    o.pos[0] = rot(R1, (w1 + w2) * R(0.5)) + p1;
+    o.normal[0] = rot(R1, axis);
+    return;
+  }
+  const bool ref1 = code < 3;
+  const int a = ref1 ? code : code - 3;
+  const V3<R> sref = ref1 ? s1 : s2, sinc = ref1 ? s2 : s1, pref = ref1 ? p1 : p2, posoi = ref1 ? pos21 : pos12;
+  const R *matref = ref1 ? R1 : R2;
+  R rinc[9];
+  for (int i = 0; i < 3; ++i)
+    for (int j = 0; j < 3; ++j) rinc[3 * i + j] = ref1 ? rm[3 * i + j] : rm[3 * j + i];
+  const R sign = posoi[a] >= R(0) ? R(1) : R(-1);
+  int inc = 0;
+  for (int c = 1; c < 3; ++c)
+    if (mabs(rinc[3 * a + c]) > mabs(rinc[3 * a + inc])) inc = c;
+  const R incsign = sign * rinc[3 * a + inc] > R(0) ? R(-1) : R(1);
+  const int ax = (a + 1) % 3, ay = (a + 2) % 3, bu = (inc + 1) % 3, bv = (inc + 2) % 3;
+  const int coords[3] = {ax, ay, a};
+  V3<R> cx, du, dv;
+  for (int r = 0; r < 3; ++r) {
+    const int c = coords[r];
+    cx[r] = posoi[c] + incsign * sinc[inc] * rinc[3 * c + inc];
+    du[r] = sinc[bu] * rinc[3 * c + bu];
+    dv[r] = sinc[bv] * rinc[3 * c + bv];
+  }
+  cx.z = sign * cx.z - sref[a];
+  du.z *= sign;
+  dv.z *= sign;
+  V3<R> poly[8];
+  for (int c = 0; c < 8; ++c) poly[c] = v3<R>(0, 0, 0);
+  for (int c = 0; c < 4; ++c) {
+    const R su = c == 0 || c == 3 ? R(1) : R(-1), sv = c < 2 ? R(1) : R(-1);
+    poly[c] = cx + du * su + dv * sv;
+  }
+  int count = 4;
+  count = clip_poly(count, poly, 0, R(1), sref[ax]);
+  count = clip_poly(count, poly, 0, R(-1), sref[ax]);
+  count = clip_poly(count, poly, 1, R(1), sref[ay]);
+  count = clip_poly(count, poly, 1, R(-1), sref[ay]);
+  int accepted = 0;
+  const R dup = R(1e-10) * (sref[ax] * sref[ax] + sref[ay] * sref[ay]);
+  for (int c = 0; c < count; ++c) {
+    if (poly[c].z > margin) continue;
+    bool dupe = false;
+    for (int q = 0; q < accepted; ++q) {
+      const R dx = o.pos[q].x - poly[c].x, dy = o.pos[q].y - poly[c].y;
+      if (dx * dx + dy * dy < dup) { dupe = true; break; }
+    }
+    if (!dupe) o.pos[accepted++] = poly[c];
+  }
+  if (!accepted) return;
+  const V3<R> normal = col(matref, a) * (ref1 ? sign : -sign);
+  for (int c = 0; c < accepted; ++c) {
+    const V3<R> v = o.pos[c];
+    V3<R> local = v3<R>(0, 0, 0);
+    local[ax] = v.x;
+    local[ay] = v.y;
+    local[a] = sign * (sref[a] + R(0.5) * v.z);
+    o.dist[c] = v.z;
+    o.pos[c] = rot(matref, local) + pref;
+    o.normal[c] = normal;
+  }
+  o.count = accepted;
+}
+
+template <class R>
+__device__ void box_pair(const Mdl<R> &M, Arena<R> &A, int pair, int g1, int g2) {
+  const int t1 = IF(geom_type)[g1];
+  const Material<R> p = material(M, g1, g2);
+  const V3<R> p1 = ld3(A.gxpos + 3 * g1), p2 = ld3(A.gxpos + 3 * g2);
+  const V3<R> s1 = ld3(RF(geom_size) + 3 * g1), s2 = ld3(RF(geom_size) + 3 * g2);
+  const R *R1 = A.gxmat + 9 * g1, *R2 = A.gxmat + 9 * g2;
+  BoxHits<R> o;
+  o.count = 1;
+  if (t1 == B200_GEOM_SPHERE) sphere_box(o, 0, p1, s1.x, p2, R2, s2);
+  else if (t1 == B200_GEOM_CAPSULE) capsule_box(o, p1, col(R1, 2), s1.x, s1.y, p2, R2, s2);
+  else box_box(o, p1, R1, s1, p2, R2, s2, p.margin + p.gap);
+  for (int c = 0; c < o.count; ++c) {
+    V3<R> fr[3];
+    frame_from_normal(o.normal[c], fr);
+    emit(M, A, p, pair, c, g1, g2, o.dist[c], o.pos[c], fr);
+  }
+}
+
+template <class R> __device__ void collide_pair(const Mdl<R> &M, Arena<R> &A, int pair) {
+  const int g1 = IF(pair_geom)[2 * pair], g2 = IF(pair_geom)[2 * pair + 1];
+  if (!candidate(M, A, g1, g2)) return;
+  const int t1 = IF(geom_type)[g1], t2 = IF(geom_type)[g2];
+  if (t1 == B200_GEOM_PLANE && t2 >= 2 && t2 <= 7) plane_pair(M, A, pair, g1, g2);
+  else if (t2 == B200_GEOM_BOX && (t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE || t1 == B200_GEOM_BOX))
+    box_pair(M, A, pair, g1, g2);
+}
+
+}  // namespace b200

@@ -1,0 +1,89 @@
+/*
+ * Field lists of the B200 physics C ABI (X-macros).
+ *
+ * One list drives three consumers that must agree byte for byte:
+ *   - include/b200phys.h builds the B200Model / B200Data structs from it;
+ *   - the CUDA kernels and the C oracle read model arrays through it;
+ *   - the Python host parses this file to build matching ctypes structs and to
+ *     pack the model arrays (gpu-libero_b200/native.py).
+ *
+ * Model arrays are packed into two flat buffers (one of reals, one of int32);
+ * each named array is addressed by its offset into its buffer.  Names follow
+ * MuJoCo's mjModel/mjData fields that the reference reads through
+ * libero/libero/gpu/host/backends/cuda_fp32/layout_specs.py:37 (MODEL) and
+ * :504 (DATA); entries without a MuJoCo counterpart are derived topology
+ * (body levels, tree blocks, ancestor masks) or the robosuite OSC_POSE
+ * configuration (libero/libero/gpu/host/backends/cuda_fp32/controller.py:46-87).
+ *
+ * Data fields carry a per-world width expression written in model size names;
+ * the host evaluates it to allocate world-major [nworld, width] buffers.
+ */
+#ifndef B200PHYS_FIELDS_H
+#define B200PHYS_FIELDS_H
+
+/* integer scalars of the model */
+#define B200_MODEL_INT_SCALARS(X) \
+  X(nq) X(nv) X(nu) X(nbody) X(njnt) X(ngeom) X(nsite) X(npair) X(ntree) \
+  X(nM) X(nlevel) X(nlimited) X(nfric) X(ncon_max) X(nefc_max) X(cone) \
+  X(iterations) X(ls_iterations) X(disable_flags) X(ee_site) X(real_bytes) \
+  X(nvs) X(kmax_dof) X(max_tree_dofs) X(osc_uncouple)
+
+/* real scalars of the model (stored as double, read as the kernel's real) */
+#define B200_MODEL_REAL_SCALARS(X) \
+  X(timestep) X(gravity_x) X(gravity_y) X(gravity_z) X(tolerance) \
+  X(ls_tolerance) X(impratio_invsqrt) X(meaninertia)
+
+/* int32 arrays: X(name, length-expression) */
+#define B200_MODEL_INT_ARRAYS(X) \
+  X(body_parentid, nbody) X(body_rootid, nbody) X(body_weldid, nbody) \
+  X(body_jntnum, nbody) X(body_jntadr, nbody) X(body_dofnum, nbody) \
+  X(body_dofadr, nbody) X(body_treeid, nbody) X(body_subtree_end, nbody) \
+  X(body_order, nbody) X(level_start, nlevel + 1) X(body_dofmask, nbody * 4) \
+  X(jnt_type, njnt) X(jnt_qposadr, njnt) X(jnt_dofadr, njnt) \
+  X(jnt_bodyid, njnt) X(jnt_limited, njnt) \
+  X(dof_bodyid, nv) X(dof_jntid, nv) X(dof_parentid, nv) X(dof_treeid, nv) \
+  X(tree_dofadr, ntree) X(tree_dofnum, ntree) X(tree_madr, ntree) \
+  X(geom_type, ngeom) X(geom_bodyid, ngeom) X(geom_condim, ngeom) \
+  X(geom_priority, ngeom) X(site_bodyid, nsite) X(pair_geom, npair * 2) \
+  X(limited_jnt, nlimited) X(fric_dof, nfric) \
+  X(actuator_trnid, nu) X(actuator_gaintype, nu) X(actuator_biastype, nu) \
+  X(actuator_ctrllimited, nu) X(actuator_forcelimited, nu) \
+  X(osc_qposadr, 7) X(osc_dofadr, 7) X(osc_actuator, 9)
+
+/* real arrays: X(name, length-expression) */
+#define B200_MODEL_REAL_ARRAYS(X) \
+  X(body_pos, nbody * 3) X(body_quat, nbody * 4) X(body_ipos, nbody * 3) \
+  X(body_iquat, nbody * 4) X(body_mass, nbody) X(body_subtreemass, nbody) \
+  X(body_inertia, nbody * 3) X(body_invweight0, nbody * 2) \
+  X(jnt_pos, njnt * 3) X(jnt_axis, njnt * 3) X(jnt_range, njnt * 2) \
+  X(jnt_margin, njnt) X(jnt_solref, njnt * 2) X(jnt_solimp, njnt * 5) \
+  X(jnt_stiffness, njnt) X(qpos0, nq) X(qpos_spring, nq) \
+  X(dof_armature, nv) X(dof_damping, nv) X(dof_frictionloss, nv) \
+  X(dof_invweight0, nv) X(dof_solref, nv * 2) X(dof_solimp, nv * 5) \
+  X(geom_size, ngeom * 3) X(geom_pos, ngeom * 3) X(geom_quat, ngeom * 4) \
+  X(geom_aabb, ngeom * 6) X(geom_rbound, ngeom) X(geom_friction, ngeom * 3) \
+  X(geom_solmix, ngeom) X(geom_solref, ngeom * 2) X(geom_solimp, ngeom * 5) \
+  X(geom_margin, ngeom) X(geom_gap, ngeom) \
+  X(site_pos, nsite * 3) X(site_quat, nsite * 4) \
+  X(actuator_gear, nu) X(actuator_gainprm, nu * 3) X(actuator_biasprm, nu * 3) \
+  X(actuator_ctrlrange, nu * 2) X(actuator_forcerange, nu * 2) \
+  X(osc_gains, 12) X(osc_q0, 7) X(osc_action_config, 25) X(osc_null, 2)
+
+/* world-major real data: X(name, per-world width) */
+#define B200_DATA_REAL(X) \
+  X(qpos, nq) X(qvel, nv) X(qacc, nv) X(qacc_warmstart, nv) X(ctrl, nu) \
+  X(time, 1) X(action, 7) X(goal_pos, 3) X(goal_rot, 9) X(gripper, 2) \
+  X(xpos, nbody * 3) X(xquat, nbody * 4) X(xmat, nbody * 9) \
+  X(geom_xpos, ngeom * 3) X(geom_xmat, ngeom * 9) X(site_xpos, nsite * 3) \
+  X(site_xmat, nsite * 9) X(subtree_com, nbody * 3) X(qfrc_bias, nv) \
+  X(qfrc_actuator, nv) X(qfrc_constraint, nv) X(qacc_smooth, nv) \
+  X(con_dist, ncon_max) X(con_pos, ncon_max * 3) X(con_frame, ncon_max * 9) \
+  X(efc_force, nefc_max)
+
+/* world-major int32 data: X(name, per-world width) */
+#define B200_DATA_INT(X) \
+  X(ncon, 1) X(nefc, 1) X(con_geom, ncon_max * 2) X(overflow, 1) \
+  X(error, 1) X(niter, 1) X(newton_total, 1) X(ls_total, 1) \
+  X(integration_count, 1)
+
+#endif
