@@ -1,0 +1,313 @@
+"""Benchmark of the B200 physics step: env control steps/s for the whole box.
+
+One "step" is one control step (25 physics substeps, OSC policy step first)
+of every world on every GPU.  Worlds shard by contiguous range, one process
+per GPU (torchrun), no data-path collective; each rank derives its worlds'
+seeds from the master seed by global world index.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--worlds PER_GPU]
+  python bench.py --impl reference ...   # the reference's CPU path (C port)
+
+Timing: CUDA events on the launching stream around each control-step graph
+replay, L2 flushed (a 256 MiB write) between timed steps, barrier +
+synchronize on both sides, max over ranks.  `e2e` times the public API
+(B200BatchEnv.step: pinned H2D actions, control step, D2H observations).
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+import __graft_entry__ as entry  # noqa: E402
+
+METRIC = 'env control steps/sec (whole box) at 16K worlds/GPU; physics substeps/sec'
+UNIT = 'env control steps/s'
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument('--gpus', type=int, default=1)
+    p.add_argument('--steps', type=int, default=30)
+    p.add_argument('--warmup', type=int, default=5)
+    p.add_argument('--worlds', type=int, default=16384, help='worlds per GPU')
+    p.add_argument('--scene', default='scene_a')
+    p.add_argument('--precision', default='fp32')
+    p.add_argument('--impl', default='b200', choices=('b200', 'reference'))
+    p.add_argument('--seed', type=int, default=0)
+    p.add_argument('--no-cpu-baseline', action='store_true')
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+    QUERY = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+             'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+             'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', '-i', str(self.index), '--query-gpu=' + self.QUERY,
+                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], 0.0, set()
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        for line in self.lines:
+            f = [x.strip() for x in line.split(',')]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, f[5:9]):
+                if flag.lower() == 'active':
+                    reasons.add(name)
+        if not sm:
+            return None
+        return dict(sm_mhz=float(np.median(sm)), sm_max_mhz=mx, reasons=sorted(reasons), samples=len(sm))
+
+
+# ---------------------------------------------------------------- CPU path
+def cpu_run(scene, worlds, steps, warmup, seed, threads):
+    """The reference's CPU path restated (C oracle port), threads over worlds."""
+    from gpu_libero_b200 import native
+    Oracle = entry.load_oracle().Oracle
+    packed = native.PackedModel(scene, 'fp32')
+    host = native.alloc_numpy(packed, worlds)
+    q, v = scene.initial_state(worlds, seed=seed)
+    host['qpos'][:] = q
+    host['qvel'][:] = v
+    ms, ds = packed.host_struct(), native.data_struct(host, worlds)
+    orc = Oracle('fp32')
+    orc.forward(ms, ds, 0, worlds, 1)
+    times = []
+    for k in range(warmup + steps):
+        host['action'][:] = scene.actions(worlds, k, seed=seed)
+        t0 = time.perf_counter()
+        orc.step_parallel(ms, ds, worlds, scene.substeps, 1, threads)
+        if k >= warmup:
+            times.append(time.perf_counter() - t0)
+    return float(np.sum(times))
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(scene, seed, budget_s=12.0):
+    threads = host_threads()
+    worlds = 4 * threads
+    probe = cpu_run(scene, worlds, 1, 0, seed, threads)
+    steps = int(max(1, min(40, budget_s / max(probe, 1e-3))))
+    secs = cpu_run(scene, worlds, steps, 0, seed, threads)
+    return dict(value=worlds * steps / secs, unit=UNIT, cores=threads, kind='port',
+                sample='%d worlds x %d control steps (25 substeps) of %s, FP32 C restatement on %d host threads'
+                       % (worlds, steps, scene.name, threads))
+
+
+def reference_arm(args, scene):
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return
+    threads = host_threads()
+    worlds = 4 * threads
+    secs = cpu_run(scene, worlds, args.steps, args.warmup, args.seed, threads)
+    value = worlds * args.steps / secs
+    line = dict(metric=METRIC, value=value, unit=UNIT, impl='reference', n_gpus=args.gpus, steps=args.steps,
+                warmup=args.warmup, ms_per_step=1e3 * secs / args.steps, higher_is_better=True, scaling='weak',
+                vs_baseline=None, dtype='f32', data='synthetic',
+                config=dict(workload=scene.name, worlds_per_gpu=args.worlds, substeps=scene.substeps),
+                substeps_per_sec=value * scene.substeps,
+                cpu_baseline=dict(value=value, unit=UNIT, cores=threads, kind='port',
+                                  sample='%d worlds per step; reference CPU MuJoCo is not installed here, so the '
+                                         'FP32 C restatement of the reference substep runs on %d host threads'
+                                         % (worlds, threads)),
+                e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU path
+def main():
+    args = parse()
+    entry.load_package()
+    from gpu_libero_b200 import scene as scenes
+    scene = scenes.scene_a() if args.scene == 'scene_a' else None
+    if scene is None:
+        raise SystemExit('unknown scene ' + args.scene)
+    if args.impl == 'reference':
+        return reference_arm(args, scene)
+
+    import torch
+    import torch.distributed as dist
+    from gpu_libero_b200 import flops, native
+    from gpu_libero_b200.runtime import Runtime, B200BatchEnv
+
+    world_size = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world_size > 1:
+        from datetime import timedelta
+        dist.init_process_group('nccl', device_id=dev, timeout=timedelta(seconds=300))
+    W = args.worlds
+    offset = rank * W
+    rt = Runtime(scene, W, device=dev, precision=args.precision, world_offset=offset)
+    q, v = scene.initial_state(W, seed=args.seed, world_offset=offset)
+    rt.set_state(np.concatenate([np.zeros((W, 1)), q, v], axis=1))
+    rt.check()
+    rt.prepare_control_graph()
+    total = args.warmup + args.steps
+    acts = torch.stack([torch.as_tensor(scene.actions(W, k, seed=args.seed, world_offset=offset), dtype=rt.dtype)
+                        for k in range(total)]).to(dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MiB > 126 MB L2
+    stream = torch.cuda.current_stream(dev)
+    for k in range(args.warmup):
+        rt.buffers['action'].copy_(acts[k])
+        rt._graph.replay()
+    torch.cuda.synchronize(dev)
+    counters0 = {k: rt.buffers[k].clone() for k in ('efc_total', 'con_total', 'newton_rows', 'ls_rows',
+                                                     'newton_total')}
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    if world_size > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    time.sleep(0.3)
+    for i in range(args.steps):
+        k = args.warmup + i
+        flush.fill_(float(i))
+        rt.buffers['action'].copy_(acts[k])
+        events[i][0].record(stream)
+        rt._graph.replay()
+        events[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    clock = clocks.stop()
+    if world_size > 1:
+        dist.barrier()
+    step_ms = np.array([a.elapsed_time(b) for a, b in events])
+    elapsed = float(step_ms.sum()) / 1e3
+    t = torch.tensor([elapsed], dtype=torch.float64, device=dev)
+    if world_size > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_max = float(t.item())
+    rt.check()
+    deltas = {k: (rt.buffers[k] - counters0[k]).cpu().numpy() for k in counters0}
+    fl = flops.substep_flops(scene.sizes, scene.ints['tree_dofnum'], deltas, scene.substeps)
+    kernel_s = elapsed / args.steps  # one kernel per graph replay
+    sm_count = torch.cuda.get_device_properties(dev).multi_processor_count
+    sm_mhz = clock['sm_mhz'] if clock else 1965.0
+    peak = flops.fp32_peak_tflops(sm_count, sm_mhz)
+    achieved = fl / args.steps / kernel_s / 1e12
+    real_b = rt.buffers['qpos'].element_size()
+    io_real = sum(scene.sizes[k] for k in ('nq',)) * 2 + scene.sizes['nv'] * 4 + scene.sizes['nu'] * 2 + 2 * (3 + 9 + 2) + 7 + 2
+    out_real = (scene.sizes['nbody'] * 16 + scene.sizes['ngeom'] * 12 + scene.sizes['nsite'] * 12 +
+                scene.sizes['nbody'] * 3 + 5 * scene.sizes['nv'] + scene.sizes['nobs'])
+    bytes_per_world = (io_real + out_real) * real_b
+    hbm_gbs = None
+    try:
+        peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text())
+        hbm_gbs, peak_src = float(peaks['hbm_gbs']), 'measured'
+    except (OSError, ValueError, KeyError):
+        hbm_gbs, peak_src = 6650.0, 'fallback'
+    traffic = None
+    tfile = ROOT / 'profiles' / 'control_step_traffic.json'
+    if tfile.is_file():
+        try:
+            traffic = float(json.loads(tfile.read_text())['bytes_per_world']) * W
+        except (ValueError, KeyError):
+            traffic = None
+
+    # e2e through the public API (pinned H2D actions, D2H observations)
+    env = B200BatchEnv(scene, W, device=dev, precision=args.precision, seed=args.seed, world_offset=offset)
+    env.runtime.prepare_control_graph()
+    host_actions = [scene.actions(W, k, seed=args.seed, world_offset=offset) for k in range(total)]
+    for k in range(args.warmup):
+        env.step(host_actions[k])
+    if world_size > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        env.step(host_actions[args.warmup + i])
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_s = e0.elapsed_time(e1) / 1e3
+    t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if world_size > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_max = float(t.item())
+
+    base = None
+    if rank == 0 and world_size == 1 and not args.no_cpu_baseline:
+        base = cpu_baseline(scene, args.seed)
+    if rank == 0:
+        value = world_size * W * args.steps / elapsed_max
+        line = dict(
+            metric=METRIC, value=value, unit=UNIT, n_gpus=world_size, steps=args.steps, warmup=args.warmup,
+            ms_per_step=1e3 * elapsed_max / args.steps, higher_is_better=True, scaling='weak', vs_baseline=None,
+            dtype='f32' if args.precision == 'fp32' else 'f64', data='synthetic (seeded scene A states and actions)',
+            config=dict(workload='%s: Franka-like arm + gripper + plane + 3 free boxes, elliptic cones, '
+                                 '25 substeps/control step' % scene.name,
+                        worlds_per_gpu=W, total_worlds=W * world_size, substeps=scene.substeps,
+                        parallelism='world shards, one process per GPU', l2='flushed (256 MiB write) between steps'),
+            substeps_per_sec=value * scene.substeps,
+            e2e=dict(value=world_size * W * args.steps / e2e_max, unit=UNIT,
+                     h2d_bytes_per_step=env.runtime.h2d_bytes_per_step(),
+                     d2h_bytes_per_step=env.runtime.d2h_bytes_per_step()),
+            roofline=dict(bound='fp32', achieved=achieved, peak=peak, unit='TFLOP/s', frac=achieved / peak,
+                          traffic=traffic, peak_source='nominal FP32 CUDA-core issue: %d SMs x 128 lanes x 2 x '
+                          '%.0f MHz (sampled)' % (sm_count, sm_mhz),
+                          flops_per_world_substep=fl / (W * args.steps * scene.substeps)),
+            roofline_hbm=dict(bound='hbm', achieved=bytes_per_world * W / kernel_s / 1e9, peak=hbm_gbs, unit='GB/s',
+                              frac=bytes_per_world * W / kernel_s / 1e9 / hbm_gbs, peak_source=peak_src,
+                              bytes_per_world=bytes_per_world),
+            kernel_ms=dict(mean=float(step_ms.mean()), min=float(step_ms.min()), max=float(step_ms.max())),
+            cpu_baseline=base, clocks=clock, gpu_launches=args.steps)
+        print(json.dumps(line), flush=True)
+    env.close()
+    rt.close()
+    if world_size > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

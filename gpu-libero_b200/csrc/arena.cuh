@@ -49,6 +49,7 @@ template <class R> struct Arena {
   R *scal;   // [0] alpha [1] improvement [2] search_dot [3] grad_dot [4] decrement [5] time
   int *iscal;  // [0] ncon [1] nefc [2] nf [3] overflow [4] niter [5] done [6] error [7] ls evals [8] raw count
   R *red;    // reduction scratch (one real per warp, times 4)
+  long long *prof;  // [0] last stamp, [1..15] per-stage cycle sums (stage profiling only)
 
   static constexpr int kOscDoubles = 600;
 
@@ -79,6 +80,7 @@ template <class R> struct Arena {
     size_t hbytes = (size_t)nv * nvs * sizeof(R), obytes = (size_t)kOscDoubles * sizeof(double);
     o[k++] = c.take<unsigned char>(hbytes > obytes ? hbytes : obytes);
     o[k++] = c.take<R>(8); o[k++] = c.take<int>(12); o[k++] = c.take<R>(4 * ((threads + 31) / 32));
+    o[k++] = c.take<long long>(16);
     size_t total = (c.at + 15) & ~size_t(15);
     if (a) {
       int i = 0;
@@ -102,7 +104,7 @@ template <class R> struct Arena {
       a->H = (R *)(base + o[i]);
       a->osc = (double *)(base + o[i]);
       ++i;
-      B200_P(scal, R); B200_P(iscal, int); B200_P(red, R);
+      B200_P(scal, R); B200_P(iscal, int); B200_P(red, R); B200_P(prof, long long);
 #undef B200_P
     }
     return total;

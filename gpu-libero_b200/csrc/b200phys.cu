@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 #include <cfloat>
 #include <cstdint>
+#include <cstdlib>
 #include "b200phys.h"
 #include "arena.cuh"
 #include "math.cuh"
@@ -41,6 +42,16 @@ template <class R, int T> __device__ R block_sum(R v, R *red) {
   for (int k = 0; k < T / 32; ++k) s += red[k];
   __syncthreads();
   return s;
+}
+
+// Stage profiling (data.stage_cycles != NULL): thread 0 stamps clock64 at
+// stage boundaries; every stamp sits right after a block barrier.
+template <class R> __device__ __forceinline__ void mark(Arena<R> &A, int stage) {
+  if (A.iscal[10] && threadIdx.x == 0) {
+    const long long t = clock64();
+    A.prof[stage] += t - A.prof[0];
+    A.prof[0] = t;
+  }
 }
 
 template <class R> __device__ __forceinline__ R warp_sum(R v) {
@@ -569,6 +580,28 @@ enum { kM = 0, kMi = 49, kN = 98, kJ = 147, kJT = 189, kMJT = 231, kJbar = 273, 
        kLp = 423, kAr = 459, kLr = 495, kMisc = 531 };
 }
 
+// In-place lower Cholesky of an n x n FP64 matrix (row stride ld), one warp,
+// lane i owning row i.  *bad is set when a pivot is not positive or is tiny
+// relative to the matrix diagonal (near-singular: caller falls back).
+__device__ void chol_warp(double *a, int n, int ld, int lane, int *bad) {
+  double dmax = 0;
+  for (int i = 0; i < n; ++i) dmax = fmax(dmax, fabs(a[i * ld + i]));
+  for (int k = 0; k < n; ++k) {
+    const double p = a[k * ld + k];
+    if (!(p > 1e-12 * dmax)) {
+      if (lane == 0) *bad = 1;
+    }
+    const double d = sqrt(fmax(p, 1e-300));
+    __syncwarp();
+    if (lane == k) a[k * ld + k] = d;
+    else if (lane > k && lane < n) a[lane * ld + k] /= d;
+    __syncwarp();
+    if (lane > k && lane < n)
+      for (int j = k + 1; j <= lane; ++j) a[lane * ld + j] -= a[lane * ld + k] * a[j * ld + k];
+    __syncwarp();
+  }
+}
+
 // one-sided Jacobi pseudoinverse of an n x n block (6-stride), one lane group
 // of 8 lanes, lane r owning row r (osc_solver.cu:120-253 pinv_group)
 __device__ void pinv_group(const double *in, double *out, int n, int lane8, unsigned mask, int *ok) {
@@ -678,11 +711,11 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
   double *S = A.osc;
   const int lane = threadIdx.x;
   // ee velocity over all dofs (non-ancestors have zero Jacobian columns)
-  if (lane < 64) {  // two full warps: 8-lane groups, groups 6 and 7 idle
-    const int ax = lane / 8, l8 = lane & 7;
+  if (lane < 32) {  // warp 0: six 4-lane groups, lanes 24..31 idle
+    const int ax = lane >> 2, l4 = lane & 3;
     R v = 0;
     const V3<R> point = ld3(A.sxpos + 3 * site), com = ld3(A.com + 3 * IF(body_rootid)[body]);
-    for (int d = l8; d < nv && ax < 6; d += 8) {
+    for (int d = l4; d < nv && ax < 6; d += 4) {
       if (!dof_ancestor(M, body, d)) continue;
       const R *mo = A.cdof + 6 * d;
       R jv;
@@ -692,8 +725,9 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
       } else jv = mo[ax - 3];
       v += jv * A.qvel[d];
     }
-    for (int o = 4; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o, 8);
-    if (l8 == 0 && ax < 6) A.ee_vel[ax] = v;
+    v += __shfl_xor_sync(0xffffffffu, v, 2, 4);
+    v += __shfl_xor_sync(0xffffffffu, v, 1, 4);
+    if (l4 == 0 && ax < 6) A.ee_vel[ax] = v;
   }
   // gathers: arm mass block, 6x7 Jacobian (and its transpose)
   for (int z = lane; z < 49; z += T) S[osc::kM + z] = (double)mass_at(M, A.M, vi[z / 7], vi[z % 7]);
@@ -714,75 +748,97 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
   SYNC();
   int *err = &A.iscal[6];
   if (*err) return;  // block-uniform
+  // M^-1 J^T, A = J M^-1 J^T and the task-space inverses.  A is symmetric
+  // positive definite away from kinematic singularities, so its
+  // pseudoinverse is its inverse: warp-parallel FP64 Cholesky factorizations
+  // replace the reference's LU and one-sided Jacobi SVD (same matrices to
+  // FP64 rounding).  When a pivot shows near-singularity the reference's
+  // Jacobi pseudoinverse runs instead (pinv_group), rank cutoff included.
   if (threadIdx.x < 32) {
-    // 7x7 inverse by Gauss-Jordan with partial pivoting, lane r owns row r of [M | I]
-    double row[14];
-    const int r = lane;
-    for (int c = 0; c < 7; ++c) row[c] = r < 7 ? S[osc::kM + r * 7 + c] : 0.0;
-    for (int c = 0; c < 7; ++c) row[7 + c] = r < 7 && c == r ? 1.0 : 0.0;
-    bool singular = false;
-    for (int c = 0; c < 7; ++c) {
-      double cand = r >= c && r < 7 ? fabs(row[c]) : -1.0;
-      int who = r;
-      for (int o = 16; o > 0; o >>= 1) {
-        const double oc = __shfl_xor_sync(0xffffffffu, cand, o);
-        const int ow = __shfl_xor_sync(0xffffffffu, who, o);
-        if (oc > cand || (oc == cand && ow < who)) { cand = oc; who = ow; }
+    __shared__ int flags[4];
+    double *L7 = S + osc::kMi;  // Cholesky factor of M (lower, row-major)
+    for (int z = lane; z < 49; z += 32) L7[z] = S[osc::kM + z];
+    if (lane < 4) flags[lane] = lane < 2 ? 0 : 1;  // [0],[1]: Cholesky failed; [2],[3]: 3x3 inverse good
+    __syncwarp();
+    chol_warp(L7, 7, 7, lane, &flags[0]);
+    if (lane < 6) {  // column c of M^-1 J^T
+      const int c = lane;
+      double y[7];
+      for (int i = 0; i < 7; ++i) {
+        double v = S[osc::kJT + i * 6 + c];
+        for (int k = 0; k < i; ++k) v -= L7[i * 7 + k] * y[k];
+        y[i] = v / L7[i * 7 + i];
       }
-      if (cand == 0.0) singular = true;
-      // swap rows c and who
-      for (int k = 0; k < 14; ++k) {
-        const double mine = row[k];
-        const double atc = __shfl_sync(0xffffffffu, mine, c);
-        const double atw = __shfl_sync(0xffffffffu, mine, who);
-        if (r == c) row[k] = atw;
-        else if (r == who) row[k] = atc;
+      for (int i = 6; i >= 0; --i) {
+        double v = y[i];
+        for (int k = i + 1; k < 7; ++k) v -= L7[k * 7 + i] * y[k];
+        y[i] = v / L7[i * 7 + i];
       }
-      const double piv = __shfl_sync(0xffffffffu, row[c], c);
-      double prow[14];
-      for (int k = 0; k < 14; ++k) prow[k] = __shfl_sync(0xffffffffu, row[k], c) / piv;
-      if (r == c) for (int k = 0; k < 14; ++k) row[k] = prow[k];
-      else if (r < 7) {
-        const double f = row[c];
-        for (int k = 0; k < 14; ++k) row[k] -= f * prow[k];
-      }
+      for (int i = 0; i < 7; ++i) S[osc::kMJT + i * 6 + c] = y[i];
     }
-    if (r < 7) for (int c = 0; c < 7; ++c) S[osc::kMi + r * 7 + c] = row[7 + c];
-    if (lane == 0 && singular) *err = 2;
-  }
-  SYNC();
-  if (*err) return;
-  for (int z = lane; z < 42; z += T) {  // MJT = Mi JT (7x6)
-    const int r = z / 6, c = z % 6;
-    double v = 0;
-    for (int k = 0; k < 7; ++k) v += S[osc::kMi + r * 7 + k] * S[osc::kJT + k * 6 + c];
-    S[osc::kMJT + z] = v;
-  }
-  SYNC();
-  for (int z = lane; z < 36; z += T) {  // A = J MJT (6x6)
-    const int r = z / 6, c = z % 6;
-    double v = 0;
-    for (int k = 0; k < 7; ++k) v += S[osc::kJ + r * 7 + k] * S[osc::kMJT + k * 6 + c];
-    S[osc::kA + z] = v;
-  }
-  SYNC();
-  for (int z = lane; z < 36; z += T) {
-    const int r = z / 6, c = z % 6;
-    S[osc::kAp + z] = r < 3 && c < 3 ? S[osc::kA + z] : 0.0;
-    S[osc::kAr + z] = r < 3 && c < 3 ? S[osc::kA + (r + 3) * 6 + c + 3] : 0.0;
-  }
-  SYNC();
-  if (threadIdx.x < 32) {
-    __shared__ int ok_flags[3];
-    const int group = lane >> 3, l8 = lane & 7;
-    const unsigned mask = 0xffu << (lane & 24);
-    if (l8 == 0 && group < 3) ok_flags[group] = 1;
     __syncwarp();
-    if (group == 0) pinv_group(S + osc::kA, S + osc::kLf, 6, l8, mask, &ok_flags[0]);
-    else if (group == 1) pinv_group(S + osc::kAp, S + osc::kLp, 3, l8, mask, &ok_flags[1]);
-    else if (group == 2) pinv_group(S + osc::kAr, S + osc::kLr, 3, l8, mask, &ok_flags[2]);
+    for (int z = lane; z < 36; z += 32) {
+      const int r = z / 6, c = z % 6;
+      double v = 0;
+      for (int k = 0; k < 7; ++k) v += S[osc::kJ + r * 7 + k] * S[osc::kMJT + k * 6 + c];
+      S[osc::kA + z] = v;
+    }
     __syncwarp();
-    if (lane == 0 && !(ok_flags[0] && ok_flags[1] && ok_flags[2])) *err = 4;
+    for (int z = lane; z < 36; z += 32) {
+      const int r = z / 6, c = z % 6;
+      S[osc::kAp + z] = r < 3 && c < 3 ? S[osc::kA + z] : 0.0;
+      S[osc::kAr + z] = r < 3 && c < 3 ? S[osc::kA + (r + 3) * 6 + c + 3] : 0.0;
+    }
+    double *LA = S + osc::kN;  // scratch: Cholesky factor of A (6x6, stride 6)
+    for (int z = lane; z < 36; z += 32) LA[z] = S[osc::kA + z];
+    __syncwarp();
+    chol_warp(LA, 6, 6, lane, &flags[1]);
+    // full inverse: lane c solves A x = e_c; 3x3 blocks by the adjugate
+    if (lane < 6) {
+      const int c = lane;
+      double y[6];
+      for (int i = 0; i < 6; ++i) {
+        double v = i == c ? 1.0 : 0.0;
+        for (int k = 0; k < i; ++k) v -= LA[i * 6 + k] * y[k];
+        y[i] = v / LA[i * 6 + i];
+      }
+      for (int i = 5; i >= 0; --i) {
+        double v = y[i];
+        for (int k = i + 1; k < 6; ++k) v -= LA[k * 6 + i] * y[k];
+        y[i] = v / LA[i * 6 + i];
+      }
+      for (int i = 0; i < 6; ++i) S[osc::kLf + i * 6 + c] = y[i];
+    } else if (lane >= 8 && lane < 26) {
+      const int blk = lane < 17 ? 0 : 1, e = (lane - 8) % 9, r = e / 3, c = e % 3;
+      const double *a = S + (blk ? osc::kAr : osc::kAp);
+      const double a00 = a[0], a01 = a[1], a02 = a[2], a10 = a[6], a11 = a[7], a12 = a[8];
+      const double a20 = a[12], a21 = a[13], a22 = a[14];
+      const double c00 = a11 * a22 - a12 * a21, c01 = a12 * a20 - a10 * a22, c02 = a10 * a21 - a11 * a20;
+      const double det = a00 * c00 + a01 * c01 + a02 * c02;
+      double adj;  // adj[r][c] = cofactor[c][r]
+      const int i0 = (c + 1) % 3, i1 = (c + 2) % 3, j0 = (r + 1) % 3, j1 = (r + 2) % 3;
+      adj = a[i0 * 6 + j0] * a[i1 * 6 + j1] - a[i0 * 6 + j1] * a[i1 * 6 + j0];
+      const bool good = det > 1e-12 * a00 * a11 * a22 && det > 0.0;
+      if (!good) flags[2 + blk] = 0;
+      double *out = S + (blk ? osc::kLr : osc::kLp);
+      out[r * 6 + c] = adj / det;
+    }
+    __syncwarp();
+    const bool fast = !flags[0] && !flags[1] && flags[2] && flags[3];
+    if (flags[0]) {
+      if (lane == 0) *err = 2;  // arm mass matrix not positive definite
+    } else if (!fast) {
+      __shared__ int ok_flags[3];
+      const int group = lane >> 3, l8 = lane & 7;
+      const unsigned mask = 0xffu << (lane & 24);
+      if (l8 == 0 && group < 3) ok_flags[group] = 1;
+      __syncwarp();
+      if (group == 0) pinv_group(S + osc::kA, S + osc::kLf, 6, l8, mask, &ok_flags[0]);
+      else if (group == 1) pinv_group(S + osc::kAp, S + osc::kLp, 3, l8, mask, &ok_flags[1]);
+      else if (group == 2) pinv_group(S + osc::kAr, S + osc::kLr, 3, l8, mask, &ok_flags[2]);
+      __syncwarp();
+      if (lane == 0 && !(ok_flags[0] && ok_flags[1] && ok_flags[2])) *err = 4;
+    }
   }
   SYNC();
   if (*err) return;
@@ -834,20 +890,21 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
   if (lane < 7)
     pd[lane] = (double)nul[0] * ((double)q0[lane] - (double)A.qpos[qi[lane]]) - (double)nul[1] * (double)A.qvel[vi[lane]];
   SYNC();
-  if (lane < 6) {
+  FOR(z, 13) {
     double v = 0;
-    if (m.osc_uncouple) {
-      const int row = lane % 3, offs = lane < 3 ? 0 : 3;
-      const double *lam = S + (lane < 3 ? osc::kLp : osc::kLr);
-      for (int k = 0; k < 3; ++k) v += lam[row * 6 + k] * desired[offs + k];
-    } else
-      for (int k = 0; k < 6; ++k) v += S[osc::kLf + lane * 6 + k] * desired[k];
-    op[lane] = v;
-  } else if (lane >= 32 && lane < 39) {
-    const int r = lane - 32;
-    double v = 0;
-    for (int k = 0; k < 7; ++k) v += S[osc::kM + r * 7 + k] * pd[k];
-    opm[r] = v;
+    if (z < 6) {
+      if (m.osc_uncouple) {
+        const int row = z % 3, offs = z < 3 ? 0 : 3;
+        const double *lam = S + (z < 3 ? osc::kLp : osc::kLr);
+        for (int k = 0; k < 3; ++k) v += lam[row * 6 + k] * desired[offs + k];
+      } else
+        for (int k = 0; k < 6; ++k) v += S[osc::kLf + z * 6 + k] * desired[k];
+      op[z] = v;
+    } else {
+      const int r = z - 6;
+      for (int k = 0; k < 7; ++k) v += S[osc::kM + r * 7 + k] * pd[k];
+      opm[r] = v;
+    }
   }
   SYNC();
   if (lane < 7) {
@@ -1350,13 +1407,18 @@ template <class R, int T> __device__ void newton(const Mdl<R> &M, Arena<R> &A) {
   eval_gradient<R, T>(M, A);
   hessian<R, T>(M, A);
   direction<R, T>(M, A);
+  mark(A, 9);
   if (m.iterations == 0) return;
   const R tol = R(m.tolerance), scale = R(m.meaninertia) * R(nv);
   for (;;) {
     linesearch<R, T>(M, A);
+    mark(A, 10);
     eval_gradient<R, T>(M, A);
+    mark(A, 11);
     hessian<R, T>(M, A);
+    mark(A, 12);
     direction<R, T>(M, A);
+    mark(A, 13);
     if (threadIdx.x == 0) {
       const int it = ++A.iscal[4];
       const R imp = A.scal[1] / scale, grad = msqrt(A.scal[3]) / scale, model = (R(0.5) * A.scal[4]) / scale;
@@ -1460,6 +1522,30 @@ template <class R, int T> __device__ void store_state(const B200Model &m, const 
   dst = row_of<R>(d.goal_rot, w, 9); FOR(i, 9) dst[i] = A.goal_rot[i];
   dst = row_of<R>(d.gripper, w, 2); FOR(i, 2) dst[i] = A.gripper[i];
   if ((dst = row_of<R>(d.qacc, w, m.nv))) FOR(i, m.nv) dst[i] = A.qacc[i];
+  // observation slab: arm+gripper qpos/qvel (current), end-effector pose and
+  // free-body poses (last substep's kinematics, as MuJoCo publishes them)
+  if ((dst = row_of<R>(d.obs, w, m.nobs))) {
+    const Mdl<R> M(m);
+    FOR(e, m.nobs) {
+      R v = 0;
+      if (e < 18) {
+        const int k = e % 9, u = k < 7 ? -1 : IF(osc_actuator)[k];
+        const int j = u < 0 ? -1 : IF(actuator_trnid)[u];
+        if (e < 9) v = A.qpos[k < 7 ? IF(osc_qposadr)[k] : IF(jnt_qposadr)[j]];
+        else v = A.qvel[k < 7 ? IF(osc_dofadr)[k] : IF(jnt_dofadr)[j]];
+      } else if (e < 21) v = A.sxpos[3 * m.ee_site + e - 18];
+      else if (e < 25) {
+        const int s = m.ee_site, b = IF(site_bodyid)[s];
+        const Q4<R> q = qmul(ldq(A.xquat + 4 * b), ldq(RF(site_quat) + 4 * s));
+        const int c = e - 21;
+        v = c == 0 ? q.w : c == 1 ? q.x : c == 2 ? q.y : q.z;
+      } else if (e < 25 + 7 * m.nfree) {
+        const int f = (e - 25) / 7, c = (e - 25) % 7, b = IF(free_bodyid)[f];
+        v = c < 3 ? A.xpos[3 * b + c] : A.xquat[4 * b + c - 3];
+      }
+      dst[e] = v;  // reward and done are 0: synthetic scenes carry no task predicates
+    }
+  }
   if (threadIdx.x == 0) {
     row_of<R>(d.time, w, 1)[0] = A.scal[5];
     irow_of(d.overflow, w, 1)[0] = A.iscal[3];
@@ -1501,14 +1587,21 @@ template <class R, int T> __device__ void store_outputs(const B200Model &m, cons
 
 template <class R, int T> __device__ void step1(const Mdl<R> &M, Arena<R> &A) {
   kinematics<R, T>(M, A);
+  mark(A, 1);
   com_crb_mass<R, T>(M, A);
+  mark(A, 2);
   FOR(t, M.m.ntree) {
     const int base = IF(tree_madr)[t];
     chol_tree(A.M + base, A.L + base, IF(tree_dofnum)[t]);
   }
+  SYNC();
+  mark(A, 3);
   collision<R, T>(M, A);
+  mark(A, 4);
   constraints<R, T>(M, A);
+  mark(A, 5);
   velocity<R, T>(M, A);
+  mark(A, 6);
 }
 
 template <class R, int T>
@@ -1520,23 +1613,42 @@ __global__ void __launch_bounds__(T) control_step(const B200Model m, const B200D
   Arena<R>::layout(m, T, &A, smem);
   const Mdl<R> M(m);
   load_world<R, T>(m, d, A, w);
+  if (threadIdx.x == 0 && d.stage_cycles) {
+    A.iscal[10] = 1;
+    for (int k = 0; k < 16; ++k) A.prof[k] = 0;
+    A.prof[0] = clock64();
+  }
+  SYNC();
   for (int s = 0; s < substeps; ++s) {
     step1<R, T>(M, A);
     osc_control<R, T>(M, A, policy && s == 0);
+    mark(A, 7);
     actuation<R, T>(M, A);
+    mark(A, 8);
     newton<R, T>(M, A);
     if (threadIdx.x == 0) {
-      if (d.niter) irow_of(d.niter, w, 1)[0] = A.iscal[4];
-      if (d.newton_total) irow_of(d.newton_total, w, 1)[0] += A.iscal[4];
+      const int it = A.iscal[4], nefc = A.iscal[1], evals = A.iscal[7] - A.iscal[9];
+      A.iscal[9] = A.iscal[7];
+      if (d.niter) irow_of(d.niter, w, 1)[0] = it;
+      if (d.newton_total) irow_of(d.newton_total, w, 1)[0] += it;
+      if (d.efc_total) irow_of(d.efc_total, w, 1)[0] += nefc;
+      if (d.con_total) irow_of(d.con_total, w, 1)[0] += A.iscal[0];
+      if (d.newton_rows) irow_of(d.newton_rows, w, 1)[0] += it * nefc;
+      if (d.ls_rows) irow_of(d.ls_rows, w, 1)[0] += evals * nefc;
     }
     if (s == substeps - 1) store_outputs<R, T>(m, d, A, w);
     euler<R, T>(M, A);
+    mark(A, 14);
   }
   if (threadIdx.x == 0) {
     if (d.ls_total) irow_of(d.ls_total, w, 1)[0] += A.iscal[7];
     if (d.integration_count) irow_of(d.integration_count, w, 1)[0] += substeps;
   }
   store_state<R, T>(m, d, A, w);
+  if (threadIdx.x == 0 && d.stage_cycles) {
+    int *out = irow_of(d.stage_cycles, w, 16);
+    for (int k = 1; k < 15; ++k) out[k] += (int)A.prof[k];
+  }
 }
 
 template <class R, int T>
@@ -1566,7 +1678,16 @@ __global__ void __launch_bounds__(T) forward_step(const B200Model m, const B200D
 
 // ============================================================ C ABI
 namespace {
-constexpr int kThreads = 128;
+// Threads per world (one CTA per world). 32 = one warp per world; the
+// B200PHYS_THREADS environment variable selects 32 or 128 for experiments.
+int threads_per_world() {
+  static int t = -1;
+  if (t < 0) {
+    const char *e = getenv("B200PHYS_THREADS");
+    t = (e && atoi(e) == 128) ? 128 : 32;
+  }
+  return t;
+}
 
 bool model_ok(const B200Model *m) {
   return m && m->real && m->ints && (m->real_bytes == 4 || m->real_bytes == 8) && m->nv >= 1 && m->nv <= 128 &&
@@ -1577,9 +1698,9 @@ bool data_ok(const B200Data *d) {
   return d && d->nworld >= 0 && d->qpos && d->qvel && d->qacc_warmstart && d->ctrl && d->time && d->goal_pos &&
          d->goal_rot && d->gripper && d->overflow && d->error;
 }
-size_t smem_for(const B200Model *m) {
-  return m->real_bytes == 4 ? b200::Arena<float>::layout(*m, kThreads, nullptr, nullptr)
-                            : b200::Arena<double>::layout(*m, kThreads, nullptr, nullptr);
+size_t smem_for(const B200Model *m, int threads) {
+  return m->real_bytes == 4 ? b200::Arena<float>::layout(*m, threads, nullptr, nullptr)
+                            : b200::Arena<double>::layout(*m, threads, nullptr, nullptr);
 }
 template <class K> int configure(K kernel, size_t smem) {
   static int max_optin = -1;
@@ -1591,6 +1712,29 @@ template <class K> int configure(K kernel, size_t smem) {
   if ((int)smem > max_optin) return (int)cudaErrorInvalidValue;
   return (int)cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
+
+template <class R, int T> int prepare_t(const B200Model *m) {
+  const size_t smem = smem_for(m, T);
+  int rc;
+  if ((rc = configure(b200::control_step<R, T>, smem))) return rc;
+  return configure(b200::forward_step<R, T>, smem);
+}
+template <class R, int T>
+int step_t(const B200Model *m, const B200Data *d, int substeps, int policy, cudaStream_t s) {
+  const size_t smem = smem_for(m, T);
+  int rc;
+  if ((rc = configure(b200::control_step<R, T>, smem))) return rc;
+  b200::control_step<R, T><<<d->nworld, T, smem, s>>>(*m, *d, substeps, policy);
+  return (int)cudaGetLastError();
+}
+template <class R, int T>
+int forward_t(const B200Model *m, const B200Data *d, int bootstrap, const int *mask, cudaStream_t s) {
+  const size_t smem = smem_for(m, T);
+  int rc;
+  if ((rc = configure(b200::forward_step<R, T>, smem))) return rc;
+  b200::forward_step<R, T><<<d->nworld, T, smem, s>>>(*m, *d, bootstrap, mask);
+  return (int)cudaGetLastError();
+}
 }  // namespace
 
 extern "C" {
@@ -1598,53 +1742,30 @@ const char *b200phys_source_id(void) { return B200PHYS_SOURCE_ID; }
 int b200phys_arch(void) { return 100; }
 size_t b200phys_model_bytes(void) { return sizeof(B200Model); }
 size_t b200phys_data_bytes(void) { return sizeof(B200Data); }
-size_t b200phys_world_smem_bytes(const B200Model *m) { return model_ok(m) ? smem_for(m) : 0; }
+size_t b200phys_world_smem_bytes(const B200Model *m) { return model_ok(m) ? smem_for(m, threads_per_world()) : 0; }
 
 int b200phys_prepare(const B200Model *m) {
   if (!model_ok(m)) return (int)cudaErrorInvalidValue;
-  const size_t smem = smem_for(m);
-  int rc;
-  if (m->real_bytes == 4) {
-    if ((rc = configure(b200::control_step<float, kThreads>, smem))) return rc;
-    return configure(b200::forward_step<float, kThreads>, smem);
-  }
-  if ((rc = configure(b200::control_step<double, kThreads>, smem))) return rc;
-  return configure(b200::forward_step<double, kThreads>, smem);
+  const int t = threads_per_world();
+  if (m->real_bytes == 4) return t == 32 ? prepare_t<float, 32>(m) : prepare_t<float, 128>(m);
+  return t == 32 ? prepare_t<double, 32>(m) : prepare_t<double, 128>(m);
 }
 
 int b200phys_step_launch(const B200Model *m, const B200Data *d, int substeps, int policy, void *stream) {
   if (!model_ok(m) || !data_ok(d) || substeps < 0) return (int)cudaErrorInvalidValue;
   if (d->nworld == 0 || substeps == 0) return 0;
-  const size_t smem = smem_for(m);
   cudaStream_t s = (cudaStream_t)stream;
-  int rc;
-  if (m->real_bytes == 4) {
-    auto k = b200::control_step<float, kThreads>;
-    if ((rc = configure(k, smem))) return rc;
-    k<<<d->nworld, kThreads, smem, s>>>(*m, *d, substeps, policy);
-  } else {
-    auto k = b200::control_step<double, kThreads>;
-    if ((rc = configure(k, smem))) return rc;
-    k<<<d->nworld, kThreads, smem, s>>>(*m, *d, substeps, policy);
-  }
-  return (int)cudaGetLastError();
+  const int t = threads_per_world();
+  if (m->real_bytes == 4) return t == 32 ? step_t<float, 32>(m, d, substeps, policy, s) : step_t<float, 128>(m, d, substeps, policy, s);
+  return t == 32 ? step_t<double, 32>(m, d, substeps, policy, s) : step_t<double, 128>(m, d, substeps, policy, s);
 }
 
 int b200phys_forward_launch(const B200Model *m, const B200Data *d, int bootstrap, const int *mask, void *stream) {
   if (!model_ok(m) || !data_ok(d)) return (int)cudaErrorInvalidValue;
   if (d->nworld == 0) return 0;
-  const size_t smem = smem_for(m);
   cudaStream_t s = (cudaStream_t)stream;
-  int rc;
-  if (m->real_bytes == 4) {
-    auto k = b200::forward_step<float, kThreads>;
-    if ((rc = configure(k, smem))) return rc;
-    k<<<d->nworld, kThreads, smem, s>>>(*m, *d, bootstrap, mask);
-  } else {
-    auto k = b200::forward_step<double, kThreads>;
-    if ((rc = configure(k, smem))) return rc;
-    k<<<d->nworld, kThreads, smem, s>>>(*m, *d, bootstrap, mask);
-  }
-  return (int)cudaGetLastError();
+  const int t = threads_per_world();
+  if (m->real_bytes == 4) return t == 32 ? forward_t<float, 32>(m, d, bootstrap, mask, s) : forward_t<float, 128>(m, d, bootstrap, mask, s);
+  return t == 32 ? forward_t<double, 32>(m, d, bootstrap, mask, s) : forward_t<double, 128>(m, d, bootstrap, mask, s);
 }
 }

@@ -95,6 +95,44 @@ class Runtime:
         else:
             self.launch_step(policy=True)
 
+    def pinned_io(self):
+        """Pinned host staging for actions (in) and the observation slab plus
+        status words (out); allocated once, reused every step."""
+        if getattr(self, '_pinned', None) is None:
+            nobs = self.scene.sizes['nobs']
+            self._pinned = dict(
+                action=torch.zeros((self.n, 7), dtype=self.dtype, pin_memory=True),
+                obs=torch.zeros((self.n, nobs), dtype=self.dtype, pin_memory=True),
+                status=torch.zeros((2, self.n), dtype=torch.int32, pin_memory=True))
+            self._status = torch.zeros((2, self.n), dtype=torch.int32, device=self.device)
+        return self._pinned
+
+    def step_host(self, actions):
+        """One control step from host actions to host observations.
+
+        H2D copy of the actions (pinned), the control graph, then one D2H copy
+        of the observation slab and one of the status words; returns views of
+        the pinned host buffers after the stream has drained."""
+        io = self.pinned_io()
+        host = io['action']
+        host.numpy()[:] = actions
+        self.buffers['action'].copy_(host, non_blocking=True)
+        if self._graph is not None:
+            self._graph.replay()
+        else:
+            self.launch_step(policy=True)
+        torch.stack([self.buffers['overflow'][:, 0], self.buffers['error'][:, 0]], out=self._status)
+        io['obs'].copy_(self.buffers['obs'], non_blocking=True)
+        io['status'].copy_(self._status, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return io['obs'], io['status']
+
+    def h2d_bytes_per_step(self):
+        return self.n * 7 * self.buffers['action'].element_size()
+
+    def d2h_bytes_per_step(self):
+        return self.buffers['obs'].numel() * self.buffers['obs'].element_size() + 2 * self.n * 4
+
     def count(self, kind, mask=None):
         """Host counters of reset/epoch events (cuda_fp32 bridges count kinds 2/3)."""
         sel = np.ones(self.n, bool) if mask is None else np.asarray(mask, bool)
@@ -201,11 +239,18 @@ class B200BatchEnv:
         if actions.shape != (self.num_envs, 7) or not np.all(np.isfinite(actions)):
             raise ValueError('actions must be finite with shape (num_envs, 7)')
         with self._lock:
-            self.runtime.enqueue_action(actions)
-            self.runtime.check()
-            obs = self.observations()
-            rewards = np.zeros(self.num_envs)
-            dones = np.zeros(self.num_envs, bool)
+            slab, status = self.runtime.step_host(actions)
+            status = status.numpy()
+            fatal = status[0] & ~OVERFLOW_LIMITS
+            if np.any(fatal) or np.any(status[1]):
+                raise RuntimeError(dict(b200_overflow=status[0].tolist(), controller_error=status[1].tolist()))
+            slab = slab.numpy().copy()
+            nfree = self.scene.sizes['nfree']
+            obs = dict(robot0_joint_pos=slab[:, :9], robot0_joint_vel=slab[:, 9:18], robot0_eef_pos=slab[:, 18:21],
+                       robot0_eef_quat=slab[:, 21:25],
+                       object_pose=slab[:, 25:25 + 7 * nfree].reshape(self.num_envs, nfree, 7))
+            rewards = slab[:, -2].astype(np.float64)
+            dones = slab[:, -1] != 0
             return obs, rewards, dones, [{} for _ in range(self.num_envs)]
 
     def observations(self):

@@ -335,6 +335,8 @@ class Scene:
         pair_dofs = [int(tree_dofnum[body_tree[gbody[a]]] if body_tree[gbody[a]] >= 0 else 0) +
                      int(tree_dofnum[body_tree[gbody[b]]] if body_tree[gbody[b]] >= 0 else 0)
                      for a, b in pairs]
+        free_bodies = [j['body'] for j in jnt if j['j'].kind == FREE]
+        self.sizes.update(nfree=len(free_bodies), nobs=9 + 9 + 3 + 4 + 7 * len(free_bodies) + 2)
         self.sizes.update(ncon_max=ncon_max, nefc_max=int(nefc_max), cone=cone,
                           iterations=opt['iterations'], ls_iterations=opt['ls_iterations'],
                           disable_flags=opt.get('disable_flags', 0),
@@ -369,7 +371,8 @@ class Scene:
             actuator_forcelimited=np.array([1 if a.get('forcerange') else 0 for a in A], np.int32),
             osc_qposadr=np.array([jnt[k]['qposadr'] for k in self.controller['joints']], np.int32),
             osc_dofadr=np.array([jnt[k]['dofadr'] for k in self.controller['joints']], np.int32),
-            osc_actuator=np.array(self.controller['actuators'], np.int32))
+            osc_actuator=np.array(self.controller['actuators'], np.int32),
+            free_bodyid=np.array(free_bodies, np.int32))
         reals.update(
             body_pos=np.array([b.pos for b in B], float), body_quat=np.array([b.quat for b in B], float),
             body_ipos=body_ipos, body_iquat=body_iquat, body_mass=body_mass,

@@ -26,7 +26,7 @@
   X(nq) X(nv) X(nu) X(nbody) X(njnt) X(ngeom) X(nsite) X(npair) X(ntree) \
   X(nM) X(nlevel) X(nlimited) X(nfric) X(ncon_max) X(nefc_max) X(cone) \
   X(iterations) X(ls_iterations) X(disable_flags) X(ee_site) X(real_bytes) \
-  X(nvs) X(kmax_dof) X(max_tree_dofs) X(osc_uncouple)
+  X(nvs) X(kmax_dof) X(max_tree_dofs) X(osc_uncouple) X(nfree) X(nobs)
 
 /* real scalars of the model (stored as double, read as the kernel's real) */
 #define B200_MODEL_REAL_SCALARS(X) \
@@ -48,7 +48,7 @@
   X(limited_jnt, nlimited) X(fric_dof, nfric) \
   X(actuator_trnid, nu) X(actuator_gaintype, nu) X(actuator_biastype, nu) \
   X(actuator_ctrllimited, nu) X(actuator_forcelimited, nu) \
-  X(osc_qposadr, 7) X(osc_dofadr, 7) X(osc_actuator, 9)
+  X(osc_qposadr, 7) X(osc_dofadr, 7) X(osc_actuator, 9) X(free_bodyid, nfree)
 
 /* real arrays: X(name, length-expression) */
 #define B200_MODEL_REAL_ARRAYS(X) \
@@ -78,12 +78,13 @@
   X(site_xmat, nsite * 9) X(subtree_com, nbody * 3) X(qfrc_bias, nv) \
   X(qfrc_actuator, nv) X(qfrc_constraint, nv) X(qacc_smooth, nv) \
   X(con_dist, ncon_max) X(con_pos, ncon_max * 3) X(con_frame, ncon_max * 9) \
-  X(efc_force, nefc_max)
+  X(efc_force, nefc_max) X(obs, nobs)
 
 /* world-major int32 data: X(name, per-world width) */
 #define B200_DATA_INT(X) \
   X(ncon, 1) X(nefc, 1) X(con_geom, ncon_max * 2) X(overflow, 1) \
   X(error, 1) X(niter, 1) X(newton_total, 1) X(ls_total, 1) \
-  X(integration_count, 1)
+  X(integration_count, 1) X(efc_total, 1) X(con_total, 1) \
+  X(newton_rows, 1) X(ls_rows, 1) X(stage_cycles, 16)
 
 #endif

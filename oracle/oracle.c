@@ -1749,6 +1749,34 @@ static void publish_outputs(const B200Model *m, const B200Data *d, Work *k, int 
   if ((ip = DI(con_geom, w, nc * 2))) for (int c = 0; c < k->ncon; ++c) { ip[2 * c] = k->con[c].g1; ip[2 * c + 1] = k->con[c].g2; }
 }
 
+/* observation slab: arm+gripper qpos/qvel (current), end-effector pose and
+ * free-body poses from the last substep's kinematics; reward/done are 0 */
+static void publish_obs(const B200Model *m, const B200Data *d, const Work *k, int w, const real *qpos,
+                        const real *qvel) {
+  real *o = DR(obs, w, m->nobs);
+  if (!o) return;
+  for (int e = 0; e < m->nobs; ++e) o[e] = 0;
+  for (int c = 0; c < 9; ++c) {
+    int jq, jd;
+    if (c < 7) { jq = MI(osc_qposadr)[c]; jd = MI(osc_dofadr)[c]; }
+    else {
+      int j = MI(actuator_trnid)[MI(osc_actuator)[c]];
+      jq = MI(jnt_qposadr)[j]; jd = MI(jnt_dofadr)[j];
+    }
+    o[c] = qpos[jq];
+    o[9 + c] = qvel[jd];
+  }
+  int s = m->ee_site, b = MI(site_bodyid)[s];
+  for (int c = 0; c < 3; ++c) o[18 + c] = k->sxpos[s][c];
+  Q4 q = qmul(qload(k->xquat[b]), qload(MF(site_quat) + 4 * s));
+  o[21] = q.w; o[22] = q.x; o[23] = q.y; o[24] = q.z;
+  for (int f = 0; f < m->nfree; ++f) {
+    int fb = MI(free_bodyid)[f];
+    for (int c = 0; c < 3; ++c) o[25 + 7 * f + c] = k->xpos[fb][c];
+    for (int c = 0; c < 4; ++c) o[25 + 7 * f + 3 + c] = k->xquat[fb][c];
+  }
+}
+
 /* position + velocity stage (reference Physics.step1, physics.py:185) */
 static void step1(const B200Model *m, Work *k, const real *qpos, const real *qvel) {
   kinematics(m, k, qpos);
@@ -1786,12 +1814,17 @@ int oracle_step(const B200Model *m, const B200Data *d, int w0, int w1, int subst
       if (d->niter) *DI(niter, w, 1) = k->niter;
       if (d->newton_total) *DI(newton_total, w, 1) += k->niter;
       if (d->ls_total) *DI(ls_total, w, 1) += k->ls_evals;
+      if (d->efc_total) *DI(efc_total, w, 1) += k->nefc;
+      if (d->con_total) *DI(con_total, w, 1) += k->ncon;
+      if (d->newton_rows) *DI(newton_rows, w, 1) += k->niter * k->nefc;
+      if (d->ls_rows) *DI(ls_rows, w, 1) += k->ls_evals * k->nefc;
       k->ls_evals = 0;
       if (s == substeps - 1) publish_outputs(m, d, k, w);
       euler(m, k, qpos, qvel, DR(qacc, w, nv), warm);
       *DR(time, w, 1) += (real)m->timestep;
       if (d->integration_count) *DI(integration_count, w, 1) += 1;
     }
+    if (substeps > 0) publish_obs(m, d, k, w, qpos, qvel);
   }
   free(k);
   return 0;
@@ -1810,7 +1843,8 @@ int oracle_forward(const B200Model *m, const B200Data *d, int w0, int w1, int bo
       int site = m->ee_site;
       for (int c = 0; c < 3; ++c) DR(goal_pos, w, 3)[c] = k->sxpos[site][c];
       for (int c = 0; c < 9; ++c) DR(goal_rot, w, 9)[c] = k->sxmat[site][c];
-      DR(gripper, w, 2)[0] = DR(gripper, w, 2)[1] = 0;
+      real *gr = DR(gripper, w, 2);
+      gr[0] = gr[1] = 0;
       *DI(error, w, 1) = 0;
     }
     actuation(m, k, qpos, qvel, DR(ctrl, w, nu));
@@ -1818,7 +1852,8 @@ int oracle_forward(const B200Model *m, const B200Data *d, int w0, int w1, int bo
     newton(m, k, warm, &of);
     *DI(overflow, w, 1) |= of;
     publish_outputs(m, d, k, w);
-    if (d->qacc) memcpy(DR(qacc, w, nv), k->qacc, sizeof(real) * nv);
+    real *qa = DR(qacc, w, nv);
+    if (qa) memcpy(qa, k->qacc, sizeof(real) * nv);
     k->ls_evals = 0;
   }
   free(k);

@@ -1,0 +1,160 @@
+"""GPU parity: the CUDA control step against the CPU oracle, through the C ABI.
+
+Tolerances: forward quantities agree to FP32 rounding (|d| <= 1e-4 relative to
+the field's scale); contact pair lists and counts are bit-exact; after 5
+control steps (125 substeps) qpos agrees within 1e-4 absolute in FP32 and
+1e-7 in FP64 (contact dynamics amplify reduction-order rounding; the
+reference itself is not bit-reproducible, its pooled atomics reorder sums).
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip('torch')
+pytestmark = pytest.mark.gpu
+
+from gpu_libero_b200 import native, scene as scenes  # noqa: E402
+
+
+@pytest.fixture(scope='module')
+def scene():
+    return scenes.scene_a()
+
+
+def make_runtime(scene, n, precision, seed):
+    from gpu_libero_b200.runtime import Runtime
+    rt = Runtime(scene, n, precision=precision)
+    q, v = scene.initial_state(n, seed=seed)
+    rng = np.random.default_rng(seed)
+    v = v + rng.normal(0, 0.05, v.shape)
+    rt.set_state(np.concatenate([np.zeros((n, 1)), q, v], axis=1))
+    torch.cuda.synchronize()
+    return rt
+
+
+def host_copy(rt, n):
+    host = native.alloc_numpy(rt.packed, n)
+    for k, t in rt.buffers.items():
+        host[k][:] = t.cpu().numpy()
+    return host
+
+
+def close(a, b, rel):
+    scale = max(1.0, float(np.max(np.abs(b))))
+    return float(np.max(np.abs(np.asarray(a, float) - np.asarray(b, float)))) <= rel * scale
+
+
+@pytest.mark.parametrize('precision,rel', [('fp32', 1e-4), ('fp64', 1e-10)])
+def test_forward_parity(scene, oracle_module, precision, rel):
+    n = 8
+    rt = make_runtime(scene, n, precision, seed=11)
+    gpu = host_copy(rt, n)
+    ref = {k: v.copy() for k, v in gpu.items()}
+    orc = oracle_module.Oracle(precision)
+    orc.forward(rt.packed.host_struct(), native.data_struct(ref, n), 0, n, 1)
+    for k in ('xpos', 'xquat', 'xmat', 'geom_xpos', 'geom_xmat', 'site_xpos', 'site_xmat', 'subtree_com',
+              'qfrc_bias', 'qacc_smooth', 'goal_pos', 'goal_rot'):
+        assert close(gpu[k], ref[k], rel), k
+    assert np.array_equal(gpu['ncon'], ref['ncon'])
+    assert np.array_equal(gpu['nefc'], ref['nefc'])
+    for w in range(n):
+        c = int(ref['ncon'][w, 0])
+        assert np.array_equal(gpu['con_geom'][w, :2 * c], ref['con_geom'][w, :2 * c])
+        assert close(gpu['con_dist'][w, :c], ref['con_dist'][w, :c], rel)
+        assert close(gpu['con_pos'][w, :3 * c], ref['con_pos'][w, :3 * c], rel)
+        assert close(gpu['con_frame'][w, :9 * c], ref['con_frame'][w, :9 * c], 10 * rel)
+    assert close(gpu['qacc'], ref['qacc'], 10 * rel)
+    assert close(gpu['qfrc_constraint'], ref['qfrc_constraint'], 10 * rel)
+
+
+@pytest.mark.parametrize('precision,tol', [('fp32', 1e-4), ('fp64', 1e-7)])
+def test_control_steps_parity(scene, oracle_module, precision, tol):
+    n = 8
+    rt = make_runtime(scene, n, precision, seed=5)
+    ref = host_copy(rt, n)
+    orc = oracle_module.Oracle(precision)
+    for step in range(5):
+        a = scene.actions(n, step, seed=5)
+        rt.enqueue_action(a)
+        ref['action'][:] = a
+        orc.step(rt.packed.host_struct(), native.data_struct(ref, n), 0, n, rt.substeps, 1)
+    torch.cuda.synchronize()
+    gpu = {k: t.cpu().numpy() for k, t in rt.buffers.items()}
+    assert np.max(np.abs(gpu['qpos'] - ref['qpos'])) < tol
+    assert np.max(np.abs(gpu['qvel'] - ref['qvel'])) < 100 * tol
+    assert np.array_equal(gpu['ncon'], ref['ncon'])
+    assert np.array_equal(gpu['integration_count'], ref['integration_count'])
+    assert np.max(np.abs(gpu['obs'] - ref['obs'])) < 10 * tol
+    assert np.max(np.abs(gpu['ctrl'] - ref['ctrl'])) < 1e4 * tol
+    assert not np.any(gpu['overflow'] & ~0x600) and not np.any(gpu['error'])
+
+
+def test_bit_reproducible_and_graph_equivalent(scene):
+    n = 16
+    outs = []
+    for use_graph in (False, True, True):
+        rt = make_runtime(scene, n, 'fp32', seed=2)
+        if use_graph:
+            rt.prepare_control_graph()
+        for step in range(3):
+            rt.enqueue_action(scene.actions(n, step, seed=2))
+        torch.cuda.synchronize()
+        outs.append(rt.buffers['qpos'].cpu().numpy().copy())
+        rt.close()
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+
+
+def test_large_batch_invariants(scene):
+    n = 4096
+    rt = make_runtime(scene, n, 'fp32', seed=9)
+    rt.prepare_control_graph()
+    for step in range(4):
+        rt.enqueue_action(scene.actions(n, step, seed=9))
+    overflow, error = rt.check()
+    b = {k: t.cpu().numpy() for k, t in rt.buffers.items()}
+    qadr = scene.ints['jnt_qposadr'][scene.ints['jnt_type'] == 0]
+    for a in qadr:
+        quat = b['qpos'][:, a + 3:a + 7]
+        assert np.allclose(np.linalg.norm(quat, axis=1), 1.0, atol=1e-5)
+        assert np.all(b['qpos'][:, a + 2] > 0.0)            # boxes stay above the floor
+    assert np.all(b["ncon"] >= 6)                           # resting boxes keep their floor contacts
+    assert np.all(b['integration_count'] == 100)
+    assert np.all(np.isfinite(b['qvel']))
+
+
+def test_masked_forward_only_touches_selected(scene):
+    n = 6
+    rt = make_runtime(scene, n, 'fp32', seed=4)
+    before = rt.buffers['xpos'].clone()
+    rt.buffers['qpos'][:, 0] += 0.3
+    mask = torch.tensor([1, 0, 1, 0, 0, 1], dtype=torch.int32, device=rt.device)
+    rt.forward(mask=mask)
+    torch.cuda.synchronize()
+    changed = (rt.buffers['xpos'] != before).any(dim=1).cpu().numpy()
+    assert changed.tolist() == [True, False, True, False, False, True]
+
+
+def test_env_api_roundtrip(scene):
+    from gpu_libero_b200.runtime import B200BatchEnv
+    env = B200BatchEnv(scene, 4, seed=1)
+    state = env.get_sim_state()
+    assert state.shape == (4, 1 + scene.sizes['nq'] + scene.sizes['nv'])
+    obs, rew, done, info = env.step(scene.actions(4, 0, seed=1))
+    assert obs['robot0_eef_pos'].shape == (4, 3) and obs['object_pose'].shape == (4, 3, 7)
+    after = env.get_sim_state()
+    assert np.allclose(after[:, 0], 25 * 0.002)
+    env.set_init_state(state)
+    assert np.allclose(env.get_sim_state(), state, atol=1e-6)
+    d = env.diagnostics()
+    assert d['physics_engine'] == 'b200'
+    with pytest.raises(ValueError):
+        env.step(np.full((4, 7), np.nan))
+    env.close()
+
+
+def test_launch_rejects_bad_model(scene):
+    from gpu_libero_b200.runtime import Runtime
+    rt = Runtime(scene, 2)
+    bad = native.B200Model.from_buffer_copy(rt.model)
+    bad.nv = 0
+    with pytest.raises(RuntimeError, match='CUDA error 1'):
+        rt.lib.step(bad, rt.data, 1, 1, torch.cuda.current_stream().cuda_stream)
