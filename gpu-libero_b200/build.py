@@ -12,7 +12,7 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 REPO = ROOT.parent
-OUT = ROOT / '_lib' / 'libb200phys.so'
+OUT = Path(os.environ.get('B200PHYS_BUILD_OUT', ROOT / '_lib' / 'libb200phys.so'))
 SOURCES = [ROOT / 'csrc' / 'b200phys.cu']
 DEPENDS = SOURCES + sorted((ROOT / 'csrc').glob('*.cuh')) + sorted((REPO / 'include').glob('*.h'))
 NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
@@ -33,7 +33,8 @@ def build(force=False, verbose=False):
         return OUT
     OUT.parent.mkdir(parents=True, exist_ok=True)
     source_id = 'b200phys-' + str(abs(hash(tuple(p.read_bytes() for p in DEPENDS))) % (1 << 32))
-    cmd = [NVCC] + FLAGS + ['-DB200PHYS_SOURCE_ID="%s"' % source_id] + [str(s) for s in SOURCES] + ['-o', str(OUT)]
+    extra = os.environ.get('B200PHYS_NVCC_EXTRA', '').split()
+    cmd = [NVCC] + FLAGS + extra + ['-DB200PHYS_SOURCE_ID="%s"' % source_id] + [str(s) for s in SOURCES] + ['-o', str(OUT)]
     if verbose:
         cmd.insert(1, '-Xptxas=-v')
     subprocess.run(cmd, check=True)

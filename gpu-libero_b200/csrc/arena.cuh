@@ -40,14 +40,22 @@ template <class R> struct Arena {
   // contacts and rows
   R *con;
   int *con_dim, *con_g1, *con_g2, *con_key, *con_order, *con_adr;
+  // constraint rows: Jacobian values over at most two kinematic trees
+  // (row_t[2r], row_t[2r+1]; -1 = none), kmax_dof values per row
   R *J, *efc_D, *efc_aref, *efc_floss, *efc_force, *efc_jaref, *efc_jv, *efc_quad;
-  int *efc_type, *efc_id, *efc_state;
+  int *efc_type, *efc_id, *efc_state, *row_t;
+  // islands: trees coupled by constraint rows; the Hessian is block diagonal
+  // over islands, each block dense in island-local dof order
+  int *tree_isl, *isl_n, *isl_off, *isl_dofstart, *isl_rowstart, *isl_dof, *dof_isl, *dof_loc, *isl_rows;
+  R *xs, *colbuf;  // permuted solve vector; double-buffered Cholesky column (2 x 32)
   // Newton Hessian, reused as OSC scratch (double) before the solve
   R *H;
   double *osc;
   // scalars and reduction scratch
   R *scal;   // [0] alpha [1] improvement [2] search_dot [3] grad_dot [4] decrement [5] time
-  int *iscal;  // [0] ncon [1] nefc [2] nf [3] overflow [4] niter [5] done [6] error [7] ls evals [8] raw count
+  int *iscal;  // [0] ncon [1] nefc [2] nf [3] overflow [4] niter [5] done [6] error [7] ls evals
+               // [8] raw contact count [9] ls evals at previous substep [10] profiling on
+               // [11] islands [12] largest island [16..19] OSC factor flags [20..22] pinv flags
   R *red;    // reduction scratch (one real per warp, times 4)
   long long *prof;  // [0] last stamp, [1..15] per-stage cycle sums (stage profiling only)
 
@@ -57,7 +65,7 @@ template <class R> struct Arena {
     Carve c;
     const int nq = m.nq, nv = m.nv, nu = m.nu, nb = m.nbody, nj = m.njnt, ng = m.ngeom, ns = m.nsite;
     const int nc = m.ncon_max, ne = m.nefc_max, nvs = m.nvs;
-    size_t o[80];
+    size_t o[96];
     int k = 0;
     o[k++] = c.take<R>(nq); o[k++] = c.take<R>(nv); o[k++] = c.take<R>(nv); o[k++] = c.take<R>(nu);
     o[k++] = c.take<R>(3); o[k++] = c.take<R>(9); o[k++] = c.take<R>(2); o[k++] = c.take<R>(7);
@@ -73,13 +81,20 @@ template <class R> struct Arena {
     o[k++] = c.take<R>(6);
     o[k++] = c.take<R>((size_t)nc * kCWidth);
     for (int i = 0; i < 6; ++i) o[k++] = c.take<int>(nc);
-    o[k++] = c.take<R>((size_t)ne * nvs);
+    o[k++] = c.take<R>((size_t)ne * m.kmax_dof);
     for (int i = 0; i < 6; ++i) o[k++] = c.take<R>(ne);
     o[k++] = c.take<R>((size_t)ne * 3);
     for (int i = 0; i < 3; ++i) o[k++] = c.take<int>(ne);
+    o[k++] = c.take<int>(2 * ne);
+    const int nt = m.ntree;
+    o[k++] = c.take<int>(nt); o[k++] = c.take<int>(nt); o[k++] = c.take<int>(nt);
+    o[k++] = c.take<int>(nt + 1); o[k++] = c.take<int>(nt + 1);
+    o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv); o[k++] = c.take<int>(ne);
+    o[k++] = c.take<R>(nv);
+    o[k++] = c.take<R>(64);
     size_t hbytes = (size_t)nv * nvs * sizeof(R), obytes = (size_t)kOscDoubles * sizeof(double);
     o[k++] = c.take<unsigned char>(hbytes > obytes ? hbytes : obytes);
-    o[k++] = c.take<R>(8); o[k++] = c.take<int>(12); o[k++] = c.take<R>(4 * ((threads + 31) / 32));
+    o[k++] = c.take<R>(8); o[k++] = c.take<int>(24); o[k++] = c.take<R>(4 * ((threads + 31) / 32));
     o[k++] = c.take<long long>(16);
     size_t total = (c.at + 15) & ~size_t(15);
     if (a) {
@@ -100,7 +115,10 @@ template <class R> struct Arena {
       B200_P(con_adr, int);
       B200_P(J, R); B200_P(efc_D, R); B200_P(efc_aref, R); B200_P(efc_floss, R); B200_P(efc_force, R);
       B200_P(efc_jaref, R); B200_P(efc_jv, R); B200_P(efc_quad, R);
-      B200_P(efc_type, int); B200_P(efc_id, int); B200_P(efc_state, int);
+      B200_P(efc_type, int); B200_P(efc_id, int); B200_P(efc_state, int); B200_P(row_t, int);
+      B200_P(tree_isl, int); B200_P(isl_n, int); B200_P(isl_off, int); B200_P(isl_dofstart, int);
+      B200_P(isl_rowstart, int); B200_P(isl_dof, int); B200_P(dof_isl, int); B200_P(dof_loc, int);
+      B200_P(isl_rows, int); B200_P(xs, R); B200_P(colbuf, R);
       a->H = (R *)(base + o[i]);
       a->osc = (double *)(base + o[i]);
       ++i;

@@ -178,7 +178,7 @@ template <class R> struct BoxHits {
 };
 
 template <class R>
-__device__ void sphere_box(BoxHits<R> &o, int id, V3<R> sphere, R radius, V3<R> center, const R *Rb, V3<R> size) {
+__device__ __noinline__ void sphere_box(BoxHits<R> &o, int id, V3<R> sphere, R radius, V3<R> center, const R *Rb, V3<R> size) {
   const V3<R> local = rotT(Rb, sphere - center);
   V3<R> clamped;
   for (int c = 0; c < 3; ++c) clamped[c] = mclamp(local[c], -size[c], size[c]);
@@ -209,7 +209,7 @@ __device__ void sphere_box(BoxHits<R> &o, int id, V3<R> sphere, R radius, V3<R> 
 }
 
 template <class R>
-__device__ void capsule_box(BoxHits<R> &o, V3<R> center, V3<R> axis, R radius, R hl, V3<R> bc, const R *Rb, V3<R> size) {
+__device__ __noinline__ void capsule_box(BoxHits<R> &o, V3<R> center, V3<R> axis, R radius, R hl, V3<R> bc, const R *Rb, V3<R> size) {
   o.count = 2;
   const V3<R> pos = rotT(Rb, center - bc);
   axis = rotT(Rb, axis);
@@ -312,7 +312,7 @@ __device__ void capsule_box(BoxHits<R> &o, V3<R> center, V3<R> axis, R radius, R
   else o.dist[1] = R(1e10);
 }
 
-template <class R> __device__ int clip_poly(int count, V3<R> *poly, int coord, R sign, R limit) {
+template <class R> __device__ __noinline__ int clip_poly(int count, V3<R> *poly, int coord, R sign, R limit) {
   R d[8];
   bool inside = true;
   for (int i = 0; i < count; ++i) {
@@ -337,7 +337,7 @@ template <class R> __device__ int clip_poly(int count, V3<R> *poly, int coord, R
 }
 
 template <class R>
-__device__ void box_box(BoxHits<R> &o, V3<R> p1, const R *R1, V3<R> s1, V3<R> p2, const R *R2, V3<R> s2, R margin) {
+__device__ __noinline__ void box_box(BoxHits<R> &o, V3<R> p1, const R *R1, V3<R> s1, V3<R> p2, const R *R2, V3<R> s2, R margin) {
   o.count = 0;
   const V3<R> pos21 = rotT(R1, p2 - p1), pos12 = rotT(R2, p1 - p2);
   R rm[9], ab[9];
