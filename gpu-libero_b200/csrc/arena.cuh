@@ -46,7 +46,7 @@ template <class R> struct Arena {
   int *efc_type, *efc_id, *efc_state, *row_t;
   // islands: trees coupled by constraint rows; the Hessian is block diagonal
   // over islands, each block dense in island-local dof order
-  int *tree_isl, *isl_n, *isl_off, *isl_dofstart, *isl_rowstart, *isl_dof, *dof_isl, *dof_loc, *isl_rows;
+  int *tree_isl, *isl_n, *isl_off, *isl_dofstart, *isl_dof, *dof_isl, *dof_loc;
   R *xs, *colbuf;  // permuted solve vector; double-buffered Cholesky column (2 x 32)
   // Newton Hessian, reused as OSC scratch (double) before the solve
   R *H;
@@ -59,24 +59,25 @@ template <class R> struct Arena {
   R *red;    // reduction scratch (one real per warp, times 4)
   long long *prof;  // [0] last stamp, [1..15] per-stage cycle sums (stage profiling only)
 
-  static constexpr int kOscDoubles = 600;
+  static constexpr int kOscDoubles = 400;
 
+  // Stage-scoped arrays share one region (U): kinematics -> CRB scratch
+  // (xipos, ximat, joint anchors/axes, crb), the RNE scratch (cvel, cacc,
+  // cfrc, cdof_dot), the FP64 OSC scratch, and finally the Newton/Euler
+  // factorization blocks (H).  Each use ends before the next begins.
   __host__ __device__ static size_t layout(const B200Model &m, int threads, Arena *a, unsigned char *base) {
     Carve c;
     const int nq = m.nq, nv = m.nv, nu = m.nu, nb = m.nbody, nj = m.njnt, ng = m.ngeom, ns = m.nsite;
-    const int nc = m.ncon_max, ne = m.nefc_max, nvs = m.nvs;
+    const int nc = m.ncon_max, ne = m.nefc_max, nt = m.ntree;
     size_t o[96];
     int k = 0;
     o[k++] = c.take<R>(nq); o[k++] = c.take<R>(nv); o[k++] = c.take<R>(nv); o[k++] = c.take<R>(nu);
     o[k++] = c.take<R>(3); o[k++] = c.take<R>(9); o[k++] = c.take<R>(2); o[k++] = c.take<R>(7);
     o[k++] = c.take<R>(nb * 3); o[k++] = c.take<R>(nb * 4); o[k++] = c.take<R>(nb * 9);
-    o[k++] = c.take<R>(nb * 3); o[k++] = c.take<R>(nb * 9); o[k++] = c.take<R>(nj * 3);
-    o[k++] = c.take<R>(nj * 3); o[k++] = c.take<R>(ng * 3); o[k++] = c.take<R>(ng * 9);
-    o[k++] = c.take<R>(ns * 3); o[k++] = c.take<R>(ns * 9);
-    o[k++] = c.take<R>(nb * 3); o[k++] = c.take<R>(nb * 10); o[k++] = c.take<R>(nb * 10);
-    o[k++] = c.take<R>(nv * 6); o[k++] = c.take<R>(m.nM); o[k++] = c.take<R>(m.nM);
-    o[k++] = c.take<R>(nb * 6); o[k++] = c.take<R>(nb * 6); o[k++] = c.take<R>(nb * 6);
-    o[k++] = c.take<R>(nv * 6); o[k++] = c.take<R>(nu); o[k++] = c.take<R>(nu);
+    o[k++] = c.take<R>(ng * 3); o[k++] = c.take<R>(ng * 9); o[k++] = c.take<R>(ns * 3); o[k++] = c.take<R>(ns * 9);
+    o[k++] = c.take<R>(nb * 3); o[k++] = c.take<R>(nb * 10); o[k++] = c.take<R>(nv * 6);
+    o[k++] = c.take<R>(m.nM); o[k++] = c.take<R>(m.nM);
+    o[k++] = c.take<R>(nu); o[k++] = c.take<R>(nu);
     for (int i = 0; i < 11; ++i) o[k++] = c.take<R>(nv);
     o[k++] = c.take<R>(6);
     o[k++] = c.take<R>((size_t)nc * kCWidth);
@@ -86,26 +87,32 @@ template <class R> struct Arena {
     o[k++] = c.take<R>((size_t)ne * 3);
     for (int i = 0; i < 3; ++i) o[k++] = c.take<int>(ne);
     o[k++] = c.take<int>(2 * ne);
-    const int nt = m.ntree;
     o[k++] = c.take<int>(nt); o[k++] = c.take<int>(nt); o[k++] = c.take<int>(nt);
-    o[k++] = c.take<int>(nt + 1); o[k++] = c.take<int>(nt + 1);
-    o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv); o[k++] = c.take<int>(ne);
+    o[k++] = c.take<int>(nt + 1);
+    o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv);
     o[k++] = c.take<R>(nv);
     o[k++] = c.take<R>(64);
-    size_t hbytes = (size_t)nv * nvs * sizeof(R), obytes = (size_t)kOscDoubles * sizeof(double);
-    o[k++] = c.take<unsigned char>(hbytes > obytes ? hbytes : obytes);
     o[k++] = c.take<R>(8); o[k++] = c.take<int>(24); o[k++] = c.take<R>(4 * ((threads + 31) / 32));
     o[k++] = c.take<long long>(16);
+    // union region
+    const size_t kin = (size_t)(nb * 3 + nb * 9 + nj * 3 + nj * 3 + nb * 10) * sizeof(R) + 5 * 16;
+    const size_t rne = (size_t)(nb * 6 * 3 + nv * 6) * sizeof(R) + 4 * 16;
+    const size_t osc = (size_t)kOscDoubles * sizeof(double);
+    const size_t hes = (size_t)nv * m.nvs * sizeof(R);
+    size_t ubytes = kin > rne ? kin : rne;
+    ubytes = ubytes > osc ? ubytes : osc;
+    ubytes = ubytes > hes ? ubytes : hes;
+    const size_t u = c.take<unsigned char>(ubytes);
     size_t total = (c.at + 15) & ~size_t(15);
     if (a) {
       int i = 0;
 #define B200_P(field, T) a->field = (T *)(base + o[i++])
       B200_P(qpos, R); B200_P(qvel, R); B200_P(warm, R); B200_P(ctrl, R);
       B200_P(goal_pos, R); B200_P(goal_rot, R); B200_P(gripper, R); B200_P(action, R);
-      B200_P(xpos, R); B200_P(xquat, R); B200_P(xmat, R); B200_P(xipos, R); B200_P(ximat, R);
-      B200_P(anchor, R); B200_P(axis, R); B200_P(gxpos, R); B200_P(gxmat, R); B200_P(sxpos, R); B200_P(sxmat, R);
-      B200_P(com, R); B200_P(cinert, R); B200_P(crb, R); B200_P(cdof, R); B200_P(M, R); B200_P(L, R);
-      B200_P(cvel, R); B200_P(cacc, R); B200_P(cfrc, R); B200_P(cdof_dot, R); B200_P(act_length, R); B200_P(act_moment, R);
+      B200_P(xpos, R); B200_P(xquat, R); B200_P(xmat, R);
+      B200_P(gxpos, R); B200_P(gxmat, R); B200_P(sxpos, R); B200_P(sxmat, R);
+      B200_P(com, R); B200_P(cinert, R); B200_P(cdof, R); B200_P(M, R); B200_P(L, R);
+      B200_P(act_length, R); B200_P(act_moment, R);
       B200_P(qfrc_bias, R); B200_P(qfrc_passive, R); B200_P(qfrc_actuator, R); B200_P(qfrc_smooth, R);
       B200_P(qacc_smooth, R); B200_P(qacc, R); B200_P(Ma, R); B200_P(Mv, R); B200_P(grad, R); B200_P(search, R);
       B200_P(qfrc_constraint, R);
@@ -117,13 +124,24 @@ template <class R> struct Arena {
       B200_P(efc_jaref, R); B200_P(efc_jv, R); B200_P(efc_quad, R);
       B200_P(efc_type, int); B200_P(efc_id, int); B200_P(efc_state, int); B200_P(row_t, int);
       B200_P(tree_isl, int); B200_P(isl_n, int); B200_P(isl_off, int); B200_P(isl_dofstart, int);
-      B200_P(isl_rowstart, int); B200_P(isl_dof, int); B200_P(dof_isl, int); B200_P(dof_loc, int);
-      B200_P(isl_rows, int); B200_P(xs, R); B200_P(colbuf, R);
-      a->H = (R *)(base + o[i]);
-      a->osc = (double *)(base + o[i]);
-      ++i;
+      B200_P(isl_dof, int); B200_P(dof_isl, int); B200_P(dof_loc, int);
+      B200_P(xs, R); B200_P(colbuf, R);
       B200_P(scal, R); B200_P(iscal, int); B200_P(red, R); B200_P(prof, long long);
 #undef B200_P
+      unsigned char *ub = base + u;
+      Carve kc;
+      a->xipos = (R *)(ub + kc.take<R>(nb * 3));
+      a->ximat = (R *)(ub + kc.take<R>(nb * 9));
+      a->anchor = (R *)(ub + kc.take<R>(nj * 3));
+      a->axis = (R *)(ub + kc.take<R>(nj * 3));
+      a->crb = (R *)(ub + kc.take<R>(nb * 10));
+      Carve vc;
+      a->cvel = (R *)(ub + vc.take<R>(nb * 6));
+      a->cacc = (R *)(ub + vc.take<R>(nb * 6));
+      a->cfrc = (R *)(ub + vc.take<R>(nb * 6));
+      a->cdof_dot = (R *)(ub + vc.take<R>(nv * 6));
+      a->osc = (double *)ub;
+      a->H = (R *)ub;
     }
     return total;
   }

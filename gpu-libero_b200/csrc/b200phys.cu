@@ -840,8 +840,11 @@ template <class R, int T> __device__ void velocity(const Mdl<R> &M, Arena<R> &A)
 // robosuite OSC_POSE as computed by the reference (fused_control_drive.cu:35-111,
 // osc_solver.cu:309-676).  Warp 0 computes; shared scratch aliases H.
 namespace osc {
-enum { kM = 0, kMi = 49, kN = 98, kJ = 147, kJT = 189, kMJT = 231, kJbar = 273, kA = 315, kLf = 351, kAp = 387,
-       kLp = 423, kAr = 459, kLr = 495, kMisc = 531 };
+// FP64 OSC scratch (doubles); regions are reused once their values are dead:
+// the Cholesky factor of M holds Jbar later, A and its factor hold N later.
+// The 3x3 blocks keep a row stride of 6 (15 doubles each).
+enum { kM = 0, kJ = 49, kMi = 91, kJbar = 91, kMJT = 140, kA = 182, kN = 182, kLA = 218, kLf = 254, kAp = 290,
+       kAr = 305, kLp = 320, kLr = 335, kMisc = 350, kEnd = 397 };
 }
 
 // In-place lower Cholesky of an n x n FP64 matrix (row stride ld), one warp,
@@ -873,7 +876,7 @@ __device__ __noinline__ void pinv_group(const double *in, double *out, int n, in
   if (lane8 < n)
     for (int c = 0; c < n; ++c) scale = fmax(scale, fabs(in[lane8 * 6 + c]));
   for (int o = 4; o > 0; o >>= 1) scale = fmax(scale, __shfl_xor_sync(mask, scale, o, 8));
-  for (int z = lane8; z < 36; z += 8) out[z] = 0;
+  for (int z = lane8; z < 6 * (n - 1) + n; z += 8) out[z] = 0;
   if (!(scale > 0)) { *ok = 0; return; }
   double b[6], v[6];
   for (int c = 0; c < 6; ++c) {
@@ -1007,7 +1010,6 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
       } else jv = (double)mo[ax - 3];
     }
     S[osc::kJ + z] = jv;
-    S[osc::kJT + (z % 7) * 6 + ax] = jv;
   }
   SYNC();
   int *err = &A.iscal[6];
@@ -1029,7 +1031,7 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
       const int c = lane;
       double y[7];
       for (int i = 0; i < 7; ++i) {
-        double v = S[osc::kJT + i * 6 + c];
+        double v = S[osc::kJ + c * 7 + i];
         for (int k = 0; k < i; ++k) v -= L7[i * 7 + k] * y[k];
         y[i] = v / L7[i * 7 + i];
       }
@@ -1048,12 +1050,12 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
       S[osc::kA + z] = v;
     }
     __syncwarp();
-    for (int z = lane; z < 36; z += 32) {
+    for (int z = lane; z < 15; z += 32) {
       const int r = z / 6, c = z % 6;
-      S[osc::kAp + z] = r < 3 && c < 3 ? S[osc::kA + z] : 0.0;
-      S[osc::kAr + z] = r < 3 && c < 3 ? S[osc::kA + (r + 3) * 6 + c + 3] : 0.0;
+      S[osc::kAp + z] = c < 3 ? S[osc::kA + z] : 0.0;
+      S[osc::kAr + z] = c < 3 ? S[osc::kA + (r + 3) * 6 + c + 3] : 0.0;
     }
-    double *LA = S + osc::kN;  // scratch: Cholesky factor of A (6x6, stride 6)
+    double *LA = S + osc::kLA;  // Cholesky factor of A (6x6, stride 6)
     for (int z = lane; z < 36; z += 32) LA[z] = S[osc::kA + z];
     __syncwarp();
     chol_warp(LA, 6, 6, lane, &flags[1]);
@@ -1174,7 +1176,7 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
   if (lane < 7) {
     const int i = lane;
     double task = 0, post = 0;
-    for (int k = 0; k < 6; ++k) task += S[osc::kJT + i * 6 + k] * op[k];
+    for (int k = 0; k < 6; ++k) task += S[osc::kJ + k * 7 + i] * op[k];
     for (int k = 0; k < 7; ++k) post += S[osc::kN + k * 7 + i] * opm[k];
     const double t = task + (double)A.qfrc_bias[vi[i]] + post;
     const R *rg = RF(actuator_ctrlrange) + 2 * ids[i];
@@ -1951,12 +1953,21 @@ int max_optin_smem() {
   }
   return v;
 }
-// worlds per CTA: as many arenas as fit the per-block shared-memory limit
+// Worlds per CTA.  Two CTAs per SM (each holding half of the SM's shared
+// memory) measured faster than one large CTA: worlds of a CTA wait for its
+// slowest world at stage barriers, and the second CTA fills those gaps.
 int worlds_per_cta(const B200Model *m, int limit) {
   const size_t arena = arena_for(m);
   if (arena == 0 || (int)arena > limit) return 0;
-  int wpc = limit / (int)arena;
-  return wpc > kMaxWorldsPerCta ? kMaxWorldsPerCta : wpc;
+  const int half = (228 * 1024) / 2 - 1024;  // per-SM capacity shared by two CTAs
+  int wpc = half / (int)arena >= 3 ? half / (int)arena : limit / (int)arena;
+  static int cap = -1;  // B200PHYS_WPC: smaller CTAs (more CTAs per SM), for tuning
+  if (cap < 0) {
+    const char *e = getenv("B200PHYS_WPC");
+    cap = e ? atoi(e) : kMaxWorldsPerCta;
+    if (cap < 1 || cap > kMaxWorldsPerCta) cap = kMaxWorldsPerCta;
+  }
+  return wpc > cap ? cap : wpc;
 }
 template <class K> int configure(K kernel, size_t smem) {
   return (int)cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -23,6 +23,15 @@ from .scene import Scene, scene_a
 OVERFLOW_LIMITS = 0x200 | 0x400  # iteration / line-search limits are legal exits
 
 
+def failure_report(overflow, error, limit=16):
+    """Fatal per-world status words (the reference raises the same pair,
+    cuda_fp32/environment.py:126-140), listing at most `limit` worlds."""
+    overflow, error = np.asarray(overflow).reshape(-1), np.asarray(error).reshape(-1)
+    bad = np.flatnonzero((overflow & ~OVERFLOW_LIMITS) | error)
+    return dict(failed_worlds=int(bad.size), b200_overflow={int(w): int(overflow[w]) for w in bad[:limit]},
+                controller_error={int(w): int(error[w]) for w in bad[:limit]})
+
+
 class Runtime:
     """Owned device buffers plus the control-step graph of one world shard."""
 
@@ -172,7 +181,7 @@ class Runtime:
         error = self.buffers['error'].cpu().numpy().reshape(-1)
         fatal = overflow & ~OVERFLOW_LIMITS
         if np.any(fatal) or np.any(error):
-            raise RuntimeError(dict(b200_overflow=overflow.tolist(), controller_error=error.tolist()))
+            raise RuntimeError(failure_report(overflow, error))
         return overflow, error
 
     def close(self):
@@ -243,7 +252,7 @@ class B200BatchEnv:
             status = status.numpy()
             fatal = status[0] & ~OVERFLOW_LIMITS
             if np.any(fatal) or np.any(status[1]):
-                raise RuntimeError(dict(b200_overflow=status[0].tolist(), controller_error=status[1].tolist()))
+                raise RuntimeError(failure_report(status[0], status[1]))
             slab = slab.numpy().copy()
             nfree = self.scene.sizes['nfree']
             obs = dict(robot0_joint_pos=slab[:, :9], robot0_joint_vel=slab[:, 9:18], robot0_eef_pos=slab[:, 18:21],
