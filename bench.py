@@ -30,6 +30,7 @@ import __graft_entry__ as entry  # noqa: E402
 
 METRIC = 'env control steps/sec (whole box) at 16K worlds/GPU; physics substeps/sec'
 UNIT = 'env control steps/s'
+TRAFFIC_BYTES_PER_WORLD = 1601
 
 
 def parse():
@@ -246,13 +247,10 @@ def main():
         hbm_gbs, peak_src = float(peaks['hbm_gbs']), 'measured'
     except (OSError, ValueError, KeyError):
         hbm_gbs, peak_src = 6650.0, 'fallback'
-    traffic = None
-    tfile = ROOT / 'profiles' / 'control_step_traffic.json'
-    if tfile.is_file():
-        try:
-            traffic = float(json.loads(tfile.read_text())['bytes_per_world']) * W
-        except (ValueError, KeyError):
-            traffic = None
+    # DRAM read+write per world per control step from one ncu capture of the
+    # same kernel at 2368 worlds, scaled by worlds (per-world state is
+    # independent): profiles/control_step_scene_a_2368w_full.md
+    traffic = TRAFFIC_BYTES_PER_WORLD * W if args.precision == 'fp32' else None
 
     # e2e through the public API (pinned H2D actions, D2H observations)
     env = B200BatchEnv(scene, W, device=dev, precision=args.precision, seed=args.seed, world_offset=offset)
@@ -298,7 +296,7 @@ def main():
                           flops_per_world_substep=fl / (W * args.steps * scene.substeps)),
             roofline_hbm=dict(bound='hbm', achieved=bytes_per_world * W / kernel_s / 1e9, peak=hbm_gbs, unit='GB/s',
                               frac=bytes_per_world * W / kernel_s / 1e9 / hbm_gbs, peak_source=peak_src,
-                              bytes_per_world=bytes_per_world),
+                              bytes_per_world=bytes_per_world, traffic=traffic),
             kernel_ms=dict(mean=float(step_ms.mean()), min=float(step_ms.min()), max=float(step_ms.max())),
             cpu_baseline=base, clocks=clock, gpu_launches=args.steps)
         print(json.dumps(line), flush=True)

@@ -118,7 +118,10 @@ class PackedModel:
         return m
 
     def host_struct(self):
-        return self.struct(self.reals.ctypes.data, self.ints.ctypes.data)
+        """B200Model over the host buffers; the struct keeps this owner alive."""
+        st = self.struct(self.reals.ctypes.data, self.ints.ctypes.data)
+        st._owner = self
+        return st
 
     def data_widths(self):
         real = {n: evaluate(e, self.sizes) for n, e in LAYOUT.data_real}

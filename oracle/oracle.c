@@ -1687,6 +1687,20 @@ static Q4 quat_integrate(Q4 q, const real *v, real dt) {
   return qnormalize(qmul(q, b));
 }
 
+/* qpos += dt * qvel on the joint manifold (mjwarp_euler.cu:34-96) */
+static void integrate_positions(const B200Model *m, real *qpos, const real *qvel, real dt) {
+  for (int j = 0; j < m->njnt; ++j) {
+    int kind = MI(jnt_type)[j];
+    real *q = qpos + MI(jnt_qposadr)[j];
+    const real *v = qvel + MI(jnt_dofadr)[j];
+    if (kind == B200_JNT_FREE) { q[0] += dt * v[0]; q[1] += dt * v[1]; q[2] += dt * v[2]; q += 3; v += 3; }
+    if (kind == B200_JNT_FREE || kind == B200_JNT_BALL) {
+      Q4 r = quat_integrate(qload(q), v, dt);
+      qstore(q, r);
+    } else q[0] += dt * v[0];
+  }
+}
+
 static void euler(const B200Model *m, Work *k, real *qpos, real *qvel, real *qacc_out, real *warmstart) {
   int nv = m->nv;
   real dt = (real)m->timestep, acc[MAXV];
@@ -1707,16 +1721,7 @@ static void euler(const B200Model *m, Work *k, real *qpos, real *qvel, real *qac
     warmstart[d] = k->qacc[d];
   }
   for (int d = 0; d < nv; ++d) qvel[d] = qvel[d] + acc[d] * dt;
-  for (int j = 0; j < m->njnt; ++j) {
-    int kind = MI(jnt_type)[j];
-    real *q = qpos + MI(jnt_qposadr)[j];
-    const real *v = qvel + MI(jnt_dofadr)[j];
-    if (kind == B200_JNT_FREE) { q[0] += dt * v[0]; q[1] += dt * v[1]; q[2] += dt * v[2]; q += 3; v += 3; }
-    if (kind == B200_JNT_FREE || kind == B200_JNT_BALL) {
-      Q4 r = quat_integrate(qload(q), v, dt);
-      qstore(q, r);
-    } else q[0] += dt * v[0];
-  }
+  integrate_positions(m, qpos, qvel, dt);
 }
 
 /* ============================================================ driver */
@@ -1898,9 +1903,13 @@ int oracle_leaf_box(int type1, const real *p1, const real *R1, const real *s1, c
   return o.count;
 }
 
-/* collision + constraint rows of one world from qpos/qvel (fixtures, tests) */
-int oracle_leaf_contacts(const B200Model *m, const real *qpos, const real *qvel, int *ncon, int *geoms, real *dist,
-                         real *pos, real *frame, int *nefc, real *efc_D, real *efc_aref, int *efc_type) {
+/* collision + constraint rows of one world from qpos/qvel (fixtures, tests).
+   Per contact: geoms[2], dim, and 28 reals (dist, pos[3], frame[9], margin,
+   friction[5], solref[2], solimp[5], solreffriction[2]); per row: the dense
+   Jacobian row (nv), D, aref, type, id. */
+int oracle_leaf_contacts(const B200Model *m, const real *qpos, const real *qvel, int *ncon, int *geoms, int *dims,
+                         real *con_reals, int *nefc, real *J, real *efc_D, real *efc_aref, int *efc_type,
+                         int *efc_id) {
   if (!check_model(m)) return 1;
   Work *k = (Work *)calloc(1, sizeof(Work));
   kinematics(m, k, qpos);
@@ -1909,13 +1918,30 @@ int oracle_leaf_contacts(const B200Model *m, const real *qpos, const real *qvel,
   build_constraints(m, k, qpos, qvel);
   *ncon = k->ncon;
   for (int c = 0; c < k->ncon; ++c) {
-    geoms[2 * c] = k->con[c].g1; geoms[2 * c + 1] = k->con[c].g2;
-    dist[c] = k->con[c].dist;
-    memcpy(pos + 3 * c, k->con[c].pos, sizeof(real) * 3);
-    memcpy(frame + 9 * c, k->con[c].frame, sizeof(real) * 9);
+    const Contact *q = &k->con[c];
+    real *o = con_reals + 28 * c;
+    geoms[2 * c] = q->g1; geoms[2 * c + 1] = q->g2; dims[c] = q->dim;
+    o[0] = q->dist;
+    memcpy(o + 1, q->pos, sizeof(real) * 3);
+    memcpy(o + 4, q->frame, sizeof(real) * 9);
+    o[13] = q->margin;
+    memcpy(o + 14, q->friction, sizeof(real) * 5);
+    memcpy(o + 19, q->solref, sizeof(real) * 2);
+    memcpy(o + 21, q->solimp, sizeof(real) * 5);
+    memcpy(o + 26, q->solreffriction, sizeof(real) * 2);
   }
   *nefc = k->nefc;
-  for (int r = 0; r < k->nefc; ++r) { efc_D[r] = k->efc_D[r]; efc_aref[r] = k->efc_aref[r]; efc_type[r] = k->efc_type[r]; }
+  for (int r = 0; r < k->nefc; ++r) {
+    for (int i = 0; i < m->nv; ++i) J[r * m->nv + i] = k->J[r][i];
+    efc_D[r] = k->efc_D[r]; efc_aref[r] = k->efc_aref[r]; efc_type[r] = k->efc_type[r]; efc_id[r] = k->efc_id[r];
+  }
   free(k);
+  return 0;
+}
+
+/* position phase of the Euler step on one world (golden-vector tests) */
+int oracle_leaf_integrate(const B200Model *m, real *qpos, const real *qvel, double dt) {
+  if (!check_model(m)) return 1;
+  integrate_positions(m, qpos, qvel, (real)dt);
   return 0;
 }

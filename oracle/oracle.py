@@ -6,6 +6,8 @@ libraries (float and double restatements of the reference substep).
 """
 import ctypes as ct
 import subprocess
+
+import numpy as np
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
@@ -24,6 +26,13 @@ class Oracle:
         if not path.is_file():
             build()
         self.lib = ct.CDLL(str(path))
+        self.dtype = np.float32 if name.endswith('f32.so') else np.float64
+        self.real = ct.c_float if self.dtype == np.float32 else ct.c_double
+        P = ct.c_void_p
+        self.lib.oracle_leaf_positions.argtypes = [P] * 11
+        self.lib.oracle_leaf_contacts.argtypes = [P] * 13
+        self.lib.oracle_leaf_box.argtypes = [ct.c_int] + [P] * 6 + [self.real] + [P] * 3
+        self.lib.oracle_leaf_integrate.argtypes = [P, P, P, ct.c_double]
         self.lib.oracle_step.restype = ct.c_int
         self.lib.oracle_step.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_int, ct.c_int, ct.c_int, ct.c_int]
         self.lib.oracle_forward.restype = ct.c_int
@@ -45,3 +54,56 @@ class Oracle:
         rc = self.lib.oracle_forward(ct.addressof(model), ct.addressof(data), w0, w1, bootstrap)
         if rc:
             raise RuntimeError('oracle_forward failed (%d)' % rc)
+
+    # ---- single-world leaves (golden-vector tests)
+    def _ptr(self, a):
+        return a.ctypes.data_as(ct.c_void_p)
+
+    def positions(self, model, sizes, qpos):
+        """Kinematics, CoM/CRB and the dense mass matrix of one world."""
+        nb, ng, nv = sizes['nbody'], sizes['ngeom'], sizes['nv']
+        out = dict(xpos=np.zeros((nb, 3)), xquat=np.zeros((nb, 4)), xipos=np.zeros((nb, 3)),
+                   geom_xpos=np.zeros((ng, 3)), geom_xmat=np.zeros((ng, 9)), com=np.zeros((nb, 3)),
+                   cinert=np.zeros((nb, 10)), cdof=np.zeros((nv, 6)), M=np.zeros((nv, nv)))
+        out = {k: v.astype(self.dtype) for k, v in out.items()}
+        q = np.ascontiguousarray(qpos, self.dtype)
+        args = [ct.c_void_p(ct.addressof(model)), self._ptr(q)] + [self._ptr(out[k]) for k in
+                ('xpos', 'xquat', 'xipos', 'geom_xpos', 'geom_xmat', 'com', 'cinert', 'cdof', 'M')]
+        if self.lib.oracle_leaf_positions(*args):
+            raise RuntimeError('oracle_leaf_positions failed')
+        return out
+
+    def contacts(self, model, sizes, qpos, qvel):
+        """Contacts (geoms, dim, 28-real records) and constraint rows of one world."""
+        nc, ne, nv = sizes['ncon_max'], sizes['nefc_max'], sizes['nv']
+        ncon, nefc = ct.c_int(), ct.c_int()
+        geoms, dims = np.zeros(2 * nc, np.int32), np.zeros(nc, np.int32)
+        rec = np.zeros((nc, 28), self.dtype)
+        J, D, aref = np.zeros((ne, nv), self.dtype), np.zeros(ne, self.dtype), np.zeros(ne, self.dtype)
+        typ, ids = np.zeros(ne, np.int32), np.zeros(ne, np.int32)
+        q, v = np.ascontiguousarray(qpos, self.dtype), np.ascontiguousarray(qvel, self.dtype)
+        if self.lib.oracle_leaf_contacts(ct.addressof(model), self._ptr(q), self._ptr(v), ct.addressof(ncon),
+                                         self._ptr(geoms), self._ptr(dims), self._ptr(rec), ct.addressof(nefc),
+                                         self._ptr(J), self._ptr(D), self._ptr(aref), self._ptr(typ), self._ptr(ids)):
+            raise RuntimeError('oracle_leaf_contacts failed')
+        c, e = ncon.value, nefc.value
+        return dict(ncon=c, geom=geoms[:2 * c].reshape(c, 2), dim=dims[:c], dist=rec[:c, 0], pos=rec[:c, 1:4],
+                    frame=rec[:c, 4:13].reshape(c, 3, 3), margin=rec[:c, 13], friction=rec[:c, 14:19],
+                    solref=rec[:c, 19:21], solimp=rec[:c, 21:26], solreffriction=rec[:c, 26:28], nefc=e,
+                    J=J[:e], D=D[:e], aref=aref[:e], type=typ[:e], id=ids[:e])
+
+    def box(self, type1, p1, R1, s1, p2, R2, s2, margin=0.0):
+        """sphere/capsule/box (geom 1) against a box (geom 2) on raw poses."""
+        arr = [np.ascontiguousarray(np.asarray(x, float).ravel(), self.dtype) for x in (p1, R1, s1, p2, R2, s2)]
+        dist, pos, nrm = np.zeros(8, self.dtype), np.zeros(24, self.dtype), np.zeros(24, self.dtype)
+        n = self.lib.oracle_leaf_box(type1, *[self._ptr(a) for a in arr], margin, self._ptr(dist), self._ptr(pos),
+                                     self._ptr(nrm))
+        return dist[:n].astype(float), pos[:3 * n].reshape(n, 3).astype(float), nrm[:3 * n].reshape(n, 3).astype(float)
+
+    def integrate(self, model, qpos, qvel, dt):
+        """qpos advanced by dt * qvel on the joint manifold (one world)."""
+        q = np.ascontiguousarray(qpos, self.dtype).copy()
+        v = np.ascontiguousarray(qvel, self.dtype)
+        if self.lib.oracle_leaf_integrate(ct.addressof(model), self._ptr(q), self._ptr(v), dt):
+            raise RuntimeError('oracle_leaf_integrate failed')
+        return q
