@@ -46,6 +46,10 @@ template <class R> __device__ __forceinline__ void mark(Arena<R> &A, int stage) 
   }
 }
 
+#ifndef B200_STAGE_ATTR
+#define B200_STAGE_ATTR
+#endif
+
 template <class R> __device__ __forceinline__ R warp_sum(R v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
@@ -90,7 +94,7 @@ template <class R> __device__ __forceinline__ R jdot(const Mdl<R> &M, const Aren
 
 // ============================================================ position stage
 // forward kinematics, level by level (mjwarp_kinematics.cu:95-212 semantics)
-template <class R, int T> __device__ void kinematics(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ B200_STAGE_ATTR void kinematics(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   if (LANE == 0) {
     A.xpos[0] = A.xpos[1] = A.xpos[2] = 0;
@@ -164,7 +168,7 @@ template <class R, int T> __device__ void kinematics(const Mdl<R> &M, Arena<R> &
 // subtree com, centred inertia, motion axes, CRB and the mass matrix
 // (mjwarp_com_pos.cu:7-88, mjwarp_mass_matrix.cu:52-104).  Subtrees are
 // contiguous body intervals, so each sum has one owner and no barrier chain.
-template <class R, int T> __device__ void com_crb_mass(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ B200_STAGE_ATTR void com_crb_mass(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int nb = m.nbody;
   const R *mass = RF(body_mass);
@@ -354,7 +358,7 @@ __device__ void chol_blocks_reg(R *H, const BlockRows &b, int maxn, R *colbuf) {
   __syncwarp();
 }
 
-template <class R> __device__ void chol_blocks(R *H, const BlockRows &b, int maxn, int nv, R *colbuf) {
+template <class R> __device__ B200_STAGE_ATTR void chol_blocks(R *H, const BlockRows &b, int maxn, int nv, R *colbuf) {
 #ifndef B200_CHOL_SMEM
   if (nv <= 32 && maxn <= 16) chol_blocks_reg<R, 16>(H, b, maxn, colbuf);
   else
@@ -363,7 +367,7 @@ template <class R> __device__ void chol_blocks(R *H, const BlockRows &b, int max
 }
 
 // solve L L^T x = x in place (x indexed by position), warp 0
-template <class R> __device__ void solve_blocks(const R *H, const BlockRows &b, R *x, int maxn, int lane) {
+template <class R> __device__ B200_STAGE_ATTR void solve_blocks(const R *H, const BlockRows &b, R *x, int maxn, int lane) {
   for (int k = 0; k < maxn; ++k) {
 #pragma unroll
     for (int s = 0; s < 4; ++s)
@@ -387,7 +391,7 @@ template <class R> __device__ void solve_blocks(const R *H, const BlockRows &b, 
 }
 
 // y = M x with the dense tree blocks (one thread per dof)
-template <class R, int T> __device__ void mass_mul(const Mdl<R> &M, const R *Mb, const R *x, R *y) {
+template <class R, int T> __device__ B200_STAGE_ATTR void mass_mul(const Mdl<R> &M, const R *Mb, const R *x, R *y) {
   FOR(i, M.m.nv) {
     const int t = IF(dof_treeid)[i], a = IF(tree_dofadr)[t], n = IF(tree_dofnum)[t];
     const R *row = Mb + IF(tree_madr)[t] + (i - a) * n;
@@ -398,7 +402,7 @@ template <class R, int T> __device__ void mass_mul(const Mdl<R> &M, const R *Mb,
 }
 
 // ============================================================ collision
-template <class R, int T> __device__ void collision(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ B200_STAGE_ATTR void collision(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   if (LANE == 0) A.iscal[8] = 0;
   SYNC();
@@ -430,7 +434,7 @@ template <class R> __device__ __forceinline__ R ipow(R a, R b) {
 }
 
 template <class R> struct KBI { R k, b, imp; };
-template <class R> __device__ KBI<R> impedance(const B200Model &m, const R *ref, const R *imp, R position) {
+template <class R> __device__ B200_STAGE_ATTR KBI<R> impedance(const B200Model &m, const R *ref, const R *imp, R position) {
   const R minval = R(1e-15), minimp = R(0.0001), maximp = R(0.9999);
   const bool refsafe = !(m.disable_flags & B200_DSBL_REFSAFE);
   const R ts = R(m.timestep);
@@ -474,7 +478,7 @@ template <class R> __device__ __forceinline__ void set_row_trees(const Mdl<R> &M
 // island and the tree layout is reused (blocks at tree_madr).  Otherwise lane
 // 0 unions trees over the coupled contacts; island ids follow the smallest
 // tree index, so the blocks are deterministic.
-template <class R> __device__ void islands(const Mdl<R> &M, Arena<R> &A, bool coupled) {
+template <class R> __device__ B200_STAGE_ATTR void islands(const Mdl<R> &M, Arena<R> &A, bool coupled) {
   const int nt = M.m.ntree, nv = M.m.nv, lane = LANE;
   if (!coupled) {
     for (int t = lane; t < nt; t += 32) {
@@ -537,7 +541,7 @@ template <class R> __device__ void islands(const Mdl<R> &M, Arena<R> &A, bool co
   __syncwarp();
 }
 
-template <class R, int T> __device__ void constraints(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ B200_STAGE_ATTR void constraints(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int cap = m.nefc_max, kmax = m.kmax_dof;
   const bool off = m.disable_flags & B200_DSBL_CONSTRAINT;
@@ -579,6 +583,7 @@ template <class R, int T> __device__ void constraints(const Mdl<R> &M, Arena<R> 
       nefc = mmin(nefc + __popc(mask), cap);
     }
     const int ncon = A.iscal[0];
+    if (lane == 0) A.iscal[13] = nefc;  // rows [0, nefc) act on one dof each
     int end = nefc;
     bool coupled = false;
     for (int base = 0; base < ncon; base += 32) {
@@ -744,7 +749,7 @@ template <class R> __device__ __forceinline__ void force_cross(const R *v, const
   o[5] = -v[1] * f[3] + v[0] * f[4];
 }
 
-template <class R, int T> __device__ void velocity(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ B200_STAGE_ATTR void velocity(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   if (LANE < 6) {
     const int c = LANE;
@@ -950,7 +955,7 @@ template <class R> __device__ R action_component(const Mdl<R> &M, R action, int 
   return (a - (p[6 + axis] + p[axis]) * R(0.5)) * scale + (p[18 + axis] + p[12 + axis]) * R(0.5);
 }
 
-template <class R> __device__ void rotation_delta(R x, R y, R z, double *r) {
+template <class R> __device__ B200_STAGE_ATTR void rotation_delta(R x, R y, R z, double *r) {
   const R angle = msqrt(x * x + y * y + z * z);
   const R f = angle == R(0) ? R(0) : msin(angle * R(0.5)) / angle;
   const R raw[4] = {x * f, y * f, z * f, angle == R(0) ? R(1) : mcos(angle * R(0.5))};
@@ -971,7 +976,7 @@ template <class R> __device__ void rotation_delta(R x, R y, R z, double *r) {
   r[7] = (double)(R)(q[2] * q[3] + q[1] * q[0]);
 }
 
-template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> &A, bool policy) {
+template <class R, int T> __device__ B200_STAGE_ATTR void osc_control(const Mdl<R> &M, Arena<R> &A, bool policy) {
   const B200Model &m = M.m;
   const int nv = m.nv, site = m.ee_site, body = IF(site_bodyid)[site];
   const int *vi = IF(osc_dofadr), *qi = IF(osc_qposadr), *ids = IF(osc_actuator);
@@ -1201,7 +1206,7 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
 }
 
 // ============================================================ actuation
-template <class R, int T> __device__ void actuation(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ B200_STAGE_ATTR void actuation(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   FOR(d, m.nv) {
     R f = 0;
@@ -1238,7 +1243,7 @@ template <class R, int T> __device__ void actuation(const Mdl<R> &M, Arena<R> &A
 // ============================================================ Newton
 // mjwarp_solver_state.cu, mjwarp_constraint.cu, mjwarp_hessian.cu,
 // mjwarp_direction.cu, mjwarp_linesearch.cu
-template <class R, int T> __device__ void eval_gradient(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ B200_STAGE_ATTR void eval_gradient(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int nefc = A.iscal[1], nf = A.iscal[2], nv = m.nv;
   const R impratio = R(m.impratio_invsqrt);
@@ -1279,9 +1284,12 @@ template <class R, int T> __device__ void eval_gradient(const Mdl<R> &M, Arena<R
   R gd = 0;
   FOR(i, nv) {
     R tot = 0;
-    const int t = IF(dof_treeid)[i];
-    for (int r = 0; r < nefc; ++r)
-      if (A.row_t[2 * r] == t || A.row_t[2 * r + 1] == t) tot += jval(M, A, r, i) * A.efc_force[r];
+    const int t = IF(dof_treeid)[i], off = i - IF(tree_dofadr)[t], kmax = m.kmax_dof;
+    for (int r = 0; r < nefc; ++r) {
+      const int t0 = A.row_t[2 * r];
+      if (t0 == t) tot += A.J[r * kmax + off] * A.efc_force[r];
+      else if (A.row_t[2 * r + 1] == t) tot += A.J[r * kmax + IF(tree_dofnum)[t0] + off] * A.efc_force[r];
+    }
     A.qfrc_constraint[i] = tot;
     const R g = A.Ma[i] - A.qfrc_smooth[i] - tot;
     A.grad[i] = g;
@@ -1292,55 +1300,122 @@ template <class R, int T> __device__ void eval_gradient(const Mdl<R> &M, Arena<R
 }
 
 // H = M + J' D J over quadratic rows + elliptic-cone curvature
-// (mjwarp_hessian.cu:33-212), one dense lower-triangular block per island
-template <class R, int T> __device__ void hessian(const Mdl<R> &M, Arena<R> &A) {
+// (mjwarp_hessian.cu:33-212), one dense block per island (lower triangle).
+// Assembly is block-structured: the mass blocks, then the single-dof rows
+// (friction loss, joint limits: J = +-1, so they add D on the diagonal), then
+// one pass per contact adding J_c' C J_c over the contact's dofs, where C is
+// diag(D) over its quadratic rows, or the elliptic-cone curvature matrix when
+// the contact is in the cone state.  Contacts run one after another, each
+// H entry of a contact on its own lane, so sums are deterministic.
+template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
-  const int nisl = A.iscal[11];
+  const int nisl = A.iscal[11], nsingle = A.iscal[13], ncon = A.iscal[0], kmax = m.kmax_dof;
   const R impratio = R(m.impratio_invsqrt);
   int total = 0;
-  for (int i = 0; i < nisl; ++i) total += A.isl_n[i] * (A.isl_n[i] + 1) / 2;
+  for (int i = 0; i < nisl; ++i) total += A.isl_n[i] * A.isl_n[i];
+  // mass blocks (the island blocks are contiguous: n^2 each, in island order)
   FOR(e, total) {
     int isl = 0, base = 0;
-    while (base + A.isl_n[isl] * (A.isl_n[isl] + 1) / 2 <= e) { base += A.isl_n[isl] * (A.isl_n[isl] + 1) / 2; ++isl; }
-    const int n = A.isl_n[isl], loc = e - base;
-    int a = (int)((msqrt(8.0f * loc + 1.0f) - 1.0f) * 0.5f);
-    while (a * (a + 1) / 2 > loc) --a;
-    while ((a + 1) * (a + 2) / 2 <= loc) ++a;
-    const int b = loc - a * (a + 1) / 2;
-    const int i = A.isl_dof[A.isl_dofstart[isl] + a], j = A.isl_dof[A.isl_dofstart[isl] + b];
-    R v = mass_at(M, A.M, i, j);
-    const int nefc = A.iscal[1];
-    for (int r = 0; r < nefc; ++r) {
-      if (A.tree_isl[A.row_t[2 * r]] != isl) continue;
-      if (A.efc_state[r] == kQuadratic) v += jval(M, A, r, i) * A.efc_D[r] * jval(M, A, r, j);
-      if (m.cone == 1 && A.efc_type[r] == 7 && A.efc_state[r] == kCone) {
-        const int c = A.efc_id[r], head = A.con_adr[c], dim = A.con_dim[c];
-        if (r != head || dim == 1) continue;
-        const R *fr = A.con + (size_t)c * kCWidth + kCFriction;
-        const R mu = fr[0] * impratio, mu2 = mu * mu, den = mu2 * (R(1) + mu2);
-        const R dm = A.efc_D[head] / (den != R(0) ? den : R(1e-15));
-        if (dm == R(0)) continue;
-        const R nrm = A.efc_jaref[head] * mu;
-        R tt = 0, p1 = 0, p2 = 0, td = 0;
-        for (int d = 1; d < dim; ++d) {
-          const R sc = fr[d - 1], u = A.efc_jaref[head + d] * sc;
-          const R z1 = sc * jval(M, A, head + d, i), z2 = sc * jval(M, A, head + d, j);
-          tt += u * u; p1 += u * z1; p2 += u * z2; td += z1 * z2;
-        }
-        const R t = mmax(msqrt(tt), R(1e-15)), it = R(1) / t, mnt = mu * nrm * it;
-        p1 *= it; p2 *= it;
-        const R z01 = mu * jval(M, A, head, i), z02 = mu * jval(M, A, head, j);
-        v += dm * (z01 * z02 - mu * (z01 * p2 + z02 * p1) + mnt * p1 * p2 + (mu2 - mnt) * td);
-      }
-    }
+    while (base + A.isl_n[isl] * A.isl_n[isl] <= e) { base += A.isl_n[isl] * A.isl_n[isl]; ++isl; }
+    const int n = A.isl_n[isl], a = (e - base) / n, b = (e - base) - a * n;
+    R v = 0;
+    if (a >= b) v = mass_at(M, A.M, A.isl_dof[A.isl_dofstart[isl] + a], A.isl_dof[A.isl_dofstart[isl] + b]);
     A.H[A.isl_off[isl] + a * n + b] = v;
   }
   SYNC();
+  // single-dof rows: D on the diagonal of their dof
+  FOR(d, m.nv) {
+    R add = 0;
+    for (int r = 0; r < nsingle; ++r) {
+      if (A.efc_state[r] != kQuadratic) continue;
+      const int dof = A.efc_type[r] == 1 ? A.efc_id[r] : IF(jnt_dofadr)[A.efc_id[r]];
+      if (dof == d) add += A.efc_D[r];
+    }
+    if (add != R(0)) {
+      const int isl = A.dof_isl[d], n = A.isl_n[isl], l = A.dof_loc[d];
+      A.H[A.isl_off[isl] + l * n + l] += add;
+    }
+  }
+  SYNC();
+  R *C = A.colbuf;  // per-contact row coupling matrix (<= 6 x 6)
+  for (int c = 0; c < ncon; ++c) {
+    const int r0 = A.con_adr[c];
+    if (r0 < 0) continue;
+    const int type = A.efc_type[r0], dim = A.con_dim[c];
+    const int cnt = type == 6 ? 2 * (dim - 1) : dim;
+    bool full = false;
+    if (type == 7 && dim > 1) {
+      const int st = A.efc_state[r0];
+      if (st == kSatisfied) continue;
+      if (st == kCone) {
+        const R *fr = A.con + (size_t)c * kCWidth + kCFriction;
+        const R mu = fr[0] * impratio, mu2 = mu * mu, den = mu2 * (R(1) + mu2);
+        const R dm = A.efc_D[r0] / (den != R(0) ? den : R(1e-15));
+        if (dm == R(0)) continue;
+        R tt = 0;
+        for (int d = 1; d < dim; ++d) {
+          const R u = A.efc_jaref[r0 + d] * fr[d - 1];
+          tt += u * u;
+        }
+        const R t = mmax(msqrt(tt), R(1e-15)), it = R(1) / t, mnt = mu * (A.efc_jaref[r0] * mu) * it;
+        for (int z = LANE; z < dim * dim; z += 32) {
+          const int p = z / dim, q = z - p * dim;
+          R v;
+          if (p == 0 && q == 0) v = mu2;
+          else if (p == 0 || q == 0) {
+            const int e = p + q;
+            v = -mu2 * (A.efc_jaref[r0 + e] * fr[e - 1] * it) * fr[e - 1];
+          } else {
+            const R up = A.efc_jaref[r0 + p] * fr[p - 1] * it, uq = A.efc_jaref[r0 + q] * fr[q - 1] * it;
+            v = mnt * up * fr[p - 1] * uq * fr[q - 1];
+            if (p == q) v += (mu2 - mnt) * fr[p - 1] * fr[p - 1];
+          }
+          C[z] = dm * v;
+        }
+        full = true;
+      }
+    }
+    if (!full) {
+      bool any = false;
+      for (int z = LANE; z < cnt; z += 32) C[z] = A.efc_state[r0 + z] == kQuadratic ? A.efc_D[r0 + z] : R(0);
+      for (int z = 0; z < cnt; ++z) any |= A.efc_state[r0 + z] == kQuadratic;
+      if (!any) continue;
+    }
+    SYNC();
+    const int t0 = A.row_t[2 * r0], t1 = A.row_t[2 * r0 + 1];
+    const int n0 = IF(tree_dofnum)[t0], k = n0 + (t1 >= 0 ? IF(tree_dofnum)[t1] : 0);
+    const int a0 = IF(tree_dofadr)[t0], a1 = t1 >= 0 ? IF(tree_dofadr)[t1] : 0;
+    const int isl = A.tree_isl[t0], n = A.isl_n[isl];
+    R *Hb = A.H + A.isl_off[isl];
+    const R *J = A.J + (size_t)r0 * kmax;
+    FOR(e, k * (k + 1) / 2) {
+      int a = (int)((msqrt(8.0f * e + 1.0f) - 1.0f) * 0.5f);
+      while (a * (a + 1) / 2 > e) --a;
+      while ((a + 1) * (a + 2) / 2 <= e) ++a;
+      const int b = e - a * (a + 1) / 2;
+      R v = 0;
+      if (full) {
+#pragma unroll 1
+        for (int p = 0; p < cnt; ++p) {
+          R cb = 0;
+#pragma unroll 1
+          for (int q = 0; q < cnt; ++q) cb += C[p * cnt + q] * J[q * kmax + b];
+          v += J[p * kmax + a] * cb;
+        }
+      } else {
+#pragma unroll 1
+        for (int p = 0; p < cnt; ++p) v += J[p * kmax + a] * C[p] * J[p * kmax + b];
+      }
+      const int la = A.dof_loc[a < n0 ? a0 + a : a1 + a - n0], lb = A.dof_loc[b < n0 ? a0 + b : a1 + b - n0];
+      Hb[la >= lb ? la * n + lb : lb * n + la] += v;
+    }
+    SYNC();
+  }
 }
 
 // Cholesky of every island block at once, H x = grad, search = -x
 // (mjwarp_direction.cu:80-160); warp 0
-template <class R, int T> __device__ void direction(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ B200_STAGE_ATTR void direction(const Mdl<R> &M, Arena<R> &A) {
   const int nv = M.m.nv;
   R *x = A.xs;
   if (LANE < 32) {
@@ -1387,7 +1462,7 @@ template <class R> struct LsRow {
   int kind, state0;
   R x, v, d, loss, q0, q1, q2, u0, v0, uu, uv, vv, dm, mu, cost0, t0, r0;
 };
-template <class R> __device__ LsRow<R> load_row(const Mdl<R> &M, const Arena<R> &A, int r, int nf) {
+template <class R> __device__ B200_STAGE_ATTR LsRow<R> load_row(const Mdl<R> &M, const Arena<R> &A, int r, int nf) {
   LsRow<R> o;
   o.kind = 0; o.state0 = 0;
   o.x = o.v = o.d = o.loss = o.q0 = o.q1 = o.q2 = o.u0 = o.v0 = o.uu = o.uv = o.vv = o.dm = o.mu = o.cost0 = o.t0 = o.r0 = 0;
@@ -1417,7 +1492,7 @@ template <class R> __device__ LsRow<R> load_row(const Mdl<R> &M, const Arena<R> 
   if (o.kind == 1) o.loss = A.efc_floss[r];
   return o;
 }
-template <class R> __device__ Pt<R> friction_point(const LsRow<R> &r, R x) {
+template <class R> __device__ B200_STAGE_ATTR Pt<R> friction_point(const LsRow<R> &r, R x) {
   const R rf = safe_div(r.loss, r.d);
   if (-rf < x && x < rf) {
     const R vd = r.v * r.d;
@@ -1426,7 +1501,7 @@ template <class R> __device__ Pt<R> friction_point(const LsRow<R> &r, R x) {
   if (x <= -rf) return {r.loss * (R(-0.5) * rf - x), -r.loss * r.v, R(0)};
   return {r.loss * (R(-0.5) * rf + x), r.loss * r.v, R(0)};
 }
-template <class R> __device__ Pt<R> eval_zero(const LsRow<R> &r) {
+template <class R> __device__ B200_STAGE_ATTR Pt<R> eval_zero(const LsRow<R> &r) {
   if (r.kind == 4) return {0, 0, 0};
   if (r.kind == 3) {
     if (r.state0 == 1) return {r.q0, r.q1, R(2) * r.q2};
@@ -1441,7 +1516,7 @@ template <class R> __device__ Pt<R> eval_zero(const LsRow<R> &r) {
   const R vd = r.v * r.d;
   return {R(0.5) * r.d * r.x * r.x, vd * r.x, r.v * vd};
 }
-template <class R> __device__ Pt<R> cone_quad_shift(const LsRow<R> &r, R alpha, R n, R tsqr) {
+template <class R> __device__ B200_STAGE_ATTR Pt<R> cone_quad_shift(const LsRow<R> &r, R alpha, R n, R tsqr) {
   const R aq2 = alpha * r.q2;
   R cost = alpha * (aq2 + r.q1);
   if (r.state0 == 4) {
@@ -1450,7 +1525,7 @@ template <class R> __device__ Pt<R> cone_quad_shift(const LsRow<R> &r, R alpha, 
   } else if (r.state0 == 0) cost = R(0.5) * r.dm * (R(1) + r.mu * r.mu) * (n * n + mmax(tsqr, R(0)));
   return {cost, R(2) * aq2 + r.q1, R(2) * r.q2};
 }
-template <class R> __device__ Pt<R> eval_shift(const LsRow<R> &r, R alpha) {
+template <class R> __device__ B200_STAGE_ATTR Pt<R> eval_shift(const LsRow<R> &r, R alpha) {
   if (r.kind == 4) return {0, 0, 0};
   if (r.kind == 3) {
     const R n = r.u0 + alpha * r.v0, tsd = alpha * (R(2) * r.uv + alpha * r.vv), tsqr = r.uu + tsd;
@@ -1491,7 +1566,7 @@ template <class R> __device__ __forceinline__ Pt<R> warp_pt(Pt<R> p) {
   return {warp_sum(p.cost), warp_sum(p.slope), warp_sum(p.curv)};
 }
 
-template <class R, int T> __device__ void linesearch(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ B200_STAGE_ATTR void linesearch(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int nv = m.nv, nefc = A.iscal[1], nf = A.iscal[2];
   mass_mul<R, T>(M, A.M, A.search, A.Mv);
@@ -1620,7 +1695,7 @@ template <class R, int T> __device__ void linesearch(const Mdl<R> &M, Arena<R> &
 
 // Newton solve (mjwarp_solver_state.cu, physics.py:47-70): initial
 // gradient/Hessian/direction, then iterations until the world's stop rule.
-template <class R, int T> __device__ void newton_init(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ B200_STAGE_ATTR void newton_init(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int nv = m.nv, nefc = A.iscal[1];
   const bool warm = !(m.disable_flags & B200_DSBL_WARMSTART);
@@ -1636,7 +1711,7 @@ template <class R, int T> __device__ void newton_init(const Mdl<R> &M, Arena<R> 
   mark(A, 9);
 }
 
-template <class R, int T> __device__ void newton_iteration(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ B200_STAGE_ATTR void newton_iteration(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const R tol = R(m.tolerance), scale = R(m.meaninertia) * R(m.nv);
   linesearch<R, T>(M, A);
@@ -1660,7 +1735,7 @@ template <class R, int T> __device__ void newton_iteration(const Mdl<R> &M, Aren
 }
 
 // ============================================================ Euler
-template <class R, int T> __device__ void euler(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ B200_STAGE_ATTR void euler(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int nv = m.nv;
   const R dt = R(m.timestep);
@@ -1718,7 +1793,7 @@ __device__ __forceinline__ int *irow_of(int *p, int w, int width) {
   return p ? p + (size_t)w * width : nullptr;
 }
 
-template <class R, int T> __device__ void load_world(const B200Model &m, const B200Data &d, Arena<R> &A, int w) {
+template <class R, int T> __device__ B200_STAGE_ATTR void load_world(const B200Model &m, const B200Data &d, Arena<R> &A, int w) {
   const R *src;
   src = row_of<R>(d.qpos, w, m.nq); FOR(i, m.nq) A.qpos[i] = src[i];
   src = row_of<R>(d.qvel, w, m.nv); FOR(i, m.nv) A.qvel[i] = src[i];
@@ -1738,7 +1813,7 @@ template <class R, int T> __device__ void load_world(const B200Model &m, const B
   SYNC();
 }
 
-template <class R, int T> __device__ void store_state(const B200Model &m, const B200Data &d, Arena<R> &A, int w) {
+template <class R, int T> __device__ __noinline__ void store_state(const B200Model &m, const B200Data &d, Arena<R> &A, int w) {
   R *dst;
   dst = row_of<R>(d.qpos, w, m.nq); FOR(i, m.nq) dst[i] = A.qpos[i];
   dst = row_of<R>(d.qvel, w, m.nv); FOR(i, m.nv) dst[i] = A.qvel[i];
@@ -1780,7 +1855,7 @@ template <class R, int T> __device__ void store_state(const B200Model &m, const 
 }
 
 // derived outputs of the last substep (pre-integration, as MuJoCo publishes)
-template <class R, int T> __device__ void store_outputs(const B200Model &m, const B200Data &d, Arena<R> &A, int w) {
+template <class R, int T> __device__ __noinline__ void store_outputs(const B200Model &m, const B200Data &d, Arena<R> &A, int w) {
   R *dst;
   const int nb = m.nbody, ng = m.ngeom, ns = m.nsite, nv = m.nv, nc = m.ncon_max;
   if ((dst = row_of<R>(d.xpos, w, nb * 3))) FOR(i, nb * 3) dst[i] = A.xpos[i];
@@ -1818,17 +1893,28 @@ template <class R, int T> __device__ void store_outputs(const B200Model &m, cons
 // code region; the Newton loop runs until every world of the CTA has met its
 // stop rule, worlds already done idle.  Warps past the last world take part
 // in the barriers only.
-#define STAGE(call, k) \
-  do {                 \
-    if (act) {         \
-      call;            \
-      mark(A, k);      \
-    }                  \
-    __syncthreads();   \
+// B200_SYNC_LEVEL: 2 = CTA barrier after every stage (lockstep worlds),
+// 1 = one CTA barrier per substep, 0 = worlds run free (warp syncs only).
+#ifndef B200_SYNC_LEVEL
+#define B200_SYNC_LEVEL 2
+#endif
+#if B200_SYNC_LEVEL == 2
+#define STAGE_SYNC() __syncthreads()
+#else
+#define STAGE_SYNC() __syncwarp()
+#endif
+#define STAGE(call, k)  \
+  do {                  \
+    if (act) {          \
+      call;             \
+      mark(A, k);       \
+    }                   \
+    STAGE_SYNC();       \
+    if (act) mark(A, 15); \
   } while (0)
 
 // factor of the mass matrix, one block per kinematic tree (mjwarp_mass_factor.cu)
-template <class R> __device__ void mass_factor(const Mdl<R> &M, Arena<R> &A) {
+template <class R> __device__ B200_STAGE_ATTR void mass_factor(const Mdl<R> &M, Arena<R> &A) {
   FOR(k, M.m.nM) A.L[k] = A.M[k];
   SYNC();
   chol_blocks(A.L, tree_rows(M, LANE), M.m.max_tree_dofs, M.m.nv, A.colbuf);
@@ -1845,9 +1931,16 @@ template <class R> __device__ void step1_stages(const Mdl<R> &M, Arena<R> &A, bo
 
 template <class R> __device__ void newton_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
   STAGE((newton_init<R, 32>(M, A)), 0);
+#if B200_SYNC_LEVEL == 2
   while (__syncthreads_or(act && !A.iscal[5])) {
+    if (act) mark(A, 15);  // barrier wait and idle iterations of worlds already done
     if (act && !A.iscal[5]) newton_iteration<R, 32>(M, A);
   }
+#else
+  if (act)
+    while (!A.iscal[5]) newton_iteration<R, 32>(M, A);  // warp-uniform: iscal[5] is read after a warp sync
+#endif
+  if (act) mark(A, 15);
 }
 
 template <class R>
@@ -1870,6 +1963,9 @@ __global__ void __launch_bounds__(256, 1) control_step(const B200Model m, const 
   }
   __syncthreads();
   for (int s = 0; s < substeps; ++s) {
+#if B200_SYNC_LEVEL == 1
+    __syncthreads();
+#endif
     step1_stages(M, A, act);
     STAGE((osc_control<R, 32>(M, A, policy && s == 0)), 7);
     STAGE((actuation<R, 32>(M, A)), 8);
@@ -1895,7 +1991,7 @@ __global__ void __launch_bounds__(256, 1) control_step(const B200Model m, const 
   store_state<R, 32>(m, d, A, w);
   if (LANE == 0 && d.stage_cycles) {
     int *out = irow_of(d.stage_cycles, w, 16);
-    for (int k = 1; k < 15; ++k) out[k] += (int)A.prof[k];
+    for (int k = 1; k < 16; ++k) out[k] += (int)A.prof[k];
   }
 }
 
