@@ -44,6 +44,7 @@ def parse():
     p.add_argument('--impl', default='b200', choices=('b200', 'reference'))
     p.add_argument('--seed', type=int, default=0)
     p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--no-gather', action='store_true', help='skip the per-step observation all-gather (N > 1)')
     return p.parse_args()
 
 
@@ -185,7 +186,7 @@ def main():
     dev = torch.device('cuda', local)
     if world_size > 1:
         from datetime import timedelta
-        dist.init_process_group('nccl', device_id=dev, timeout=timedelta(seconds=300))
+        dist.init_process_group('nccl', device_id=dev, timeout=timedelta(seconds=120))
     W = args.worlds
     offset = rank * W
     rt = Runtime(scene, W, device=dev, precision=args.precision, world_offset=offset)
@@ -198,9 +199,17 @@ def main():
                         for k in range(total)]).to(dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MiB > 126 MB L2
     stream = torch.cuda.current_stream(dev)
+    gather = None
+    if world_size > 1 and not args.no_gather:
+        from gpu_libero_b200.shard import ObservationGather
+        gather = ObservationGather(rt)  # every rank's obs slab to rank 0, overlapped with the next step
     for k in range(args.warmup):
         rt.buffers['action'].copy_(acts[k])
         rt._graph.replay()
+        if gather:
+            gather.launch()
+    if gather:
+        gather.wait()
     torch.cuda.synchronize(dev)
     counters0 = {k: rt.buffers[k].clone() for k in ('efc_total', 'con_total', 'newton_rows', 'ls_rows',
                                                      'newton_total')}
@@ -217,7 +226,12 @@ def main():
         rt.buffers['action'].copy_(acts[k])
         events[i][0].record(stream)
         rt._graph.replay()
+        if gather:
+            gather.launch()
         events[i][1].record(stream)
+    if gather:
+        gather.wait()
+        events[-1][1].record(stream)  # the last gather ends inside the timed region
     torch.cuda.synchronize(dev)
     clock = clocks.stop()
     if world_size > 1:
@@ -234,7 +248,8 @@ def main():
     kernel_s = elapsed / args.steps  # one kernel per graph replay
     sm_count = torch.cuda.get_device_properties(dev).multi_processor_count
     sm_mhz = clock['sm_mhz'] if clock else 1965.0
-    peak = flops.fp32_peak_tflops(sm_count, sm_mhz)
+    fp64 = args.precision == 'fp64'
+    peak = (flops.fp64_peak_tflops if fp64 else flops.fp32_peak_tflops)(sm_count, sm_mhz)
     achieved = fl / args.steps / kernel_s / 1e12
     real_b = rt.buffers['qpos'].element_size()
     io_real = sum(scene.sizes[k] for k in ('nq',)) * 2 + scene.sizes['nv'] * 4 + scene.sizes['nu'] * 2 + 2 * (3 + 9 + 2) + 7 + 2
@@ -285,14 +300,18 @@ def main():
             config=dict(workload='%s: Franka-like arm + gripper + plane + 3 free boxes, elliptic cones, '
                                  '25 substeps/control step' % scene.name,
                         worlds_per_gpu=W, total_worlds=W * world_size, substeps=scene.substeps,
-                        parallelism='world shards, one process per GPU', l2='flushed (256 MiB write) between steps'),
+                        parallelism='world shards, one process per GPU', l2='flushed (256 MiB write) between steps',
+                        obs_gather=('NCCL all-gather of the [W, %d] observation slab every step, side stream, '
+                                    '%d bytes per step' % (scene.sizes['nobs'], gather.bytes_per_launch())
+                                    if gather else None)),
             substeps_per_sec=value * scene.substeps,
             e2e=dict(value=world_size * W * args.steps / e2e_max, unit=UNIT,
                      h2d_bytes_per_step=env.runtime.h2d_bytes_per_step(),
                      d2h_bytes_per_step=env.runtime.d2h_bytes_per_step()),
-            roofline=dict(bound='fp32', achieved=achieved, peak=peak, unit='TFLOP/s', frac=achieved / peak,
-                          traffic=traffic, peak_source='nominal FP32 CUDA-core issue: %d SMs x 128 lanes x 2 x '
-                          '%.0f MHz (sampled)' % (sm_count, sm_mhz),
+            roofline=dict(bound='fp64' if fp64 else 'fp32', achieved=achieved, peak=peak, unit='TFLOP/s',
+                          frac=achieved / peak, traffic=traffic,
+                          peak_source='nominal %s CUDA-core issue: %d SMs x %d lanes x 2 x %.0f MHz (sampled)'
+                          % ('FP64' if fp64 else 'FP32', sm_count, 64 if fp64 else 128, sm_mhz),
                           flops_per_world_substep=fl / (W * args.steps * scene.substeps)),
             roofline_hbm=dict(bound='hbm', achieved=bytes_per_world * W / kernel_s / 1e9, peak=hbm_gbs, unit='GB/s',
                               frac=bytes_per_world * W / kernel_s / 1e9 / hbm_gbs, peak_source=peak_src,

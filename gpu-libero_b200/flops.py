@@ -46,3 +46,8 @@ def osc_flops(worlds, substeps):
 def fp32_peak_tflops(sm_count, sm_mhz):
     """Nominal FP32 CUDA-core peak: 128 FP32 lanes per SM, 2 FLOPs per FMA."""
     return sm_count * 128 * 2 * sm_mhz * 1e6 / 1e12
+
+
+def fp64_peak_tflops(sm_count, sm_mhz):
+    """Nominal FP64 CUDA-core peak: 64 FP64 lanes per SM, 2 FLOPs per FMA."""
+    return sm_count * 64 * 2 * sm_mhz * 1e6 / 1e12

@@ -479,10 +479,15 @@ class Scene:
             qpos[adr + 3:adr + 7] = axis_quat((0, 0, 1), yaw)
 
     def actions(self, nworld, step, seed=0, world_offset=0):
-        """Seeded OSC_POSE actions: U[-1,1]^6 plus a gripper sign in {-1,1}."""
-        rng = np.random.default_rng([seed, 7919, step, world_offset])
-        a = rng.uniform(-1.0, 1.0, (nworld, 7))
-        a[:, 6] = np.where(rng.uniform(size=nworld) < 0.5, -1.0, 1.0)
+        """Seeded OSC_POSE actions: U[-1,1]^6 plus a gripper sign in {-1,1}.
+
+        Drawn per global world index (one stream per step, the first
+        world_offset + nworld draws), so a shard's actions do not depend on
+        the GPU count."""
+        n = world_offset + nworld
+        a = np.random.default_rng([seed, 7919, step, 0]).uniform(-1.0, 1.0, (n, 7))[world_offset:]
+        grip = np.random.default_rng([seed, 7919, step, 1]).uniform(size=n)[world_offset:]
+        a[:, 6] = np.where(grip < 0.5, -1.0, 1.0)
         return a
 
     @property

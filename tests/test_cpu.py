@@ -74,6 +74,8 @@ def test_seeds_do_not_depend_on_shard_layout(scene):
     assert np.array_equal(q_all[4:], q_hi)
     a = scene.actions(4, 2, seed=3, world_offset=0)
     assert a.shape == (4, 7) and np.all(np.abs(a) <= 1) and set(np.unique(a[:, 6])) <= {-1.0, 1.0}
+    assert np.array_equal(scene.actions(8, 2, seed=3)[5:], scene.actions(3, 2, seed=3, world_offset=5))
+    assert np.array_equal(scene.actions(8, 2, seed=3)[:1], scene.actions(1, 2, seed=3))
 
 
 def run_oracle(oracle_module, scene, precision, n, steps, seed):
@@ -134,3 +136,15 @@ def test_product_path_fails_loudly_without_cuda(scene):
     from gpu_libero_b200.runtime import B200BatchEnv
     with pytest.raises(RuntimeError, match='CUDA'):
         B200BatchEnv(scene, 2)
+
+
+def test_oracle_pyramidal_cones_rest_and_track_fp64(oracle_module):
+    pyr = scenes.scene_a(cone='pyramidal')
+    assert pyr.sizes['cone'] == 0 and pyr.sizes['nefc_max'] == 9 + 9 + 4 * pyr.sizes['ncon_max']
+    a = run_oracle(oracle_module, pyr, 'fp32', 2, 10, seed=6)
+    b = run_oracle(oracle_module, pyr, 'fp64', 2, 10, seed=6)
+    assert not np.any(a['overflow'] & ~0x600) and not np.any(a['error'])
+    assert np.max(np.abs(a['qpos'] - b['qpos'])) < 1e-3
+    for j in np.flatnonzero(pyr.ints['jnt_type'] == 0):
+        z = a['qpos'][:, pyr.ints['jnt_qposadr'][j] + 2]
+        assert np.all(z > 0.015) and np.all(z < 0.06)

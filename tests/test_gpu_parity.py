@@ -66,8 +66,24 @@ def test_forward_parity(scene, oracle_module, precision, rel):
     assert close(gpu['qfrc_constraint'], ref['qfrc_constraint'], 10 * rel)
 
 
+@pytest.fixture(scope='module')
+def pyramidal():
+    return scenes.scene_a(cone='pyramidal')
+
+
 @pytest.mark.parametrize('precision,tol', [('fp32', 1e-4), ('fp64', 1e-7)])
 def test_control_steps_parity(scene, oracle_module, precision, tol):
+    control_steps_parity(scene, oracle_module, precision, tol)
+
+
+@pytest.mark.parametrize('precision,tol', [('fp32', 1e-4), ('fp64', 1e-7)])
+def test_pyramidal_control_steps_parity(pyramidal, oracle_module, precision, tol):
+    """Pyramidal friction cones: 2(condim-1) rows per contact, each an
+    independent inequality row (mjwarp_constraint_build.cu row counts)."""
+    control_steps_parity(pyramidal, oracle_module, precision, tol)
+
+
+def control_steps_parity(scene, oracle_module, precision, tol):
     n = 8
     rt = make_runtime(scene, n, precision, seed=5)
     ref = host_copy(rt, n)
