@@ -402,12 +402,14 @@ template <class R, int T> __device__ B200_STAGE_ATTR void mass_mul(const Mdl<R> 
 }
 
 // ============================================================ collision
-template <class R, int T> __device__ B200_STAGE_ATTR void collision(const Mdl<R> &M, Arena<R> &A) {
+// CONVEX: the kernel variant for models with mesh geoms (plane-mesh and the
+// GJK/EPA pairs); models without meshes run the smaller variant.
+template <class R, int T, bool CONVEX> __device__ B200_STAGE_ATTR void collision(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   if (LANE == 0) A.iscal[8] = 0;
   SYNC();
   if (!(m.disable_flags & (B200_DSBL_CONSTRAINT | B200_DSBL_CONTACT))) {
-    FOR(p, m.npair) collide_pair(M, A, p);
+    FOR(p, m.npair) collide_pair<R, CONVEX>(M, A, p);
   }
   SYNC();
   const int n = mmin(A.iscal[8], m.ncon_max);
@@ -1920,11 +1922,11 @@ template <class R> __device__ B200_STAGE_ATTR void mass_factor(const Mdl<R> &M, 
   chol_blocks(A.L, tree_rows(M, LANE), M.m.max_tree_dofs, M.m.nv, A.colbuf);
 }
 
-template <class R> __device__ void step1_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
+template <class R, bool CONVEX> __device__ void step1_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
   STAGE((kinematics<R, 32>(M, A)), 1);
   STAGE((com_crb_mass<R, 32>(M, A)), 2);
   STAGE((mass_factor<R>(M, A)), 3);
-  STAGE((collision<R, 32>(M, A)), 4);
+  STAGE((collision<R, 32, CONVEX>(M, A)), 4);
   STAGE((constraints<R, 32>(M, A)), 5);
   STAGE((velocity<R, 32>(M, A)), 6);
 }
@@ -1943,7 +1945,7 @@ template <class R> __device__ void newton_stages(const Mdl<R> &M, Arena<R> &A, b
   if (act) mark(A, 15);
 }
 
-template <class R>
+template <class R, bool CONVEX>
 __global__ void __launch_bounds__(256, 1) control_step(const B200Model m, const B200Data d, int substeps, int policy, int wpc,
                                                      int arena) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -1966,7 +1968,7 @@ __global__ void __launch_bounds__(256, 1) control_step(const B200Model m, const 
 #if B200_SYNC_LEVEL == 1
     __syncthreads();
 #endif
-    step1_stages(M, A, act);
+    step1_stages<R, CONVEX>(M, A, act);
     STAGE((osc_control<R, 32>(M, A, policy && s == 0)), 7);
     STAGE((actuation<R, 32>(M, A)), 8);
     newton_stages(M, A, act);
@@ -1995,7 +1997,7 @@ __global__ void __launch_bounds__(256, 1) control_step(const B200Model m, const 
   }
 }
 
-template <class R>
+template <class R, bool CONVEX>
 __global__ void __launch_bounds__(256, 1) forward_step(const B200Model m, const B200Data d, int bootstrap, const int *mask,
                                                      int wpc, int arena) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -2006,7 +2008,7 @@ __global__ void __launch_bounds__(256, 1) forward_step(const B200Model m, const 
   const Mdl<R> M(m);
   if (act) load_world<R, 32>(m, d, A, w);
   __syncthreads();
-  step1_stages(M, A, act);
+  step1_stages<R, CONVEX>(M, A, act);
   if (act && bootstrap) {
     FOR(i, 3) A.goal_pos[i] = A.sxpos[3 * m.ee_site + i];
     FOR(i, 9) A.goal_rot[i] = A.sxmat[9 * m.ee_site + i];
@@ -2068,17 +2070,29 @@ int worlds_per_cta(const B200Model *m, int limit) {
 template <class K> int configure(K kernel, size_t smem) {
   return (int)cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
-template <class R> int prepare_t(const B200Model *m, int wpc) {
+template <class R, bool C> int prepare_t(const B200Model *m, int wpc) {
   const size_t smem = (size_t)wpc * arena_for(m);
   int rc;
-  if ((rc = configure(b200::control_step<R>, smem))) return rc;
-  return configure(b200::forward_step<R>, smem);
+  if ((rc = configure(b200::control_step<R, C>, smem))) return rc;
+  return configure(b200::forward_step<R, C>, smem);
 }
 int launch_shape(const B200Model *m, int *wpc) {
   const int limit = max_optin_smem();
   *wpc = worlds_per_cta(m, limit);
   if (*wpc < 1) return (int)cudaErrorInvalidValue;
-  return m->real_bytes == 4 ? prepare_t<float>(m, *wpc) : prepare_t<double>(m, *wpc);
+  const bool convex = m->nmesh > 0;
+  if (m->real_bytes == 4) return convex ? prepare_t<float, true>(m, *wpc) : prepare_t<float, false>(m, *wpc);
+  return convex ? prepare_t<double, true>(m, *wpc) : prepare_t<double, false>(m, *wpc);
+}
+template <class R, bool C>
+void launch_step(const B200Model &m, const B200Data &d, int substeps, int policy, int wpc, int arena, int grid,
+                 size_t smem, cudaStream_t s) {
+  b200::control_step<R, C><<<grid, 32 * wpc, smem, s>>>(m, d, substeps, policy, wpc, arena);
+}
+template <class R, bool C>
+void launch_forward(const B200Model &m, const B200Data &d, int bootstrap, const int *mask, int wpc, int arena,
+                    int grid, size_t smem, cudaStream_t s) {
+  b200::forward_step<R, C><<<grid, 32 * wpc, smem, s>>>(m, d, bootstrap, mask, wpc, arena);
 }
 }  // namespace
 
@@ -2103,10 +2117,10 @@ int b200phys_step_launch(const B200Model *m, const B200Data *d, int substeps, in
   const int arena = (int)arena_for(m), grid = (d->nworld + wpc - 1) / wpc;
   const size_t smem = (size_t)wpc * arena;
   cudaStream_t s = (cudaStream_t)stream;
-  if (m->real_bytes == 4)
-    b200::control_step<float><<<grid, 32 * wpc, smem, s>>>(*m, *d, substeps, policy, wpc, arena);
-  else
-    b200::control_step<double><<<grid, 32 * wpc, smem, s>>>(*m, *d, substeps, policy, wpc, arena);
+  // kernel variant by precision and by the presence of mesh geoms
+  auto f = m->real_bytes == 4 ? (m->nmesh > 0 ? launch_step<float, true> : launch_step<float, false>)
+                              : (m->nmesh > 0 ? launch_step<double, true> : launch_step<double, false>);
+  f(*m, *d, substeps, policy, wpc, arena, grid, smem, s);
   return (int)cudaGetLastError();
 }
 
@@ -2118,10 +2132,9 @@ int b200phys_forward_launch(const B200Model *m, const B200Data *d, int bootstrap
   const int arena = (int)arena_for(m), grid = (d->nworld + wpc - 1) / wpc;
   const size_t smem = (size_t)wpc * arena;
   cudaStream_t s = (cudaStream_t)stream;
-  if (m->real_bytes == 4)
-    b200::forward_step<float><<<grid, 32 * wpc, smem, s>>>(*m, *d, bootstrap, mask, wpc, arena);
-  else
-    b200::forward_step<double><<<grid, 32 * wpc, smem, s>>>(*m, *d, bootstrap, mask, wpc, arena);
+  auto f = m->real_bytes == 4 ? (m->nmesh > 0 ? launch_forward<float, true> : launch_forward<float, false>)
+                              : (m->nmesh > 0 ? launch_forward<double, true> : launch_forward<double, false>);
+  f(*m, *d, bootstrap, mask, wpc, arena, grid, smem, s);
   return (int)cudaGetLastError();
 }
 }

@@ -12,6 +12,8 @@
 //   plane     mjwarp_plane.cu:18-60 (sphere, capsule, box)
 //   box       mjwarp_box.cu:14-176 (sphere-box, capsule-box, box-box SAT+clip)
 //   material  mjwarp_contact.cuh:60-98
+// plus the sphere/capsule primitives, plane-mesh and the convex (GJK/EPA)
+// pairs of dropped objects (see the sections below).
 #pragma once
 #include "arena.cuh"
 #include "math.cuh"
@@ -511,13 +513,505 @@ __device__ void box_pair(const Mdl<R> &M, Arena<R> &A, int pair, int g1, int g2)
   }
 }
 
-template <class R> __device__ void collide_pair(const Mdl<R> &M, Arena<R> &A, int pair) {
+// ---------------------------------------------------------------- sphere / capsule pairs
+// MuJoCo's primitive colliders as the reference's native engine carries them
+// (collision_detect_primitive.cuh: _SphereSphere :261-292, mjc_SphereCapsule
+// :306-322, mjc_CapsuleCapsule :401-490 with its two-contact parallel case).
+template <class R> struct PrimHits {
+  int count;
+  R dist[2];
+  V3<R> pos[2], normal[2];
+};
+
+template <class R>
+__device__ int prim_sphere_sphere(PrimHits<R> &o, R margin, V3<R> p1, const R *m1, R r1, V3<R> p2, const R *m2, R r2) {
+  const V3<R> dif = p1 - p2;
+  const R cd2 = dot(dif, dif), mind = margin + r1 + r2;
+  if (cd2 > mind * mind) return 0;
+  const int c = o.count;
+  const R dist = msqrt(cd2) - r1 - r2;
+  V3<R> n = p2 - p1;
+  R len = msqrt(dot(n, n));
+  if (len < R(1e-15)) {
+    n = cross(col(m1, 2), col(m2, 2));
+    len = msqrt(dot(n, n));
+    n = len > R(0) ? n * (R(1) / len) : v3<R>(1, 0, 0);
+  } else
+    n = n * (R(1) / len);
+  o.dist[c] = dist;
+  o.normal[c] = n;
+  o.pos[c] = p1 + n * (r1 + dist * R(0.5));
+  o.count = c + 1;
+  return 1;
+}
+
+template <class R>
+__device__ __noinline__ void prim_pair(const Mdl<R> &M, Arena<R> &A, int pair, int g1, int g2) {
+  const Material<R> p = material(M, g1, g2);
+  const int t1 = IF(geom_type)[g1], t2 = IF(geom_type)[g2];
+  const V3<R> p1 = ld3(A.gxpos + 3 * g1), p2 = ld3(A.gxpos + 3 * g2);
+  const R *m1 = A.gxmat + 9 * g1, *m2 = A.gxmat + 9 * g2;
+  const R *s1 = RF(geom_size) + 3 * g1, *s2 = RF(geom_size) + 3 * g2;
+  const R margin = p.margin + p.gap;
+  PrimHits<R> o;
+  o.count = 0;
+  if (t1 == B200_GEOM_SPHERE && t2 == B200_GEOM_SPHERE) {
+    prim_sphere_sphere(o, margin, p1, m1, s1[0], p2, m2, s2[0]);
+  } else if (t1 == B200_GEOM_SPHERE) {
+    const V3<R> axis = col(m2, 2);
+    const R x = mclamp(dot(axis, p1 - p2), -s2[1], s2[1]);
+    prim_sphere_sphere(o, margin, p1, m1, s1[0], p2 + axis * x, m2, s2[0]);
+  } else {
+    const V3<R> a1 = col(m1, 2) * s1[1], a2 = col(m2, 2) * s2[1], dif = p1 - p2;
+    const R ma = dot(a1, a1), mb = -dot(a1, a2), mc = dot(a2, a2), u = -dot(a1, dif), v = dot(a2, dif);
+    const R det = ma * mc - mb * mb;
+    if (mabs(det) >= R(1e-15)) {
+      R x1 = (mc * u - mb * v) / det, x2 = (ma * v - mb * u) / det;
+      if (x1 > R(1)) { x1 = 1; x2 = (v - mb) / mc; }
+      else if (x1 < R(-1)) { x1 = -1; x2 = (v + mb) / mc; }
+      if (x2 > R(1)) { x2 = 1; x1 = mclamp((u - mb) / ma, R(-1), R(1)); }
+      else if (x2 < R(-1)) { x2 = -1; x1 = mclamp((u + mb) / ma, R(-1), R(1)); }
+      prim_sphere_sphere(o, margin, p1 + a1 * x1, m1, s1[0], p2 + a2 * x2, m2, s2[0]);
+    } else {
+      R x2 = mclamp((v - mb) / mc, R(-1), R(1));
+      int n = prim_sphere_sphere(o, margin, p1 + a1, m1, s1[0], p2 + a2 * x2, m2, s2[0]);
+      x2 = mclamp((v + mb) / mc, R(-1), R(1));
+      n += prim_sphere_sphere(o, margin, p1 - a1, m1, s1[0], p2 + a2 * x2, m2, s2[0]);
+      if (n < 2) {
+        R x1 = mclamp((u - mb) / ma, R(-1), R(1));
+        n += prim_sphere_sphere(o, margin, p1 + a1 * x1, m1, s1[0], p2 + a2, m2, s2[0]);
+        if (n < 2) {
+          x1 = mclamp((u + mb) / ma, R(-1), R(1));
+          prim_sphere_sphere(o, margin, p1 + a1 * x1, m1, s1[0], p2 - a2, m2, s2[0]);
+        }
+      }
+    }
+  }
+  for (int c = 0; c < o.count; ++c) {
+    V3<R> fr[3];
+    frame_from_normal(o.normal[c], fr);
+    emit(M, A, p, pair, c, g1, g2, o.dist[c], o.pos[c], fr);
+  }
+}
+
+// ---------------------------------------------------------------- plane - mesh
+// The deepest vertex, then up to three more vertices of its most plane-facing
+// incident polygon (mjwarp_plane.cu mesh manifold; restated in
+// tools/validation/mjwarp_plane_reference.py mesh_manifold).
+template <class R>
+__device__ __noinline__ void plane_mesh(const Mdl<R> &M, Arena<R> &A, const Material<R> &p, int pair, int g1, int g2) {
+  const V3<R> origin = ld3(A.gxpos + 3 * g1), n = col(A.gxmat + 9 * g1, 2), center = ld3(A.gxpos + 3 * g2);
+  const R *Rg = A.gxmat + 9 * g2;
+  const int mesh = IF(geom_dataid)[g2], nvert = IF(mesh_vertnum)[mesh];
+  const R *vert = RF(mesh_vert) + 3 * IF(mesh_vertadr)[mesh];
+  const V3<R> local = rotT(Rg, n);
+  int best = 0;
+  R top = -dot(ld3(vert), local);
+  for (int i = 1; i < nvert; ++i) {
+    const R s = -dot(ld3(vert + 3 * i), local);
+    if (s > top) { top = s; best = i; }
+  }
+  V3<R> fr[3];
+  frame_from_normal(n, fr);
+  const V3<R> world = center + rot(Rg, ld3(vert + 3 * best));
+  const R dist = dot(n, world - origin);
+  emit(M, A, p, pair, 0, g1, g2, dist, world - n * (R(0.5) * dist), fr);
+  if (IF(mesh_polynum)[mesh] <= 0 || dist > p.margin + p.gap) return;
+  const int vg = IF(mesh_vertadr)[mesh] + best, madr = IF(mesh_polymapadr)[vg], mnum = IF(mesh_polymapnum)[vg];
+  const int pbase = IF(mesh_polyadr)[mesh];
+  int face = -1;
+  R lowest = 1;
+  for (int f = 0; f < mnum; ++f) {
+    const int poly = pbase + IF(mesh_polymap)[madr + f];
+    const R d = dot(ld3(RF(mesh_polynormal) + 3 * poly), local);
+    if (d < R(1) && (face < 0 || d < lowest)) { lowest = d; face = poly; }
+  }
+  if (face < 0) return;
+  const int *pv = IF(mesh_polyvert) + IF(mesh_polyvertadr)[face];
+  const int count = IF(mesh_polyvertnum)[face];
+  int a = 0;
+  for (int i = 0; i < count; ++i)
+    if (pv[i] == best) { a = i; break; }
+  int sel[4] = {a, (a + 1) % count, (a + 2) % count, (a + 3) % count};
+  if (count > 4) {
+    auto area = [&](int b, int c, int d) {
+      const V3<R> x = cross(ld3(vert + 3 * pv[a]) - ld3(vert + 3 * pv[c]), ld3(vert + 3 * pv[b]) - ld3(vert + 3 * pv[d]));
+      return R(0.5) * msqrt(dot(x, x));
+    };
+    int b = sel[1], c = sel[2], d = sel[3];
+    R cur = area(b, c, d);
+    while (area(b, c, (d + 1) % count) > cur) {
+      d = (d + 1) % count; cur = area(b, c, d);
+      while (area(b, (c + 1) % count, d) > cur) { c = (c + 1) % count; cur = area(b, c, d); }
+      while (area((b + 1) % count, c, d) > cur) { b = (b + 1) % count; cur = area(b, c, d); }
+    }
+    sel[1] = b; sel[2] = c; sel[3] = d;
+  }
+  const int nsel = count < 4 ? count : 4;
+  for (int i = 1; i < nsel; ++i) {
+    const V3<R> w = center + rot(Rg, ld3(vert + 3 * pv[sel[i]]));
+    if (dot(n, w - center) > R(0)) continue;
+    const R d = dot(n, w - origin);
+    emit(M, A, p, pair, i, g1, g2, d, w - n * (R(0.5) * d), fr);
+  }
+}
+
+// ---------------------------------------------------------------- convex pairs (GJK / EPA)
+// The reference's CCD contract (mjwarp_convex_collision.cuh:46-78,
+// mjwarp_convex_epa.cuh gjk_phase): supports inflated by half the pair margin
+// on each shape, sphere / capsule cores first, GJK distance with a separation
+// cutoff, EPA for penetration, one contact at the witness midpoint.  The
+// distance subalgorithm searches every sub-simplex of the current simplex;
+// EPA is the expanding polytope method (van den Bergen 2001).  One thread
+// runs one pair; the polytope lives in the thread's local memory.
+template <class R> struct CShape {
+  int type, nvert;
+  V3<R> pos, size;
+  const R *rot, *vert;
+  R margin;
+};
+
+template <class R> __device__ V3<R> cs_support(const CShape<R> &s, V3<R> d) {
+  if (s.type == B200_GEOM_SPHERE) return s.pos + d * (s.size.x + R(0.5) * s.margin);
+  const V3<R> l = rotT(s.rot, d);
+  V3<R> r;
+  if (s.type == B200_GEOM_CAPSULE) {
+    r = l * s.size.x;
+    r.z += (l.z > R(0) ? R(1) : l.z < R(0) ? R(-1) : R(0)) * s.size.y;
+  } else if (s.type == B200_GEOM_BOX) {
+    r = v3<R>(l.x > R(0) ? s.size.x : -s.size.x, l.y > R(0) ? s.size.y : -s.size.y, l.z > R(0) ? s.size.z : -s.size.z);
+  } else {
+    int best = 0;
+    R top = dot(ld3(s.vert), l);
+    for (int i = 1; i < s.nvert; ++i) {
+      const R v = dot(ld3(s.vert + 3 * i), l);
+      if (v > top) { top = v; best = i; }
+    }
+    r = ld3(s.vert + 3 * best);
+  }
+  V3<R> p = rot(s.rot, r) + s.pos;
+  if (s.margin > R(0)) p = p + d * (R(0.5) * s.margin);
+  return p;
+}
+
+template <class R> struct Simplex {
+  V3<R> w[4], a[4], b[4];
+  R lam[4];
+  int n;
+};
+
+template <class R> __device__ R det3(const R G[3][3]) {
+  return G[0][0] * (G[1][1] * G[2][2] - G[1][2] * G[2][1]) - G[0][1] * (G[1][0] * G[2][2] - G[1][2] * G[2][0]) +
+         G[0][2] * (G[1][0] * G[2][1] - G[1][1] * G[2][0]);
+}
+
+template <class R> __device__ void simplex_reduce(Simplex<R> &s) {
+  R best = R(1e30), lam_best[4] = {0, 0, 0, 0};
+  int mask_best = 0;
+  for (int mask = 1; mask < (1 << s.n); ++mask) {
+    int idx[4], k = 0;
+    for (int i = 0; i < s.n; ++i)
+      if (mask & (1 << i)) idx[k++] = i;
+    R lam[4] = {0, 0, 0, 0}, mu[3] = {0, 0, 0};
+    if (k > 1) {
+      V3<R> e[3];
+      const V3<R> w0 = s.w[idx[0]];
+      for (int j = 1; j < k; ++j) e[j - 1] = s.w[idx[j]] - w0;
+      const int q = k - 1;
+      R G[3][3], rhs[3];
+      for (int i = 0; i < q; ++i) {
+        rhs[i] = -dot(e[i], w0);
+        for (int j = 0; j < q; ++j) G[i][j] = dot(e[i], e[j]);
+      }
+      if (q == 1) {
+        const R det = G[0][0];
+        if (!(det > R(1e-30))) continue;
+        mu[0] = rhs[0] / det;
+      } else if (q == 2) {
+        const R det = G[0][0] * G[1][1] - G[0][1] * G[1][0];
+        if (!(mabs(det) > R(1e-30))) continue;
+        mu[0] = (rhs[0] * G[1][1] - G[0][1] * rhs[1]) / det;
+        mu[1] = (G[0][0] * rhs[1] - rhs[0] * G[1][0]) / det;
+      } else {
+        const R det = det3(G);
+        if (!(mabs(det) > R(1e-30))) continue;
+        for (int c = 0; c < 3; ++c) {
+          R M3[3][3];
+          for (int i = 0; i < 3; ++i)
+            for (int j = 0; j < 3; ++j) M3[i][j] = j == c ? rhs[i] : G[i][j];
+          mu[c] = det3(M3) / det;
+        }
+      }
+      R l0 = 1;
+      for (int j = 0; j < q; ++j) { lam[j + 1] = mu[j]; l0 -= mu[j]; }
+      lam[0] = l0;
+      bool ok = true;
+      for (int j = 0; j < k; ++j) ok &= lam[j] > R(0);
+      if (!ok) continue;
+    } else
+      lam[0] = 1;
+    V3<R> x = v3<R>(0, 0, 0);
+    for (int j = 0; j < k; ++j) x = x + s.w[idx[j]] * lam[j];
+    const R d = dot(x, x);
+    if (d < best) {
+      best = d; mask_best = mask;
+      for (int j = 0; j < 4; ++j) lam_best[j] = lam[j];
+    }
+  }
+  Simplex<R> t;
+  int k = 0;
+  for (int i = 0; i < s.n; ++i)
+    if (mask_best & (1 << i)) { t.w[k] = s.w[i]; t.a[k] = s.a[i]; t.b[k] = s.b[i]; t.lam[k] = lam_best[k]; ++k; }
+  t.n = k;
+  s = t;
+}
+
+template <class R> struct GjkOut {
+  bool separated;
+  R dist;
+  V3<R> x1, x2;
+  Simplex<R> s;
+};
+
+template <class R> __device__ GjkOut<R> gjk(const CShape<R> &A, const CShape<R> &B, R tol, int iterations, R cutoff) {
+  GjkOut<R> o;
+  o.separated = false;
+  Simplex<R> &s = o.s;
+  s.n = 0;
+  V3<R> x = A.pos - B.pos;
+  R norm = msqrt(dot(x, x)), prev = -1;
+  for (int it = 0; it < iterations; ++it) {
+    if (norm < tol || mabs(prev - norm) < R(1e-15)) break;
+    const V3<R> d = x * (R(1) / norm);
+    const V3<R> a = cs_support(A, -d), b = cs_support(B, d), w = a - b;
+    if (dot(x, x - w) < R(0.5) * tol * tol) break;
+    const R lower = dot(x, w);
+    if (lower > R(0) && (cutoff == R(0) || lower >= cutoff * norm)) {
+      o.separated = true;
+      o.dist = R(1e30);
+      return o;
+    }
+    s.w[s.n] = w; s.a[s.n] = a; s.b[s.n] = b; s.n++;
+    simplex_reduce(s);
+    x = v3<R>(0, 0, 0);
+    for (int i = 0; i < s.n; ++i) x = x + s.w[i] * s.lam[i];
+    prev = norm;
+    norm = msqrt(dot(x, x));
+    if (s.n == 4) break;
+  }
+  o.x1 = v3<R>(0, 0, 0); o.x2 = v3<R>(0, 0, 0);
+  for (int i = 0; i < s.n; ++i) { o.x1 = o.x1 + s.a[i] * s.lam[i]; o.x2 = o.x2 + s.b[i] * s.lam[i]; }
+  if (s.n == 0) { o.x1 = A.pos; o.x2 = B.pos; }
+  o.dist = s.n == 4 ? R(0) : norm;
+  return o;
+}
+
+constexpr int kEpaMaxV = 48, kEpaMaxF = 96;
+template <class R> struct Polytope {
+  V3<R> w[kEpaMaxV], a[kEpaMaxV], b[kEpaMaxV];
+  int nv, nf, face[kEpaMaxF][3];
+  V3<R> n[kEpaMaxF];
+  R d[kEpaMaxF];
+  bool alive[kEpaMaxF];
+};
+
+template <class R> __device__ int epa_add_face(Polytope<R> &P, int i, int j, int l) {
+  if (P.nf >= kEpaMaxF) return -1;
+  V3<R> n = cross(P.w[j] - P.w[i], P.w[l] - P.w[i]);
+  const R len = msqrt(dot(n, n));
+  if (!(len > R(1e-30))) return -1;
+  n = n * (R(1) / len);
+  const int f = P.nf++;
+  P.face[f][0] = i; P.face[f][1] = j; P.face[f][2] = l;
+  P.n[f] = n; P.d[f] = dot(n, P.w[i]); P.alive[f] = true;
+  return f;
+}
+
+template <class R> __device__ int epa_push(Polytope<R> &P, const CShape<R> &A, const CShape<R> &B, V3<R> d) {
+  if (P.nv >= kEpaMaxV) return -1;
+  const int v = P.nv++;
+  P.a[v] = cs_support(A, d); P.b[v] = cs_support(B, -d); P.w[v] = P.a[v] - P.b[v];
+  return v;
+}
+
+template <class R> __device__ bool epa_seed(Polytope<R> &P, const CShape<R> &A, const CShape<R> &B, const Simplex<R> &s) {
+  P.nf = 0;
+  for (int i = 0; i < s.n; ++i) { P.w[i] = s.w[i]; P.a[i] = s.a[i]; P.b[i] = s.b[i]; }
+  P.nv = s.n;
+  for (int k = 0; P.nv < 2 && k < 6; ++k) {
+    V3<R> ax = v3<R>(0, 0, 0);
+    ax[k / 2] = k % 2 ? R(-1) : R(1);
+    const int v = epa_push(P, A, B, ax);
+    const V3<R> e = P.w[v] - P.w[0];
+    if (dot(e, e) < R(1e-20)) P.nv--;
+  }
+  if (P.nv < 2) return false;
+  if (P.nv == 2) {
+    const V3<R> e = P.w[1] - P.w[0];
+    int m = 0;
+    for (int c = 1; c < 3; ++c)
+      if (mabs(e[c]) < mabs(e[m])) m = c;
+    V3<R> ax = v3<R>(0, 0, 0);
+    ax[m] = 1;
+    const V3<R> d = normalize(cross(e, ax));
+    int v = epa_push(P, A, B, d);
+    V3<R> cr = cross(P.w[v] - P.w[0], e);
+    if (dot(cr, cr) < R(1e-20)) { P.nv--; v = epa_push(P, A, B, -d); cr = cross(P.w[v] - P.w[0], e); }
+    if (dot(cr, cr) < R(1e-20)) return false;
+  }
+  if (P.nv == 3) {
+    const V3<R> n = normalize(cross(P.w[1] - P.w[0], P.w[2] - P.w[0]));
+    int v = epa_push(P, A, B, n);
+    R h = dot(n, P.w[v] - P.w[0]);
+    if (mabs(h) < R(1e-12) || dot(n, P.w[0]) > R(0)) {
+      P.nv--;
+      v = epa_push(P, A, B, -n);
+      h = dot(n, P.w[v] - P.w[0]);
+    }
+    if (mabs(h) < R(1e-12)) return false;
+  }
+  const V3<R> c = (P.w[0] + P.w[1] + P.w[2] + P.w[3]) * R(0.25);
+  const int tf[4][3] = {{0, 1, 2}, {0, 3, 1}, {0, 2, 3}, {1, 3, 2}};
+  for (int f = 0; f < 4; ++f) {
+    int i = tf[f][0], j = tf[f][1], l = tf[f][2];
+    const V3<R> n = cross(P.w[j] - P.w[i], P.w[l] - P.w[i]);
+    if (dot(n, P.w[i] - c) < R(0)) { const int t = j; j = l; l = t; }
+    if (epa_add_face(P, i, j, l) < 0) return false;
+    if (P.d[P.nf - 1] < -R(1e-12)) return false;
+  }
+  return true;
+}
+
+template <class R> struct EpaOut {
+  bool ok;
+  R depth;
+  V3<R> x1, x2;
+};
+
+template <class R>
+__device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R> &s, R tol, int iterations) {
+  EpaOut<R> o;
+  o.ok = false;
+  Polytope<R> P;
+  if (!epa_seed(P, A, B, s)) return o;
+  int best = -1;
+  for (int it = 0; it <= iterations; ++it) {
+    best = -1;
+    for (int f = 0; f < P.nf; ++f)
+      if (P.alive[f] && (best < 0 || P.d[f] < P.d[best])) best = f;
+    if (best < 0) return o;
+    if (it == iterations) break;
+    const V3<R> n = P.n[best];
+    const int v = epa_push(P, A, B, n);
+    if (v < 0) break;
+    if (dot(P.w[v], n) - P.d[best] < tol) { P.nv--; break; }
+    int edges[3 * kEpaMaxF][2], ne = 0;
+    for (int f = 0; f < P.nf; ++f) {
+      if (!P.alive[f] || dot(P.n[f], P.w[v] - P.w[P.face[f][0]]) <= R(0)) continue;
+      P.alive[f] = false;
+      for (int e = 0; e < 3; ++e) {
+        const int i = P.face[f][e], j = P.face[f][(e + 1) % 3];
+        int dup = -1;
+        for (int q = 0; q < ne; ++q)
+          if (edges[q][0] == j && edges[q][1] == i) { dup = q; break; }
+        if (dup >= 0) { edges[dup][0] = edges[ne - 1][0]; edges[dup][1] = edges[ne - 1][1]; --ne; }
+        else if (ne < 3 * kEpaMaxF) { edges[ne][0] = i; edges[ne][1] = j; ++ne; }
+      }
+    }
+    bool full = false;
+    for (int q = 0; q < ne; ++q)
+      if (epa_add_face(P, edges[q][0], edges[q][1], v) < 0) { full = true; break; }
+    if (full) break;
+  }
+  if (best < 0) return o;
+  const int i = P.face[best][0], j = P.face[best][1], l = P.face[best][2];
+  const V3<R> pt = P.n[best] * P.d[best];
+  const V3<R> e0 = P.w[j] - P.w[i], e1 = P.w[l] - P.w[i], e2 = pt - P.w[i];
+  const R d00 = dot(e0, e0), d01 = dot(e0, e1), d11 = dot(e1, e1), d20 = dot(e2, e0), d21 = dot(e2, e1);
+  const R den = d00 * d11 - d01 * d01;
+  const R lv = den != R(0) ? (d11 * d20 - d01 * d21) / den : R(0), lw = den != R(0) ? (d00 * d21 - d01 * d20) / den : R(0);
+  const R lu = R(1) - lv - lw;
+  o.x1 = P.a[i] * lu + P.a[j] * lv + P.a[l] * lw;
+  o.x2 = P.b[i] * lu + P.b[j] * lv + P.b[l] * lw;
+  o.depth = P.d[best];
+  o.ok = true;
+  return o;
+}
+
+template <class R>
+__device__ CShape<R> cs_make(const Mdl<R> &M, const Arena<R> &A, int g, V3<R> origin, R margin) {
+  CShape<R> s;
+  s.type = IF(geom_type)[g];
+  s.pos = ld3(A.gxpos + 3 * g) - origin;
+  s.size = ld3(RF(geom_size) + 3 * g);
+  s.rot = A.gxmat + 9 * g;
+  s.margin = margin;
+  s.vert = nullptr;
+  s.nvert = 0;
+  if (s.type == B200_GEOM_MESH) {
+    const int mesh = IF(geom_dataid)[g];
+    s.vert = RF(mesh_vert) + 3 * IF(mesh_vertadr)[mesh];
+    s.nvert = IF(mesh_vertnum)[mesh];
+  }
+  return s;
+}
+
+template <class R>
+__device__ __noinline__ void convex_pair(const Mdl<R> &M, Arena<R> &A, int pair, int g1, int g2) {
+  const Material<R> p = material(M, g1, g2);
+  const V3<R> origin = ld3(A.gxpos + 3 * g1);
+  const CShape<R> S1 = cs_make(M, A, g1, origin, p.margin), S2 = cs_make(M, A, g2, origin, p.margin);
+  const R tol = R(M.m.ccd_tolerance);
+  const int iters = M.m.ccd_iterations;
+  R dist = 0;
+  V3<R> x1 = v3<R>(0, 0, 0), x2 = v3<R>(0, 0, 0);
+  bool found = false;
+  R full1 = 0, full2 = 0;
+  CShape<R> C1 = S1, C2 = S2;
+  if (S1.type == B200_GEOM_SPHERE || S1.type == B200_GEOM_CAPSULE) { full1 = S1.size.x + R(0.5) * S1.margin; C1.size.x = 0; C1.margin = 0; }
+  if (S2.type == B200_GEOM_SPHERE || S2.type == B200_GEOM_CAPSULE) { full2 = S2.size.x + R(0.5) * S2.margin; C2.size.x = 0; C2.margin = 0; }
+  if (full1 + full2 > R(0)) {
+    const GjkOut<R> r = gjk(C1, C2, tol, iters, p.gap + full1 + full2);
+    if (r.separated) return;
+    if (r.dist > tol) {
+      const V3<R> nrm = normalize(r.x2 - r.x1);
+      x1 = r.x1 + nrm * full1;
+      x2 = r.x2 - nrm * full2;
+      dist = r.dist - (full1 + full2);
+      found = true;
+    }
+  }
+  if (!found) {
+    const GjkOut<R> r = gjk(S1, S2, tol, iters, p.gap);
+    if (r.separated) return;
+    if (r.dist > tol) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
+    else {
+      const EpaOut<R> e = epa(S1, S2, r.s, tol, M.m.epa_iterations);
+      if (!e.ok) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
+      else { dist = -e.depth; x1 = e.x1; x2 = e.x2; }
+    }
+  }
+  if (!(dist < p.gap)) return;
+  const R distance = dist + p.margin;
+  V3<R> fr[3];
+  frame_from_normal(distance <= p.margin ? x1 - x2 : x2 - x1, fr);
+  emit(M, A, p, pair, 0, g1, g2, distance, (x1 + x2) * R(0.5) + origin, fr);
+}
+
+template <class R, bool CONVEX> __device__ void collide_pair(const Mdl<R> &M, Arena<R> &A, int pair) {
   const int g1 = IF(pair_geom)[2 * pair], g2 = IF(pair_geom)[2 * pair + 1];
   if (!candidate(M, A, g1, g2)) return;
   const int t1 = IF(geom_type)[g1], t2 = IF(geom_type)[g2];
-  if (t1 == B200_GEOM_PLANE && t2 >= 2 && t2 <= 7) plane_pair(M, A, pair, g1, g2);
+  if (t2 == B200_GEOM_MESH) {
+    if constexpr (CONVEX) {
+      if (t1 == B200_GEOM_PLANE) plane_mesh(M, A, material(M, g1, g2), pair, g1, g2);
+      else convex_pair(M, A, pair, g1, g2);
+    }
+  } else if (t1 == B200_GEOM_PLANE && t2 >= 2 && t2 <= 6) plane_pair(M, A, pair, g1, g2);
   else if (t2 == B200_GEOM_BOX && (t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE || t1 == B200_GEOM_BOX))
     box_pair(M, A, pair, g1, g2);
+  else if ((t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE) && (t2 == B200_GEOM_SPHERE || t2 == B200_GEOM_CAPSULE))
+    prim_pair(M, A, pair, g1, g2);
 }
 
 }  // namespace b200

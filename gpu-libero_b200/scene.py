@@ -22,7 +22,7 @@ import math
 import numpy as np
 
 FREE, BALL, SLIDE, HINGE = 0, 1, 2, 3
-PLANE, SPHERE, CAPSULE, BOX = 0, 2, 3, 6
+PLANE, SPHERE, CAPSULE, BOX, MESH = 0, 2, 3, 6, 7
 
 # robosuite Panda defaults (robosuite 1.4 panda robot + PandaGripper models).
 PANDA_INIT_QPOS = [0.0, math.pi / 16.0, 0.0, -math.pi / 2.0 - math.pi / 3.0,
@@ -99,6 +99,50 @@ def geom_inertia(kind, size, mass):
     raise ValueError('no inertia for geom type %d' % kind)
 
 
+def convex_mesh(points):
+    """Convex hull of a point cloud as a mesh about its volume centroid.
+
+    Returns the hull vertices (shifted so the centroid is the origin), its
+    triangular faces wound outward with their unit normals, the volume and the
+    inertia tensor per unit density about the centroid (signed tetrahedra
+    from the centroid; Tonon 2004 / Blow-Binstock moment formulas)."""
+    from scipy.spatial import ConvexHull
+    pts = np.asarray(points, float)
+    hull = ConvexHull(pts)
+    keep = np.array(sorted(set(hull.vertices.tolist())))
+    remap = {int(v): k for k, v in enumerate(keep)}
+    vert = pts[keep]
+    faces = []
+    inside = vert.mean(axis=0)
+    for simplex in hull.simplices:
+        a, b, c = (remap[int(v)] for v in simplex)
+        n = np.cross(vert[b] - vert[a], vert[c] - vert[a])
+        if np.dot(n, vert[a] - inside) < 0:
+            b, c = c, b
+        faces.append((a, b, c))
+    # volume and centroid
+    vol, cen = 0.0, np.zeros(3)
+    for a, b, c in faces:
+        v = np.dot(vert[a] - inside, np.cross(vert[b] - inside, vert[c] - inside)) / 6.0
+        vol += v
+        cen += v * (vert[a] + vert[b] + vert[c] + inside) / 4.0
+    cen /= vol
+    vert = vert - cen
+    # second moments of the tetrahedra (origin, a, b, c): integral of x x^T
+    cov = np.zeros((3, 3))
+    for a, b, c in faces:
+        A = np.stack([vert[a], vert[b], vert[c]], axis=1)
+        detA = np.linalg.det(A)
+        canon = np.full((3, 3), 1.0 / 120.0) + np.eye(3) * (1.0 / 120.0)
+        cov += detA * A @ canon @ A.T
+    inertia = np.trace(cov) * np.eye(3) - cov
+    normals = []
+    for a, b, c in faces:
+        n = np.cross(vert[b] - vert[a], vert[c] - vert[a])
+        normals.append(n / np.linalg.norm(n))
+    return dict(vert=vert, faces=faces, normals=np.array(normals), volume=vol, inertia=inertia)
+
+
 @dataclass
 class Geom:
     name: str
@@ -113,6 +157,7 @@ class Geom:
     margin: float = 0.0
     mass: float = 0.0
     rgba: str = '0.7 0.7 0.7 1'
+    mesh: dict = None  # convex_mesh() output for MESH geoms
 
 
 @dataclass
@@ -248,7 +293,11 @@ class Scene:
                 if g.mass <= 0:
                     continue
                 r = quat_mat(np.asarray(g.quat, float) / np.linalg.norm(g.quat))
-                tensor += r @ np.diag(geom_inertia(g.kind, g.size, g.mass)) @ r.T
+                if g.kind == MESH:
+                    local = g.mass / g.mesh['volume'] * g.mesh['inertia']
+                else:
+                    local = np.diag(geom_inertia(g.kind, g.size, g.mass))
+                tensor += r @ local @ r.T
                 d = np.asarray(g.pos, float) - com
                 tensor += g.mass * (np.dot(d, d) * np.eye(3) - np.outer(d, d))
             vals, vecs = np.linalg.eigh(tensor)
@@ -283,6 +332,39 @@ class Scene:
             elif g.kind == PLANE:
                 aabb[k, 3:] = [1e10, 1e10, 0.0]
                 rbound[k] = 0.0
+            elif g.kind == MESH:
+                v = g.mesh['vert']
+                lo, hi = v.min(axis=0), v.max(axis=0)
+                aabb[k, :3], aabb[k, 3:] = (lo + hi) / 2, (hi - lo) / 2
+                gsize[k] = (hi - lo) / 2
+                rbound[k] = float(np.max(np.linalg.norm(v, axis=1)))
+        # mesh data (geom_dataid; vertices, polygons and the vertex -> polygon map)
+        dataid = np.full(ng, -1, np.int32)
+        mesh_vertadr, mesh_vertnum, mesh_polyadr, mesh_polynum = [], [], [], []
+        mesh_vert, polyvertadr, polyvertnum, polyvert, polynormal = [], [], [], [], []
+        polymapadr, polymapnum, polymap = [], [], []
+        for k, (_, g) in enumerate(G):
+            if g.kind != MESH:
+                continue
+            dataid[k] = len(mesh_vertadr)
+            v, faces = g.mesh['vert'], g.mesh['faces']
+            mesh_vertadr.append(len(mesh_vert))
+            mesh_vertnum.append(len(v))
+            mesh_polyadr.append(len(polyvertadr))
+            mesh_polynum.append(len(faces))
+            incident = [[] for _ in range(len(v))]
+            for f, face in enumerate(faces):
+                polyvertadr.append(len(polyvert))
+                polyvertnum.append(len(face))
+                polyvert.extend(int(x) for x in face)
+                polynormal.append(g.mesh['normals'][f])
+                for x in face:
+                    incident[x].append(f)
+            for x in range(len(v)):
+                polymapadr.append(len(polymap))
+                polymapnum.append(len(incident[x]))
+                polymap.extend(incident[x])
+            mesh_vert.extend(v.tolist())
         # collision pair filter (cuda_fp32/model.py:171-186 prepare_collision)
         contype = np.array([g.contype for _, g in G], np.int64)
         conaff = np.array([g.conaffinity for _, g in G], np.int64)
@@ -326,7 +408,10 @@ class Scene:
         cap = self.capacities
         self.sizes = dict(nq=nq, nv=nv, nu=nu, nbody=nb, njnt=nj, ngeom=ng, nsite=ns,
                           npair=len(pairs), ntree=ntree, nM=nM, nlevel=nlevel,
-                          nlimited=int(limited.sum()), nfric=int(np.sum(fric > 0)))
+                          nlimited=int(limited.sum()), nfric=int(np.sum(fric > 0)),
+                          nmesh=len(mesh_vertadr), nmeshvert=len(mesh_vert), nmeshpoly=len(polyvertadr),
+                          nmeshpolyvert=len(polyvert), nmeshpolymap=len(polymap),
+                          ccd_iterations=opt.get('ccd_iterations', 50), epa_iterations=opt.get('epa_iterations', 32))
         ncon_max = cap['nconmax']
         cone = opt['cone']
         rows_per_contact = 3 if cone == 1 else 4
@@ -372,7 +457,13 @@ class Scene:
             osc_qposadr=np.array([jnt[k]['qposadr'] for k in self.controller['joints']], np.int32),
             osc_dofadr=np.array([jnt[k]['dofadr'] for k in self.controller['joints']], np.int32),
             osc_actuator=np.array(self.controller['actuators'], np.int32),
-            free_bodyid=np.array(free_bodies, np.int32))
+            free_bodyid=np.array(free_bodies, np.int32),
+            geom_dataid=dataid, mesh_vertadr=np.array(mesh_vertadr, np.int32),
+            mesh_vertnum=np.array(mesh_vertnum, np.int32), mesh_polyadr=np.array(mesh_polyadr, np.int32),
+            mesh_polynum=np.array(mesh_polynum, np.int32), mesh_polyvertadr=np.array(polyvertadr, np.int32),
+            mesh_polyvertnum=np.array(polyvertnum, np.int32), mesh_polyvert=np.array(polyvert, np.int32),
+            mesh_polymapadr=np.array(polymapadr, np.int32), mesh_polymapnum=np.array(polymapnum, np.int32),
+            mesh_polymap=np.array(polymap, np.int32))
         reals.update(
             body_pos=np.array([b.pos for b in B], float), body_quat=np.array([b.quat for b in B], float),
             body_ipos=body_ipos, body_iquat=body_iquat, body_mass=body_mass,
@@ -395,7 +486,8 @@ class Scene:
             actuator_gainprm=np.array([a['gainprm'] for a in A], float),
             actuator_biasprm=np.array([a['biasprm'] for a in A], float),
             actuator_ctrlrange=np.array([a.get('ctrlrange') or (0, 0) for a in A], float),
-            actuator_forcerange=np.array([a.get('forcerange') or (0, 0) for a in A], float))
+            actuator_forcerange=np.array([a.get('forcerange') or (0, 0) for a in A], float),
+            mesh_vert=np.array(mesh_vert, float).reshape(-1), mesh_polynormal=np.array(polynormal, float).reshape(-1))
         c = self.controller
         kp = np.broadcast_to(np.asarray(c['kp'], float), (6,))
         kd = 2 * np.sqrt(kp) * np.asarray(c.get('damping_ratio', 1.0))
@@ -410,7 +502,7 @@ class Scene:
         self.scalars = dict(timestep=opt['timestep'], gravity_x=0.0, gravity_y=0.0, gravity_z=-9.81,
                             tolerance=max(opt['tolerance'], 1e-6), ls_tolerance=opt.get('ls_tolerance', 0.01),
                             impratio_invsqrt=1.0 / math.sqrt(max(opt.get('impratio', 1.0), 1e-15)),
-                            meaninertia=1.0)
+                            meaninertia=1.0, ccd_tolerance=opt.get('ccd_tolerance', 1e-6))
         self.geom_names = [g.name for _, g in G]
         self.body_names = [b.name for b in B]
         self._set_const()
@@ -474,9 +566,12 @@ class Scene:
                     break
             placed.append((x, y, body['radius']))
             z = body['rest_z'] if body['drop'] is None else rng.uniform(*body['drop'])
-            yaw = rng.uniform(-math.pi, math.pi)
             qpos[adr:adr + 3] = [x, y, z]
-            qpos[adr + 3:adr + 7] = axis_quat((0, 0, 1), yaw)
+            if body.get('tumble'):  # dropped objects: uniformly random orientation
+                q = rng.normal(size=4)
+                qpos[adr + 3:adr + 7] = q / np.linalg.norm(q)
+            else:
+                qpos[adr + 3:adr + 7] = axis_quat((0, 0, 1), rng.uniform(-math.pi, math.pi))
 
     def actions(self, nworld, step, seed=0, world_offset=0):
         """Seeded OSC_POSE actions: U[-1,1]^6 plus a gripper sign in {-1,1}.
@@ -492,15 +587,15 @@ class Scene:
 
     @property
     def supported(self):
-        known = {(PLANE, SPHERE), (PLANE, CAPSULE), (PLANE, BOX), (SPHERE, BOX),
+        known = {(PLANE, SPHERE), (PLANE, CAPSULE), (PLANE, BOX), (PLANE, MESH), (SPHERE, BOX),
                  (CAPSULE, BOX), (BOX, BOX), (SPHERE, SPHERE), (SPHERE, CAPSULE),
-                 (CAPSULE, CAPSULE)}
+                 (CAPSULE, CAPSULE), (SPHERE, MESH), (CAPSULE, MESH), (BOX, MESH), (MESH, MESH)}
         return all(f in known for f in self.pair_families)
 
     # ------------------------------------------------------------------ mjcf
     def mjcf(self):
         """MJCF text of this scene (explicit inertials; compiles in MuJoCo)."""
-        names = {PLANE: 'plane', SPHERE: 'sphere', CAPSULE: 'capsule', BOX: 'box'}
+        names = {PLANE: 'plane', SPHERE: 'sphere', CAPSULE: 'capsule', BOX: 'box', MESH: 'mesh'}
         kinds = {FREE: 'free', BALL: 'ball', SLIDE: 'slide', HINGE: 'hinge'}
         o = self.options
         out = ['<mujoco model="%s">' % self.name,
@@ -508,7 +603,15 @@ class Scene:
                'cone="%s" impratio="%g" solver="Newton" integrator="Euler" jacobian="dense"/>' % (
                    o['timestep'], o['iterations'], o['ls_iterations'], o['tolerance'],
                    'elliptic' if o['cone'] == 1 else 'pyramidal', o.get('impratio', 1.0)),
-               '  <worldbody>']
+               ]
+        meshes = [g for b in self.bodies for g in b.geoms if g.kind == MESH]
+        if meshes:
+            out.append('  <asset>')
+            for g in meshes:
+                out.append('    <mesh name="%s_mesh" vertex="%s"/>' % (
+                    g.name, ' '.join('%.9g' % v for v in g.mesh['vert'].reshape(-1))))
+            out.append('  </asset>')
+        out.append('  <worldbody>')
         depth = {0: 1}
         stack = [0]
         r = self.reals
@@ -537,9 +640,10 @@ class Scene:
                 s += ' damping="%g" armature="%g" frictionloss="%g"/>' % (j.damping, j.armature, j.frictionloss)
                 out.append(ind + s)
             for g in b.geoms:
-                out.append(ind + '<geom name="%s" type="%s" size="%s" pos="%s" quat="%s" contype="%d" '
+                out.append(ind + '<geom name="%s" type="%s" %s pos="%s" quat="%s" contype="%d" '
                            'conaffinity="%d" condim="%d" friction="%s" margin="%g" mass="%g"/>' % (
-                               g.name, names[g.kind], ' '.join('%.9g' % v for v in g.size),
+                               g.name, names[g.kind], ('mesh="%s_mesh"' % g.name) if g.kind == MESH else
+                               'size="%s"' % ' '.join('%.9g' % v for v in g.size),
                                ' '.join('%.9g' % v for v in g.pos), ' '.join('%.9g' % v for v in g.quat),
                                g.contype, g.conaffinity, g.condim, ' '.join('%g' % v for v in g.friction),
                                g.margin, g.mass))
@@ -662,6 +766,57 @@ def scene_a(seed=0, cone='elliptic', nconmax=32, njmax=None, iterations=50, ls_i
     scene = Scene('scene_a', bodies, actuators, opt, dict(nconmax=nconmax, njmax=njmax), controller)
     scene.objects = objects
     scene.object_square = 0.4
+    scene.object_center = _ee_xy(scene)
+    scene.substeps = 25
+    return scene
+
+
+def scene_b(seed=0, cone='elliptic', nconmax=96, njmax=None, iterations=50, ls_iterations=50,
+            tolerance=1e-8):
+    """BASELINE scene B: scene A's arm plus 12 dropped free objects (nq=93, nv=81).
+
+    4 boxes (half-extents U[0.02,0.05]), 4 capsules (radius U[0.015,0.04],
+    half-length U[0.02,0.05]), 2 spheres (radius U[0.02,0.05]) and 2 convex
+    hulls of 32 random points on an ellipsoid with semi-axes U[0.02,0.06];
+    masses U[0.05,0.3] kg, friction 1; dropped from z U[0.05,0.15] m with a
+    random orientation.  Boxes and hulls carry a 1 mm margin."""
+    rng = np.random.default_rng([seed, 0xB])
+    bodies = [Body('world', -1)]
+    bodies[0].geoms.append(Geom('floor', PLANE, (0, 0, 0.05), contype=1, conaffinity=3))
+    actuators, controller = _panda(bodies)
+    objects = []
+    kinds = [BOX] * 4 + [CAPSULE] * 4 + [SPHERE] * 2 + [MESH] * 2
+    for k, kind in enumerate(kinds):
+        mass = rng.uniform(0.05, 0.3)
+        mesh, margin = None, 0.0
+        if kind == BOX:
+            size = tuple(rng.uniform(0.02, 0.05, 3))
+            radius, margin = float(np.linalg.norm(size)), 0.001
+        elif kind == CAPSULE:
+            size = (rng.uniform(0.015, 0.04), rng.uniform(0.02, 0.05))
+            radius = size[0] + size[1]
+        elif kind == SPHERE:
+            size = (rng.uniform(0.02, 0.05),)
+            radius = size[0]
+        else:
+            axes = rng.uniform(0.02, 0.06, 3)
+            d = rng.normal(size=(32, 3))
+            d /= np.linalg.norm(d, axis=1, keepdims=True)
+            mesh = convex_mesh(d * axes)
+            size, margin = tuple(np.ptp(mesh['vert'], axis=0) / 2), 0.001
+            radius = float(np.max(np.linalg.norm(mesh['vert'], axis=1)))
+        name = {BOX: 'box', CAPSULE: 'capsule', SPHERE: 'sphere', MESH: 'hull'}[kind]
+        b = Body('%s%d' % (name, k), 0, (0.5, 0.0, 0.1))
+        b.joints.append(Joint('%s%d_free' % (name, k), FREE))
+        b.geoms.append(Geom('%s%d_geom' % (name, k), kind, size, contype=1, conaffinity=3,
+                            friction=(1.0, 0.005, 0.0001), margin=margin, mass=mass, mesh=mesh))
+        bodies.append(b)
+        objects.append(dict(id=len(bodies) - 1, radius=radius, rest_z=None, drop=(0.05, 0.15), tumble=True))
+    opt = dict(timestep=0.002, iterations=iterations, ls_iterations=ls_iterations, tolerance=tolerance,
+               cone=1 if cone == 'elliptic' else 0, impratio=1.0, ls_tolerance=0.01)
+    scene = Scene('scene_b', bodies, actuators, opt, dict(nconmax=nconmax, njmax=njmax), controller)
+    scene.objects = objects
+    scene.object_square = 0.5
     scene.object_center = _ee_xy(scene)
     scene.substeps = 25
     return scene

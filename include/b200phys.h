@@ -60,6 +60,7 @@ extern "C" {
 #define B200_GEOM_SPHERE 2
 #define B200_GEOM_CAPSULE 3
 #define B200_GEOM_BOX 6
+#define B200_GEOM_MESH 7
 
 /* Joint types (MuJoCo mjtJoint). */
 #define B200_JNT_FREE 0

@@ -26,12 +26,14 @@
   X(nq) X(nv) X(nu) X(nbody) X(njnt) X(ngeom) X(nsite) X(npair) X(ntree) \
   X(nM) X(nlevel) X(nlimited) X(nfric) X(ncon_max) X(nefc_max) X(cone) \
   X(iterations) X(ls_iterations) X(disable_flags) X(ee_site) X(real_bytes) \
-  X(nvs) X(kmax_dof) X(max_tree_dofs) X(osc_uncouple) X(nfree) X(nobs)
+  X(nvs) X(kmax_dof) X(max_tree_dofs) X(osc_uncouple) X(nfree) X(nobs) \
+  X(nmesh) X(nmeshvert) X(nmeshpoly) X(nmeshpolyvert) X(nmeshpolymap) \
+  X(ccd_iterations) X(epa_iterations)
 
 /* real scalars of the model (stored as double, read as the kernel's real) */
 #define B200_MODEL_REAL_SCALARS(X) \
   X(timestep) X(gravity_x) X(gravity_y) X(gravity_z) X(tolerance) \
-  X(ls_tolerance) X(impratio_invsqrt) X(meaninertia)
+  X(ls_tolerance) X(impratio_invsqrt) X(meaninertia) X(ccd_tolerance)
 
 /* int32 arrays: X(name, length-expression) */
 #define B200_MODEL_INT_ARRAYS(X) \
@@ -48,7 +50,11 @@
   X(limited_jnt, nlimited) X(fric_dof, nfric) \
   X(actuator_trnid, nu) X(actuator_gaintype, nu) X(actuator_biastype, nu) \
   X(actuator_ctrllimited, nu) X(actuator_forcelimited, nu) \
-  X(osc_qposadr, 7) X(osc_dofadr, 7) X(osc_actuator, 9) X(free_bodyid, nfree)
+  X(osc_qposadr, 7) X(osc_dofadr, 7) X(osc_actuator, 9) X(free_bodyid, nfree) \
+  X(geom_dataid, ngeom) X(mesh_vertadr, nmesh) X(mesh_vertnum, nmesh) \
+  X(mesh_polyadr, nmesh) X(mesh_polynum, nmesh) X(mesh_polyvertadr, nmeshpoly) \
+  X(mesh_polyvertnum, nmeshpoly) X(mesh_polyvert, nmeshpolyvert) \
+  X(mesh_polymapadr, nmeshvert) X(mesh_polymapnum, nmeshvert) X(mesh_polymap, nmeshpolymap)
 
 /* real arrays: X(name, length-expression) */
 #define B200_MODEL_REAL_ARRAYS(X) \
@@ -67,7 +73,8 @@
   X(site_pos, nsite * 3) X(site_quat, nsite * 4) \
   X(actuator_gear, nu) X(actuator_gainprm, nu * 3) X(actuator_biasprm, nu * 3) \
   X(actuator_ctrlrange, nu * 2) X(actuator_forcerange, nu * 2) \
-  X(osc_gains, 12) X(osc_q0, 7) X(osc_action_config, 25) X(osc_null, 2)
+  X(osc_gains, 12) X(osc_q0, 7) X(osc_action_config, 25) X(osc_null, 2) \
+  X(mesh_vert, nmeshvert * 3) X(mesh_polynormal, nmeshpoly * 3)
 
 /* world-major real data: X(name, per-world width) */
 #define B200_DATA_REAL(X) \

@@ -1,0 +1,489 @@
+/* Narrowphase families beyond plane/box (included by oracle.c; test
+ * infrastructure only).
+ *
+ * Primitive sphere/capsule pairs follow MuJoCo's colliders that the
+ * reference's native engine carries (libero/libero/gpu/cuda/collision/
+ * collision_detect_primitive.cuh: _SphereSphere :261-292, mjc_SphereCapsule
+ * :306-322, mjc_CapsuleCapsule :401-490, including the two-contact parallel
+ * case).  Plane-mesh follows the FP32 engine's polygon manifold
+ * (mjwarp_plane.cu, restated in tools/validation/mjwarp_plane_reference.py
+ * mesh_manifold): the deepest vertex, then up to three more vertices of its
+ * most plane-facing incident face.  Convex pairs (anything against a mesh)
+ * follow the reference's CCD contract (mjwarp_convex_collision.cuh:46-78,
+ * mjwarp_convex_epa.cuh gjk_phase): supports inflated by half the pair margin
+ * on each shape, sphere and capsule cores shrunk to a point / segment first,
+ * GJK distance with a separation cutoff, EPA for penetration, one contact at
+ * the witness midpoint whose normal is x1 - x2 when the inflated shapes
+ * overlap.  The GJK distance subalgorithm here is an exhaustive search over
+ * the sub-simplices of the current simplex (the minimum-norm point of the
+ * best face whose affine weights are positive), and EPA is the expanding
+ * polytope method of van den Bergen (2001); both give the reference's
+ * geometric answer (distance, depth, normal) to the CCD tolerance.
+ */
+
+/* ------------------------------------------------------------ primitives */
+typedef struct { int count; real dist[2]; V3 pos[2], normal[2]; } PrimOut;
+
+/* MuJoCo _SphereSphere: depth along the centre line; coincident centres use
+ * the cross product of the two z axes, then +x */
+static int prim_sphere_sphere(PrimOut *o, real margin, V3 p1, const real *m1, real r1, V3 p2, const real *m2, real r2) {
+  V3 dif = vsub(p1, p2);
+  real cd2 = vdot(dif, dif), mind = margin + r1 + r2;
+  if (cd2 > mind * mind) return 0;
+  int c = o->count;
+  real dist = rsqrt_(cd2) - r1 - r2;
+  V3 n = vsub(p2, p1);
+  real len = rsqrt_(vdot(n, n));
+  if (len < R(1e-15)) {
+    n = vcross(mcol(m1, 2), mcol(m2, 2));
+    len = rsqrt_(vdot(n, n));
+    n = len > 0 ? vscale(n, R(1) / len) : v3(1, 0, 0);
+  } else
+    n = vscale(n, R(1) / len);
+  o->dist[c] = dist;
+  o->normal[c] = n;
+  o->pos[c] = vadd(p1, vscale(n, r1 + dist * R(0.5)));
+  o->count = c + 1;
+  return 1;
+}
+
+static void prim_sphere_capsule(PrimOut *o, real margin, V3 p1, const real *m1, real r1, V3 p2, const real *m2,
+                                real r2, real hl) {
+  V3 axis = mcol(m2, 2);
+  real x = rclamp(vdot(axis, vsub(p1, p2)), -hl, hl);
+  prim_sphere_sphere(o, margin, p1, m1, r1, vadd(p2, vscale(axis, x)), m2, r2);
+}
+
+static void prim_capsule_capsule(PrimOut *o, real margin, V3 p1, const real *m1, const real *s1, V3 p2,
+                                 const real *m2, const real *s2) {
+  V3 a1 = vscale(mcol(m1, 2), s1[1]), a2 = vscale(mcol(m2, 2), s2[1]), dif = vsub(p1, p2);
+  real ma = vdot(a1, a1), mb = -vdot(a1, a2), mc = vdot(a2, a2), u = -vdot(a1, dif), v = vdot(a2, dif);
+  real det = ma * mc - mb * mb;
+  if (rabs(det) >= R(1e-15)) {
+    real x1 = (mc * u - mb * v) / det, x2 = (ma * v - mb * u) / det;
+    if (x1 > 1) { x1 = 1; x2 = (v - mb) / mc; }
+    else if (x1 < -1) { x1 = -1; x2 = (v + mb) / mc; }
+    if (x2 > 1) { x2 = 1; x1 = rclamp((u - mb) / ma, -1, 1); }
+    else if (x2 < -1) { x2 = -1; x1 = rclamp((u + mb) / ma, -1, 1); }
+    prim_sphere_sphere(o, margin, vadd(p1, vscale(a1, x1)), m1, s1[0], vadd(p2, vscale(a2, x2)), m2, s2[0]);
+    return;
+  }
+  /* parallel axes: segment ends of capsule 1, then of capsule 2 */
+  real x2 = rclamp((v - mb) / mc, -1, 1);
+  int n = prim_sphere_sphere(o, margin, vadd(p1, a1), m1, s1[0], vadd(p2, vscale(a2, x2)), m2, s2[0]);
+  x2 = rclamp((v + mb) / mc, -1, 1);
+  n += prim_sphere_sphere(o, margin, vsub(p1, a1), m1, s1[0], vadd(p2, vscale(a2, x2)), m2, s2[0]);
+  if (n >= 2) return;
+  real x1 = rclamp((u - mb) / ma, -1, 1);
+  n += prim_sphere_sphere(o, margin, vadd(p1, vscale(a1, x1)), m1, s1[0], vadd(p2, a2), m2, s2[0]);
+  if (n >= 2) return;
+  x1 = rclamp((u + mb) / ma, -1, 1);
+  prim_sphere_sphere(o, margin, vadd(p1, vscale(a1, x1)), m1, s1[0], vsub(p2, a2), m2, s2[0]);
+}
+
+static void prim_collide(Work *k, const B200Model *m, int g1, int g2) {
+  Material p = material(m, g1, g2);
+  int t1 = MI(geom_type)[g1], t2 = MI(geom_type)[g2];
+  V3 p1 = vload(k->gxpos[g1]), p2 = vload(k->gxpos[g2]);
+  const real *m1 = k->gxmat[g1], *m2 = k->gxmat[g2], *s1 = MF(geom_size) + 3 * g1, *s2 = MF(geom_size) + 3 * g2;
+  PrimOut o;
+  o.count = 0;
+  real margin = p.margin + p.gap;
+  if (t1 == B200_GEOM_SPHERE && t2 == B200_GEOM_SPHERE) prim_sphere_sphere(&o, margin, p1, m1, s1[0], p2, m2, s2[0]);
+  else if (t1 == B200_GEOM_SPHERE && t2 == B200_GEOM_CAPSULE) prim_sphere_capsule(&o, margin, p1, m1, s1[0], p2, m2, s2[0], s2[1]);
+  else prim_capsule_capsule(&o, margin, p1, m1, s1, p2, m2, s2);
+  for (int c = 0; c < o.count; ++c) {
+    real frame[9];
+    contact_frame(o.normal[c], frame);
+    publish(k, m, &p, g1, g2, o.dist[c], o.pos[c], frame);
+  }
+}
+
+/* ------------------------------------------------------------ plane - mesh */
+static void plane_mesh(Work *k, const B200Model *m, const Material *p, int g1, int g2, V3 n, V3 origin) {
+  int mesh = MI(geom_dataid)[g2];
+  V3 center = vload(k->gxpos[g2]);
+  const real *Rg = k->gxmat[g2], *vert = MF(mesh_vert) + 3 * MI(mesh_vertadr)[mesh];
+  int nvert = MI(mesh_vertnum)[mesh];
+  V3 local = mrotT(Rg, n);
+  int best = 0;
+  real top = -vdot(vload(vert), local);
+  for (int i = 1; i < nvert; ++i) {
+    real s = -vdot(vload(vert + 3 * i), local);
+    if (s > top) { top = s; best = i; }
+  }
+  real frame[9];
+  contact_frame(n, frame);
+  V3 world = vadd(center, mrot(Rg, vload(vert + 3 * best)));
+  real dist = vdot(n, vsub(world, origin));
+  publish(k, m, p, g1, g2, dist, vsub(world, vscale(n, R(0.5) * dist)), frame);
+  if (MI(mesh_polynum)[mesh] <= 0 || dist > p->margin + p->gap) return;
+  /* most plane-facing polygon among those at the deepest vertex */
+  int vglobal = MI(mesh_vertadr)[mesh] + best;
+  int madr = MI(mesh_polymapadr)[vglobal], mnum = MI(mesh_polymapnum)[vglobal];
+  int pbase = MI(mesh_polyadr)[mesh], face = -1;
+  real lowest = R(1);
+  for (int f = 0; f < mnum; ++f) {
+    int poly = pbase + MI(mesh_polymap)[madr + f];
+    real d = vdot(vload(MF(mesh_polynormal) + 3 * poly), local);
+    if (d < R(1) && (face < 0 || d < lowest)) { lowest = d; face = poly; }
+  }
+  if (face < 0) return;
+  const int *pv = MI(mesh_polyvert) + MI(mesh_polyvertadr)[face];
+  int count = MI(mesh_polyvertnum)[face], a = 0;
+  for (int i = 0; i < count; ++i)
+    if (pv[i] == best) { a = i; break; }
+  int sel[4] = {a, (a + 1) % count, (a + 2) % count, (a + 3) % count};
+  if (count > 4) { /* grow the quadrilateral of largest area (mesh_manifold) */
+    #define QAREA(b, c, d) (R(0.5) * rsqrt_(vdot(vcross(vsub(vload(vert + 3 * pv[a]), vload(vert + 3 * pv[c])), \
+                            vsub(vload(vert + 3 * pv[b]), vload(vert + 3 * pv[d]))), \
+                            vcross(vsub(vload(vert + 3 * pv[a]), vload(vert + 3 * pv[c])), \
+                            vsub(vload(vert + 3 * pv[b]), vload(vert + 3 * pv[d]))))))
+    int b = sel[1], c = sel[2], d = sel[3];
+    real cur = QAREA(b, c, d);
+    while (QAREA(b, c, (d + 1) % count) > cur) {
+      d = (d + 1) % count; cur = QAREA(b, c, d);
+      while (QAREA(b, (c + 1) % count, d) > cur) { c = (c + 1) % count; cur = QAREA(b, c, d); }
+      while (QAREA((b + 1) % count, c, d) > cur) { b = (b + 1) % count; cur = QAREA(b, c, d); }
+    }
+    sel[1] = b; sel[2] = c; sel[3] = d;
+    #undef QAREA
+  }
+  int nsel = count < 4 ? count : 4;
+  for (int i = 1; i < nsel; ++i) {
+    V3 w = vadd(center, mrot(Rg, vload(vert + 3 * pv[sel[i]])));
+    if (vdot(n, vsub(w, center)) > 0) continue;
+    real d = vdot(n, vsub(w, origin));
+    publish(k, m, p, g1, g2, d, vsub(w, vscale(n, R(0.5) * d)), frame);
+  }
+}
+
+/* ------------------------------------------------------------ convex (GJK / EPA) */
+typedef struct {
+  int type;
+  V3 pos, size;
+  const real *rot, *vert;
+  int nvert;
+  real margin; /* inflation: half the pair margin is added along the support direction */
+} CShape;
+
+/* support point of a shape in unit direction d (mjwarp_convex_geometry.cuh:17-68 contract) */
+static V3 cs_support(const CShape *s, V3 d) {
+  V3 p;
+  if (s->type == B200_GEOM_SPHERE) return vadd(s->pos, vscale(d, s->size.v[0] + R(0.5) * s->margin));
+  V3 l = mrotT(s->rot, d), r;
+  if (s->type == B200_GEOM_CAPSULE) {
+    r = vscale(l, s->size.v[0]);
+    r.v[2] += (l.v[2] > 0 ? 1 : l.v[2] < 0 ? -1 : 0) * s->size.v[1];
+  } else if (s->type == B200_GEOM_BOX) {
+    for (int c = 0; c < 3; ++c) r.v[c] = (l.v[c] > 0 ? 1 : -1) * s->size.v[c];
+  } else {
+    int best = 0;
+    real top = vdot(vload(s->vert), l);
+    for (int i = 1; i < s->nvert; ++i) {
+      real v = vdot(vload(s->vert + 3 * i), l);
+      if (v > top) { top = v; best = i; }
+    }
+    r = vload(s->vert + 3 * best);
+  }
+  p = vadd(mrot(s->rot, r), s->pos);
+  if (s->margin > 0) p = vadd(p, vscale(d, R(0.5) * s->margin));
+  return p;
+}
+
+typedef struct { V3 w[4], a[4], b[4]; real lam[4]; int n; } Simplex;
+
+/* minimum-norm point of the simplex: best sub-simplex with positive affine
+ * weights (exhaustive over the <= 15 non-empty subsets) */
+static void simplex_reduce(Simplex *s) {
+  real best = R(1e30), lam_best[4] = {0, 0, 0, 0};
+  int mask_best = 0;
+  for (int mask = 1; mask < (1 << s->n); ++mask) {
+    int idx[4], k = 0;
+    for (int i = 0; i < s->n; ++i)
+      if (mask & (1 << i)) idx[k++] = i;
+    real lam[4] = {0, 0, 0, 0}, mu[3] = {0, 0, 0};
+    if (k > 1) { /* minimise |w0 + sum mu_j (w_j - w0)|: normal equations by Cramer's rule */
+      V3 e[3];
+      V3 w0 = s->w[idx[0]];
+      for (int j = 1; j < k; ++j) e[j - 1] = vsub(s->w[idx[j]], w0);
+      int q = k - 1;
+      real G[3][3], rhs[3];
+      for (int i = 0; i < q; ++i) {
+        rhs[i] = -vdot(e[i], w0);
+        for (int j = 0; j < q; ++j) G[i][j] = vdot(e[i], e[j]);
+      }
+      real det;
+      if (q == 1) {
+        det = G[0][0];
+        if (!(det > R(1e-30))) continue;
+        mu[0] = rhs[0] / det;
+      } else if (q == 2) {
+        det = G[0][0] * G[1][1] - G[0][1] * G[1][0];
+        if (!(rabs(det) > R(1e-30))) continue;
+        mu[0] = (rhs[0] * G[1][1] - G[0][1] * rhs[1]) / det;
+        mu[1] = (G[0][0] * rhs[1] - rhs[0] * G[1][0]) / det;
+      } else {
+        det = G[0][0] * (G[1][1] * G[2][2] - G[1][2] * G[2][1]) - G[0][1] * (G[1][0] * G[2][2] - G[1][2] * G[2][0]) +
+              G[0][2] * (G[1][0] * G[2][1] - G[1][1] * G[2][0]);
+        if (!(rabs(det) > R(1e-30))) continue;
+        for (int c = 0; c < 3; ++c) {
+          real M3[3][3];
+          for (int i = 0; i < 3; ++i)
+            for (int j = 0; j < 3; ++j) M3[i][j] = j == c ? rhs[i] : G[i][j];
+          mu[c] = (M3[0][0] * (M3[1][1] * M3[2][2] - M3[1][2] * M3[2][1]) -
+                   M3[0][1] * (M3[1][0] * M3[2][2] - M3[1][2] * M3[2][0]) +
+                   M3[0][2] * (M3[1][0] * M3[2][1] - M3[1][1] * M3[2][0])) / det;
+        }
+      }
+      real l0 = 1;
+      for (int j = 0; j < q; ++j) { lam[j + 1] = mu[j]; l0 -= mu[j]; }
+      lam[0] = l0;
+      int ok = 1;
+      for (int j = 0; j < k; ++j) ok &= lam[j] > 0;
+      if (!ok) continue;
+    } else
+      lam[0] = 1;
+    V3 x = v3(0, 0, 0);
+    for (int j = 0; j < k; ++j) x = vadd(x, vscale(s->w[idx[j]], lam[j]));
+    real d = vdot(x, x);
+    if (d < best) {
+      best = d; mask_best = mask;
+      for (int j = 0; j < 4; ++j) lam_best[j] = lam[j];
+    }
+  }
+  Simplex t;
+  int k = 0;
+  for (int i = 0; i < s->n; ++i)
+    if (mask_best & (1 << i)) {
+      t.w[k] = s->w[i]; t.a[k] = s->a[i]; t.b[k] = s->b[i]; t.lam[k] = lam_best[k]; ++k;
+    }
+  t.n = k;
+  *s = t;
+}
+
+typedef struct { int separated; real dist; V3 x1, x2; Simplex s; } GjkOut;
+
+/* distance between two convex shapes; `cutoff` > 0 ends early once the
+ * distance is proven larger (reference gjk_distance cutoff semantics) */
+static GjkOut gjk(const CShape *A, const CShape *B, real tol, int iterations, real cutoff) {
+  GjkOut o;
+  memset(&o, 0, sizeof(o));
+  Simplex *s = &o.s;
+  s->n = 0;
+  V3 x = vsub(A->pos, B->pos);
+  real norm = rsqrt_(vdot(x, x)), prev = -1;
+  for (int it = 0; it < iterations; ++it) {
+    if (norm < tol || rabs(prev - norm) < R(1e-15)) break;
+    V3 d = vscale(x, R(1) / norm);
+    V3 a = cs_support(A, vneg(d)), b = cs_support(B, d), w = vsub(a, b);
+    if (vdot(x, vsub(x, w)) < R(0.5) * tol * tol) break;
+    real lower = vdot(x, w);
+    if (lower > 0 && (cutoff == 0 || lower >= cutoff * norm)) {
+      o.separated = 1; o.dist = R(1e30);
+      return o;
+    }
+    s->w[s->n] = w; s->a[s->n] = a; s->b[s->n] = b; s->n++;
+    simplex_reduce(s);
+    x = v3(0, 0, 0);
+    for (int i = 0; i < s->n; ++i) x = vadd(x, vscale(s->w[i], s->lam[i]));
+    prev = norm;
+    norm = rsqrt_(vdot(x, x));
+    if (s->n == 4) break;
+  }
+  o.x1 = v3(0, 0, 0); o.x2 = v3(0, 0, 0);
+  for (int i = 0; i < s->n; ++i) { o.x1 = vadd(o.x1, vscale(s->a[i], s->lam[i])); o.x2 = vadd(o.x2, vscale(s->b[i], s->lam[i])); }
+  if (s->n == 0) { o.x1 = A->pos; o.x2 = B->pos; }
+  o.dist = s->n == 4 ? 0 : norm;
+  return o;
+}
+
+#define EPA_MAXV 48
+#define EPA_MAXF 96
+typedef struct {
+  V3 w[EPA_MAXV], a[EPA_MAXV], b[EPA_MAXV];
+  int nv, nf, face[EPA_MAXF][3];
+  V3 n[EPA_MAXF];
+  real d[EPA_MAXF];
+  int alive[EPA_MAXF];
+} Polytope;
+
+static int epa_add_face(Polytope *P, int i, int j, int l) {
+  if (P->nf >= EPA_MAXF) return -1;
+  V3 n = vcross(vsub(P->w[j], P->w[i]), vsub(P->w[l], P->w[i]));
+  real len = rsqrt_(vdot(n, n));
+  if (!(len > R(1e-30))) return -1;
+  n = vscale(n, R(1) / len);
+  int f = P->nf++;
+  P->face[f][0] = i; P->face[f][1] = j; P->face[f][2] = l;
+  P->n[f] = n; P->d[f] = vdot(n, P->w[i]); P->alive[f] = 1;
+  return f;
+}
+
+static int epa_push(Polytope *P, const CShape *A, const CShape *B, V3 d) {
+  if (P->nv >= EPA_MAXV) return -1;
+  int v = P->nv++;
+  P->a[v] = cs_support(A, d); P->b[v] = cs_support(B, vneg(d)); P->w[v] = vsub(P->a[v], P->b[v]);
+  return v;
+}
+
+/* grow the GJK simplex to a tetrahedron that encloses the origin; 0 if the
+ * shapes only touch (no volume around the origin) */
+static int epa_seed(Polytope *P, const CShape *A, const CShape *B, const Simplex *s) {
+  P->nv = 0; P->nf = 0;
+  for (int i = 0; i < s->n; ++i) { P->w[i] = s->w[i]; P->a[i] = s->a[i]; P->b[i] = s->b[i]; }
+  P->nv = s->n;
+  static const real axes[6][3] = {{1, 0, 0}, {-1, 0, 0}, {0, 1, 0}, {0, -1, 0}, {0, 0, 1}, {0, 0, -1}};
+  for (int k = 0; P->nv < 2 && k < 6; ++k) {
+    int v = epa_push(P, A, B, v3(axes[k][0], axes[k][1], axes[k][2]));
+    V3 e = vsub(P->w[v], P->w[0]);
+    if (vdot(e, e) < R(1e-20)) P->nv--;
+  }
+  if (P->nv < 2) return 0;
+  if (P->nv == 2) {
+    V3 e = vsub(P->w[1], P->w[0]);
+    int m = 0;
+    for (int c = 1; c < 3; ++c) if (rabs(e.v[c]) < rabs(e.v[m])) m = c;
+    V3 ax = v3(0, 0, 0);
+    ax.v[m] = 1;
+    V3 d = vnormalize(vcross(e, ax));
+    int v = epa_push(P, A, B, d);
+    V3 cr = vcross(vsub(P->w[v], P->w[0]), e);
+    if (vdot(cr, cr) < R(1e-20)) { P->nv--; v = epa_push(P, A, B, vneg(d)); cr = vcross(vsub(P->w[v], P->w[0]), e); }
+    if (vdot(cr, cr) < R(1e-20)) return 0;
+  }
+  if (P->nv == 3) {
+    V3 n = vnormalize(vcross(vsub(P->w[1], P->w[0]), vsub(P->w[2], P->w[0])));
+    int v = epa_push(P, A, B, n);
+    real h = vdot(n, vsub(P->w[v], P->w[0]));
+    if (rabs(h) < R(1e-12) || vdot(n, P->w[0]) > 0) { /* take the other side: the origin must lie between */
+      P->nv--;
+      v = epa_push(P, A, B, vneg(n));
+      h = vdot(n, vsub(P->w[v], P->w[0]));
+    }
+    if (rabs(h) < R(1e-12)) return 0;
+  }
+  /* orient the tetrahedron's faces outward */
+  V3 c = vscale(vadd(vadd(P->w[0], P->w[1]), vadd(P->w[2], P->w[3])), R(0.25));
+  static const int tf[4][3] = {{0, 1, 2}, {0, 3, 1}, {0, 2, 3}, {1, 3, 2}};
+  for (int f = 0; f < 4; ++f) {
+    int i = tf[f][0], j = tf[f][1], l = tf[f][2];
+    V3 n = vcross(vsub(P->w[j], P->w[i]), vsub(P->w[l], P->w[i]));
+    if (vdot(n, vsub(P->w[i], c)) < 0) { int t = j; j = l; l = t; }
+    if (epa_add_face(P, i, j, l) < 0) return 0;
+    if (P->d[P->nf - 1] < -R(1e-12)) return 0; /* origin outside the tetrahedron */
+  }
+  return 1;
+}
+
+typedef struct { int ok; real depth; V3 x1, x2; } EpaOut;
+
+static EpaOut epa(const CShape *A, const CShape *B, const Simplex *s, real tol, int iterations) {
+  EpaOut o;
+  memset(&o, 0, sizeof(o));
+  Polytope P;
+  if (!epa_seed(&P, A, B, s)) return o;
+  int best = -1;
+  for (int it = 0; it <= iterations; ++it) {
+    best = -1;
+    for (int f = 0; f < P.nf; ++f)
+      if (P.alive[f] && (best < 0 || P.d[f] < P.d[best])) best = f;
+    if (best < 0) return o;
+    if (it == iterations) break;
+    V3 n = P.n[best];
+    int v = epa_push(&P, A, B, n);
+    if (v < 0) break;
+    if (vdot(P.w[v], n) - P.d[best] < tol) { P.nv--; break; }
+    /* remove the faces that see the new vertex; keep their horizon */
+    int edges[3 * EPA_MAXF][2], ne = 0;
+    for (int f = 0; f < P.nf; ++f) {
+      if (!P.alive[f] || vdot(P.n[f], vsub(P.w[v], P.w[P.face[f][0]])) <= 0) continue;
+      P.alive[f] = 0;
+      for (int e = 0; e < 3; ++e) {
+        int i = P.face[f][e], j = P.face[f][(e + 1) % 3], dup = -1;
+        for (int q = 0; q < ne; ++q)
+          if (edges[q][0] == j && edges[q][1] == i) { dup = q; break; }
+        if (dup >= 0) { edges[dup][0] = edges[ne - 1][0]; edges[dup][1] = edges[ne - 1][1]; --ne; }
+        else if (ne < 3 * EPA_MAXF) { edges[ne][0] = i; edges[ne][1] = j; ++ne; }
+      }
+    }
+    int full = 0;
+    for (int q = 0; q < ne; ++q)
+      if (epa_add_face(&P, edges[q][0], edges[q][1], v) < 0) { full = 1; break; }
+    if (full) break;
+  }
+  if (best < 0) return o;
+  /* witness points: barycentric coordinates of the origin's projection */
+  int i = P.face[best][0], j = P.face[best][1], l = P.face[best][2];
+  V3 p = vscale(P.n[best], P.d[best]);
+  V3 e0 = vsub(P.w[j], P.w[i]), e1 = vsub(P.w[l], P.w[i]), e2 = vsub(p, P.w[i]);
+  real d00 = vdot(e0, e0), d01 = vdot(e0, e1), d11 = vdot(e1, e1), d20 = vdot(e2, e0), d21 = vdot(e2, e1);
+  real den = d00 * d11 - d01 * d01;
+  real lv = den != 0 ? (d11 * d20 - d01 * d21) / den : 0, lw = den != 0 ? (d00 * d21 - d01 * d20) / den : 0;
+  real lu = 1 - lv - lw;
+  o.x1 = vadd(vadd(vscale(P.a[i], lu), vscale(P.a[j], lv)), vscale(P.a[l], lw));
+  o.x2 = vadd(vadd(vscale(P.b[i], lu), vscale(P.b[j], lv)), vscale(P.b[l], lw));
+  o.depth = P.d[best];
+  o.ok = 1;
+  return o;
+}
+
+static CShape cs_make(const B200Model *m, const Work *k, int g, V3 origin, real margin) {
+  CShape s;
+  s.type = MI(geom_type)[g];
+  s.pos = vsub(vload(k->gxpos[g]), origin);
+  s.size = vload(MF(geom_size) + 3 * g);
+  s.rot = k->gxmat[g];
+  s.margin = margin;
+  s.vert = 0; s.nvert = 0;
+  if (s.type == B200_GEOM_MESH) {
+    int mesh = MI(geom_dataid)[g];
+    s.vert = MF(mesh_vert) + 3 * MI(mesh_vertadr)[mesh];
+    s.nvert = MI(mesh_vertnum)[mesh];
+  }
+  return s;
+}
+
+/* one convex pair (mjwarp_convex_collision.cuh:46-78 contract), computed in a
+ * frame translated to geom 1 */
+static void convex_collide(Work *k, const B200Model *m, int g1, int g2) {
+  Material p = material(m, g1, g2);
+  V3 origin = vload(k->gxpos[g1]);
+  CShape A = cs_make(m, k, g1, origin, p.margin), B = cs_make(m, k, g2, origin, p.margin);
+  real tol = (real)m->ccd_tolerance, cutoff = p.gap;
+  int iters = m->ccd_iterations;
+  real dist;
+  V3 x1, x2;
+  int found = 0;
+  /* sphere / capsule cores first (gjk_phase): distance minus the radii */
+  real full1 = 0, full2 = 0;
+  CShape Ac = A, Bc = B;
+  if (A.type == B200_GEOM_SPHERE || A.type == B200_GEOM_CAPSULE) { full1 = A.size.v[0] + R(0.5) * A.margin; Ac.size.v[0] = 0; Ac.margin = 0; }
+  if (B.type == B200_GEOM_SPHERE || B.type == B200_GEOM_CAPSULE) { full2 = B.size.v[0] + R(0.5) * B.margin; Bc.size.v[0] = 0; Bc.margin = 0; }
+  if (full1 + full2 > 0) {
+    GjkOut r = gjk(&Ac, &Bc, tol, iters, cutoff + full1 + full2);
+    if (r.separated) return;
+    if (r.dist > tol) {
+      V3 nrm = vnormalize(vsub(r.x2, r.x1));
+      x1 = vadd(r.x1, vscale(nrm, full1));
+      x2 = vsub(r.x2, vscale(nrm, full2));
+      dist = r.dist - (full1 + full2);
+      found = 1;
+    }
+  }
+  if (!found) {
+    GjkOut r = gjk(&A, &B, tol, iters, cutoff);
+    if (r.separated) return;
+    if (r.dist > tol) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
+    else {
+      EpaOut e = epa(&A, &B, &r.s, tol, m->epa_iterations);
+      if (!e.ok) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
+      else { dist = -e.depth; x1 = e.x1; x2 = e.x2; }
+    }
+  }
+  if (!(dist < p.gap)) return;
+  real distance = dist + p.margin;
+  real frame[9];
+  contact_frame(distance <= p.margin ? vsub(x1, x2) : vsub(x2, x1), frame);
+  publish(k, m, &p, g1, g2, distance, vadd(vscale(vadd(x1, x2), R(0.5)), origin), frame);
+}

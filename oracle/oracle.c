@@ -466,6 +466,7 @@ static void plane_sphere_one(Work *k, const B200Model *m, const Material *p, int
   real d = vdot(vsub(c, o), n) - r;
   publish(k, m, p, g1, g2, d, vsub(c, vscale(n, r + R(0.5) * d)), frame);
 }
+static void plane_mesh(Work *k, const B200Model *m, const Material *p, int g1, int g2, V3 n, V3 origin);
 static void plane_collide(Work *k, const B200Model *m, int g1, int g2) {
   Material p = material(m, g1, g2);
   V3 o = vload(k->gxpos[g1]), c = vload(k->gxpos[g2]), n = mcol(k->gxmat[g1], 2);
@@ -494,7 +495,8 @@ static void plane_collide(Work *k, const B200Model *m, int g1, int g2) {
       real d = cd + vdot(n, corner);
       publish(k, m, &p, g1, g2, d, vsub(vadd(corner, c), vscale(n, R(0.5) * d)), frame);
     }
-  }
+  } else if (type == B200_GEOM_MESH)
+    plane_mesh(k, m, &p, g1, g2, n, o);
 }
 
 /* ---- sphere/capsule/box - box: mjwarp_box.cu:14-176 */
@@ -808,6 +810,8 @@ static void box_collide(Work *k, const B200Model *m, int g1, int g2) {
   }
 }
 
+#include "narrow.c"
+
 static void collision(const B200Model *m, Work *k) {
   k->ncon = 0;
   if (m->disable_flags & (B200_DSBL_CONSTRAINT | B200_DSBL_CONTACT)) return;
@@ -817,8 +821,11 @@ static void collision(const B200Model *m, Work *k) {
     if (!broadphase(m, k, g1, g2)) continue;
     int t1 = gt[g1], t2 = gt[g2];
     if (t1 == B200_GEOM_PLANE && t2 >= 2 && t2 <= 7) plane_collide(k, m, g1, g2);
+    else if (t2 == B200_GEOM_MESH) convex_collide(k, m, g1, g2);
     else if (t2 == B200_GEOM_BOX && (t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE || t1 == B200_GEOM_BOX))
       box_collide(k, m, g1, g2);
+    else if ((t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE) && (t2 == B200_GEOM_SPHERE || t2 == B200_GEOM_CAPSULE))
+      prim_collide(k, m, g1, g2);
   }
 }
 
@@ -1944,4 +1951,46 @@ int oracle_leaf_integrate(const B200Model *m, real *qpos, const real *qvel, doub
   if (!check_model(m)) return 1;
   integrate_positions(m, qpos, qvel, (real)dt);
   return 0;
+}
+
+/* convex narrowphase on raw poses (golden-vector tests): geom 2 is a mesh
+ * given by `vert2` (nvert2 local vertices) unless type2 is a primitive;
+ * geom 1 likewise.  Returns the contact count (0 or 1). */
+int oracle_leaf_convex(int type1, const real *p1, const real *R1, const real *s1, const real *vert1, int nvert1,
+                       int type2, const real *p2, const real *R2, const real *s2, const real *vert2, int nvert2,
+                       real margin, real tol, int iterations, int epa_iterations, real *dist, real *pos,
+                       real *normal) {
+  V3 origin = vload(p1);
+  CShape A = {type1, v3(0, 0, 0), vload(s1), R1, vert1, nvert1, margin};
+  CShape B = {type2, vsub(vload(p2), origin), vload(s2), R2, vert2, nvert2, margin};
+  real full1 = 0, full2 = 0, d;
+  V3 x1, x2;
+  int found = 0;
+  CShape Ac = A, Bc = B;
+  if (A.type == B200_GEOM_SPHERE || A.type == B200_GEOM_CAPSULE) { full1 = A.size.v[0] + R(0.5) * margin; Ac.size.v[0] = 0; Ac.margin = 0; }
+  if (B.type == B200_GEOM_SPHERE || B.type == B200_GEOM_CAPSULE) { full2 = B.size.v[0] + R(0.5) * margin; Bc.size.v[0] = 0; Bc.margin = 0; }
+  if (full1 + full2 > 0) {
+    GjkOut r = gjk(&Ac, &Bc, tol, iterations, full1 + full2);
+    if (r.separated) return 0;
+    if (r.dist > tol) {
+      V3 nrm = vnormalize(vsub(r.x2, r.x1));
+      x1 = vadd(r.x1, vscale(nrm, full1)); x2 = vsub(r.x2, vscale(nrm, full2));
+      d = r.dist - (full1 + full2); found = 1;
+    }
+  }
+  if (!found) {
+    GjkOut r = gjk(&A, &B, tol, iterations, 0);
+    if (r.separated) return 0;
+    if (r.dist > tol) { d = r.dist; x1 = r.x1; x2 = r.x2; }
+    else {
+      EpaOut e = epa(&A, &B, &r.s, tol, epa_iterations);
+      if (!e.ok) { d = r.dist; x1 = r.x1; x2 = r.x2; }
+      else { d = -e.depth; x1 = e.x1; x2 = e.x2; }
+    }
+  }
+  if (!(d < 0)) return 0;
+  *dist = d + margin;
+  vstore(pos, vadd(vscale(vadd(x1, x2), R(0.5)), origin));
+  vstore(normal, vnormalize(*dist <= margin ? vsub(x1, x2) : vsub(x2, x1)));
+  return 1;
 }

@@ -33,6 +33,8 @@ class Oracle:
         self.lib.oracle_leaf_contacts.argtypes = [P] * 13
         self.lib.oracle_leaf_box.argtypes = [ct.c_int] + [P] * 6 + [self.real] + [P] * 3
         self.lib.oracle_leaf_integrate.argtypes = [P, P, P, ct.c_double]
+        self.lib.oracle_leaf_convex.argtypes = ([ct.c_int] + [P] * 4 + [ct.c_int]) * 2 + [self.real] * 2 + \
+            [ct.c_int] * 2 + [P] * 3
         self.lib.oracle_step.restype = ct.c_int
         self.lib.oracle_step.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_int, ct.c_int, ct.c_int, ct.c_int]
         self.lib.oracle_forward.restype = ct.c_int
@@ -107,3 +109,18 @@ class Oracle:
         if self.lib.oracle_leaf_integrate(ct.addressof(model), self._ptr(q), self._ptr(v), dt):
             raise RuntimeError('oracle_leaf_integrate failed')
         return q
+
+    def convex(self, kind1, p1, R1, s1, v1, kind2, p2, R2, s2, v2, margin=0.0, tol=1e-6, iterations=50,
+               epa_iterations=32):
+        """Convex narrowphase of two shapes on raw poses; v1 / v2 are local
+        mesh vertices (None for primitives).  Returns (dist, pos, normal) or None."""
+        def arr(x, n):
+            return np.ascontiguousarray(np.zeros(n) if x is None else np.asarray(x, float).ravel(), self.dtype)
+        a = [arr(p1, 3), arr(R1, 9), arr(s1, 3), arr(v1, 3), arr(p2, 3), arr(R2, 9), arr(s2, 3), arr(v2, 3)]
+        n1 = 0 if v1 is None else len(np.asarray(v1).reshape(-1, 3))
+        n2 = 0 if v2 is None else len(np.asarray(v2).reshape(-1, 3))
+        dist, pos, nrm = np.zeros(1, self.dtype), np.zeros(3, self.dtype), np.zeros(3, self.dtype)
+        n = self.lib.oracle_leaf_convex(kind1, *[self._ptr(x) for x in a[:4]], n1, kind2,
+                                        *[self._ptr(x) for x in a[4:]], n2, margin, tol, iterations,
+                                        epa_iterations, self._ptr(dist), self._ptr(pos), self._ptr(nrm))
+        return (float(dist[0]), pos.astype(float), nrm.astype(float)) if n else None

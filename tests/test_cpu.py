@@ -148,3 +148,40 @@ def test_oracle_pyramidal_cones_rest_and_track_fp64(oracle_module):
     for j in np.flatnonzero(pyr.ints['jnt_type'] == 0):
         z = a['qpos'][:, pyr.ints['jnt_qposadr'][j] + 2]
         assert np.all(z > 0.015) and np.all(z < 0.06)
+
+
+@pytest.fixture(scope='module')
+def scene_b():
+    return scenes.scene_b()
+
+
+def test_scene_b_sizes_and_families(scene_b):
+    s = scene_b.sizes
+    assert (s['nq'], s['nv'], s['nfree'], s['nobs']) == (93, 81, 12, 111)
+    assert s['nmesh'] == 2 and s['nmeshvert'] == 64
+    assert scene_b.supported
+    fam = set(scene_b.pair_families)
+    assert {(2, 2), (2, 3), (3, 3), (0, 7), (2, 7), (3, 7), (6, 7), (7, 7)} <= fam
+    root = ET.fromstring(scene_b.mjcf())
+    assert len(root.findall('.//asset/mesh')) == 2
+    assert len(root.findall('.//geom')) == s['ngeom']
+    # hull mass properties: centroid at the geom origin, symmetric positive inertia
+    for b in scene_b.bodies:
+        for g in b.geoms:
+            if g.kind == scenes.MESH:
+                v = g.mesh['vert']
+                assert len(v) == 32 and g.mesh['volume'] > 0
+                assert np.all(np.linalg.eigvalsh(g.mesh['inertia']) > 0)
+                n = g.mesh['normals']
+                for (a, bb, c), nn in zip(g.mesh['faces'], n):   # outward faces
+                    assert np.dot(nn, v[a]) > 0
+
+
+def test_oracle_scene_b_drops_and_settles(oracle_module, scene_b):
+    h = run_oracle(oracle_module, scene_b, 'fp32', 2, 15, seed=3)
+    assert np.all(np.isfinite(h['qpos'])) and not np.any(h['error'])
+    assert not np.any(h['overflow'] & ~0x600)
+    assert np.all(h['ncon'] >= 12) and np.all(h['nefc'] >= 40)
+    for j in np.flatnonzero(scene_b.ints['jnt_type'] == 0):
+        z = h['qpos'][:, scene_b.ints['jnt_qposadr'][j] + 2]
+        assert np.all(z > 0.005) and np.all(z < 0.2)

@@ -188,3 +188,35 @@ def test_reference_boxbox_fixtures(oracle):
     for x, y, z, count in fx['unit_boxes']['cases']:
         d, p, n = orc.box(6, [0, 0, 0], np.eye(3), [1, 1, 1], [x, y, z], np.eye(3), [1, 1, 1])
         assert len(unique_points(p, 16 * EPS32 * 3)) == count
+
+
+def box_corners(size):
+    return np.array([[sx * size[0], sy * size[1], sz * size[2]] for sx in (-1, 1) for sy in (-1, 1) for sz in (-1, 1)])
+
+
+def test_convex_path_against_reference_box_geometry(oracle):
+    """GJK/EPA on hulls built from box corners reproduces the reference's
+    independent SAT separation (box pairs) and segment-box distances
+    (sphere / capsule against a box hull, centres outside the box)."""
+    precision, orc, _ = oracle
+    tol = 1e-12 if precision == 'fp64' else 2e-5
+    checked = {2: 0, 3: 0, 6: 0}
+    for case in box_cases():
+        kind = case['kind']
+        v1 = box_corners(case['s1']) if kind == 6 else None
+        got = orc.convex(7 if kind == 6 else kind, case['p1'], case['R1'], case['s1'], v1, 7, case['p2'], case['R2'],
+                         case['s2'], box_corners(case['s2']))
+        if kind == 6:
+            want = case['separation']
+        elif case['inside']:
+            continue
+        else:
+            want = case['closest']
+        if want < -max(tol, 1e-9):
+            assert got is not None, case
+            assert abs(got[0] - want) <= tol, (kind, got[0], want)
+            assert abs(np.linalg.norm(got[2]) - 1) < 1e-5
+            checked[kind] += 1
+        elif want > max(tol, 1e-9):
+            assert got is None
+    assert min(checked.values()) >= 20

@@ -174,3 +174,72 @@ def test_launch_rejects_bad_model(scene):
     bad.nv = 0
     with pytest.raises(RuntimeError, match='CUDA error 1'):
         rt.lib.step(bad, rt.data, 1, 1, torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.fixture(scope='module')
+def scene_b_state(oracle_module):
+    """Scene B worlds after 6 control steps of the FP64 oracle: objects have
+    landed and touch the floor, each other and sometimes the arm."""
+    b = scenes.scene_b()
+    n = 8
+    packed = native.PackedModel(b, 'fp64')
+    host = native.alloc_numpy(packed, n)
+    q, v = b.initial_state(n, seed=21)
+    host['qpos'][:] = q
+    host['qvel'][:] = v
+    orc = oracle_module.Oracle('fp64')
+    ms, ds = packed.host_struct(), native.data_struct(host, n)
+    orc.forward(ms, ds, 0, n, 1)
+    for k in range(6):
+        host['action'][:] = b.actions(n, k, seed=21)
+        orc.step(ms, ds, 0, n, b.substeps, 1)
+    return b, np.concatenate([host['time'], host['qpos'], host['qvel']], axis=1)
+
+
+@pytest.mark.parametrize('precision,rel', [('fp32', 1e-4), ('fp64', 1e-9)])
+def test_scene_b_forward_parity(scene_b_state, oracle_module, precision, rel):
+    """Contact lists (all families: primitives, plane-mesh, GJK/EPA) bit-exact
+    against the oracle; contact geometry to the precision's rounding."""
+    from gpu_libero_b200.runtime import Runtime
+    b, state = scene_b_state
+    n = len(state)
+    rt = Runtime(b, n, precision=precision)
+    rt.set_state(state)
+    torch.cuda.synchronize()
+    gpu = host_copy(rt, n)
+    ref = {k: v.copy() for k, v in gpu.items()}
+    orc = oracle_module.Oracle(precision)
+    orc.forward(rt.packed.host_struct(), native.data_struct(ref, n), 0, n, 0)
+    assert np.array_equal(gpu['ncon'], ref['ncon'])
+    assert np.all(ref['ncon'] >= 12)
+    for w in range(n):
+        c = int(ref['ncon'][w, 0])
+        assert np.array_equal(gpu['con_geom'][w, :2 * c], ref['con_geom'][w, :2 * c])
+        assert close(gpu['con_dist'][w, :c], ref['con_dist'][w, :c], rel)
+        assert close(gpu['con_pos'][w, :3 * c], ref['con_pos'][w, :3 * c], rel)
+        assert close(gpu['con_frame'][w, :9 * c], ref['con_frame'][w, :9 * c], 100 * rel)
+    for k in ('xpos', 'xquat', 'qfrc_bias', 'qacc_smooth'):
+        assert close(gpu[k], ref[k], 10 * rel), k
+    assert close(gpu['qacc'], ref['qacc'], 1000 * rel)
+
+
+@pytest.mark.parametrize('precision,tol', [('fp32', 1e-3), ('fp64', 1e-6)])
+def test_scene_b_control_steps_parity(scene_b_state, oracle_module, precision, tol):
+    from gpu_libero_b200.runtime import Runtime
+    b, state = scene_b_state
+    n = len(state)
+    rt = Runtime(b, n, precision=precision)
+    rt.set_state(state)
+    torch.cuda.synchronize()
+    ref = host_copy(rt, n)
+    orc = oracle_module.Oracle(precision)
+    for step in range(2):
+        a = b.actions(n, 10 + step, seed=21)
+        rt.enqueue_action(a)
+        ref['action'][:] = a
+        orc.step(rt.packed.host_struct(), native.data_struct(ref, n), 0, n, b.substeps, 1)
+    torch.cuda.synchronize()
+    gpu = {k: t.cpu().numpy() for k, t in rt.buffers.items()}
+    assert np.max(np.abs(gpu['qpos'] - ref['qpos'])) < tol
+    assert np.array_equal(gpu['integration_count'], ref['integration_count'])
+    assert not np.any(gpu['overflow'] & ~0x600) and not np.any(gpu['error'])
