@@ -1,0 +1,138 @@
+// C ABI of the B200 physics step: argument checks, launch shape, dispatch
+// to the kernel instances (inst.cu).
+#include <cuda_runtime.h>
+#include <cstdlib>
+#include "b200phys.h"
+#include "arena.cuh"
+#include "launch.h"
+
+#ifndef B200PHYS_SOURCE_ID
+#define B200PHYS_SOURCE_ID "b200phys-dev"
+#endif
+
+// ============================================================ C ABI
+namespace {
+constexpr int kMaxWorldsPerCta = 8;
+
+bool model_ok(const B200Model *m) {
+  return m && m->real && m->ints && (m->real_bytes == 4 || m->real_bytes == 8) && m->nv >= 1 && m->nv <= 128 &&
+         m->nbody >= 2 && m->ncon_max >= 1 && m->nefc_max >= 1 && m->nvs >= m->nv && m->nsite > m->ee_site &&
+         m->nu >= 9 && m->ntree >= 1 && m->ntree <= 32 && m->kmax_dof >= m->max_tree_dofs;
+}
+bool data_ok(const B200Data *d) {
+  return d && d->nworld >= 0 && d->qpos && d->qvel && d->qacc_warmstart && d->ctrl && d->time && d->goal_pos &&
+         d->goal_rot && d->gripper && d->overflow && d->error;
+}
+size_t arena_for(const B200Model *m) {
+  return m->real_bytes == 4 ? b200::Arena<float>::layout(*m, 32, nullptr, nullptr)
+                            : b200::Arena<double>::layout(*m, 32, nullptr, nullptr);
+}
+int max_optin_smem() {
+  static int v = -1;
+  if (v < 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) v = 0;
+  }
+  return v;
+}
+// Worlds per CTA.  Two CTAs per SM (each holding half of the SM's shared
+// memory) measured faster than one large CTA: worlds of a CTA wait for its
+// slowest world at stage barriers, and the second CTA fills those gaps.
+int worlds_per_cta(const B200Model *m, int limit) {
+  const size_t arena = arena_for(m);
+  if (arena == 0 || (int)arena > limit) return 0;
+  const int half = (228 * 1024) / 2 - 1024;  // per-SM capacity shared by two CTAs
+  int wpc = half / (int)arena >= 3 ? half / (int)arena : limit / (int)arena;
+  static int cap = -1;  // B200PHYS_WPC: smaller CTAs (more CTAs per SM), for tuning
+  if (cap < 0) {
+    const char *e = getenv("B200PHYS_WPC");
+    cap = e ? atoi(e) : kMaxWorldsPerCta;
+    if (cap < 1 || cap > kMaxWorldsPerCta) cap = kMaxWorldsPerCta;
+  }
+  return wpc > cap ? cap : wpc;
+}
+// Launch shape: worlds per CTA and threads per world.  A world is one warp,
+// or four warps when at most two worlds fit on an SM (large models), so that
+// an SM still runs eight warps.
+struct Shape {
+  int wpc, T;
+};
+template <class R, bool C> int prepare_rc(const B200Model *m, const Shape &sh) {
+  const size_t smem = (size_t)sh.wpc * arena_for(m);
+  return sh.T == 32 ? b200::configure_kernels<R, C, 32>(smem) : b200::configure_kernels<R, C, 128>(smem);
+}
+int launch_shape(const B200Model *m, Shape *sh) {
+  const int limit = max_optin_smem();
+  sh->wpc = worlds_per_cta(m, limit);
+  if (sh->wpc < 1) return (int)cudaErrorInvalidValue;
+  const int arena = (int)arena_for(m);
+  const int per_sm = ((228 * 1024) / (sh->wpc * arena + 1024)) * sh->wpc;
+  sh->T = per_sm <= 2 ? 128 : 32;
+  static int force = -1;  // B200PHYS_THREADS: 32 or 128 threads per world, for tuning
+  if (force < 0) {
+    const char *e = getenv("B200PHYS_THREADS");
+    force = e ? atoi(e) : 0;
+  }
+  if (force == 32 || force == 128) sh->T = force;
+  if (sh->T * sh->wpc > 256) sh->wpc = 256 / sh->T;
+  const bool convex = m->nmesh > 0;
+  if (m->real_bytes == 4) return convex ? prepare_rc<float, true>(m, *sh) : prepare_rc<float, false>(m, *sh);
+  return convex ? prepare_rc<double, true>(m, *sh) : prepare_rc<double, false>(m, *sh);
+}
+// kernel instance by precision, mesh support and threads per world
+template <template <class, bool, int> class F, class... A> void dispatch(const B200Model *m, const Shape &sh, A... a) {
+  const bool c = m->nmesh > 0, t = sh.T == 128;
+  if (m->real_bytes == 4) {
+    if (c) t ? F<float, true, 128>::run(a...) : F<float, true, 32>::run(a...);
+    else t ? F<float, false, 128>::run(a...) : F<float, false, 32>::run(a...);
+  } else {
+    if (c) t ? F<double, true, 128>::run(a...) : F<double, true, 32>::run(a...);
+    else t ? F<double, false, 128>::run(a...) : F<double, false, 32>::run(a...);
+  }
+}
+template <class R, bool C, int T> struct StepLaunch {
+  template <class... A> static void run(A... a) { b200::launch_step<R, C, T>(a...); }
+};
+template <class R, bool C, int T> struct ForwardLaunch {
+  template <class... A> static void run(A... a) { b200::launch_forward<R, C, T>(a...); }
+};
+}  // namespace
+
+extern "C" {
+const char *b200phys_source_id(void) { return B200PHYS_SOURCE_ID; }
+int b200phys_arch(void) { return 100; }
+size_t b200phys_model_bytes(void) { return sizeof(B200Model); }
+size_t b200phys_data_bytes(void) { return sizeof(B200Data); }
+size_t b200phys_world_smem_bytes(const B200Model *m) { return model_ok(m) ? arena_for(m) : 0; }
+
+int b200phys_prepare(const B200Model *m) {
+  if (!model_ok(m)) return (int)cudaErrorInvalidValue;
+  Shape sh;
+  return launch_shape(m, &sh);
+}
+
+int b200phys_step_launch(const B200Model *m, const B200Data *d, int substeps, int policy, void *stream) {
+  if (!model_ok(m) || !data_ok(d) || substeps < 0) return (int)cudaErrorInvalidValue;
+  if (d->nworld == 0 || substeps == 0) return 0;
+  Shape sh;
+  int rc;
+  if ((rc = launch_shape(m, &sh))) return rc;
+  const int arena = (int)arena_for(m), grid = (d->nworld + sh.wpc - 1) / sh.wpc;
+  dispatch<StepLaunch>(m, sh, *m, *d, substeps, policy, sh.wpc, arena, grid, (size_t)sh.wpc * arena,
+                       (cudaStream_t)stream);
+  return (int)cudaGetLastError();
+}
+
+int b200phys_forward_launch(const B200Model *m, const B200Data *d, int bootstrap, const int *mask, void *stream) {
+  if (!model_ok(m) || !data_ok(d)) return (int)cudaErrorInvalidValue;
+  if (d->nworld == 0) return 0;
+  Shape sh;
+  int rc;
+  if ((rc = launch_shape(m, &sh))) return rc;
+  const int arena = (int)arena_for(m), grid = (d->nworld + sh.wpc - 1) / sh.wpc;
+  dispatch<ForwardLaunch>(m, sh, *m, *d, bootstrap, mask, sh.wpc, arena, grid, (size_t)sh.wpc * arena,
+                          (cudaStream_t)stream);
+  return (int)cudaGetLastError();
+}
+}

@@ -47,7 +47,7 @@ template <class R> struct Arena {
   // islands: trees coupled by constraint rows; the Hessian is block diagonal
   // over islands, each block dense in island-local dof order
   int *tree_isl, *isl_n, *isl_off, *isl_dofstart, *isl_dof, *dof_isl, *dof_loc;
-  R *xs, *colbuf;  // permuted solve vector; double-buffered Cholesky column (2 x 32)
+  R *xs, *colbuf;  // permuted solve vector; Cholesky column buffers (2 x nv) / per-warp contact scratch
   // Newton Hessian, reused as OSC scratch (double) before the solve
   R *H;
   double *osc;
@@ -56,7 +56,7 @@ template <class R> struct Arena {
   int *iscal;  // [0] ncon [1] nefc [2] nf [3] overflow [4] niter [5] done [6] error [7] ls evals
                // [8] raw contact count [9] ls evals at previous substep [10] profiling on
                // [11] islands [12] largest island [16..19] OSC factor flags [20..22] pinv flags
-  R *red;    // reduction scratch (one real per warp, times 4)
+  R *red;    // reduction scratch (one real per warp of the world)
   long long *prof;  // [0] last stamp, [1..15] per-stage cycle sums (stage profiling only)
 
   static constexpr int kOscDoubles = 400;
@@ -91,8 +91,8 @@ template <class R> struct Arena {
     o[k++] = c.take<int>(nt + 1);
     o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv);
     o[k++] = c.take<R>(nv);
-    o[k++] = c.take<R>(64);
-    o[k++] = c.take<R>(8); o[k++] = c.take<int>(24); o[k++] = c.take<R>(4 * ((threads + 31) / 32));
+    o[k++] = c.take<R>(2 * nv > 160 ? 2 * nv : 160);  // colbuf
+    o[k++] = c.take<R>(8); o[k++] = c.take<int>(24); o[k++] = c.take<R>(32);  // red: one real per warp of a world
     o[k++] = c.take<long long>(16);
     // union region
     const size_t kin = (size_t)(nb * 3 + nb * 9 + nj * 3 + nj * 3 + nb * 10) * sizeof(R) + 5 * 16;

@@ -1,6 +1,8 @@
-// B200-native batched rigid-body physics step (sm_100a).
+// B200-native batched rigid-body physics step (sm_100a): device code.
+// Included by inst.cu, which instantiates the kernels per precision and
+// mesh support; abi.cu holds the C ABI and the launch shape.
 //
-// One CTA owns one world for a whole control step.  The world's state is
+// A CTA owns one or more worlds for a whole control step.  The world's state is
 // loaded from HBM once, every substep of the control step runs out of shared
 // memory (forward kinematics, composite-rigid-body mass matrix and factor,
 // collision, constraint rows, RNE, FP64 OSC, actuation, Newton with exact line
@@ -13,6 +15,7 @@
 // Build: nvcc -gencode arch=compute_100a,code=sm_100a --fmad=true
 //        --prec-div=true --prec-sqrt=true --ftz=false (the reference's
 //        FP32 flags, libero/libero/gpu/cmake/MjwarpBox.cmake:15).
+#pragma once
 #include <cuda_runtime.h>
 #include <cfloat>
 #include <cstdint>
@@ -32,14 +35,27 @@ constexpr int kSatisfied = 0, kQuadratic = 1, kLinearNeg = 2, kLinearPos = 3, kC
 
 // One warp owns one world: loops stride over the warp's lanes and barriers
 // are warp barriers.  Worlds of a CTA meet at CTA barriers between stages.
+// A world is T consecutive threads of the CTA (T = 32: one warp; T = 128:
+// four warps for models whose arena leaves room for few worlds per SM).
+// TID is the thread's index in its world, FOR strides a loop over the
+// world's threads and SYNC() is the world's barrier (a warp barrier for
+// T = 32, else the named barrier 1 + world slot).  WARP0 marks the world's
+// first warp, which runs the warp-collective sections (shuffles, ballots,
+// per-lane factor rows).  Every macro needs T in scope.
 #define LANE ((int)(threadIdx.x & 31))
-#define FOR(i, n) for (int i = LANE; i < (n); i += 32)
-#define SYNC() __syncwarp()
+#define TID ((int)(threadIdx.x % T))
+#define WARP0 (TID < 32)
+#define FOR(i, n) for (int i = TID; i < (n); i += T)
+#define SYNC() world_sync<T>()
+template <int T> __device__ __forceinline__ void world_sync() {
+  if (T == 32) __syncwarp();
+  else asm volatile("bar.sync %0, %1;" ::"r"(1 + (int)(threadIdx.x / T)), "r"(T) : "memory");
+}
 
 // Stage profiling (data.stage_cycles != NULL): lane 0 of each world stamps
 // clock64 at stage boundaries, after a barrier.
-template <class R> __device__ __forceinline__ void mark(Arena<R> &A, int stage) {
-  if (stage > 0 && A.iscal[10] && LANE == 0) {
+template <int T, class R> __device__ __forceinline__ void mark(Arena<R> &A, int stage) {
+  if (stage > 0 && A.iscal[10] && TID == 0) {
     const long long t = clock64();
     A.prof[stage] += t - A.prof[0];
     A.prof[0] = t;
@@ -53,6 +69,18 @@ template <class R> __device__ __forceinline__ void mark(Arena<R> &A, int stage) 
 template <class R> __device__ __forceinline__ R warp_sum(R v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+// sum over the world's threads; red: T / 32 reals of scratch
+template <int T, class R> __device__ __forceinline__ R world_sum(R v, R *red) {
+  v = warp_sum(v);
+  if (T == 32) return v;
+  SYNC();
+  if (LANE == 0) red[TID >> 5] = v;
+  SYNC();
+  R s = 0;
+  for (int k = 0; k < T / 32; ++k) s += red[k];
+  return s;
 }
 
 // M[i][j] from the per-tree dense blocks (0 across trees)
@@ -96,7 +124,7 @@ template <class R> __device__ __forceinline__ R jdot(const Mdl<R> &M, const Aren
 // forward kinematics, level by level (mjwarp_kinematics.cu:95-212 semantics)
 template <class R, int T> __device__ B200_STAGE_ATTR void kinematics(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
-  if (LANE == 0) {
+  if (TID == 0) {
     A.xpos[0] = A.xpos[1] = A.xpos[2] = 0;
     A.xquat[0] = 1; A.xquat[1] = A.xquat[2] = A.xquat[3] = 0;
   }
@@ -248,43 +276,36 @@ template <class R, int T> __device__ B200_STAGE_ATTR void com_crb_mass(const Mdl
   SYNC();
 }
 
-// Block-diagonal dense factorizations, one warp: lane owns matrix rows at
-// positions p = lane + 32 s (s < 4).  Each position knows its block size n,
-// its row a inside the block, the block's storage base (dense n x n,
-// row-major) and the block's first position.  Blocks are kinematic trees
-// (mass matrix, implicit-damping matrix) or constraint islands (Newton
-// Hessian); all blocks advance together, so a factorization takes as many
-// steps as the largest block, not as nv.
-struct BlockRows { int n[4], a[4], base[4], start[4]; };
+// Block-diagonal dense factorizations.  Blocks (kinematic trees for the
+// mass matrix and the implicit-damping matrix, constraint islands for the
+// Newton Hessian) are dealt to the world's warps round robin; within a warp,
+// lane l owns the rows q = l + 32 s (s < 4) of the concatenation of its
+// blocks.  Each owned row knows its block size n, its row a inside the
+// block, the block's storage base (dense n x n, row-major) and the block's
+// first position in the solve vector.  A warp's blocks advance together, so
+// a factorization takes as many steps as its largest block.
+struct BlockRows { int n[4], a[4], base[4], start[4], rows; };
 
-template <class R> __device__ __forceinline__ BlockRows tree_rows(const Mdl<R> &M, int lane) {
+__device__ __forceinline__ BlockRows owned_rows(int nblocks, const int *bn, const int *bstart, const int *bbase,
+                                                int lane, int wi, int nw) {
   BlockRows b;
 #pragma unroll
-  for (int s = 0; s < 4; ++s) {
-    const int p = lane + 32 * s;
-    b.n[s] = 0; b.a[s] = -1; b.base[s] = 0; b.start[s] = 0;
-    if (p < M.m.nv) {
-      const int t = IF(dof_treeid)[p];
-      b.n[s] = IF(tree_dofnum)[t]; b.start[s] = IF(tree_dofadr)[t];
-      b.a[s] = p - b.start[s]; b.base[s] = IF(tree_madr)[t];
-    }
-  }
-  return b;
-}
-
-template <class R> __device__ __forceinline__ BlockRows island_rows(const Arena<R> &A, int nv, int lane) {
-  BlockRows b;
+  for (int s = 0; s < 4; ++s) { b.n[s] = 0; b.a[s] = -1; b.base[s] = 0; b.start[s] = 0; }
+  int acc = 0;
+  for (int k = wi; k < nblocks; k += nw) {
+    const int n = bn[k];
 #pragma unroll
-  for (int s = 0; s < 4; ++s) {
-    const int p = lane + 32 * s;
-    b.n[s] = 0; b.a[s] = -1; b.base[s] = 0; b.start[s] = 0;
-    if (p < nv) {
-      const int d = A.isl_dof[p], isl = A.dof_isl[d];
-      b.n[s] = A.isl_n[isl]; b.a[s] = A.dof_loc[d]; b.base[s] = A.isl_off[isl]; b.start[s] = A.isl_dofstart[isl];
+    for (int s = 0; s < 4; ++s) {
+      const int q = lane + 32 * s;
+      if (q >= acc && q < acc + n) { b.n[s] = n; b.a[s] = q - acc; b.base[s] = bbase[k]; b.start[s] = bstart[k]; }
     }
+    acc += n;
   }
+  b.rows = acc;
   return b;
 }
+#define TREE_ROWS(T) owned_rows(M.m.ntree, IF(tree_dofnum), IF(tree_dofadr), IF(tree_madr), LANE, TID >> 5, (T) / 32)
+#define ISLAND_ROWS(T) owned_rows(A.iscal[11], A.isl_n, A.isl_dofstart, A.isl_off, LANE, TID >> 5, (T) / 32)
 
 // in-place lower Cholesky L L^T of every block (right-looking, warp 0)
 template <class R> __device__ void chol_blocks_smem(R *H, const BlockRows &b, int maxn) {
@@ -315,13 +336,13 @@ template <class R> __device__ void chol_blocks_smem(R *H, const BlockRows &b, in
 // factor is written back to H (lower triangle, diagonal = pivots) for the
 // triangular solves.
 template <class R, int MAXN>
-__device__ void chol_blocks_reg(R *H, const BlockRows &b, int maxn, R *colbuf) {
+__device__ void chol_blocks_reg(R *H, const BlockRows &b, int maxn, R *colbuf, int stride) {
   const int n = b.n[0], a = b.a[0];
   R row[MAXN];
 #pragma unroll
   for (int j = 0; j < MAXN; ++j) row[j] = (n > 0 && j <= a && j < n) ? H[b.base[0] + a * n + j] : R(0);
   for (int k = 0; k < maxn; ++k) {
-    R *col = colbuf + (k & 1) * 32;
+    R *col = colbuf + (k & 1) * stride;
     R rk = 0;
 #pragma unroll
     for (int j = 0; j < MAXN; ++j)
@@ -358,9 +379,10 @@ __device__ void chol_blocks_reg(R *H, const BlockRows &b, int maxn, R *colbuf) {
   __syncwarp();
 }
 
+// colbuf: 2 x nv reals (the register variant's double-buffered column, indexed by position)
 template <class R> __device__ B200_STAGE_ATTR void chol_blocks(R *H, const BlockRows &b, int maxn, int nv, R *colbuf) {
 #ifndef B200_CHOL_SMEM
-  if (nv <= 32 && maxn <= 16) chol_blocks_reg<R, 16>(H, b, maxn, colbuf);
+  if (b.rows <= 32 && maxn <= 16) chol_blocks_reg<R, 16>(H, b, maxn, colbuf, nv);
   else
 #endif
     chol_blocks_smem(H, b, maxn);
@@ -371,21 +393,21 @@ template <class R> __device__ B200_STAGE_ATTR void solve_blocks(const R *H, cons
   for (int k = 0; k < maxn; ++k) {
 #pragma unroll
     for (int s = 0; s < 4; ++s)
-      if (b.n[s] > k && b.a[s] == k) x[lane + 32 * s] /= H[b.base[s] + k * b.n[s] + k];
+      if (b.n[s] > k && b.a[s] == k) x[b.start[s] + b.a[s]] /= H[b.base[s] + k * b.n[s] + k];
     __syncwarp();
 #pragma unroll
     for (int s = 0; s < 4; ++s)
-      if (b.n[s] > k && b.a[s] > k) x[lane + 32 * s] -= H[b.base[s] + b.a[s] * b.n[s] + k] * x[b.start[s] + k];
+      if (b.n[s] > k && b.a[s] > k) x[b.start[s] + b.a[s]] -= H[b.base[s] + b.a[s] * b.n[s] + k] * x[b.start[s] + k];
     __syncwarp();
   }
   for (int k = maxn - 1; k >= 0; --k) {
 #pragma unroll
     for (int s = 0; s < 4; ++s)
-      if (b.n[s] > k && b.a[s] == k) x[lane + 32 * s] /= H[b.base[s] + k * b.n[s] + k];
+      if (b.n[s] > k && b.a[s] == k) x[b.start[s] + b.a[s]] /= H[b.base[s] + k * b.n[s] + k];
     __syncwarp();
 #pragma unroll
     for (int s = 0; s < 4; ++s)
-      if (b.n[s] > k && b.a[s] < k) x[lane + 32 * s] -= H[b.base[s] + k * b.n[s] + b.a[s]] * x[b.start[s] + k];
+      if (b.n[s] > k && b.a[s] < k) x[b.start[s] + b.a[s]] -= H[b.base[s] + k * b.n[s] + b.a[s]] * x[b.start[s] + k];
     __syncwarp();
   }
 }
@@ -406,7 +428,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void mass_mul(const Mdl<R> 
 // GJK/EPA pairs); models without meshes run the smaller variant.
 template <class R, int T, bool CONVEX> __device__ B200_STAGE_ATTR void collision(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
-  if (LANE == 0) A.iscal[8] = 0;
+  if (TID == 0) A.iscal[8] = 0;
   SYNC();
   if (!(m.disable_flags & (B200_DSBL_CONSTRAINT | B200_DSBL_CONTACT))) {
     FOR(p, m.npair) collide_pair<R, CONVEX>(M, A, p);
@@ -420,7 +442,7 @@ template <class R, int T, bool CONVEX> __device__ B200_STAGE_ATTR void collision
     for (int k = 0; k < n; ++k) rank += A.con_key[k] < key;
     A.con_order[rank] = c;
   }
-  if (LANE == 0) A.iscal[0] = n;
+  if (TID == 0) A.iscal[0] = n;
   SYNC();
 }
 
@@ -550,7 +572,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void constraints(const Mdl<
   const bool elliptic = m.cone == 1;
   // row allocation (warp 0): friction rows, active limits, then contacts in
   // sorted order, each contact all-or-nothing; prefix sums by warp scans
-  if (LANE < 32) {
+  if (WARP0) {
     const int lane = LANE;
     const unsigned below = (1u << lane) - 1u;
     int of = 0;
@@ -753,8 +775,8 @@ template <class R> __device__ __forceinline__ void force_cross(const R *v, const
 
 template <class R, int T> __device__ B200_STAGE_ATTR void velocity(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
-  if (LANE < 6) {
-    const int c = LANE;
+  if (TID < 6) {
+    const int c = TID;
     A.cvel[c] = 0;
     R g = 0;
     if (c >= 3 && !(m.disable_flags & B200_DSBL_GRAVITY))
@@ -857,7 +879,7 @@ enum { kM = 0, kJ = 49, kMi = 91, kJbar = 91, kMJT = 140, kA = 182, kN = 182, kL
 // In-place lower Cholesky of an n x n FP64 matrix (row stride ld), one warp,
 // lane i owning row i.  *bad is set when a pivot is not positive or is tiny
 // relative to the matrix diagonal (near-singular: caller falls back).
-__device__ void chol_warp(double *a, int n, int ld, int lane, int *bad) {
+static __device__ void chol_warp(double *a, int n, int ld, int lane, int *bad) {
   double dmax = 0;
   for (int i = 0; i < n; ++i) dmax = fmax(dmax, fabs(a[i * ld + i]));
   for (int k = 0; k < n; ++k) {
@@ -878,7 +900,7 @@ __device__ void chol_warp(double *a, int n, int ld, int lane, int *bad) {
 
 // one-sided Jacobi pseudoinverse of an n x n block (6-stride), one lane group
 // of 8 lanes, lane r owning row r (osc_solver.cu:120-253 pinv_group)
-__device__ __noinline__ void pinv_group(const double *in, double *out, int n, int lane8, unsigned mask, int *ok) {
+static __device__ __noinline__ void pinv_group(const double *in, double *out, int n, int lane8, unsigned mask, int *ok) {
   double scale = 0;
   if (lane8 < n)
     for (int c = 0; c < n; ++c) scale = fmax(scale, fabs(in[lane8 * 6 + c]));
@@ -983,7 +1005,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void osc_control(const Mdl<
   const int nv = m.nv, site = m.ee_site, body = IF(site_bodyid)[site];
   const int *vi = IF(osc_dofadr), *qi = IF(osc_qposadr), *ids = IF(osc_actuator);
   double *S = A.osc;
-  const int lane = LANE;
+  const int lane = TID;
   // ee velocity over all dofs (non-ancestors have zero Jacobian columns)
   if (lane < 32) {  // warp 0: six 4-lane groups, lanes 24..31 idle
     const int ax = lane >> 2, l4 = lane & 3;
@@ -1027,7 +1049,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void osc_control(const Mdl<
   // replace the reference's LU and one-sided Jacobi SVD (same matrices to
   // FP64 rounding).  When a pivot shows near-singularity the reference's
   // Jacobi pseudoinverse runs instead (pinv_group), rank cutoff included.
-  if (LANE < 32) {
+  if (WARP0) {
     int *flags = A.iscal + 16;
     double *L7 = S + osc::kMi;  // Cholesky factor of M (lower, row-major)
     for (int z = lane; z < 49; z += 32) L7[z] = S[osc::kM + z];
@@ -1238,7 +1260,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void actuation(const Mdl<R>
     A.qacc_smooth[d] = A.qfrc_smooth[d];
   }
   SYNC();
-  if (LANE < 32) solve_blocks(A.L, tree_rows(M, LANE), A.qacc_smooth, m.max_tree_dofs, LANE);
+  solve_blocks(A.L, TREE_ROWS(T), A.qacc_smooth, m.max_tree_dofs, LANE);
   SYNC();
 }
 
@@ -1297,8 +1319,8 @@ template <class R, int T> __device__ B200_STAGE_ATTR void eval_gradient(const Md
     A.grad[i] = g;
     gd += g * g;
   }
-  gd = warp_sum(gd);
-  if (LANE == 0) A.scal[3] = gd;
+  gd = world_sum<T>(gd, A.red);
+  if (TID == 0) A.scal[3] = gd;
 }
 
 // H = M + J' D J over quadratic rows + elliptic-cone curvature
@@ -1339,10 +1361,16 @@ template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &
     }
   }
   SYNC();
-  R *C = A.colbuf;  // per-contact row coupling matrix (<= 6 x 6)
+  // contacts: islands are dealt to the world's warps; a warp adds its
+  // islands' contacts one after another (each H entry of a contact on its
+  // own lane), so different warps never touch the same block
+  const int lane = LANE, wi = TID >> 5, nw = T / 32;
+  R *C = A.colbuf + 36 * wi;  // this warp's row coupling matrix (<= 6 x 6)
   for (int c = 0; c < ncon; ++c) {
     const int r0 = A.con_adr[c];
     if (r0 < 0) continue;
+    const int isl = A.tree_isl[A.row_t[2 * r0]];
+    if (isl % nw != wi) continue;
     const int type = A.efc_type[r0], dim = A.con_dim[c];
     const int cnt = type == 6 ? 2 * (dim - 1) : dim;
     bool full = false;
@@ -1360,7 +1388,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &
           tt += u * u;
         }
         const R t = mmax(msqrt(tt), R(1e-15)), it = R(1) / t, mnt = mu * (A.efc_jaref[r0] * mu) * it;
-        for (int z = LANE; z < dim * dim; z += 32) {
+        for (int z = lane; z < dim * dim; z += 32) {
           const int p = z / dim, q = z - p * dim;
           R v;
           if (p == 0 && q == 0) v = mu2;
@@ -1379,18 +1407,18 @@ template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &
     }
     if (!full) {
       bool any = false;
-      for (int z = LANE; z < cnt; z += 32) C[z] = A.efc_state[r0 + z] == kQuadratic ? A.efc_D[r0 + z] : R(0);
+      for (int z = lane; z < cnt; z += 32) C[z] = A.efc_state[r0 + z] == kQuadratic ? A.efc_D[r0 + z] : R(0);
       for (int z = 0; z < cnt; ++z) any |= A.efc_state[r0 + z] == kQuadratic;
       if (!any) continue;
     }
-    SYNC();
+    __syncwarp();
     const int t0 = A.row_t[2 * r0], t1 = A.row_t[2 * r0 + 1];
     const int n0 = IF(tree_dofnum)[t0], k = n0 + (t1 >= 0 ? IF(tree_dofnum)[t1] : 0);
     const int a0 = IF(tree_dofadr)[t0], a1 = t1 >= 0 ? IF(tree_dofadr)[t1] : 0;
-    const int isl = A.tree_isl[t0], n = A.isl_n[isl];
+    const int n = A.isl_n[isl];
     R *Hb = A.H + A.isl_off[isl];
     const R *J = A.J + (size_t)r0 * kmax;
-    FOR(e, k * (k + 1) / 2) {
+    for (int e = lane; e < k * (k + 1) / 2; e += 32) {
       int a = (int)((msqrt(8.0f * e + 1.0f) - 1.0f) * 0.5f);
       while (a * (a + 1) / 2 > e) --a;
       while ((a + 1) * (a + 2) / 2 <= e) ++a;
@@ -1411,40 +1439,39 @@ template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &
       const int la = A.dof_loc[a < n0 ? a0 + a : a1 + a - n0], lb = A.dof_loc[b < n0 ? a0 + b : a1 + b - n0];
       Hb[la >= lb ? la * n + lb : lb * n + la] += v;
     }
-    SYNC();
+    __syncwarp();
   }
+  SYNC();
 }
 
-// Cholesky of every island block at once, H x = grad, search = -x
-// (mjwarp_direction.cu:80-160); warp 0
+// Cholesky of every island block (islands dealt to the world's warps),
+// H x = grad, search = -x (mjwarp_direction.cu:80-160)
 template <class R, int T> __device__ B200_STAGE_ATTR void direction(const Mdl<R> &M, Arena<R> &A) {
   const int nv = M.m.nv;
   R *x = A.xs;
-  if (LANE < 32) {
-    const int lane = LANE, maxn = A.iscal[12];
-    const BlockRows b = island_rows(A, nv, lane);
+  const int lane = LANE, maxn = A.iscal[12];
+  const BlockRows b = ISLAND_ROWS(T);
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      const int p = lane + 32 * s;
-      if (p < nv) x[p] = A.grad[A.isl_dof[p]];
+  for (int s = 0; s < 4; ++s)
+    if (b.n[s] > 0) {
+      const int p = b.start[s] + b.a[s];
+      x[p] = A.grad[A.isl_dof[p]];
     }
-    chol_blocks(A.H, b, maxn, nv, A.colbuf);
-    solve_blocks(A.H, b, x, maxn, lane);
-    R sq = 0, dec = 0;
+  __syncwarp();
+  chol_blocks(A.H, b, maxn, nv, A.colbuf);
+  solve_blocks(A.H, b, x, maxn, lane);
+  R sq = 0, dec = 0;
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      const int p = lane + 32 * s;
-      if (p < nv) {
-        const int d = A.isl_dof[p];
-        A.search[d] = -x[p];
-        sq += x[p] * x[p];
-        dec += A.grad[d] * x[p];
-      }
+  for (int s = 0; s < 4; ++s)
+    if (b.n[s] > 0) {
+      const int p = b.start[s] + b.a[s], d = A.isl_dof[p];
+      A.search[d] = -x[p];
+      sq += x[p] * x[p];
+      dec += A.grad[d] * x[p];
     }
-    sq = warp_sum(sq);
-    dec = warp_sum(dec);
-    if (lane == 0) { A.scal[2] = sq; A.scal[4] = dec; }
-  }
+  sq = world_sum<T>(sq, A.red);
+  dec = world_sum<T>(dec, A.red);
+  if (TID == 0) { A.scal[2] = sq; A.scal[4] = dec; }
   SYNC();
 }
 
@@ -1599,7 +1626,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void linesearch(const Mdl<R
     q[8] = d / (mu2 * (R(1) + mu2));
   }
   SYNC();
-  if (LANE < 32) {
+  if (WARP0) {
     const int lane = LANE;
     const R tol = R(m.tolerance), lstol = R(m.ls_tolerance), scale = R(m.meaninertia) * R(nv);
     const R gtol = mmax(tol * lstol * msqrt(A.scal[2]) * scale, R(1e-6));
@@ -1705,26 +1732,26 @@ template <class R, int T> __device__ B200_STAGE_ATTR void newton_init(const Mdl<
   SYNC();
   mass_mul<R, T>(M, A.M, A.qacc, A.Ma);
   FOR(r, nefc) A.efc_jaref[r] = jdot(M, A, r, A.qacc) - A.efc_aref[r];
-  if (LANE == 0) { A.iscal[4] = 0; A.iscal[5] = m.iterations == 0; }
+  if (TID == 0) { A.iscal[4] = 0; A.iscal[5] = m.iterations == 0; }
   SYNC();
   eval_gradient<R, T>(M, A);
   hessian<R, T>(M, A);
   direction<R, T>(M, A);
-  mark(A, 9);
+  mark<T>(A, 9);
 }
 
 template <class R, int T> __device__ B200_STAGE_ATTR void newton_iteration(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const R tol = R(m.tolerance), scale = R(m.meaninertia) * R(m.nv);
   linesearch<R, T>(M, A);
-  mark(A, 10);
+  mark<T>(A, 10);
   eval_gradient<R, T>(M, A);
-  mark(A, 11);
+  mark<T>(A, 11);
   hessian<R, T>(M, A);
-  mark(A, 12);
+  mark<T>(A, 12);
   direction<R, T>(M, A);
-  mark(A, 13);
-  if (LANE == 0) {
+  mark<T>(A, 13);
+  if (TID == 0) {
     const int it = ++A.iscal[4];
     const R imp = A.scal[1] / scale, grad = msqrt(A.scal[3]) / scale, model = (R(0.5) * A.scal[4]) / scale;
     const bool done = A.scal[0] == R(0) || (imp > R(0) && imp < tol) || grad < tol || model < tol;
@@ -1753,11 +1780,9 @@ template <class R, int T> __device__ B200_STAGE_ATTR void euler(const Mdl<R> &M,
       acc[d] = A.Ma[d];
     }
     SYNC();
-    if (LANE < 32) {
-      const BlockRows b = tree_rows(M, LANE);
-      chol_blocks(A.H, b, m.max_tree_dofs, nv, A.colbuf);
-      solve_blocks(A.H, b, acc, m.max_tree_dofs, LANE);
-    }
+    const BlockRows b = TREE_ROWS(T);
+    chol_blocks(A.H, b, m.max_tree_dofs, nv, A.colbuf);
+    solve_blocks(A.H, b, acc, m.max_tree_dofs, LANE);
   } else
     FOR(d, nv) acc[d] = A.qacc[d];
   SYNC();
@@ -1783,7 +1808,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void euler(const Mdl<R> &M,
       stq(q, r);
     } else q[0] += dt * v[0];
   }
-  if (LANE == 0) A.scal[5] += dt;
+  if (TID == 0) A.scal[5] += dt;
   SYNC();
 }
 
@@ -1806,7 +1831,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void load_world(const B200M
   src = row_of<R>(d.gripper, w, 2); FOR(i, 2) A.gripper[i] = src[i];
   if (d.action) { src = row_of<R>(d.action, w, 7); FOR(i, 7) A.action[i] = src[i]; }
   else FOR(i, 7) A.action[i] = 0;
-  if (LANE == 0) {
+  if (TID == 0) {
     A.scal[5] = row_of<R>(d.time, w, 1)[0];
     for (int k = 0; k < 24; ++k) A.iscal[k] = 0;
     A.iscal[3] = irow_of(d.overflow, w, 1)[0];
@@ -1849,7 +1874,7 @@ template <class R, int T> __device__ __noinline__ void store_state(const B200Mod
       dst[e] = v;  // reward and done are 0: synthetic scenes carry no task predicates
     }
   }
-  if (LANE == 0) {
+  if (TID == 0) {
     row_of<R>(d.time, w, 1)[0] = A.scal[5];
     irow_of(d.overflow, w, 1)[0] = A.iscal[3];
     irow_of(d.error, w, 1)[0] = A.iscal[6];
@@ -1882,7 +1907,7 @@ template <class R, int T> __device__ __noinline__ void store_outputs(const B200M
   int *idst;
   if ((idst = irow_of(d.con_geom, w, nc * 2)))
     FOR(e, ncon * 2) idst[e] = e & 1 ? A.con_g2[A.con_order[e >> 1]] : A.con_g1[A.con_order[e >> 1]];
-  if (LANE == 0) {
+  if (TID == 0) {
     if (d.ncon) irow_of(d.ncon, w, 1)[0] = ncon;
     if (d.nefc) irow_of(d.nefc, w, 1)[0] = nefc;
   }
@@ -1909,54 +1934,55 @@ template <class R, int T> __device__ __noinline__ void store_outputs(const B200M
   do {                  \
     if (act) {          \
       call;             \
-      mark(A, k);       \
+      mark<T>(A, k);       \
     }                   \
     STAGE_SYNC();       \
-    if (act) mark(A, 15); \
+    if (act) mark<T>(A, 15); \
   } while (0)
 
 // factor of the mass matrix, one block per kinematic tree (mjwarp_mass_factor.cu)
-template <class R> __device__ B200_STAGE_ATTR void mass_factor(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ B200_STAGE_ATTR void mass_factor(const Mdl<R> &M, Arena<R> &A) {
   FOR(k, M.m.nM) A.L[k] = A.M[k];
   SYNC();
-  chol_blocks(A.L, tree_rows(M, LANE), M.m.max_tree_dofs, M.m.nv, A.colbuf);
+  chol_blocks(A.L, TREE_ROWS(T), M.m.max_tree_dofs, M.m.nv, A.colbuf);
+  SYNC();
 }
 
-template <class R, bool CONVEX> __device__ void step1_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
-  STAGE((kinematics<R, 32>(M, A)), 1);
-  STAGE((com_crb_mass<R, 32>(M, A)), 2);
-  STAGE((mass_factor<R>(M, A)), 3);
-  STAGE((collision<R, 32, CONVEX>(M, A)), 4);
-  STAGE((constraints<R, 32>(M, A)), 5);
-  STAGE((velocity<R, 32>(M, A)), 6);
+template <class R, bool CONVEX, int T> __device__ void step1_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
+  STAGE((kinematics<R, T>(M, A)), 1);
+  STAGE((com_crb_mass<R, T>(M, A)), 2);
+  STAGE((mass_factor<R, T>(M, A)), 3);
+  STAGE((collision<R, T, CONVEX>(M, A)), 4);
+  STAGE((constraints<R, T>(M, A)), 5);
+  STAGE((velocity<R, T>(M, A)), 6);
 }
 
-template <class R> __device__ void newton_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
-  STAGE((newton_init<R, 32>(M, A)), 0);
+template <class R, int T> __device__ void newton_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
+  STAGE((newton_init<R, T>(M, A)), 0);
 #if B200_SYNC_LEVEL == 2
   while (__syncthreads_or(act && !A.iscal[5])) {
-    if (act) mark(A, 15);  // barrier wait and idle iterations of worlds already done
-    if (act && !A.iscal[5]) newton_iteration<R, 32>(M, A);
+    if (act) mark<T>(A, 15);  // barrier wait and idle iterations of worlds already done
+    if (act && !A.iscal[5]) newton_iteration<R, T>(M, A);
   }
 #else
   if (act)
-    while (!A.iscal[5]) newton_iteration<R, 32>(M, A);  // warp-uniform: iscal[5] is read after a warp sync
+    while (!A.iscal[5]) newton_iteration<R, T>(M, A);  // world-uniform: iscal[5] is read after a world sync
 #endif
-  if (act) mark(A, 15);
+  if (act) mark<T>(A, 15);
 }
 
-template <class R, bool CONVEX>
+template <class R, bool CONVEX, int T>
 __global__ void __launch_bounds__(256, 1) control_step(const B200Model m, const B200Data d, int substeps, int policy, int wpc,
                                                      int arena) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const int warp = threadIdx.x >> 5, w = blockIdx.x * wpc + warp;
-  const bool act = warp < wpc && w < d.nworld;
+  const int slot = threadIdx.x / T, w = blockIdx.x * wpc + slot;
+  const bool act = slot < wpc && w < d.nworld;
   Arena<R> A;
-  Arena<R>::layout(m, 32, &A, smem + (size_t)(warp < wpc ? warp : 0) * arena);
+  Arena<R>::layout(m, T, &A, smem + (size_t)(slot < wpc ? slot : 0) * arena);
   const Mdl<R> M(m);
   if (act) {
-    load_world<R, 32>(m, d, A, w);
-    if (LANE == 0 && d.stage_cycles) {
+    load_world<R, T>(m, d, A, w);
+    if (TID == 0 && d.stage_cycles) {
       A.iscal[10] = 1;
       for (int k = 0; k < 16; ++k) A.prof[k] = 0;
       A.prof[0] = clock64();
@@ -1968,11 +1994,11 @@ __global__ void __launch_bounds__(256, 1) control_step(const B200Model m, const 
 #if B200_SYNC_LEVEL == 1
     __syncthreads();
 #endif
-    step1_stages<R, CONVEX>(M, A, act);
-    STAGE((osc_control<R, 32>(M, A, policy && s == 0)), 7);
-    STAGE((actuation<R, 32>(M, A)), 8);
-    newton_stages(M, A, act);
-    if (act && LANE == 0) {
+    step1_stages<R, CONVEX, T>(M, A, act);
+    STAGE((osc_control<R, T>(M, A, policy && s == 0)), 7);
+    STAGE((actuation<R, T>(M, A)), 8);
+    newton_stages<R, T>(M, A, act);
+    if (act && TID == 0) {
       const int it = A.iscal[4], nefc = A.iscal[1], evals = A.iscal[7] - A.iscal[9];
       A.iscal[9] = A.iscal[7];
       if (d.niter) irow_of(d.niter, w, 1)[0] = it;
@@ -1982,159 +2008,63 @@ __global__ void __launch_bounds__(256, 1) control_step(const B200Model m, const 
       if (d.newton_rows) irow_of(d.newton_rows, w, 1)[0] += it * nefc;
       if (d.ls_rows) irow_of(d.ls_rows, w, 1)[0] += evals * nefc;
     }
-    if (act && s == substeps - 1) store_outputs<R, 32>(m, d, A, w);
-    STAGE((euler<R, 32>(M, A)), 14);
+    if (act && s == substeps - 1) store_outputs<R, T>(m, d, A, w);
+    STAGE((euler<R, T>(M, A)), 14);
   }
   if (!act) return;
-  if (LANE == 0) {
+  if (TID == 0) {
     if (d.ls_total) irow_of(d.ls_total, w, 1)[0] += A.iscal[7];
     if (d.integration_count) irow_of(d.integration_count, w, 1)[0] += substeps;
   }
-  store_state<R, 32>(m, d, A, w);
-  if (LANE == 0 && d.stage_cycles) {
+  store_state<R, T>(m, d, A, w);
+  if (TID == 0 && d.stage_cycles) {
     int *out = irow_of(d.stage_cycles, w, 16);
     for (int k = 1; k < 16; ++k) out[k] += (int)A.prof[k];
   }
 }
 
-template <class R, bool CONVEX>
+template <class R, bool CONVEX, int T>
 __global__ void __launch_bounds__(256, 1) forward_step(const B200Model m, const B200Data d, int bootstrap, const int *mask,
                                                      int wpc, int arena) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const int warp = threadIdx.x >> 5, w = blockIdx.x * wpc + warp;
-  const bool act = warp < wpc && w < d.nworld && (!mask || mask[w]);
+  const int slot = threadIdx.x / T, w = blockIdx.x * wpc + slot;
+  const bool act = slot < wpc && w < d.nworld && (!mask || mask[w]);
   Arena<R> A;
-  Arena<R>::layout(m, 32, &A, smem + (size_t)(warp < wpc ? warp : 0) * arena);
+  Arena<R>::layout(m, T, &A, smem + (size_t)(slot < wpc ? slot : 0) * arena);
   const Mdl<R> M(m);
-  if (act) load_world<R, 32>(m, d, A, w);
+  if (act) load_world<R, T>(m, d, A, w);
   __syncthreads();
-  step1_stages<R, CONVEX>(M, A, act);
+  step1_stages<R, CONVEX, T>(M, A, act);
   if (act && bootstrap) {
     FOR(i, 3) A.goal_pos[i] = A.sxpos[3 * m.ee_site + i];
     FOR(i, 9) A.goal_rot[i] = A.sxmat[9 * m.ee_site + i];
     FOR(i, 2) A.gripper[i] = 0;
-    if (LANE == 0) A.iscal[6] = 0;
+    if (TID == 0) A.iscal[6] = 0;
     SYNC();
   }
-  STAGE((actuation<R, 32>(M, A)), 8);
-  newton_stages(M, A, act);
+  STAGE((actuation<R, T>(M, A)), 8);
+  newton_stages<R, T>(M, A, act);
   if (!act) return;
-  store_outputs<R, 32>(m, d, A, w);
-  store_state<R, 32>(m, d, A, w);
+  store_outputs<R, T>(m, d, A, w);
+  store_state<R, T>(m, d, A, w);
 }
 
 }  // namespace b200
 
-// ============================================================ C ABI
-namespace {
-constexpr int kMaxWorldsPerCta = 8;
-
-bool model_ok(const B200Model *m) {
-  return m && m->real && m->ints && (m->real_bytes == 4 || m->real_bytes == 8) && m->nv >= 1 && m->nv <= 128 &&
-         m->nbody >= 2 && m->ncon_max >= 1 && m->nefc_max >= 1 && m->nvs >= m->nv && m->nsite > m->ee_site &&
-         m->nu >= 9 && m->ntree >= 1 && m->ntree <= 32 && m->kmax_dof >= m->max_tree_dofs;
+namespace b200 {
+template <class R, bool C, int T> int configure_kernels(size_t smem) {
+  int rc = (int)cudaFuncSetAttribute(control_step<R, C, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (rc) return rc;
+  return (int)cudaFuncSetAttribute(forward_step<R, C, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
-bool data_ok(const B200Data *d) {
-  return d && d->nworld >= 0 && d->qpos && d->qvel && d->qacc_warmstart && d->ctrl && d->time && d->goal_pos &&
-         d->goal_rot && d->gripper && d->overflow && d->error;
-}
-size_t arena_for(const B200Model *m) {
-  return m->real_bytes == 4 ? b200::Arena<float>::layout(*m, 32, nullptr, nullptr)
-                            : b200::Arena<double>::layout(*m, 32, nullptr, nullptr);
-}
-int max_optin_smem() {
-  static int v = -1;
-  if (v < 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) v = 0;
-  }
-  return v;
-}
-// Worlds per CTA.  Two CTAs per SM (each holding half of the SM's shared
-// memory) measured faster than one large CTA: worlds of a CTA wait for its
-// slowest world at stage barriers, and the second CTA fills those gaps.
-int worlds_per_cta(const B200Model *m, int limit) {
-  const size_t arena = arena_for(m);
-  if (arena == 0 || (int)arena > limit) return 0;
-  const int half = (228 * 1024) / 2 - 1024;  // per-SM capacity shared by two CTAs
-  int wpc = half / (int)arena >= 3 ? half / (int)arena : limit / (int)arena;
-  static int cap = -1;  // B200PHYS_WPC: smaller CTAs (more CTAs per SM), for tuning
-  if (cap < 0) {
-    const char *e = getenv("B200PHYS_WPC");
-    cap = e ? atoi(e) : kMaxWorldsPerCta;
-    if (cap < 1 || cap > kMaxWorldsPerCta) cap = kMaxWorldsPerCta;
-  }
-  return wpc > cap ? cap : wpc;
-}
-template <class K> int configure(K kernel, size_t smem) {
-  return (int)cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-}
-template <class R, bool C> int prepare_t(const B200Model *m, int wpc) {
-  const size_t smem = (size_t)wpc * arena_for(m);
-  int rc;
-  if ((rc = configure(b200::control_step<R, C>, smem))) return rc;
-  return configure(b200::forward_step<R, C>, smem);
-}
-int launch_shape(const B200Model *m, int *wpc) {
-  const int limit = max_optin_smem();
-  *wpc = worlds_per_cta(m, limit);
-  if (*wpc < 1) return (int)cudaErrorInvalidValue;
-  const bool convex = m->nmesh > 0;
-  if (m->real_bytes == 4) return convex ? prepare_t<float, true>(m, *wpc) : prepare_t<float, false>(m, *wpc);
-  return convex ? prepare_t<double, true>(m, *wpc) : prepare_t<double, false>(m, *wpc);
-}
-template <class R, bool C>
+template <class R, bool C, int T>
 void launch_step(const B200Model &m, const B200Data &d, int substeps, int policy, int wpc, int arena, int grid,
                  size_t smem, cudaStream_t s) {
-  b200::control_step<R, C><<<grid, 32 * wpc, smem, s>>>(m, d, substeps, policy, wpc, arena);
+  control_step<R, C, T><<<grid, T * wpc, smem, s>>>(m, d, substeps, policy, wpc, arena);
 }
-template <class R, bool C>
+template <class R, bool C, int T>
 void launch_forward(const B200Model &m, const B200Data &d, int bootstrap, const int *mask, int wpc, int arena,
                     int grid, size_t smem, cudaStream_t s) {
-  b200::forward_step<R, C><<<grid, 32 * wpc, smem, s>>>(m, d, bootstrap, mask, wpc, arena);
+  forward_step<R, C, T><<<grid, T * wpc, smem, s>>>(m, d, bootstrap, mask, wpc, arena);
 }
-}  // namespace
-
-extern "C" {
-const char *b200phys_source_id(void) { return B200PHYS_SOURCE_ID; }
-int b200phys_arch(void) { return 100; }
-size_t b200phys_model_bytes(void) { return sizeof(B200Model); }
-size_t b200phys_data_bytes(void) { return sizeof(B200Data); }
-size_t b200phys_world_smem_bytes(const B200Model *m) { return model_ok(m) ? arena_for(m) : 0; }
-
-int b200phys_prepare(const B200Model *m) {
-  if (!model_ok(m)) return (int)cudaErrorInvalidValue;
-  int wpc;
-  return launch_shape(m, &wpc);
-}
-
-int b200phys_step_launch(const B200Model *m, const B200Data *d, int substeps, int policy, void *stream) {
-  if (!model_ok(m) || !data_ok(d) || substeps < 0) return (int)cudaErrorInvalidValue;
-  if (d->nworld == 0 || substeps == 0) return 0;
-  int wpc, rc;
-  if ((rc = launch_shape(m, &wpc))) return rc;
-  const int arena = (int)arena_for(m), grid = (d->nworld + wpc - 1) / wpc;
-  const size_t smem = (size_t)wpc * arena;
-  cudaStream_t s = (cudaStream_t)stream;
-  // kernel variant by precision and by the presence of mesh geoms
-  auto f = m->real_bytes == 4 ? (m->nmesh > 0 ? launch_step<float, true> : launch_step<float, false>)
-                              : (m->nmesh > 0 ? launch_step<double, true> : launch_step<double, false>);
-  f(*m, *d, substeps, policy, wpc, arena, grid, smem, s);
-  return (int)cudaGetLastError();
-}
-
-int b200phys_forward_launch(const B200Model *m, const B200Data *d, int bootstrap, const int *mask, void *stream) {
-  if (!model_ok(m) || !data_ok(d)) return (int)cudaErrorInvalidValue;
-  if (d->nworld == 0) return 0;
-  int wpc, rc;
-  if ((rc = launch_shape(m, &wpc))) return rc;
-  const int arena = (int)arena_for(m), grid = (d->nworld + wpc - 1) / wpc;
-  const size_t smem = (size_t)wpc * arena;
-  cudaStream_t s = (cudaStream_t)stream;
-  auto f = m->real_bytes == 4 ? (m->nmesh > 0 ? launch_forward<float, true> : launch_forward<float, false>)
-                              : (m->nmesh > 0 ? launch_forward<double, true> : launch_forward<double, false>);
-  f(*m, *d, bootstrap, mask, wpc, arena, grid, smem, s);
-  return (int)cudaGetLastError();
-}
-}
+}  // namespace b200
