@@ -58,6 +58,7 @@ template <class R> struct Arena {
                // [11] islands [12] largest island [16..19] OSC factor flags [20..22] pinv flags
   R *red;    // reduction scratch (one real per warp of the world)
   long long *prof;  // [0] last stamp, [1..15] per-stage cycle sums (stage profiling only)
+  int ubytes;       // size of the stage-scoped union region (H, OSC and kinematics scratch)
 
   static constexpr int kOscDoubles = 400;
 
@@ -142,6 +143,7 @@ template <class R> struct Arena {
       a->cdof_dot = (R *)(ub + vc.take<R>(nv * 6));
       a->osc = (double *)ub;
       a->H = (R *)ub;
+      a->ubytes = (int)ubytes;
     }
     return total;
   }

@@ -998,20 +998,29 @@ __device__ __noinline__ void convex_pair(const Mdl<R> &M, Arena<R> &A, int pair,
   emit(M, A, p, pair, 0, g1, g2, distance, (x1 + x2) * R(0.5) + origin, fr);
 }
 
-template <class R, bool CONVEX> __device__ void collide_pair(const Mdl<R> &M, Arena<R> &A, int pair) {
+// narrowphase family of a candidate pair (-1: filtered out or unsupported):
+// 0 plane-primitive, 1 box family, 2 sphere/capsule, 3 plane-mesh, 4 convex
+template <class R, bool CONVEX> __device__ int pair_family(const Mdl<R> &M, const Arena<R> &A, int pair) {
   const int g1 = IF(pair_geom)[2 * pair], g2 = IF(pair_geom)[2 * pair + 1];
-  if (!candidate(M, A, g1, g2)) return;
+  if (!candidate(M, A, g1, g2)) return -1;
   const int t1 = IF(geom_type)[g1], t2 = IF(geom_type)[g2];
-  if (t2 == B200_GEOM_MESH) {
-    if constexpr (CONVEX) {
-      if (t1 == B200_GEOM_PLANE) plane_mesh(M, A, material(M, g1, g2), pair, g1, g2);
-      else convex_pair(M, A, pair, g1, g2);
-    }
-  } else if (t1 == B200_GEOM_PLANE && t2 >= 2 && t2 <= 6) plane_pair(M, A, pair, g1, g2);
-  else if (t2 == B200_GEOM_BOX && (t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE || t1 == B200_GEOM_BOX))
-    box_pair(M, A, pair, g1, g2);
-  else if ((t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE) && (t2 == B200_GEOM_SPHERE || t2 == B200_GEOM_CAPSULE))
-    prim_pair(M, A, pair, g1, g2);
+  if (t2 == B200_GEOM_MESH) return CONVEX ? (t1 == B200_GEOM_PLANE ? 3 : 4) : -1;
+  if (t1 == B200_GEOM_PLANE && t2 >= 2 && t2 <= 6) return 0;
+  if (t2 == B200_GEOM_BOX && (t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE || t1 == B200_GEOM_BOX)) return 1;
+  if ((t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE) && (t2 == B200_GEOM_SPHERE || t2 == B200_GEOM_CAPSULE))
+    return 2;
+  return -1;
+}
+
+template <class R, bool CONVEX> __device__ void narrow_pair(const Mdl<R> &M, Arena<R> &A, int pair, int family) {
+  const int g1 = IF(pair_geom)[2 * pair], g2 = IF(pair_geom)[2 * pair + 1];
+  if (family == 0) plane_pair(M, A, pair, g1, g2);
+  else if (family == 1) box_pair(M, A, pair, g1, g2);
+  else if (family == 2) prim_pair(M, A, pair, g1, g2);
+  else if constexpr (CONVEX) {
+    if (family == 3) plane_mesh(M, A, material(M, g1, g2), pair, g1, g2);
+    else if (family == 4) convex_pair(M, A, pair, g1, g2);
+  }
 }
 
 }  // namespace b200

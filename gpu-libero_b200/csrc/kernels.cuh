@@ -428,10 +428,39 @@ template <class R, int T> __device__ B200_STAGE_ATTR void mass_mul(const Mdl<R> 
 // GJK/EPA pairs); models without meshes run the smaller variant.
 template <class R, int T, bool CONVEX> __device__ B200_STAGE_ATTR void collision(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
+  // Broadphase first, then the narrowphase over the surviving pairs grouped
+  // by family, so that the threads of a warp run the same collider.  The
+  // pair lists live in the stage-scoped union region (free between the mass
+  // factor and the RNE).  Contact order is fixed by the key sort below, not
+  // by the order in which pairs are processed.
+  constexpr int kFam = 5;
+  int *fam = (int *)A.H, *cnt = fam + m.npair, *fill = cnt + kFam, *list = fill + kFam;
+  const bool grouped = (2 * m.npair + 2 * kFam) * (int)sizeof(int) <= A.ubytes;
   if (TID == 0) A.iscal[8] = 0;
+  if (grouped && TID < 2 * kFam) cnt[TID] = 0;
   SYNC();
   if (!(m.disable_flags & (B200_DSBL_CONSTRAINT | B200_DSBL_CONTACT))) {
-    FOR(p, m.npair) collide_pair<R, CONVEX>(M, A, p);
+    if (grouped) {
+      FOR(p, m.npair) {
+        const int f = pair_family<R, CONVEX>(M, A, p);
+        fam[p] = f;
+        if (f >= 0) atomicAdd(&cnt[f], 1);
+      }
+      SYNC();
+      int off[kFam], total = 0;
+      for (int f = 0; f < kFam; ++f) { off[f] = total; total += cnt[f]; }
+      FOR(p, m.npair) {
+        const int f = fam[p];
+        if (f >= 0) list[off[f] + atomicAdd(&fill[f], 1)] = p;
+      }
+      SYNC();
+      FOR(i, total) narrow_pair<R, CONVEX>(M, A, list[i], fam[list[i]]);
+    } else {
+      FOR(p, m.npair) {
+        const int f = pair_family<R, CONVEX>(M, A, p);
+        if (f >= 0) narrow_pair<R, CONVEX>(M, A, p, f);
+      }
+    }
   }
   SYNC();
   const int n = mmin(A.iscal[8], m.ncon_max);
@@ -1475,7 +1504,8 @@ template <class R, int T> __device__ B200_STAGE_ATTR void direction(const Mdl<R>
   SYNC();
 }
 
-// ---- exact line search (mjwarp_linesearch.cu:80-365), warp 0
+// ---- exact line search (mjwarp_linesearch.cu:80-365); row evaluations are
+// spread over the world's threads
 template <class R> struct Pt { R cost, slope, curv; };
 template <class R> __device__ __forceinline__ Pt<R> padd(Pt<R> a, Pt<R> b) {
   return {a.cost + b.cost, a.slope + b.slope, a.curv + b.curv};
@@ -1591,8 +1621,17 @@ template <class R> __device__ B200_STAGE_ATTR Pt<R> eval_shift(const LsRow<R> &r
   const R vd = r.v * r.d, h = r.v * vd, ah = alpha * h;
   return {alpha * (vd * r.x + R(0.5) * ah) + (quad0 - cost0), vd * r.x + ah, h};
 }
-template <class R> __device__ __forceinline__ Pt<R> warp_pt(Pt<R> p) {
-  return {warp_sum(p.cost), warp_sum(p.slope), warp_sum(p.curv)};
+// (cost, slope, curvature) summed over the world's threads; every thread
+// gets the same sums (same order), so the search runs identically on all
+template <int T, class R> __device__ __forceinline__ Pt<R> world_pt(Pt<R> p, R *red) {
+  p = {warp_sum(p.cost), warp_sum(p.slope), warp_sum(p.curv)};
+  if (T == 32) return p;
+  SYNC();
+  if (LANE == 0) { red[3 * (TID >> 5)] = p.cost; red[3 * (TID >> 5) + 1] = p.slope; red[3 * (TID >> 5) + 2] = p.curv; }
+  SYNC();
+  Pt<R> s = {0, 0, 0};
+  for (int k = 0; k < T / 32; ++k) s = padd(s, Pt<R>{red[3 * k], red[3 * k + 1], red[3 * k + 2]});
+  return s;
 }
 
 template <class R, int T> __device__ B200_STAGE_ATTR void linesearch(const Mdl<R> &M, Arena<R> &A) {
@@ -1626,20 +1665,19 @@ template <class R, int T> __device__ B200_STAGE_ATTR void linesearch(const Mdl<R
     q[8] = d / (mu2 * (R(1) + mu2));
   }
   SYNC();
-  if (WARP0) {
-    const int lane = LANE;
+  {  // every thread of the world runs the search on identical reduced values
     const R tol = R(m.tolerance), lstol = R(m.ls_tolerance), scale = R(m.meaninertia) * R(nv);
     const R gtol = mmax(tol * lstol * msqrt(A.scal[2]) * scale, R(1e-6));
     R g1 = 0, g2 = 0;
-    for (int i = lane; i < nv; i += 32) {
+    FOR(i, nv) {
       g1 += A.search[i] * (A.Ma[i] - A.qfrc_smooth[i]);
       g2 += R(0.5) * A.search[i] * A.Mv[i];
     }
-    g1 = warp_sum(g1);
-    g2 = warp_sum(g2);
+    g1 = world_sum<T>(g1, A.red);
+    g2 = world_sum<T>(g2, A.red);
     Pt<R> loc = {0, 0, 0};
-    for (int r = lane; r < nefc; r += 32) loc = padd(loc, eval_zero(load_row(M, A, r, nf)));
-    const Pt<R> rows = warp_pt(loc);
+    FOR(r, nefc) loc = padd(loc, eval_zero(load_row(M, A, r, nf)));
+    const Pt<R> rows = world_pt<T>(loc, A.red);
     int evals = 1;
     const Pt<R> p0 = {rows.cost, g1 + rows.slope, R(2) * g2 + rows.curv};
     const Pt<R> delta = {0, p0.slope, p0.curv};
@@ -1652,8 +1690,8 @@ template <class R, int T> __device__ B200_STAGE_ATTR void linesearch(const Mdl<R
     Pt<R> init = {0, 0, 0};
     if (!converged) {
       loc = {0, 0, 0};
-      for (int r = lane; r < nefc; r += 32) loc = padd(loc, eval_shift(load_row(M, A, r, nf), a0));
-      init = padd(quadratic(g1, g2, a0), warp_pt(loc));
+      FOR(r, nefc) loc = padd(loc, eval_shift(load_row(M, A, r, nf), a0));
+      init = padd(quadratic(g1, g2, a0), world_pt<T>(loc, A.red));
       ++evals;
       if (mabs(init.slope) < gacc && init.cost < R(0)) { converged = true; alpha = a0; improvement = -init.cost; }
     }
@@ -1664,15 +1702,15 @@ template <class R, int T> __device__ B200_STAGE_ATTR void linesearch(const Mdl<R
       for (int it = 0; it < m.ls_iterations; ++it) {
         const R ln = la - safe_div(lo.slope, lo.curv), hn = ha - safe_div(hi.slope, hi.curv), ma = R(0.5) * (la + ha);
         Pt<R> sl = {0, 0, 0}, sh = {0, 0, 0}, sm = {0, 0, 0};
-        for (int r = lane; r < nefc; r += 32) {
+        FOR(r, nefc) {
           const LsRow<R> row = load_row(M, A, r, nf);
           sl = padd(sl, eval_shift(row, ln));
           sh = padd(sh, eval_shift(row, hn));
           sm = padd(sm, eval_shift(row, ma));
         }
-        const Pt<R> nl = padd(quadratic(g1, g2, ln), warp_pt(sl));
-        const Pt<R> nh = padd(quadratic(g1, g2, hn), warp_pt(sh));
-        const Pt<R> mid = padd(quadratic(g1, g2, ma), warp_pt(sm));
+        const Pt<R> nl = padd(quadratic(g1, g2, ln), world_pt<T>(sl, A.red));
+        const Pt<R> nh = padd(quadratic(g1, g2, hn), world_pt<T>(sh, A.red));
+        const Pt<R> mid = padd(quadratic(g1, g2, ma), world_pt<T>(sm, A.red));
         evals += 3;
         const bool cl = mabs(nl.slope) < gacc && nl.cost < R(0), ch = mabs(nh.slope) < gacc && nh.cost < R(0);
         const bool cm = mabs(mid.slope) < gacc && mid.cost < R(0);
@@ -1705,7 +1743,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void linesearch(const Mdl<R
         if (done) { converged = true; break; }
       }
     }
-    if (lane == 0) {
+    if (TID == 0) {
       A.scal[0] = alpha;
       A.scal[1] = improvement;
       A.iscal[7] += evals;
