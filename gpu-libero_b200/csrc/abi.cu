@@ -53,8 +53,8 @@ int worlds_per_cta(const B200Model *m, int limit) {
   return wpc > cap ? cap : wpc;
 }
 // Launch shape: worlds per CTA and threads per world.  A world is one warp,
-// or four warps when at most two worlds fit on an SM (large models), so that
-// an SM still runs eight warps.
+// or four warps when at most three worlds fit on an SM (large models), so
+// that an SM still runs eight to twelve warps.
 struct Shape {
   int wpc, T;
 };
@@ -68,14 +68,14 @@ int launch_shape(const B200Model *m, Shape *sh) {
   if (sh->wpc < 1) return (int)cudaErrorInvalidValue;
   const int arena = (int)arena_for(m);
   const int per_sm = ((228 * 1024) / (sh->wpc * arena + 1024)) * sh->wpc;
-  sh->T = per_sm <= 2 ? 128 : 32;
+  sh->T = per_sm <= 3 ? 128 : 32;
   static int force = -1;  // B200PHYS_THREADS: 32 or 128 threads per world, for tuning
   if (force < 0) {
     const char *e = getenv("B200PHYS_THREADS");
     force = e ? atoi(e) : 0;
   }
   if (force == 32 || force == 128) sh->T = force;
-  if (sh->T * sh->wpc > 256) sh->wpc = 256 / sh->T;
+  if (sh->T * sh->wpc > 384) sh->wpc = 384 / sh->T;  // the kernels' launch bound
   const bool convex = m->nmesh > 0;
   if (m->real_bytes == 4) return convex ? prepare_rc<float, true>(m, *sh) : prepare_rc<float, false>(m, *sh);
   return convex ? prepare_rc<double, true>(m, *sh) : prepare_rc<double, false>(m, *sh);

@@ -10,11 +10,9 @@
 
 namespace b200 {
 
-// Per-contact record, in reals.
-enum ContactField {
-  kCDist = 0, kCPos = 1, kCFrame = 4, kCMargin = 13, kCFriction = 14,
-  kCSolref = 19, kCSolrefFriction = 21, kCSolimp = 23, kCWidth = 28
-};
+// Per-contact record, in reals (solref / solimp are recomputed from the
+// geom pair where rows are built).
+enum ContactField { kCDist = 0, kCPos = 1, kCFrame = 4, kCMargin = 13, kCFriction = 14, kCWidth = 19 };
 
 struct Carve {
   size_t at = 0;
@@ -77,7 +75,7 @@ template <class R> struct Arena {
     o[k++] = c.take<R>(nb * 3); o[k++] = c.take<R>(nb * 4); o[k++] = c.take<R>(nb * 9);
     o[k++] = c.take<R>(ng * 3); o[k++] = c.take<R>(ng * 9); o[k++] = c.take<R>(ns * 3); o[k++] = c.take<R>(ns * 9);
     o[k++] = c.take<R>(nb * 3); o[k++] = c.take<R>(nb * 10); o[k++] = c.take<R>(nv * 6);
-    o[k++] = c.take<R>(m.nM); o[k++] = c.take<R>(m.nM);
+    o[k++] = c.take<R>(m.nM); o[k++] = c.take<R>(m.nL);  // M (dense tree blocks), L (packed)
     o[k++] = c.take<R>(nu); o[k++] = c.take<R>(nu);
     for (int i = 0; i < 11; ++i) o[k++] = c.take<R>(nv);
     o[k++] = c.take<R>(6);
@@ -99,7 +97,7 @@ template <class R> struct Arena {
     const size_t kin = (size_t)(nb * 3 + nb * 9 + nj * 3 + nj * 3 + nb * 10) * sizeof(R) + 5 * 16;
     const size_t rne = (size_t)(nb * 6 * 3 + nv * 6) * sizeof(R) + 4 * 16;
     const size_t osc = (size_t)kOscDoubles * sizeof(double);
-    const size_t hes = (size_t)nv * m.nvs * sizeof(R);
+    const size_t hes = (size_t)nv * (nv + 1) / 2 * sizeof(R);  // packed island blocks, one island at worst
     size_t ubytes = kin > rne ? kin : rne;
     ubytes = ubytes > osc ? ubytes : osc;
     ubytes = ubytes > hes ? ubytes : hes;

@@ -93,8 +93,7 @@ __device__ void emit(const Mdl<R> &M, Arena<R> &A, const Material<R> &p, int pai
   st3(c + kCPos, pos);
   st3(c + kCFrame, frame[0]); st3(c + kCFrame + 3, frame[1]); st3(c + kCFrame + 6, frame[2]);
   c[kCMargin] = p.margin;
-  for (int k = 0; k < 5; ++k) { c[kCFriction + k] = p.friction[k]; c[kCSolimp + k] = p.solimp[k]; }
-  for (int k = 0; k < 2; ++k) { c[kCSolref + k] = p.solref[k]; c[kCSolrefFriction + k] = p.solreffriction[k]; }
+  for (int k = 0; k < 5; ++k) c[kCFriction + k] = p.friction[k];
   A.con_dim[slot] = p.dim;
   A.con_g1[slot] = g1;
   A.con_g2[slot] = g2;

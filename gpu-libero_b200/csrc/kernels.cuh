@@ -285,6 +285,9 @@ template <class R, int T> __device__ B200_STAGE_ATTR void com_crb_mass(const Mdl
 // first position in the solve vector.  A warp's blocks advance together, so
 // a factorization takes as many steps as its largest block.
 struct BlockRows { int n[4], a[4], base[4], start[4], rows; };
+// Factor blocks are stored packed lower-triangular: entry (i, j), j <= i, of
+// a block at base sits at base + i (i + 1) / 2 + j.
+__device__ __forceinline__ int tri(int i, int j) { return i * (i + 1) / 2 + j; }
 
 __device__ __forceinline__ BlockRows owned_rows(int nblocks, const int *bn, const int *bstart, const int *bbase,
                                                 int lane, int wi, int nw) {
@@ -304,7 +307,7 @@ __device__ __forceinline__ BlockRows owned_rows(int nblocks, const int *bn, cons
   b.rows = acc;
   return b;
 }
-#define TREE_ROWS(T) owned_rows(M.m.ntree, IF(tree_dofnum), IF(tree_dofadr), IF(tree_madr), LANE, TID >> 5, (T) / 32)
+#define TREE_ROWS(T) owned_rows(M.m.ntree, IF(tree_dofnum), IF(tree_dofadr), IF(tree_padr), LANE, TID >> 5, (T) / 32)
 #define ISLAND_ROWS(T) owned_rows(A.iscal[11], A.isl_n, A.isl_dofstart, A.isl_off, LANE, TID >> 5, (T) / 32)
 
 // in-place lower Cholesky L L^T of every block (right-looking, warp 0)
@@ -312,19 +315,18 @@ template <class R> __device__ void chol_blocks_smem(R *H, const BlockRows &b, in
   for (int k = 0; k < maxn; ++k) {
 #pragma unroll
     for (int s = 0; s < 4; ++s)
-      if (b.n[s] > k && b.a[s] == k) H[b.base[s] + k * b.n[s] + k] = msqrt(H[b.base[s] + k * b.n[s] + k]);
+      if (b.n[s] > k && b.a[s] == k) H[b.base[s] + tri(k, k)] = msqrt(H[b.base[s] + tri(k, k)]);
     __syncwarp();
 #pragma unroll
     for (int s = 0; s < 4; ++s)
-      if (b.n[s] > k && b.a[s] > k) H[b.base[s] + b.a[s] * b.n[s] + k] /= H[b.base[s] + k * b.n[s] + k];
+      if (b.n[s] > k && b.a[s] > k) H[b.base[s] + tri(b.a[s], k)] /= H[b.base[s] + tri(k, k)];
     __syncwarp();
 #pragma unroll
     for (int s = 0; s < 4; ++s)
       if (b.n[s] > k && b.a[s] > k) {
-        const int n = b.n[s];
-        R *row = H + b.base[s] + b.a[s] * n;
+        R *row = H + b.base[s] + tri(b.a[s], 0);
         const R l = row[k];
-        for (int j = k + 1; j <= b.a[s]; ++j) row[j] -= l * H[b.base[s] + j * n + k];
+        for (int j = k + 1; j <= b.a[s]; ++j) row[j] -= l * H[b.base[s] + tri(j, k)];
       }
     __syncwarp();
   }
@@ -340,7 +342,7 @@ __device__ void chol_blocks_reg(R *H, const BlockRows &b, int maxn, R *colbuf, i
   const int n = b.n[0], a = b.a[0];
   R row[MAXN];
 #pragma unroll
-  for (int j = 0; j < MAXN; ++j) row[j] = (n > 0 && j <= a && j < n) ? H[b.base[0] + a * n + j] : R(0);
+  for (int j = 0; j < MAXN; ++j) row[j] = (n > 0 && j <= a && j < n) ? H[b.base[0] + tri(a, j)] : R(0);
   for (int k = 0; k < maxn; ++k) {
     R *col = colbuf + (k & 1) * stride;
     R rk = 0;
@@ -374,7 +376,7 @@ __device__ void chol_blocks_reg(R *H, const BlockRows &b, int maxn, R *colbuf, i
   if (n > 0) {
 #pragma unroll
     for (int j = 0; j < MAXN; ++j)
-      if (j <= a && j < n) H[b.base[0] + a * n + j] = row[j];
+      if (j <= a && j < n) H[b.base[0] + tri(a, j)] = row[j];
   }
   __syncwarp();
 }
@@ -393,22 +395,35 @@ template <class R> __device__ B200_STAGE_ATTR void solve_blocks(const R *H, cons
   for (int k = 0; k < maxn; ++k) {
 #pragma unroll
     for (int s = 0; s < 4; ++s)
-      if (b.n[s] > k && b.a[s] == k) x[b.start[s] + b.a[s]] /= H[b.base[s] + k * b.n[s] + k];
+      if (b.n[s] > k && b.a[s] == k) x[b.start[s] + b.a[s]] /= H[b.base[s] + tri(k, k)];
     __syncwarp();
 #pragma unroll
     for (int s = 0; s < 4; ++s)
-      if (b.n[s] > k && b.a[s] > k) x[b.start[s] + b.a[s]] -= H[b.base[s] + b.a[s] * b.n[s] + k] * x[b.start[s] + k];
+      if (b.n[s] > k && b.a[s] > k) x[b.start[s] + b.a[s]] -= H[b.base[s] + tri(b.a[s], k)] * x[b.start[s] + k];
     __syncwarp();
   }
   for (int k = maxn - 1; k >= 0; --k) {
 #pragma unroll
     for (int s = 0; s < 4; ++s)
-      if (b.n[s] > k && b.a[s] == k) x[b.start[s] + b.a[s]] /= H[b.base[s] + k * b.n[s] + k];
+      if (b.n[s] > k && b.a[s] == k) x[b.start[s] + b.a[s]] /= H[b.base[s] + tri(k, k)];
     __syncwarp();
 #pragma unroll
     for (int s = 0; s < 4; ++s)
-      if (b.n[s] > k && b.a[s] < k) x[b.start[s] + b.a[s]] -= H[b.base[s] + k * b.n[s] + b.a[s]] * x[b.start[s] + k];
+      if (b.n[s] > k && b.a[s] < k) x[b.start[s] + b.a[s]] -= H[b.base[s] + tri(k, b.a[s])] * x[b.start[s] + k];
     __syncwarp();
+  }
+}
+
+// lower triangles of the dense tree blocks of M into packed blocks at tree_padr
+template <class R, int T> __device__ void pack_tree_blocks(const Mdl<R> &M, const R *Mb, R *P) {
+  FOR(e, M.m.nL) {
+    int t = 0;
+    while (t + 1 < M.m.ntree && IF(tree_padr)[t + 1] <= e) ++t;
+    const int loc = e - IF(tree_padr)[t], n = IF(tree_dofnum)[t];
+    int a = (int)((msqrt(8.0f * loc + 1.0f) - 1.0f) * 0.5f);
+    while (tri(a, 0) > loc) --a;
+    while (tri(a + 1, 0) <= loc) ++a;
+    P[e] = Mb[IF(tree_madr)[t] + a * n + (loc - tri(a, 0))];
   }
 }
 
@@ -528,7 +543,7 @@ template <class R> __device__ __forceinline__ void set_row_trees(const Mdl<R> &M
 
 // Islands: kinematic trees coupled by a two-tree constraint row share one
 // Newton Hessian block.  Warp 0.  Without coupling rows every tree is its own
-// island and the tree layout is reused (blocks at tree_madr).  Otherwise lane
+// island and the tree layout is reused (packed blocks at tree_padr).  Otherwise lane
 // 0 unions trees over the coupled contacts; island ids follow the smallest
 // tree index, so the blocks are deterministic.
 template <class R> __device__ B200_STAGE_ATTR void islands(const Mdl<R> &M, Arena<R> &A, bool coupled) {
@@ -537,7 +552,7 @@ template <class R> __device__ B200_STAGE_ATTR void islands(const Mdl<R> &M, Aren
     for (int t = lane; t < nt; t += 32) {
       A.tree_isl[t] = t;
       A.isl_n[t] = IF(tree_dofnum)[t];
-      A.isl_off[t] = IF(tree_madr)[t];
+      A.isl_off[t] = IF(tree_padr)[t];
       A.isl_dofstart[t] = IF(tree_dofadr)[t];
     }
     if (lane == 0) { A.isl_dofstart[nt] = nv; A.iscal[11] = nt; A.iscal[12] = M.m.max_tree_dofs; }
@@ -574,7 +589,7 @@ template <class R> __device__ B200_STAGE_ATTR void islands(const Mdl<R> &M, Aren
       A.isl_dofstart[i] = at;
       A.isl_off[i] = off;
       at += A.isl_n[i];
-      off += A.isl_n[i] * A.isl_n[i];
+      off += A.isl_n[i] * (A.isl_n[i] + 1) / 2;
       maxn = A.isl_n[i] > maxn ? A.isl_n[i] : maxn;
     }
     A.isl_dofstart[nisl] = at;
@@ -771,12 +786,15 @@ template <class R, int T> __device__ B200_STAGE_ATTR void constraints(const Mdl<
         weight = weight + fr[0] * fr[0] * weight;
         weight = weight * R(2) * fr[0] * fr[0] * ratio * ratio;
       }
-      row_params(m, A, r, pos_aref, position, weight, cr + kCSolref, cr + kCSolimp, jqv, R(0), type, c);
+      // solref / solimp are recomputed from the geom pair (mjwarp_contact.cuh:60-98 mixing)
+      // rather than stored per contact
+      const Material<R> mat = material(M, A.con_g1[c], A.con_g2[c]);
+      row_params(m, A, r, pos_aref, position, weight, mat.solref, mat.solimp, jqv, R(0), type, c);
       if (elliptic && comp > 0) {
         A.efc_D[r] /= scale;
-        const R *ref = cr + kCSolref;
-        if (cr[kCSolrefFriction] != R(0) || cr[kCSolrefFriction + 1] != R(0)) ref = cr + kCSolrefFriction;
-        A.efc_aref[r] = -impedance(m, ref, cr + kCSolimp, position).b * jqv;
+        const R *ref = mat.solref;
+        if (mat.solreffriction[0] != R(0) || mat.solreffriction[1] != R(0)) ref = mat.solreffriction;
+        A.efc_aref[r] = -impedance(m, ref, mat.solimp, position).b * jqv;
       }
     }
   }
@@ -1365,15 +1383,18 @@ template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &
   const int nisl = A.iscal[11], nsingle = A.iscal[13], ncon = A.iscal[0], kmax = m.kmax_dof;
   const R impratio = R(m.impratio_invsqrt);
   int total = 0;
-  for (int i = 0; i < nisl; ++i) total += A.isl_n[i] * A.isl_n[i];
-  // mass blocks (the island blocks are contiguous: n^2 each, in island order)
+  for (int i = 0; i < nisl; ++i) total += A.isl_n[i] * (A.isl_n[i] + 1) / 2;
+  // mass blocks (the packed island blocks are contiguous, in island order)
   FOR(e, total) {
     int isl = 0, base = 0;
-    while (base + A.isl_n[isl] * A.isl_n[isl] <= e) { base += A.isl_n[isl] * A.isl_n[isl]; ++isl; }
-    const int n = A.isl_n[isl], a = (e - base) / n, b = (e - base) - a * n;
-    R v = 0;
-    if (a >= b) v = mass_at(M, A.M, A.isl_dof[A.isl_dofstart[isl] + a], A.isl_dof[A.isl_dofstart[isl] + b]);
-    A.H[A.isl_off[isl] + a * n + b] = v;
+    while (base + A.isl_n[isl] * (A.isl_n[isl] + 1) / 2 <= e) { base += A.isl_n[isl] * (A.isl_n[isl] + 1) / 2; ++isl; }
+    const int loc = e - base;
+    int a = (int)((msqrt(8.0f * loc + 1.0f) - 1.0f) * 0.5f);
+    while (tri(a, 0) > loc) --a;
+    while (tri(a + 1, 0) <= loc) ++a;
+    const int b = loc - tri(a, 0);
+    A.H[A.isl_off[isl] + loc] =
+        mass_at(M, A.M, A.isl_dof[A.isl_dofstart[isl] + a], A.isl_dof[A.isl_dofstart[isl] + b]);
   }
   SYNC();
   // single-dof rows: D on the diagonal of their dof
@@ -1385,8 +1406,8 @@ template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &
       if (dof == d) add += A.efc_D[r];
     }
     if (add != R(0)) {
-      const int isl = A.dof_isl[d], n = A.isl_n[isl], l = A.dof_loc[d];
-      A.H[A.isl_off[isl] + l * n + l] += add;
+      const int isl = A.dof_isl[d], l = A.dof_loc[d];
+      A.H[A.isl_off[isl] + tri(l, l)] += add;
     }
   }
   SYNC();
@@ -1444,7 +1465,6 @@ template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &
     const int t0 = A.row_t[2 * r0], t1 = A.row_t[2 * r0 + 1];
     const int n0 = IF(tree_dofnum)[t0], k = n0 + (t1 >= 0 ? IF(tree_dofnum)[t1] : 0);
     const int a0 = IF(tree_dofadr)[t0], a1 = t1 >= 0 ? IF(tree_dofadr)[t1] : 0;
-    const int n = A.isl_n[isl];
     R *Hb = A.H + A.isl_off[isl];
     const R *J = A.J + (size_t)r0 * kmax;
     for (int e = lane; e < k * (k + 1) / 2; e += 32) {
@@ -1466,7 +1486,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &
         for (int p = 0; p < cnt; ++p) v += J[p * kmax + a] * C[p] * J[p * kmax + b];
       }
       const int la = A.dof_loc[a < n0 ? a0 + a : a1 + a - n0], lb = A.dof_loc[b < n0 ? a0 + b : a1 + b - n0];
-      Hb[la >= lb ? la * n + lb : lb * n + la] += v;
+      Hb[la >= lb ? tri(la, lb) : tri(lb, la)] += v;
     }
     __syncwarp();
   }
@@ -1810,11 +1830,11 @@ template <class R, int T> __device__ B200_STAGE_ATTR void euler(const Mdl<R> &M,
   // the mass factor is dead after the smooth solve: reuse it for M + dt*D
   R *acc = A.Mv;
   if (damped) {
-    FOR(k, m.nM) A.H[k] = A.M[k];
+    pack_tree_blocks<R, T>(M, A.M, A.H);
     SYNC();
     FOR(d, nv) {
-      const int t = IF(dof_treeid)[d], a = IF(tree_dofadr)[t], n = IF(tree_dofnum)[t];
-      A.H[IF(tree_madr)[t] + (d - a) * n + (d - a)] += dt * RF(dof_damping)[d];
+      const int t = IF(dof_treeid)[d], l = d - IF(tree_dofadr)[t];
+      A.H[IF(tree_padr)[t] + tri(l, l)] += dt * RF(dof_damping)[d];
       acc[d] = A.Ma[d];
     }
     SYNC();
@@ -1980,7 +2000,7 @@ template <class R, int T> __device__ __noinline__ void store_outputs(const B200M
 
 // factor of the mass matrix, one block per kinematic tree (mjwarp_mass_factor.cu)
 template <class R, int T> __device__ B200_STAGE_ATTR void mass_factor(const Mdl<R> &M, Arena<R> &A) {
-  FOR(k, M.m.nM) A.L[k] = A.M[k];
+  pack_tree_blocks<R, T>(M, A.M, A.L);
   SYNC();
   chol_blocks(A.L, TREE_ROWS(T), M.m.max_tree_dofs, M.m.nv, A.colbuf);
   SYNC();
@@ -2010,7 +2030,7 @@ template <class R, int T> __device__ void newton_stages(const Mdl<R> &M, Arena<R
 }
 
 template <class R, bool CONVEX, int T>
-__global__ void __launch_bounds__(256, 1) control_step(const B200Model m, const B200Data d, int substeps, int policy, int wpc,
+__global__ void __launch_bounds__(384, 1) control_step(const B200Model m, const B200Data d, int substeps, int policy, int wpc,
                                                      int arena) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int slot = threadIdx.x / T, w = blockIdx.x * wpc + slot;
@@ -2062,7 +2082,7 @@ __global__ void __launch_bounds__(256, 1) control_step(const B200Model m, const 
 }
 
 template <class R, bool CONVEX, int T>
-__global__ void __launch_bounds__(256, 1) forward_step(const B200Model m, const B200Data d, int bootstrap, const int *mask,
+__global__ void __launch_bounds__(384, 1) forward_step(const B200Model m, const B200Data d, int bootstrap, const int *mask,
                                                      int wpc, int arena) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int slot = threadIdx.x / T, w = blockIdx.x * wpc + slot;

@@ -261,6 +261,9 @@ class Scene:
             assert np.all(np.flatnonzero(dof_tree == t) == tree_dofadr[t] + np.arange(tree_dofnum[t]))
         tree_madr = np.r_[0, np.cumsum(tree_dofnum ** 2)[:-1]].astype(np.int32)
         nM = int(np.sum(tree_dofnum ** 2))
+        tri_sizes = tree_dofnum * (tree_dofnum + 1) // 2   # packed lower-triangular factor blocks
+        tree_padr = np.r_[0, np.cumsum(tri_sizes)[:-1]].astype(np.int32)
+        nL = int(np.sum(tri_sizes))
         # subtree intervals (depth-first order => contiguous)
         subtree_end = np.arange(nb, dtype=np.int32) + 1
         for bi in range(nb - 1, 0, -1):
@@ -407,7 +410,7 @@ class Scene:
         opt = self.options
         cap = self.capacities
         self.sizes = dict(nq=nq, nv=nv, nu=nu, nbody=nb, njnt=nj, ngeom=ng, nsite=ns,
-                          npair=len(pairs), ntree=ntree, nM=nM, nlevel=nlevel,
+                          npair=len(pairs), ntree=ntree, nM=nM, nL=nL, nlevel=nlevel,
                           nlimited=int(limited.sum()), nfric=int(np.sum(fric > 0)),
                           nmesh=len(mesh_vertadr), nmeshvert=len(mesh_vert), nmeshpoly=len(polyvertadr),
                           nmeshpolyvert=len(polyvert), nmeshpolymap=len(polymap),
@@ -441,7 +444,7 @@ class Scene:
             dof_bodyid=np.array([d['body'] for d in dofs], np.int32),
             dof_jntid=np.array([d['jnt'] for d in dofs], np.int32),
             dof_parentid=dof_parent, dof_treeid=dof_tree,
-            tree_dofadr=tree_dofadr, tree_dofnum=tree_dofnum, tree_madr=tree_madr,
+            tree_dofadr=tree_dofadr, tree_dofnum=tree_dofnum, tree_madr=tree_madr, tree_padr=tree_padr,
             geom_type=gtype, geom_bodyid=gbody,
             geom_condim=np.array([g.condim for _, g in G], np.int32),
             geom_priority=np.zeros(ng, np.int32),

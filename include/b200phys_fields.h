@@ -28,7 +28,7 @@
   X(iterations) X(ls_iterations) X(disable_flags) X(ee_site) X(real_bytes) \
   X(nvs) X(kmax_dof) X(max_tree_dofs) X(osc_uncouple) X(nfree) X(nobs) \
   X(nmesh) X(nmeshvert) X(nmeshpoly) X(nmeshpolyvert) X(nmeshpolymap) \
-  X(ccd_iterations) X(epa_iterations)
+  X(ccd_iterations) X(epa_iterations) X(nL)
 
 /* real scalars of the model (stored as double, read as the kernel's real) */
 #define B200_MODEL_REAL_SCALARS(X) \
@@ -44,7 +44,7 @@
   X(jnt_type, njnt) X(jnt_qposadr, njnt) X(jnt_dofadr, njnt) \
   X(jnt_bodyid, njnt) X(jnt_limited, njnt) \
   X(dof_bodyid, nv) X(dof_jntid, nv) X(dof_parentid, nv) X(dof_treeid, nv) \
-  X(tree_dofadr, ntree) X(tree_dofnum, ntree) X(tree_madr, ntree) \
+  X(tree_dofadr, ntree) X(tree_dofnum, ntree) X(tree_madr, ntree) X(tree_padr, ntree) \
   X(geom_type, ngeom) X(geom_bodyid, ngeom) X(geom_condim, ngeom) \
   X(geom_priority, ngeom) X(site_bodyid, nsite) X(pair_geom, npair * 2) \
   X(limited_jnt, nlimited) X(fric_dof, nfric) \
