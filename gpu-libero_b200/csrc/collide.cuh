@@ -660,8 +660,8 @@ __device__ __noinline__ void plane_mesh(const Mdl<R> &M, Arena<R> &A, const Mate
 // mjwarp_convex_epa.cuh gjk_phase): supports inflated by half the pair margin
 // on each shape, sphere / capsule cores first, GJK distance with a separation
 // cutoff, EPA for penetration, one contact at the witness midpoint.  The
-// distance subalgorithm searches every sub-simplex of the current simplex;
-// EPA is the expanding polytope method (van den Bergen 2001).  One thread
+// distance subalgorithm searches the sub-simplices that contain the newest
+// support point; EPA is the expanding polytope method (van den Bergen 2001).  One thread
 // runs one pair; the polytope lives in the thread's local memory.
 template <class R> struct CShape {
   int type, nvert;
@@ -704,29 +704,44 @@ template <class R> __device__ R det3(const R G[3][3]) {
          G[0][2] * (G[1][0] * G[2][1] - G[1][1] * G[2][0]);
 }
 
+// Minimum-norm point of the simplex.  Candidates are the sub-simplices that
+// contain the newest support point (the last vertex; standard GJK), each
+// solved for its affine minimiser; the best one with positive weights wins.
+// Every loop is unrolled over constant vertex masks, so the simplex stays in
+// registers.
 template <class R> __device__ void simplex_reduce(Simplex<R> &s) {
+  const int n = s.n, last = n - 1;
   R best = R(1e30), lam_best[4] = {0, 0, 0, 0};
-  int mask_best = 0;
-  for (int mask = 1; mask < (1 << s.n); ++mask) {
-    int idx[4], k = 0;
-    for (int i = 0; i < s.n; ++i)
-      if (mask & (1 << i)) idx[k++] = i;
-    R lam[4] = {0, 0, 0, 0}, mu[3] = {0, 0, 0};
-    if (k > 1) {
+  int mask_best = 1 << last;
+#pragma unroll
+  for (int mask = 1; mask < 16; ++mask) {
+    if (mask >= (1 << n) || !((mask >> last) & 1)) continue;
+    V3<R> p[4];
+    int k = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if ((mask >> i) & 1) p[k++] = s.w[i];
+    R lam[4] = {0, 0, 0, 0};
+    if (k == 1) {
+      lam[0] = 1;
+    } else {
       V3<R> e[3];
-      const V3<R> w0 = s.w[idx[0]];
-      for (int j = 1; j < k; ++j) e[j - 1] = s.w[idx[j]] - w0;
-      const int q = k - 1;
-      R G[3][3], rhs[3];
-      for (int i = 0; i < q; ++i) {
-        rhs[i] = -dot(e[i], w0);
-        for (int j = 0; j < q; ++j) G[i][j] = dot(e[i], e[j]);
-      }
-      if (q == 1) {
-        const R det = G[0][0];
-        if (!(det > R(1e-30))) continue;
-        mu[0] = rhs[0] / det;
-      } else if (q == 2) {
+#pragma unroll
+      for (int j = 1; j < 4; ++j)
+        if (j < k) e[j - 1] = p[j] - p[0];
+      R G[3][3] = {{0, 0, 0}, {0, 0, 0}, {0, 0, 0}}, rhs[3] = {0, 0, 0}, mu[3] = {0, 0, 0};
+#pragma unroll
+      for (int a = 0; a < 3; ++a)
+        if (a < k - 1) {
+          rhs[a] = -dot(e[a], p[0]);
+#pragma unroll
+          for (int b = 0; b < 3; ++b)
+            if (b < k - 1) G[a][b] = dot(e[a], e[b]);
+        }
+      if (k == 2) {
+        if (!(G[0][0] > R(1e-30))) continue;
+        mu[0] = rhs[0] / G[0][0];
+      } else if (k == 3) {
         const R det = G[0][0] * G[1][1] - G[0][1] * G[1][0];
         if (!(mabs(det) > R(1e-30))) continue;
         mu[0] = (rhs[0] * G[1][1] - G[0][1] * rhs[1]) / det;
@@ -734,33 +749,47 @@ template <class R> __device__ void simplex_reduce(Simplex<R> &s) {
       } else {
         const R det = det3(G);
         if (!(mabs(det) > R(1e-30))) continue;
+#pragma unroll
         for (int c = 0; c < 3; ++c) {
           R M3[3][3];
-          for (int i = 0; i < 3; ++i)
-            for (int j = 0; j < 3; ++j) M3[i][j] = j == c ? rhs[i] : G[i][j];
+#pragma unroll
+          for (int a = 0; a < 3; ++a)
+#pragma unroll
+            for (int b = 0; b < 3; ++b) M3[a][b] = b == c ? rhs[a] : G[a][b];
           mu[c] = det3(M3) / det;
         }
       }
       R l0 = 1;
-      for (int j = 0; j < q; ++j) { lam[j + 1] = mu[j]; l0 -= mu[j]; }
-      lam[0] = l0;
       bool ok = true;
-      for (int j = 0; j < k; ++j) ok &= lam[j] > R(0);
-      if (!ok) continue;
-    } else
-      lam[0] = 1;
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+        if (j < k - 1) { lam[j + 1] = mu[j]; l0 -= mu[j]; ok &= mu[j] > R(0); }
+      lam[0] = l0;
+      if (!(ok && l0 > R(0))) continue;
+    }
     V3<R> x = v3<R>(0, 0, 0);
-    for (int j = 0; j < k; ++j) x = x + s.w[idx[j]] * lam[j];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < k) x = x + p[j] * lam[j];
     const R d = dot(x, x);
     if (d < best) {
-      best = d; mask_best = mask;
+      best = d;
+      mask_best = mask;
+#pragma unroll
       for (int j = 0; j < 4; ++j) lam_best[j] = lam[j];
     }
   }
   Simplex<R> t;
+  t.n = 0;
   int k = 0;
-  for (int i = 0; i < s.n; ++i)
-    if (mask_best & (1 << i)) { t.w[k] = s.w[i]; t.a[k] = s.a[i]; t.b[k] = s.b[i]; t.lam[k] = lam_best[k]; ++k; }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if ((mask_best >> i) & 1) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j == k) { t.w[j] = s.w[i]; t.a[j] = s.a[i]; t.b[j] = s.b[i]; t.lam[j] = lam_best[j]; }
+      ++k;
+    }
   t.n = k;
   s = t;
 }
@@ -790,16 +819,23 @@ template <class R> __device__ GjkOut<R> gjk(const CShape<R> &A, const CShape<R> 
       o.dist = R(1e30);
       return o;
     }
-    s.w[s.n] = w; s.a[s.n] = a; s.b[s.n] = b; s.n++;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (i == s.n) { s.w[i] = w; s.a[i] = a; s.b[i] = b; }
+    s.n++;
     simplex_reduce(s);
     x = v3<R>(0, 0, 0);
-    for (int i = 0; i < s.n; ++i) x = x + s.w[i] * s.lam[i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (i < s.n) x = x + s.w[i] * s.lam[i];
     prev = norm;
     norm = msqrt(dot(x, x));
     if (s.n == 4) break;
   }
   o.x1 = v3<R>(0, 0, 0); o.x2 = v3<R>(0, 0, 0);
-  for (int i = 0; i < s.n; ++i) { o.x1 = o.x1 + s.a[i] * s.lam[i]; o.x2 = o.x2 + s.b[i] * s.lam[i]; }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (i < s.n) { o.x1 = o.x1 + s.a[i] * s.lam[i]; o.x2 = o.x2 + s.b[i] * s.lam[i]; }
   if (s.n == 0) { o.x1 = A.pos; o.x2 = B.pos; }
   o.dist = s.n == 4 ? R(0) : norm;
   return o;
@@ -835,7 +871,9 @@ template <class R> __device__ int epa_push(Polytope<R> &P, const CShape<R> &A, c
 
 template <class R> __device__ bool epa_seed(Polytope<R> &P, const CShape<R> &A, const CShape<R> &B, const Simplex<R> &s) {
   P.nf = 0;
-  for (int i = 0; i < s.n; ++i) { P.w[i] = s.w[i]; P.a[i] = s.a[i]; P.b[i] = s.b[i]; }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (i < s.n) { P.w[i] = s.w[i]; P.a[i] = s.a[i]; P.b[i] = s.b[i]; }
   P.nv = s.n;
   for (int k = 0; P.nv < 2 && k < 6; ++k) {
     V3<R> ax = v3<R>(0, 0, 0);

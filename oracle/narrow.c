@@ -14,9 +14,9 @@
  * on each shape, sphere and capsule cores shrunk to a point / segment first,
  * GJK distance with a separation cutoff, EPA for penetration, one contact at
  * the witness midpoint whose normal is x1 - x2 when the inflated shapes
- * overlap.  The GJK distance subalgorithm here is an exhaustive search over
- * the sub-simplices of the current simplex (the minimum-norm point of the
- * best face whose affine weights are positive), and EPA is the expanding
+ * overlap.  The GJK distance subalgorithm here searches the sub-simplices of
+ * the current simplex that contain the newest support point (the minimum-norm
+ * point of the best face whose affine weights are positive), and EPA is the expanding
  * polytope method of van den Bergen (2001); both give the reference's
  * geometric answer (distance, depth, normal) to the CCD tolerance.
  */
@@ -194,11 +194,12 @@ static V3 cs_support(const CShape *s, V3 d) {
 typedef struct { V3 w[4], a[4], b[4]; real lam[4]; int n; } Simplex;
 
 /* minimum-norm point of the simplex: best sub-simplex with positive affine
- * weights (exhaustive over the <= 15 non-empty subsets) */
+ * weights among those containing the newest support point (the last vertex) */
 static void simplex_reduce(Simplex *s) {
   real best = R(1e30), lam_best[4] = {0, 0, 0, 0};
-  int mask_best = 0;
+  int mask_best = 1 << (s->n - 1);
   for (int mask = 1; mask < (1 << s->n); ++mask) {
+    if (!((mask >> (s->n - 1)) & 1)) continue;
     int idx[4], k = 0;
     for (int i = 0; i < s->n; ++i)
       if (mask & (1 << i)) idx[k++] = i;
