@@ -53,7 +53,8 @@ template <class R> struct Arena {
   R *scal;   // [0] alpha [1] improvement [2] search_dot [3] grad_dot [4] decrement [5] time
   int *iscal;  // [0] ncon [1] nefc [2] nf [3] overflow [4] niter [5] done [6] error [7] ls evals
                // [8] raw contact count [9] ls evals at previous substep [10] profiling on
-               // [11] islands [12] largest island [16..19] OSC factor flags [20..22] pinv flags
+               // [11] islands [12] largest island [13] single-dof rows [14] refactor Newton H
+               // [16..19] OSC factor flags [20..22] pinv flags
   R *red;    // reduction scratch (one real per warp of the world)
   long long *prof;  // [0] last stamp, [1..15] per-stage cycle sums (stage profiling only)
   int ubytes;       // size of the stage-scoped union region (H, OSC and kinematics scratch)

@@ -1349,6 +1349,9 @@ template <class R, int T> __device__ B200_STAGE_ATTR void eval_gradient(const Md
     } else if (res >= R(0)) { force = 0; state = kSatisfied; }
     else { force = -d * res; state = kQuadratic; }
     A.efc_force[r] = force;
+    // H depends on the states (and, for cone-state contacts, on jaref):
+    // flag a refactorization when a state changes or a contact is in the cone
+    if (A.efc_state[r] != state || state == kCone) A.iscal[14] = 1;
     A.efc_state[r] = state;
   }
   SYNC();
@@ -1379,6 +1382,9 @@ template <class R, int T> __device__ B200_STAGE_ATTR void eval_gradient(const Md
 // the contact is in the cone state.  Contacts run one after another, each
 // H entry of a contact on its own lane, so sums are deterministic.
 template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &M, Arena<R> &A) {
+  // unchanged constraint states and no cone-state contact: H, and its factor
+  // still held in A.H, are exactly what this assembly would produce again
+  if (!A.iscal[14]) return;
   const B200Model &m = M.m;
   const int nisl = A.iscal[11], nsingle = A.iscal[13], ncon = A.iscal[0], kmax = m.kmax_dof;
   const R impratio = R(m.impratio_invsqrt);
@@ -1499,6 +1505,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void direction(const Mdl<R>
   const int nv = M.m.nv;
   R *x = A.xs;
   const int lane = LANE, maxn = A.iscal[12];
+  const bool refactor = A.iscal[14];
   const BlockRows b = ISLAND_ROWS(T);
 #pragma unroll
   for (int s = 0; s < 4; ++s)
@@ -1507,7 +1514,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void direction(const Mdl<R>
       x[p] = A.grad[A.isl_dof[p]];
     }
   __syncwarp();
-  chol_blocks(A.H, b, maxn, nv, A.colbuf);
+  if (refactor) chol_blocks(A.H, b, maxn, nv, A.colbuf);
   solve_blocks(A.H, b, x, maxn, lane);
   R sq = 0, dec = 0;
 #pragma unroll
@@ -1522,6 +1529,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void direction(const Mdl<R>
   dec = world_sum<T>(dec, A.red);
   if (TID == 0) { A.scal[2] = sq; A.scal[4] = dec; }
   SYNC();
+  if (TID == 0) A.iscal[14] = 0;  // H holds the factor of the current states
 }
 
 // ---- exact line search (mjwarp_linesearch.cu:80-365); row evaluations are
@@ -1790,7 +1798,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void newton_init(const Mdl<
   SYNC();
   mass_mul<R, T>(M, A.M, A.qacc, A.Ma);
   FOR(r, nefc) A.efc_jaref[r] = jdot(M, A, r, A.qacc) - A.efc_aref[r];
-  if (TID == 0) { A.iscal[4] = 0; A.iscal[5] = m.iterations == 0; }
+  if (TID == 0) { A.iscal[4] = 0; A.iscal[5] = m.iterations == 0; A.iscal[14] = 1; }
   SYNC();
   eval_gradient<R, T>(M, A);
   hessian<R, T>(M, A);
