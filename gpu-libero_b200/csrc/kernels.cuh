@@ -130,48 +130,53 @@ template <class R, int T> __device__ B200_STAGE_ATTR void kinematics(const Mdl<R
   }
   SYNC();
   const int *order = IF(body_order), *lstart = IF(level_start);
-  for (int level = 1; level < m.nlevel; ++level) {
-    const int a = lstart[level], n = lstart[level + 1] - a;
-    FOR(k, n) {
-      const int b = order[a + k];
-      const int first = IF(body_jntadr)[b], count = IF(body_jntnum)[b], p = IF(body_parentid)[b];
-      V3<R> pos;
-      Q4<R> quat;
-      if (count == 1 && IF(jnt_type)[first] == B200_JNT_FREE) {
-        const R *q = A.qpos + IF(jnt_qposadr)[first];
-        pos = v3<R>(q[0], q[1], q[2]);
-        quat = qnormalize(Q4<R>{q[3], q[4], q[5], q[6]});
-        st3(A.anchor + 3 * first, pos);
-        st3(A.axis + 3 * first, ld3(RF(jnt_axis) + 3 * first));
-      } else {
-        const Q4<R> pq = ldq(A.xquat + 4 * p);
-        pos = qrot(ld3(RF(body_pos) + 3 * b), pq) + ld3(A.xpos + 3 * p);
-        quat = qmul(pq, ldq(RF(body_quat) + 4 * b));
-        for (int j = first; j < first + count; ++j) {
-          const int kind = IF(jnt_type)[j], qa = IF(jnt_qposadr)[j];
-          const V3<R> lpos = ld3(RF(jnt_pos) + 3 * j), lax = ld3(RF(jnt_axis) + 3 * j);
-          const V3<R> anchor = qrot(lpos, quat) + pos, axis = qrot(lax, quat);
-          if (kind == B200_JNT_BALL) {
-            quat = qmul(quat, qnormalize(ldq(A.qpos + qa)));
-            pos = anchor - qrot(lpos, quat);
-          } else if (kind == B200_JNT_SLIDE) {
-            pos = pos + axis * (A.qpos[qa] - RF(qpos0)[qa]);
-          } else if (kind == B200_JNT_HINGE) {
-            const R angle = (A.qpos[qa] - RF(qpos0)[qa]) * R(0.5);
-            const R s = msin(angle), c = mcos(angle);
-            quat = qmul(quat, Q4<R>{c, lax.x * s, lax.y * s, lax.z * s});
-            pos = anchor - qrot(lpos, quat);
+  // tree levels hold few bodies: the world's first warp walks them with warp
+  // barriers; the other warps wait once
+  if (WARP0) {
+    for (int level = 1; level < m.nlevel; ++level) {
+      const int a = lstart[level], n = lstart[level + 1] - a;
+      for (int k = LANE; k < n; k += 32) {
+        const int b = order[a + k];
+        const int first = IF(body_jntadr)[b], count = IF(body_jntnum)[b], p = IF(body_parentid)[b];
+        V3<R> pos;
+        Q4<R> quat;
+        if (count == 1 && IF(jnt_type)[first] == B200_JNT_FREE) {
+          const R *q = A.qpos + IF(jnt_qposadr)[first];
+          pos = v3<R>(q[0], q[1], q[2]);
+          quat = qnormalize(Q4<R>{q[3], q[4], q[5], q[6]});
+          st3(A.anchor + 3 * first, pos);
+          st3(A.axis + 3 * first, ld3(RF(jnt_axis) + 3 * first));
+        } else {
+          const Q4<R> pq = ldq(A.xquat + 4 * p);
+          pos = qrot(ld3(RF(body_pos) + 3 * b), pq) + ld3(A.xpos + 3 * p);
+          quat = qmul(pq, ldq(RF(body_quat) + 4 * b));
+          for (int j = first; j < first + count; ++j) {
+            const int kind = IF(jnt_type)[j], qa = IF(jnt_qposadr)[j];
+            const V3<R> lpos = ld3(RF(jnt_pos) + 3 * j), lax = ld3(RF(jnt_axis) + 3 * j);
+            const V3<R> anchor = qrot(lpos, quat) + pos, axis = qrot(lax, quat);
+            if (kind == B200_JNT_BALL) {
+              quat = qmul(quat, qnormalize(ldq(A.qpos + qa)));
+              pos = anchor - qrot(lpos, quat);
+            } else if (kind == B200_JNT_SLIDE) {
+              pos = pos + axis * (A.qpos[qa] - RF(qpos0)[qa]);
+            } else if (kind == B200_JNT_HINGE) {
+              const R angle = (A.qpos[qa] - RF(qpos0)[qa]) * R(0.5);
+              const R s = msin(angle), c = mcos(angle);
+              quat = qmul(quat, Q4<R>{c, lax.x * s, lax.y * s, lax.z * s});
+              pos = anchor - qrot(lpos, quat);
+            }
+            st3(A.anchor + 3 * j, anchor);
+            st3(A.axis + 3 * j, axis);
           }
-          st3(A.anchor + 3 * j, anchor);
-          st3(A.axis + 3 * j, axis);
+          quat = qnormalize(quat);
         }
-        quat = qnormalize(quat);
+        st3(A.xpos + 3 * b, pos);
+        stq(A.xquat + 4 * b, quat);
       }
-      st3(A.xpos + 3 * b, pos);
-      stq(A.xquat + 4 * b, quat);
+      __syncwarp();
     }
-    SYNC();
   }
+  SYNC();
   FOR(b, m.nbody) {
     const Q4<R> q = ldq(A.xquat + 4 * b);
     qmat(A.xmat + 9 * b, q);
@@ -832,40 +837,45 @@ template <class R, int T> __device__ B200_STAGE_ATTR void velocity(const Mdl<R> 
   }
   SYNC();
   const int *order = IF(body_order), *lstart = IF(level_start);
-  for (int level = 1; level < m.nlevel; ++level) {
-    const int a = lstart[level], n = lstart[level + 1] - a;
-    FOR(k, n) {
-      const int b = order[a + k], p = IF(body_parentid)[b];
-      R vel[6], acc[6];
-      for (int c = 0; c < 6; ++c) { vel[c] = A.cvel[6 * p + c]; acc[c] = A.cacc[6 * p + c]; }
-      int dof = IF(body_dofadr)[b];
-      const int j0 = IF(body_jntadr)[b], j1 = j0 + IF(body_jntnum)[b];
-      for (int j = j0; j < j1; ++j) {
-        const int type = IF(jnt_type)[j];
-        if (type == B200_JNT_FREE) {
-          for (int i = 0; i < 3; ++i) {
+  // tree levels hold few bodies: the world's first warp walks them with warp
+  // barriers; the other warps wait once
+  if (WARP0) {
+    for (int level = 1; level < m.nlevel; ++level) {
+      const int a = lstart[level], n = lstart[level + 1] - a;
+      for (int k = LANE; k < n; k += 32) {
+        const int b = order[a + k], p = IF(body_parentid)[b];
+        R vel[6], acc[6];
+        for (int c = 0; c < 6; ++c) { vel[c] = A.cvel[6 * p + c]; acc[c] = A.cacc[6 * p + c]; }
+        int dof = IF(body_dofadr)[b];
+        const int j0 = IF(body_jntadr)[b], j1 = j0 + IF(body_jntnum)[b];
+        for (int j = j0; j < j1; ++j) {
+          const int type = IF(jnt_type)[j];
+          if (type == B200_JNT_FREE) {
+            for (int i = 0; i < 3; ++i) {
+              for (int c = 0; c < 6; ++c) vel[c] += A.cdof[6 * (dof + i) + c] * A.qvel[dof + i];
+              for (int c = 0; c < 6; ++c) A.cdof_dot[6 * (dof + i) + c] = 0;
+            }
+            dof += 3;
+          }
+          const int width = type == B200_JNT_FREE || type == B200_JNT_BALL ? 3 : 1;
+          for (int i = 0; i < width; ++i) {
+            R dd[6];
+            motion_cross(vel, A.cdof + 6 * (dof + i), dd);
+            for (int c = 0; c < 6; ++c) {
+              A.cdof_dot[6 * (dof + i) + c] = dd[c];
+              acc[c] += dd[c] * A.qvel[dof + i];
+            }
+          }
+          for (int i = 0; i < width; ++i)
             for (int c = 0; c < 6; ++c) vel[c] += A.cdof[6 * (dof + i) + c] * A.qvel[dof + i];
-            for (int c = 0; c < 6; ++c) A.cdof_dot[6 * (dof + i) + c] = 0;
-          }
-          dof += 3;
+          dof += width;
         }
-        const int width = type == B200_JNT_FREE || type == B200_JNT_BALL ? 3 : 1;
-        for (int i = 0; i < width; ++i) {
-          R dd[6];
-          motion_cross(vel, A.cdof + 6 * (dof + i), dd);
-          for (int c = 0; c < 6; ++c) {
-            A.cdof_dot[6 * (dof + i) + c] = dd[c];
-            acc[c] += dd[c] * A.qvel[dof + i];
-          }
-        }
-        for (int i = 0; i < width; ++i)
-          for (int c = 0; c < 6; ++c) vel[c] += A.cdof[6 * (dof + i) + c] * A.qvel[dof + i];
-        dof += width;
+        for (int c = 0; c < 6; ++c) { A.cvel[6 * b + c] = vel[c]; A.cacc[6 * b + c] = acc[c]; }
       }
-      for (int c = 0; c < 6; ++c) { A.cvel[6 * b + c] = vel[c]; A.cacc[6 * b + c] = acc[c]; }
+      __syncwarp();
     }
-    SYNC();
   }
+  SYNC();
   // raw body forces (into cfrc), then subtree sums
   FOR(b, m.nbody) {
     R f[6], mom[6], corr[6];
