@@ -1,8 +1,8 @@
 // Per-world shared-memory arena of the fused control-step kernel.
 //
-// One CTA owns one world for a whole control step; every array the substep
-// touches lives here, so HBM is read once (state in) and written once (state
-// and outputs out) per control step.  The layout is computed identically on
+// A world (one or four warps of a CTA) owns its arena for a whole control
+// step; every array the substep touches lives here, so HBM is read once
+// (state in) and written once (state and outputs out) per control step.  The layout is computed identically on
 // the host (to size the dynamic shared memory) and on the device.
 #pragma once
 #include <cstddef>

@@ -95,14 +95,6 @@ template <class R> __device__ __forceinline__ bool dof_ancestor(const Mdl<R> &M,
   return (((unsigned)IF(body_dofmask)[4 * body + (dof >> 5)]) >> (dof & 31)) & 1u;
 }
 
-// value of compressed constraint row r at global dof d (0 outside its trees)
-template <class R> __device__ __forceinline__ R jval(const Mdl<R> &M, const Arena<R> &A, int r, int d) {
-  const int t = IF(dof_treeid)[d], t0 = A.row_t[2 * r], t1 = A.row_t[2 * r + 1];
-  const R *row = A.J + (size_t)r * M.m.kmax_dof;
-  if (t == t0) return row[d - IF(tree_dofadr)[t]];
-  if (t == t1) return row[IF(tree_dofnum)[t0] + d - IF(tree_dofadr)[t]];
-  return R(0);
-}
 // row r times a dof vector, over the row's tree segments
 template <class R> __device__ __forceinline__ R jdot(const Mdl<R> &M, const Arena<R> &A, int r, const R *x) {
   const int t0 = A.row_t[2 * r], t1 = A.row_t[2 * r + 1];
@@ -315,7 +307,7 @@ __device__ __forceinline__ BlockRows owned_rows(int nblocks, const int *bn, cons
 #define TREE_ROWS(T) owned_rows(M.m.ntree, IF(tree_dofnum), IF(tree_dofadr), IF(tree_padr), LANE, TID >> 5, (T) / 32)
 #define ISLAND_ROWS(T) owned_rows(A.iscal[11], A.isl_n, A.isl_dofstart, A.isl_off, LANE, TID >> 5, (T) / 32)
 
-// in-place lower Cholesky L L^T of every block (right-looking, warp 0)
+// in-place lower Cholesky L L^T of a warp's blocks (right-looking)
 template <class R> __device__ void chol_blocks_smem(R *H, const BlockRows &b, int maxn) {
   for (int k = 0; k < maxn; ++k) {
 #pragma unroll
@@ -395,7 +387,7 @@ template <class R> __device__ B200_STAGE_ATTR void chol_blocks(R *H, const Block
     chol_blocks_smem(H, b, maxn);
 }
 
-// solve L L^T x = x in place (x indexed by position), warp 0
+// solve L L^T x = x in place over a warp's blocks (x indexed by position)
 template <class R> __device__ B200_STAGE_ATTR void solve_blocks(const R *H, const BlockRows &b, R *x, int maxn, int lane) {
   for (int k = 0; k < maxn; ++k) {
 #pragma unroll
@@ -619,7 +611,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void constraints(const Mdl<
   const int cap = m.nefc_max, kmax = m.kmax_dof;
   const bool off = m.disable_flags & B200_DSBL_CONSTRAINT;
   const bool elliptic = m.cone == 1;
-  // row allocation (warp 0): friction rows, active limits, then contacts in
+  // row allocation (the world's first warp): friction rows, active limits, then contacts in
   // sorted order, each contact all-or-nothing; prefix sums by warp scans
   if (WARP0) {
     const int lane = LANE;
@@ -1064,7 +1056,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void osc_control(const Mdl<
   double *S = A.osc;
   const int lane = TID;
   // ee velocity over all dofs (non-ancestors have zero Jacobian columns)
-  if (lane < 32) {  // warp 0: six 4-lane groups, lanes 24..31 idle
+  if (lane < 32) {  // first warp: six 4-lane groups, lanes 24..31 idle
     const int ax = lane >> 2, l4 = lane & 3;
     R v = 0;
     const V3<R> point = ld3(A.sxpos + 3 * site), com = ld3(A.com + 3 * IF(body_rootid)[body]);
