@@ -1990,13 +1990,17 @@ template <class R, int T> __device__ __noinline__ void store_outputs(const B200M
 // in the barriers only.
 // B200_SYNC_LEVEL: 2 = CTA barrier after every stage (lockstep worlds),
 // 1 = one CTA barrier per substep, 0 = worlds run free (warp syncs only).
+// B200_SYNC_LEVEL 3: the CTA barrier follows every stage from collision to
+// actuation; the Newton loop, Euler and the next substep's kinematics, CoM /
+// CRB and mass factor run per world, so worlds that meet the Newton stop
+// rule early continue instead of idling.
 #ifndef B200_SYNC_LEVEL
 #define B200_SYNC_LEVEL 2
 #endif
-#if B200_SYNC_LEVEL == 2
+#if B200_SYNC_LEVEL >= 2
 #define STAGE_SYNC() __syncthreads()
 #else
-#define STAGE_SYNC() __syncwarp()
+#define STAGE_SYNC() SYNC()
 #endif
 #define STAGE(call, k)  \
   do {                  \
@@ -2007,6 +2011,20 @@ template <class R, int T> __device__ __noinline__ void store_outputs(const B200M
     STAGE_SYNC();       \
     if (act) mark<T>(A, 15); \
   } while (0)
+// a stage that level 3 runs without the CTA barrier (world barrier only)
+#if B200_SYNC_LEVEL == 3
+#define STAGE_FREE(call, k) \
+  do {                      \
+    if (act) {              \
+      call;                 \
+      mark<T>(A, k);        \
+      SYNC();               \
+      mark<T>(A, 15);       \
+    }                       \
+  } while (0)
+#else
+#define STAGE_FREE(call, k) STAGE(call, k)
+#endif
 
 // factor of the mass matrix, one block per kinematic tree (mjwarp_mass_factor.cu)
 template <class R, int T> __device__ B200_STAGE_ATTR void mass_factor(const Mdl<R> &M, Arena<R> &A) {
@@ -2017,16 +2035,20 @@ template <class R, int T> __device__ B200_STAGE_ATTR void mass_factor(const Mdl<
 }
 
 template <class R, bool CONVEX, int T> __device__ void step1_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
-  STAGE((kinematics<R, T>(M, A)), 1);
-  STAGE((com_crb_mass<R, T>(M, A)), 2);
-  STAGE((mass_factor<R, T>(M, A)), 3);
+  STAGE_FREE((kinematics<R, T>(M, A)), 1);
+  STAGE_FREE((com_crb_mass<R, T>(M, A)), 2);
+  STAGE_FREE((mass_factor<R, T>(M, A)), 3);
+#if B200_SYNC_LEVEL == 3
+  __syncthreads();  // worlds meet again before the collision code
+  if (act) mark<T>(A, 15);
+#endif
   STAGE((collision<R, T, CONVEX>(M, A)), 4);
   STAGE((constraints<R, T>(M, A)), 5);
   STAGE((velocity<R, T>(M, A)), 6);
 }
 
 template <class R, int T> __device__ void newton_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
-  STAGE((newton_init<R, T>(M, A)), 0);
+  STAGE_FREE((newton_init<R, T>(M, A)), 0);
 #if B200_SYNC_LEVEL == 2
   while (__syncthreads_or(act && !A.iscal[5])) {
     if (act) mark<T>(A, 15);  // barrier wait and idle iterations of worlds already done
@@ -2077,7 +2099,7 @@ __global__ void __launch_bounds__(384, 1) control_step(const B200Model m, const 
       if (d.ls_rows) irow_of(d.ls_rows, w, 1)[0] += evals * nefc;
     }
     if (act && s == substeps - 1) store_outputs<R, T>(m, d, A, w);
-    STAGE((euler<R, T>(M, A)), 14);
+    STAGE_FREE((euler<R, T>(M, A)), 14);
   }
   if (!act) return;
   if (TID == 0) {
