@@ -221,7 +221,7 @@ def main():
         gather.wait()
     torch.cuda.synchronize(dev)
     counters0 = {k: rt.buffers[k].clone() for k in ('efc_total', 'con_total', 'newton_rows', 'ls_rows',
-                                                     'newton_total')}
+                                                     'newton_total', 'efc_k', 'efc_k2', 'fact_blk')}
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     clocks = ClockSampler(local)
     if world_size > 1:
@@ -252,14 +252,19 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     elapsed_max = float(t.item())
     rt.check()
-    deltas = {k: (rt.buffers[k] - counters0[k]).cpu().numpy() for k in counters0}
+    # int32 device counters; the difference is taken modulo 2^32 so that a counter
+    # that wraps during the interval still gives its delta
+    deltas = {k: (rt.buffers[k].long() - counters0[k].long()).remainder(1 << 32).cpu().numpy()
+              for k in counters0}
     fl = flops.substep_flops(scene.sizes, scene.ints['tree_dofnum'], deltas, scene.substeps)
+    fl_dense = flops.dense_substep_flops(scene.sizes, scene.ints['tree_dofnum'], deltas, scene.substeps)
     kernel_s = elapsed / args.steps  # one kernel per graph replay
     sm_count = torch.cuda.get_device_properties(dev).multi_processor_count
     sm_mhz = clock['sm_mhz'] if clock else 1965.0
     fp64 = args.precision == 'fp64'
     peak = (flops.fp64_peak_tflops if fp64 else flops.fp32_peak_tflops)(sm_count, sm_mhz)
     achieved = fl / args.steps / kernel_s / 1e12
+    achieved_dense = fl_dense / args.steps / kernel_s / 1e12
     real_b = rt.buffers['qpos'].element_size()
     io_real = sum(scene.sizes[k] for k in ('nq',)) * 2 + scene.sizes['nv'] * 4 + scene.sizes['nu'] * 2 + 2 * (3 + 9 + 2) + 7 + 2
     out_real = (scene.sizes['nbody'] * 16 + scene.sizes['ngeom'] * 12 + scene.sizes['nsite'] * 12 +
@@ -320,7 +325,11 @@ def main():
                           frac=achieved / peak, traffic=traffic,
                           peak_source='nominal %s CUDA-core issue: %d SMs x %d lanes x 2 x %.0f MHz (sampled)'
                           % ('FP64' if fp64 else 'FP32', sm_count, 64 if fp64 else 128, sm_mhz),
-                          flops_per_world_substep=fl / (W * args.steps * scene.substeps)),
+                          flops_per_world_substep=fl / (W * args.steps * scene.substeps),
+                          counting='block-sparse: k_r = dofs of the trees a row touches, Newton blocks = islands, island factor counted where executed'),
+            roofline_dense=dict(achieved=achieved_dense, peak=peak, unit='TFLOP/s', frac=achieved_dense / peak,
+                                flops_per_world_substep=fl_dense / (W * args.steps * scene.substeps),
+                                counting='dense-equivalent: k_r = nv, one nv x nv Newton block'),
             roofline_hbm=dict(bound='hbm', achieved=bytes_per_world * W / kernel_s / 1e9, peak=hbm_gbs, unit='GB/s',
                               frac=bytes_per_world * W / kernel_s / 1e9 / hbm_gbs, peak_source=peak_src,
                               bytes_per_world=bytes_per_world, traffic=traffic),

@@ -54,7 +54,8 @@ template <class R> struct Arena {
   int *iscal;  // [0] ncon [1] nefc [2] nf [3] overflow [4] niter [5] done [6] error [7] ls evals
                // [8] raw contact count [9] ls evals at previous substep [10] profiling on
                // [11] islands [12] largest island [13] single-dof rows [14] refactor Newton H
-               // [16..19] OSC factor flags [20..22] pinv flags
+               // [15] sum of row widths k_r [16..19] OSC factor flags [20..22] pinv flags
+               // [23] sum of k_r^2 [24] factored block work (n^3 + 6 n^2)
   R *red;    // reduction scratch (one real per warp of the world)
   long long *prof;  // [0] last stamp, [1..15] per-stage cycle sums (stage profiling only)
   int ubytes;       // size of the stage-scoped union region (H, OSC and kinematics scratch)
@@ -92,7 +93,7 @@ template <class R> struct Arena {
     o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv);
     o[k++] = c.take<R>(nv);
     o[k++] = c.take<R>(2 * nv > 160 ? 2 * nv : 160);  // colbuf
-    o[k++] = c.take<R>(8); o[k++] = c.take<int>(24); o[k++] = c.take<R>(32);  // red: one real per warp of a world
+    o[k++] = c.take<R>(8); o[k++] = c.take<int>(32); o[k++] = c.take<R>(32);  // red: one real per warp of a world
     o[k++] = c.take<long long>(16);
     // union region
     const size_t kin = (size_t)(nb * 3 + nb * 9 + nj * 3 + nj * 3 + nb * 10) * sizeof(R) + 5 * 16;

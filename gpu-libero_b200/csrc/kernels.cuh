@@ -751,8 +751,15 @@ template <class R, int T> __device__ B200_STAGE_ATTR void constraints(const Mdl<
     A.J[(size_t)r * kmax + k] = v;
   }
   SYNC();
-  // row parameters (impedance, D, aref)
+  // row parameters (impedance, D, aref); sum of row widths for the FLOP counters
+  int ksum = 0, k2sum = 0;
   FOR(r, nefc) {
+    {
+      const int t0 = A.row_t[2 * r], t1 = A.row_t[2 * r + 1];
+      const int k = (t0 >= 0 ? IF(tree_dofnum)[t0] : 0) + (t1 >= 0 ? IF(tree_dofnum)[t1] : 0);
+      ksum += k;
+      k2sum += k * k;
+    }
     const int type = A.efc_type[r];
     const R jqv = jdot(M, A, r, A.qvel);
     if (type == 1) {
@@ -795,6 +802,9 @@ template <class R, int T> __device__ B200_STAGE_ATTR void constraints(const Mdl<
       }
     }
   }
+  ksum = world_sum<T>(ksum, (int *)A.red);
+  k2sum = world_sum<T>(k2sum, (int *)A.red);
+  if (TID == 0) { A.iscal[15] = ksum; A.iscal[23] = k2sum; }
   SYNC();
 }
 
@@ -1517,6 +1527,13 @@ template <class R, int T> __device__ B200_STAGE_ATTR void direction(const Mdl<R>
     }
   __syncwarp();
   if (refactor) chol_blocks(A.H, b, maxn, nv, A.colbuf);
+  if (TID == 0) {
+    // FLOP counter, 3x the executed block work: n^3 + 6 n^2 when a block is
+    // factored and solved, 6 n^2 when its factor is reused
+    int blk = 0;
+    for (int i = 0; i < A.iscal[11]; ++i) blk += A.isl_n[i] * A.isl_n[i] * (refactor ? A.isl_n[i] + 6 : 6);
+    A.iscal[24] += blk;
+  }
   solve_blocks(A.H, b, x, maxn, lane);
   R sq = 0, dec = 0;
 #pragma unroll
@@ -1901,7 +1918,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void load_world(const B200M
   else FOR(i, 7) A.action[i] = 0;
   if (TID == 0) {
     A.scal[5] = row_of<R>(d.time, w, 1)[0];
-    for (int k = 0; k < 24; ++k) A.iscal[k] = 0;
+    for (int k = 0; k < 32; ++k) A.iscal[k] = 0;
     A.iscal[3] = irow_of(d.overflow, w, 1)[0];
     A.iscal[6] = irow_of(d.error, w, 1)[0];
   }
@@ -2097,6 +2114,10 @@ __global__ void __launch_bounds__(384, 1) control_step(const B200Model m, const 
       if (d.con_total) irow_of(d.con_total, w, 1)[0] += A.iscal[0];
       if (d.newton_rows) irow_of(d.newton_rows, w, 1)[0] += it * nefc;
       if (d.ls_rows) irow_of(d.ls_rows, w, 1)[0] += evals * nefc;
+      if (d.efc_k) irow_of(d.efc_k, w, 1)[0] += A.iscal[15];
+      if (d.efc_k2) irow_of(d.efc_k2, w, 1)[0] += A.iscal[23];
+      if (d.fact_blk) irow_of(d.fact_blk, w, 1)[0] += A.iscal[24];
+      A.iscal[24] = 0;
     }
     if (act && s == substeps - 1) store_outputs<R, T>(m, d, A, w);
     STAGE_FREE((euler<R, T>(M, A)), 14);

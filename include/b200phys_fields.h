@@ -92,6 +92,7 @@
   X(ncon, 1) X(nefc, 1) X(con_geom, ncon_max * 2) X(overflow, 1) \
   X(error, 1) X(niter, 1) X(newton_total, 1) X(ls_total, 1) \
   X(integration_count, 1) X(efc_total, 1) X(con_total, 1) \
-  X(newton_rows, 1) X(ls_rows, 1) X(stage_cycles, 16)
+  X(newton_rows, 1) X(ls_rows, 1) X(efc_k, 1) X(efc_k2, 1) X(fact_blk, 1) \
+  X(stage_cycles, 16)
 
 #endif

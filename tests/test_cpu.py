@@ -185,3 +185,24 @@ def test_oracle_scene_b_drops_and_settles(oracle_module, scene_b):
     for j in np.flatnonzero(scene_b.ints['jnt_type'] == 0):
         z = h['qpos'][:, scene_b.ints['jnt_qposadr'][j] + 2]
         assert np.all(z > 0.005) and np.all(z < 0.2)
+
+
+def test_flop_count_block_sparse_reduces_to_dense():
+    """With every row dense (k_r = nv) and one nv-block factored every
+    iteration, the block-sparse count equals the dense-equivalent count; with
+    narrower rows and reused factors it is smaller."""
+    from gpu_libero_b200 import flops
+    s = scenes.scene_a()
+    nv, W = s.sizes['nv'], 4
+    nefc, iters, ls = 50, 3, 5
+    base = dict(efc_total=np.full(W, nefc), con_total=np.full(W, 10), newton_rows=np.full(W, iters * nefc),
+                ls_rows=np.full(W, ls * nefc), newton_total=np.full(W, iters))
+    dense_like = dict(base, efc_k=np.full(W, nefc * nv), efc_k2=np.full(W, nefc * nv * nv),
+                      fact_blk=np.full(W, iters * nv * nv * (nv + 6)))
+    td = s.ints['tree_dofnum']
+    a = flops.substep_flops(s.sizes, td, dense_like, 1)
+    b = flops.dense_substep_flops(s.sizes, td, dense_like, 1)
+    assert a == pytest.approx(b, rel=1e-12)
+    sparse = dict(base, efc_k=np.full(W, nefc * 7), efc_k2=np.full(W, nefc * 49),
+                  fact_blk=np.full(W, 7 * 7 * (7 + 6) + 2 * 7 * 7 * 6))
+    assert flops.substep_flops(s.sizes, td, sparse, 1) < 0.5 * b

@@ -243,3 +243,12 @@ def test_scene_b_control_steps_parity(scene_b_state, oracle_module, precision, t
     assert np.max(np.abs(gpu['qpos'] - ref['qpos'])) < tol
     assert np.array_equal(gpu['integration_count'], ref['integration_count'])
     assert not np.any(gpu['overflow'] & ~0x600) and not np.any(gpu['error'])
+    # FLOP counters: every row touches 1..kmax dofs (its one or two trees)
+    td = np.sort(b.ints['tree_dofnum'])
+    kmax = int(td[-1] + td[-2])
+    e, k1, k2 = (gpu[k][:, 0].astype(np.int64) for k in ('efc_total', 'efc_k', 'efc_k2'))
+    assert np.all(e > 0) and np.all(k1 >= e) and np.all(k1 <= kmax * e)
+    assert np.all(k2 >= k1) and np.all(k2 <= kmax * k1)
+    nv = b.sizes['nv']
+    assert np.all(gpu['fact_blk'][:, 0] > 0)
+    assert np.all(gpu['fact_blk'][:, 0] <= gpu['newton_total'][:, 0].astype(np.int64) * nv * nv * (nv + 6))
