@@ -45,7 +45,7 @@ template <class R> struct Arena {
   // islands: trees coupled by constraint rows; the Hessian is block diagonal
   // over islands, each block dense in island-local dof order
   int *tree_isl, *isl_n, *isl_off, *isl_dofstart, *isl_dof, *dof_isl, *dof_loc;
-  R *xs, *colbuf;  // permuted solve vector; Cholesky column buffers (2 x nv) / per-warp contact scratch
+  R *xs, *colbuf;  // permuted solve vector; Cholesky column buffers (2 x nv) / per-warp 6 x 6 contact scratch
   // Newton Hessian, reused as OSC scratch (double) before the solve
   R *H;
   double *osc;
@@ -61,6 +61,10 @@ template <class R> struct Arena {
   int ubytes;       // size of the stage-scoped union region (H, OSC and kinematics scratch)
 
   static constexpr int kOscDoubles = 400;
+  // colbuf holds the Cholesky column buffers (2 x nv) or one 6 x 6 contact
+  // coupling matrix per warp of a world (at most four warps)
+  static constexpr int kColbufWarps = 4, kColbufMin = 160;
+  static_assert(kColbufWarps * 36 <= kColbufMin, "colbuf holds a 6 x 6 matrix per warp");
 
   // Stage-scoped arrays share one region (U): kinematics -> CRB scratch
   // (xipos, ximat, joint anchors/axes, crb), the RNE scratch (cvel, cacc,
@@ -92,7 +96,7 @@ template <class R> struct Arena {
     o[k++] = c.take<int>(nt + 1);
     o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv);
     o[k++] = c.take<R>(nv);
-    o[k++] = c.take<R>(2 * nv > 160 ? 2 * nv : 160);  // colbuf
+    o[k++] = c.take<R>(2 * nv > kColbufMin ? 2 * nv : kColbufMin);  // colbuf
     o[k++] = c.take<R>(8); o[k++] = c.take<int>(32); o[k++] = c.take<R>(32);  // red: one real per warp of a world
     o[k++] = c.take<long long>(16);
     // union region

@@ -2081,6 +2081,7 @@ template <class R, int T> __device__ void newton_stages(const Mdl<R> &M, Arena<R
 template <class R, bool CONVEX, int T>
 __global__ void __launch_bounds__(384, 1) control_step(const B200Model m, const B200Data d, int substeps, int policy, int wpc,
                                                      int arena) {
+  static_assert(T % 32 == 0 && T / 32 <= Arena<R>::kColbufWarps, "per-warp scratch covers at most four warps");
   extern __shared__ __align__(16) unsigned char smem[];
   const int slot = threadIdx.x / T, w = blockIdx.x * wpc + slot;
   const bool act = slot < wpc && w < d.nworld;
