@@ -16,7 +16,7 @@ constexpr int kMaxWorldsPerCta = 8;
 
 bool model_ok(const B200Model *m) {
   return m && m->real && m->ints && (m->real_bytes == 4 || m->real_bytes == 8) && m->nv >= 1 && m->nv <= 128 &&
-         m->nbody >= 2 && m->ncon_max >= 1 && m->nefc_max >= 1 && m->nvs >= m->nv && m->nsite > m->ee_site &&
+         m->nbody >= 2 && m->ncon_max >= 1 && m->nefc_max >= 1 && m->nefc_max <= 65535 && m->nvs >= m->nv && m->nsite > m->ee_site &&
          m->nu >= 9 && m->ntree >= 1 && m->ntree <= 32 && m->kmax_dof >= m->max_tree_dofs;
 }
 bool data_ok(const B200Data *d) {

@@ -45,6 +45,13 @@ template <class R> struct Arena {
   // islands: trees coupled by constraint rows; the Hessian is block diagonal
   // over islands, each block dense in island-local dof order
   int *tree_isl, *isl_n, *isl_off, *isl_dofstart, *isl_dof, *dof_isl, *dof_loc;
+  // per-tree segment lists, rebuilt with the rows every substep: the
+  // single-dof rows and the contacts (row ranges) acting on tree t are
+  // tree_seg[tree_segadr[t] .. tree_segadr[t + 1]), in ascending row order;
+  // entry = first row | rows << 16 | (column of the tree's first dof in the
+  // row's Jacobian values) << 24
+  int *tree_segadr;
+  unsigned *tree_seg;
   R *xs, *colbuf;  // permuted solve vector; Cholesky column buffers (2 x nv) / per-warp 6 x 6 contact scratch
   // Newton Hessian, reused as OSC scratch (double) before the solve
   R *H;
@@ -61,6 +68,8 @@ template <class R> struct Arena {
   int ubytes;       // size of the stage-scoped union region (H, OSC and kinematics scratch)
 
   static constexpr int kOscDoubles = 400;
+  // single-dof rows appear in one tree's list, contacts in at most two
+  __host__ __device__ static int seg_capacity(const B200Model &m) { return m.nfric + m.nlimited + 2 * m.ncon_max; }
   // colbuf holds the Cholesky column buffers (2 x nv) or one 6 x 6 contact
   // coupling matrix per warp of a world (at most four warps)
   static constexpr int kColbufWarps = 4, kColbufMin = 160;
@@ -95,6 +104,7 @@ template <class R> struct Arena {
     o[k++] = c.take<int>(nt); o[k++] = c.take<int>(nt); o[k++] = c.take<int>(nt);
     o[k++] = c.take<int>(nt + 1);
     o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv); o[k++] = c.take<int>(nv);
+    o[k++] = c.take<int>(nt + 1); o[k++] = c.take<unsigned>(seg_capacity(m));
     o[k++] = c.take<R>(nv);
     o[k++] = c.take<R>(2 * nv > kColbufMin ? 2 * nv : kColbufMin);  // colbuf
     o[k++] = c.take<R>(8); o[k++] = c.take<int>(32); o[k++] = c.take<R>(32);  // red: one real per warp of a world
@@ -130,6 +140,7 @@ template <class R> struct Arena {
       B200_P(efc_type, int); B200_P(efc_id, int); B200_P(efc_state, int); B200_P(row_t, int);
       B200_P(tree_isl, int); B200_P(isl_n, int); B200_P(isl_off, int); B200_P(isl_dofstart, int);
       B200_P(isl_dof, int); B200_P(dof_isl, int); B200_P(dof_loc, int);
+      B200_P(tree_segadr, int); B200_P(tree_seg, unsigned);
       B200_P(xs, R); B200_P(colbuf, R);
       B200_P(scal, R); B200_P(iscal, int); B200_P(red, R); B200_P(prof, long long);
 #undef B200_P

@@ -606,6 +606,58 @@ template <class R> __device__ B200_STAGE_ATTR void islands(const Mdl<R> &M, Aren
   __syncwarp();
 }
 
+// Per-tree segment lists (warp 0, after row allocation): a segment is one
+// single-dof row or one contact's rows; each goes to the list of every tree
+// it acts on, in ascending row order.  Rows are taken 32 at a time, one per
+// lane; per tree a ballot selects the chunk's segments and lane t keeps tree
+// t's running count (first pass) or write position (second pass).
+template <class R> __device__ void tree_segments(const Mdl<R> &M, Arena<R> &A, int nsingle, int nefc) {
+  const int nt = M.m.ntree, lane = LANE;
+  const unsigned full = 0xffffffffu, below = (1u << lane) - 1u;
+  int mine = 0;  // lane t < nt: tree t's segment count, then its write position
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1) {
+      int incl = mine;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(full, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const int total = __shfl_sync(full, incl, 31);
+      mine = incl - mine;
+      if (lane < nt) A.tree_segadr[lane] = mine;
+      if (lane == 0) A.tree_segadr[nt] = total;
+    }
+    for (int base = 0; base < nefc; base += 32) {
+      const int r = base + lane;
+      int t0 = -1, t1 = -1;
+      unsigned code = 0, col1 = 0;
+      if (r < nefc) {
+        int len = 0;
+        if (r < nsingle) len = 1;
+        else {
+          const int c = A.efc_id[r];
+          if (A.con_adr[c] == r) len = A.efc_type[r] == 6 ? 2 * (A.con_dim[c] - 1) : A.con_dim[c];
+        }
+        if (len) {
+          t0 = A.row_t[2 * r];
+          t1 = A.row_t[2 * r + 1];
+          code = (unsigned)r | (unsigned)len << 16;
+          col1 = (unsigned)IF(tree_dofnum)[t0] << 24;
+        }
+      }
+      for (int t = 0; t < nt; ++t) {
+        const unsigned m0 = __ballot_sync(full, t0 == t), m1 = __ballot_sync(full, t1 == t), mm = m0 | m1;
+        if (pass == 1) {
+          const int pos = __shfl_sync(full, mine, t) + __popc(mm & below);
+          if ((mm >> lane) & 1u) A.tree_seg[pos] = code | ((m1 >> lane) & 1u ? col1 : 0u);
+        }
+        if (lane == t) mine += __popc(mm);
+      }
+    }
+  }
+  __syncwarp();
+}
+
 template <class R, int T> __device__ B200_STAGE_ATTR void constraints(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int cap = m.nefc_max, kmax = m.kmax_dof;
@@ -698,6 +750,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void constraints(const Mdl<
     }
     __syncwarp();
     islands(M, A, coupled);
+    tree_segments(M, A, A.iscal[13], end);
   }
   SYNC();
   const int nefc = A.iscal[1];
@@ -1371,10 +1424,11 @@ template <class R, int T> __device__ B200_STAGE_ATTR void eval_gradient(const Md
   FOR(i, nv) {
     R tot = 0;
     const int t = IF(dof_treeid)[i], off = i - IF(tree_dofadr)[t], kmax = m.kmax_dof;
-    for (int r = 0; r < nefc; ++r) {
-      const int t0 = A.row_t[2 * r];
-      if (t0 == t) tot += A.J[r * kmax + off] * A.efc_force[r];
-      else if (A.row_t[2 * r + 1] == t) tot += A.J[r * kmax + IF(tree_dofnum)[t0] + off] * A.efc_force[r];
+    // rows acting on the dof's tree, ascending (the same sum order as a scan of all rows)
+    for (int e = A.tree_segadr[t], end = A.tree_segadr[t + 1]; e < end; ++e) {
+      const unsigned sg = A.tree_seg[e];
+      const int r0 = sg & 0xffffu, len = (sg >> 16) & 0xffu, col = (int)(sg >> 24) + off;
+      for (int p = 0; p < len; ++p) tot += A.J[(r0 + p) * kmax + col] * A.efc_force[r0 + p];
     }
     A.qfrc_constraint[i] = tot;
     const R g = A.Ma[i] - A.qfrc_smooth[i] - tot;
@@ -1387,12 +1441,15 @@ template <class R, int T> __device__ B200_STAGE_ATTR void eval_gradient(const Md
 
 // H = M + J' D J over quadratic rows + elliptic-cone curvature
 // (mjwarp_hessian.cu:33-212), one dense block per island (lower triangle).
-// Assembly is block-structured: the mass blocks, then the single-dof rows
-// (friction loss, joint limits: J = +-1, so they add D on the diagonal), then
-// one pass per contact adding J_c' C J_c over the contact's dofs, where C is
-// diag(D) over its quadratic rows, or the elliptic-cone curvature matrix when
-// the contact is in the cone state.  Contacts run one after another, each
-// H entry of a contact on its own lane, so sums are deterministic.
+// One thread per H entry (a, b) of an island forms, in this order: the mass
+// entry; the D of the single-dof rows on the entry's dof (diagonal only);
+// then, contact by contact in ascending row order, J_c' C J_c over the
+// contacts acting on both dofs' trees.  C is diag(D) over the contact's
+// quadratic rows, or the elliptic-cone curvature matrix when the contact is in
+// the cone state.  Each contact term is evaluated over the contact-local dof
+// pair, larger index first, so every entry's sum is deterministic.  The cone
+// matrices' scalars are staged per contact in efc_quad, which the line search
+// rewrites before its next use.
 template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &M, Arena<R> &A) {
   // unchanged constraint states and no cone-state contact: H, and its factor
   // still held in A.H, are exactly what this assembly would produce again
@@ -1400,10 +1457,28 @@ template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &
   const B200Model &m = M.m;
   const int nisl = A.iscal[11], nsingle = A.iscal[13], ncon = A.iscal[0], kmax = m.kmax_dof;
   const R impratio = R(m.impratio_invsqrt);
+  // cone-state contacts: dm, mu^2 and mu n / t at the head row, u_p = jaref_p fr_p / t at friction row p
+  FOR(c, ncon) {
+    const int r0 = A.con_adr[c];
+    if (r0 < 0 || A.efc_type[r0] != 7 || A.con_dim[c] <= 1 || A.efc_state[r0] != kCone) continue;
+    const int dim = A.con_dim[c];
+    const R *fr = A.con + (size_t)c * kCWidth + kCFriction;
+    const R mu = fr[0] * impratio, mu2 = mu * mu, den = mu2 * (R(1) + mu2);
+    const R dm = A.efc_D[r0] / (den != R(0) ? den : R(1e-15));
+    R tt = 0;
+    for (int d = 1; d < dim; ++d) {
+      const R u = A.efc_jaref[r0 + d] * fr[d - 1];
+      tt += u * u;
+    }
+    const R t = mmax(msqrt(tt), R(1e-15)), it = R(1) / t, mnt = mu * (A.efc_jaref[r0] * mu) * it;
+    R *q = A.efc_quad + 3 * r0;
+    q[0] = dm; q[1] = mu2; q[2] = mnt;
+    for (int d = 1; d < dim; ++d) A.efc_quad[3 * (r0 + d)] = A.efc_jaref[r0 + d] * fr[d - 1] * it;
+  }
+  SYNC();
   int total = 0;
   for (int i = 0; i < nisl; ++i) total += A.isl_n[i] * (A.isl_n[i] + 1) / 2;
-  // mass blocks (the packed island blocks are contiguous, in island order)
-  FOR(e, total) {
+  FOR(e, total) {  // the packed island blocks are contiguous, in island order
     int isl = 0, base = 0;
     while (base + A.isl_n[isl] * (A.isl_n[isl] + 1) / 2 <= e) { base += A.isl_n[isl] * (A.isl_n[isl] + 1) / 2; ++isl; }
     const int loc = e - base;
@@ -1411,102 +1486,70 @@ template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &
     while (tri(a, 0) > loc) --a;
     while (tri(a + 1, 0) <= loc) ++a;
     const int b = loc - tri(a, 0);
-    A.H[A.isl_off[isl] + loc] =
-        mass_at(M, A.M, A.isl_dof[A.isl_dofstart[isl] + a], A.isl_dof[A.isl_dofstart[isl] + b]);
-  }
-  SYNC();
-  // single-dof rows: D on the diagonal of their dof
-  FOR(d, m.nv) {
+    const int da = A.isl_dof[A.isl_dofstart[isl] + a], db = A.isl_dof[A.isl_dofstart[isl] + b];
+    const int ta = IF(dof_treeid)[da], tb = IF(dof_treeid)[db];
+    const int oa = da - IF(tree_dofadr)[ta], ob = db - IF(tree_dofadr)[tb];
+    R h = mass_at(M, A.M, da, db);
+    int k = A.tree_segadr[ta];
+    const int kend = A.tree_segadr[ta + 1];
+    // single-dof rows lead the tree's list
     R add = 0;
-    for (int r = 0; r < nsingle; ++r) {
-      if (A.efc_state[r] != kQuadratic) continue;
+    for (; k < kend && (int)(A.tree_seg[k] & 0xffffu) < nsingle; ++k) {
+      const int r = A.tree_seg[k] & 0xffffu;
+      if (da != db || A.efc_state[r] != kQuadratic) continue;
       const int dof = A.efc_type[r] == 1 ? A.efc_id[r] : IF(jnt_dofadr)[A.efc_id[r]];
-      if (dof == d) add += A.efc_D[r];
+      if (dof == da) add += A.efc_D[r];
     }
-    if (add != R(0)) {
-      const int isl = A.dof_isl[d], l = A.dof_loc[d];
-      A.H[A.isl_off[isl] + tri(l, l)] += add;
-    }
-  }
-  SYNC();
-  // contacts: islands are dealt to the world's warps; a warp adds its
-  // islands' contacts one after another (each H entry of a contact on its
-  // own lane), so different warps never touch the same block
-  const int lane = LANE, wi = TID >> 5, nw = T / 32;
-  R *C = A.colbuf + 36 * wi;  // this warp's row coupling matrix (<= 6 x 6)
-  for (int c = 0; c < ncon; ++c) {
-    const int r0 = A.con_adr[c];
-    if (r0 < 0) continue;
-    const int isl = A.tree_isl[A.row_t[2 * r0]];
-    if (isl % nw != wi) continue;
-    const int type = A.efc_type[r0], dim = A.con_dim[c];
-    const int cnt = type == 6 ? 2 * (dim - 1) : dim;
-    bool full = false;
-    if (type == 7 && dim > 1) {
-      const int st = A.efc_state[r0];
-      if (st == kSatisfied) continue;
-      if (st == kCone) {
-        const R *fr = A.con + (size_t)c * kCWidth + kCFriction;
-        const R mu = fr[0] * impratio, mu2 = mu * mu, den = mu2 * (R(1) + mu2);
-        const R dm = A.efc_D[r0] / (den != R(0) ? den : R(1e-15));
-        if (dm == R(0)) continue;
-        R tt = 0;
-        for (int d = 1; d < dim; ++d) {
-          const R u = A.efc_jaref[r0 + d] * fr[d - 1];
-          tt += u * u;
-        }
-        const R t = mmax(msqrt(tt), R(1e-15)), it = R(1) / t, mnt = mu * (A.efc_jaref[r0] * mu) * it;
-        for (int z = lane; z < dim * dim; z += 32) {
-          const int p = z / dim, q = z - p * dim;
-          R v;
-          if (p == 0 && q == 0) v = mu2;
-          else if (p == 0 || q == 0) {
-            const int e = p + q;
-            v = -mu2 * (A.efc_jaref[r0 + e] * fr[e - 1] * it) * fr[e - 1];
-          } else {
-            const R up = A.efc_jaref[r0 + p] * fr[p - 1] * it, uq = A.efc_jaref[r0 + q] * fr[q - 1] * it;
-            v = mnt * up * fr[p - 1] * uq * fr[q - 1];
-            if (p == q) v += (mu2 - mnt) * fr[p - 1] * fr[p - 1];
-          }
-          C[z] = dm * v;
-        }
-        full = true;
-      }
-    }
-    if (!full) {
-      bool any = false;
-      for (int z = lane; z < cnt; z += 32) C[z] = A.efc_state[r0 + z] == kQuadratic ? A.efc_D[r0 + z] : R(0);
-      for (int z = 0; z < cnt; ++z) any |= A.efc_state[r0 + z] == kQuadratic;
-      if (!any) continue;
-    }
-    __syncwarp();
-    const int t0 = A.row_t[2 * r0], t1 = A.row_t[2 * r0 + 1];
-    const int n0 = IF(tree_dofnum)[t0], k = n0 + (t1 >= 0 ? IF(tree_dofnum)[t1] : 0);
-    const int a0 = IF(tree_dofadr)[t0], a1 = t1 >= 0 ? IF(tree_dofadr)[t1] : 0;
-    R *Hb = A.H + A.isl_off[isl];
-    const R *J = A.J + (size_t)r0 * kmax;
-    for (int e = lane; e < k * (k + 1) / 2; e += 32) {
-      int a = (int)((msqrt(8.0f * e + 1.0f) - 1.0f) * 0.5f);
-      while (a * (a + 1) / 2 > e) --a;
-      while ((a + 1) * (a + 2) / 2 <= e) ++a;
-      const int b = e - a * (a + 1) / 2;
+    if (add != R(0)) h += add;
+    for (; k < kend; ++k) {
+      const unsigned sg = A.tree_seg[k];
+      const int r0 = sg & 0xffffu, cnt = (sg >> 16) & 0xffu;
+      const int t0 = A.row_t[2 * r0], t1 = A.row_t[2 * r0 + 1];
+      if (tb != ta && tb != t0 && tb != t1) continue;
+      const int ca = (int)(sg >> 24) + oa;
+      const int cb = (tb == ta ? (int)(sg >> 24) : tb == t0 ? 0 : IF(tree_dofnum)[t0]) + ob;
+      const int x = ca >= cb ? ca : cb, y = ca >= cb ? cb : ca;
+      const int c = A.efc_id[r0], dim = A.con_dim[c];
+      const R *J = A.J + (size_t)r0 * kmax;
       R v = 0;
-      if (full) {
+      if (A.efc_type[r0] == 7 && dim > 1 && A.efc_state[r0] != kQuadratic) {
+        const int st = A.efc_state[r0];
+        if (st == kSatisfied) continue;
+        const R *q = A.efc_quad + 3 * r0;
+        const R dm = q[0], mu2 = q[1], mnt = q[2];
+        if (dm == R(0)) continue;
+        const R *fr = A.con + (size_t)c * kCWidth + kCFriction;
 #pragma unroll 1
         for (int p = 0; p < cnt; ++p) {
-          R cb = 0;
+          R cbv = 0;
 #pragma unroll 1
-          for (int q = 0; q < cnt; ++q) cb += C[p * cnt + q] * J[q * kmax + b];
-          v += J[p * kmax + a] * cb;
+          for (int qq = 0; qq < cnt; ++qq) {
+            R w;
+            if (p == 0 && qq == 0) w = mu2;
+            else if (p == 0 || qq == 0) {
+              const int ee = p + qq;
+              w = -mu2 * A.efc_quad[3 * (r0 + ee)] * fr[ee - 1];
+            } else {
+              w = mnt * A.efc_quad[3 * (r0 + p)] * fr[p - 1] * A.efc_quad[3 * (r0 + qq)] * fr[qq - 1];
+              if (p == qq) w += (mu2 - mnt) * fr[p - 1] * fr[p - 1];
+            }
+            cbv += (dm * w) * J[qq * kmax + y];
+          }
+          v += J[p * kmax + x] * cbv;
         }
       } else {
+        bool any = false;
 #pragma unroll 1
-        for (int p = 0; p < cnt; ++p) v += J[p * kmax + a] * C[p] * J[p * kmax + b];
+        for (int p = 0; p < cnt; ++p) {
+          const bool quad = A.efc_state[r0 + p] == kQuadratic;
+          any |= quad;
+          v += J[p * kmax + x] * (quad ? A.efc_D[r0 + p] : R(0)) * J[p * kmax + y];
+        }
+        if (!any) continue;
       }
-      const int la = A.dof_loc[a < n0 ? a0 + a : a1 + a - n0], lb = A.dof_loc[b < n0 ? a0 + b : a1 + b - n0];
-      Hb[la >= lb ? tri(la, lb) : tri(lb, la)] += v;
+      h += v;
     }
-    __syncwarp();
+    A.H[A.isl_off[isl] + loc] = h;
   }
   SYNC();
 }
