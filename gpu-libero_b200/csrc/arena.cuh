@@ -81,6 +81,7 @@ template <class R> struct Arena {
   // factorization blocks (H).  Each use ends before the next begins.
   __host__ __device__ static size_t layout(const B200Model &m, int threads, Arena *a, unsigned char *base) {
     Carve c;
+    c.at = sizeof(Arena);  // the descriptor itself heads the world's region
     const int nq = m.nq, nv = m.nv, nu = m.nu, nb = m.nbody, nj = m.njnt, ng = m.ngeom, ns = m.nsite;
     const int nc = m.ncon_max, ne = m.nefc_max, nt = m.ntree;
     size_t o[96];

@@ -378,6 +378,75 @@ __device__ void chol_blocks_reg(R *H, const BlockRows &b, int maxn, R *colbuf, i
   __syncwarp();
 }
 
+// Factor (optional) and solve L L^T x = x of a warp's blocks when each lane
+// owns at most one row (b.rows <= 32, blocks of at most MAXN): the lane's
+// row of L stays in registers, so the substitutions exchange the solved
+// entries by shuffles instead of shared memory and warp barriers.  The
+// operations and their order match chol_blocks_reg + solve_blocks.  xin: the
+// lane's entry of the right-hand side; returns its entry of the solution.
+template <class R, int MAXN>
+__device__ R chol_solve_reg(R *H, const BlockRows &b, int maxn, R *colbuf, int stride, bool factor, R xin) {
+  const int n = b.n[0], a = b.a[0], lane = LANE;
+  const unsigned full = 0xffffffffu;
+  R row[MAXN];
+#pragma unroll
+  for (int j = 0; j < MAXN; ++j) row[j] = (n > 0 && j <= a && j < n) ? H[b.base[0] + tri(a, j)] : R(0);
+  if (factor) {
+    for (int k = 0; k < maxn; ++k) {
+      R *col = colbuf + (k & 1) * stride;
+      R rk = 0;
+#pragma unroll
+      for (int j = 0; j < MAXN; ++j)
+        if (j == k) rk = row[j];
+      if (n > k && a == k) col[b.start[0] + k] = msqrt(rk);
+      __syncwarp();
+      if (n > k && a > k) {
+        const R l = rk / col[b.start[0] + k];
+        col[b.start[0] + a] = l;
+#pragma unroll
+        for (int j = 0; j < MAXN; ++j)
+          if (j == k) row[j] = l;
+      } else if (n > k && a == k) {
+#pragma unroll
+        for (int j = 0; j < MAXN; ++j)
+          if (j == k) row[j] = col[b.start[0] + k];
+      }
+      __syncwarp();
+      if (n > k && a > k) {
+        const R l = col[b.start[0] + a];
+#pragma unroll
+        for (int j = 0; j < MAXN; ++j)
+          if (j > k && j <= a) row[j] -= l * col[b.start[0] + j];
+      }
+    }
+    if (n > 0) {
+#pragma unroll
+      for (int j = 0; j < MAXN; ++j)
+        if (j <= a && j < n) H[b.base[0] + tri(a, j)] = row[j];
+    }
+  }
+  R x = xin;
+  // forward: L y = x
+#pragma unroll
+  for (int k = 0; k < MAXN; ++k) {
+    if (k >= maxn) break;
+    if (n > k && a == k) x /= row[k];
+    const R xk = __shfl_sync(full, x, (lane - a + k) & 31);
+    if (n > k && a > k) x -= row[k] * xk;
+  }
+  // backward: L^T x = y; column entries of L come from shared memory
+#pragma unroll
+  for (int k = MAXN - 1; k >= 0; --k) {
+    if (k >= maxn) continue;
+    const R lka = (n > k && a < k) ? H[b.base[0] + tri(k, a)] : R(0);
+    if (n > k && a == k) x /= row[k];
+    const R xk = __shfl_sync(full, x, (lane - a + k) & 31);
+    if (n > k && a < k) x -= lka * xk;
+  }
+  __syncwarp();
+  return x;
+}
+
 // colbuf: 2 x nv reals (the register variant's double-buffered column, indexed by position)
 template <class R> __device__ B200_STAGE_ATTR void chol_blocks(R *H, const BlockRows &b, int maxn, int nv, R *colbuf) {
 #ifndef B200_CHOL_SMEM
@@ -409,6 +478,24 @@ template <class R> __device__ B200_STAGE_ATTR void solve_blocks(const R *H, cons
       if (b.n[s] > k && b.a[s] < k) x[b.start[s] + b.a[s]] -= H[b.base[s] + tri(k, b.a[s])] * x[b.start[s] + k];
     __syncwarp();
   }
+}
+
+// L L^T x = x over the kinematic-tree blocks (positions are dofs), factoring
+// first when `factor`; registers and shuffles when each lane owns at most one row
+template <class R, int T> __device__ void tree_solve(const Mdl<R> &M, R *L, R *x, R *colbuf, bool factor) {
+  const BlockRows b = TREE_ROWS(T);
+  const int maxn = M.m.max_tree_dofs;
+#ifndef B200_CHOL_SMEM
+  if (b.rows <= 32 && maxn <= 16) {
+    const int p = b.start[0] + b.a[0];
+    const R v = chol_solve_reg<R, 16>(L, b, maxn, colbuf, M.m.nv, factor, b.n[0] > 0 ? x[p] : R(0));
+    if (b.n[0] > 0) x[p] = v;
+    __syncwarp();
+    return;
+  }
+#endif
+  if (factor) chol_blocks_smem(L, b, maxn);
+  solve_blocks(L, b, x, maxn, LANE);
 }
 
 // lower triangles of the dense tree blocks of M into packed blocks at tree_padr
@@ -608,11 +695,13 @@ template <class R> __device__ B200_STAGE_ATTR void islands(const Mdl<R> &M, Aren
 
 // Per-tree segment lists (warp 0, after row allocation): a segment is one
 // single-dof row or one contact's rows; each goes to the list of every tree
-// it acts on, in ascending row order.  Rows are taken 32 at a time, one per
-// lane; per tree a ballot selects the chunk's segments and lane t keeps tree
-// t's running count (first pass) or write position (second pass).
-template <class R> __device__ void tree_segments(const Mdl<R> &M, Arena<R> &A, int nsingle, int nefc) {
-  const int nt = M.m.ntree, lane = LANE;
+// it acts on, in ascending row order.  Segments are taken 32 at a time, one
+// per lane (the single-dof rows, then the contacts in their sorted order,
+// which is their row order); per tree present in the chunk a ballot selects
+// its segments, and lane t keeps tree t's running count (first pass) or
+// write position (second pass).
+template <class R> __device__ void tree_segments(const Mdl<R> &M, Arena<R> &A, int nsingle, int ncon) {
+  const int nt = M.m.ntree, lane = LANE, items = nsingle + ncon;
   const unsigned full = 0xffffffffu, below = (1u << lane) - 1u;
   int mine = 0;  // lane t < nt: tree t's segment count, then its write position
   for (int pass = 0; pass < 2; ++pass) {
@@ -627,16 +716,16 @@ template <class R> __device__ void tree_segments(const Mdl<R> &M, Arena<R> &A, i
       if (lane < nt) A.tree_segadr[lane] = mine;
       if (lane == 0) A.tree_segadr[nt] = total;
     }
-    for (int base = 0; base < nefc; base += 32) {
-      const int r = base + lane;
+    for (int base = 0; base < items; base += 32) {
+      const int i = base + lane;
       int t0 = -1, t1 = -1;
       unsigned code = 0, col1 = 0;
-      if (r < nefc) {
-        int len = 0;
-        if (r < nsingle) len = 1;
-        else {
-          const int c = A.efc_id[r];
-          if (A.con_adr[c] == r) len = A.efc_type[r] == 6 ? 2 * (A.con_dim[c] - 1) : A.con_dim[c];
+      if (i < items) {
+        int r = i, len = i < nsingle ? 1 : 0;
+        if (!len) {
+          const int c = A.con_order[i - nsingle];
+          r = A.con_adr[c];
+          if (r >= 0) len = A.efc_type[r] == 6 ? 2 * (A.con_dim[c] - 1) : A.con_dim[c];
         }
         if (len) {
           t0 = A.row_t[2 * r];
@@ -645,7 +734,10 @@ template <class R> __device__ void tree_segments(const Mdl<R> &M, Arena<R> &A, i
           col1 = (unsigned)IF(tree_dofnum)[t0] << 24;
         }
       }
-      for (int t = 0; t < nt; ++t) {
+      unsigned present = __reduce_or_sync(full, (t0 >= 0 ? 1u << t0 : 0u) | (t1 >= 0 ? 1u << t1 : 0u));
+      while (present) {
+        const int t = __ffs(present) - 1;
+        present &= present - 1u;
         const unsigned m0 = __ballot_sync(full, t0 == t), m1 = __ballot_sync(full, t1 == t), mm = m0 | m1;
         if (pass == 1) {
           const int pos = __shfl_sync(full, mine, t) + __popc(mm & below);
@@ -750,7 +842,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void constraints(const Mdl<
     }
     __syncwarp();
     islands(M, A, coupled);
-    tree_segments(M, A, A.iscal[13], end);
+    tree_segments(M, A, A.iscal[13], ncon);
   }
   SYNC();
   const int nefc = A.iscal[1];
@@ -1372,7 +1464,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void actuation(const Mdl<R>
     A.qacc_smooth[d] = A.qfrc_smooth[d];
   }
   SYNC();
-  solve_blocks(A.L, TREE_ROWS(T), A.qacc_smooth, m.max_tree_dofs, LANE);
+  tree_solve<R, T>(M, A.L, A.qacc_smooth, A.colbuf, false);
   SYNC();
 }
 
@@ -1562,14 +1654,26 @@ template <class R, int T> __device__ B200_STAGE_ATTR void direction(const Mdl<R>
   const int lane = LANE, maxn = A.iscal[12];
   const bool refactor = A.iscal[14];
   const BlockRows b = ISLAND_ROWS(T);
+#ifndef B200_CHOL_SMEM
+  const bool reg = b.rows <= 32 && maxn <= 16;
+#else
+  const bool reg = false;
+#endif
+  if (reg) {  // one row per lane: factor and solve in registers
+    const int p = b.start[0] + b.a[0];
+    const R xv = chol_solve_reg<R, 16>(A.H, b, maxn, A.colbuf, nv, refactor, b.n[0] > 0 ? A.grad[A.isl_dof[p]] : R(0));
+    if (b.n[0] > 0) x[p] = xv;
+  } else {
 #pragma unroll
-  for (int s = 0; s < 4; ++s)
-    if (b.n[s] > 0) {
-      const int p = b.start[s] + b.a[s];
-      x[p] = A.grad[A.isl_dof[p]];
-    }
-  __syncwarp();
-  if (refactor) chol_blocks(A.H, b, maxn, nv, A.colbuf);
+    for (int s = 0; s < 4; ++s)
+      if (b.n[s] > 0) {
+        const int p = b.start[s] + b.a[s];
+        x[p] = A.grad[A.isl_dof[p]];
+      }
+    __syncwarp();
+    if (refactor) chol_blocks_smem(A.H, b, maxn);
+    solve_blocks(A.H, b, x, maxn, lane);
+  }
   if (TID == 0) {
     // FLOP counter, 3x the executed block work: n^3 + 6 n^2 when a block is
     // factored and solved, 6 n^2 when its factor is reused
@@ -1577,7 +1681,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void direction(const Mdl<R>
     for (int i = 0; i < A.iscal[11]; ++i) blk += A.isl_n[i] * A.isl_n[i] * (refactor ? A.isl_n[i] + 6 : 6);
     A.iscal[24] += blk;
   }
-  solve_blocks(A.H, b, x, maxn, lane);
+  __syncwarp();
   R sq = 0, dec = 0;
 #pragma unroll
   for (int s = 0; s < 4; ++s)
@@ -1908,9 +2012,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void euler(const Mdl<R> &M,
       acc[d] = A.Ma[d];
     }
     SYNC();
-    const BlockRows b = TREE_ROWS(T);
-    chol_blocks(A.H, b, m.max_tree_dofs, nv, A.colbuf);
-    solve_blocks(A.H, b, acc, m.max_tree_dofs, LANE);
+    tree_solve<R, T>(M, A.H, acc, A.colbuf, true);
   } else
     FOR(d, nv) acc[d] = A.qacc[d];
   SYNC();
@@ -2122,14 +2224,18 @@ template <class R, int T> __device__ void newton_stages(const Mdl<R> &M, Arena<R
 }
 
 template <class R, bool CONVEX, int T>
-__global__ void __launch_bounds__(384, 1) control_step(const B200Model m, const B200Data d, int substeps, int policy, int wpc,
-                                                     int arena) {
+__global__ void __launch_bounds__(384, 1) control_step(const __grid_constant__ B200Model m, const __grid_constant__ B200Data d,
+                                                     int substeps, int policy, int wpc, int arena) {
   static_assert(T % 32 == 0 && T / 32 <= Arena<R>::kColbufWarps, "per-warp scratch covers at most four warps");
   extern __shared__ __align__(16) unsigned char smem[];
   const int slot = threadIdx.x / T, w = blockIdx.x * wpc + slot;
   const bool act = slot < wpc && w < d.nworld;
-  Arena<R> A;
-  Arena<R>::layout(m, T, &A, smem + (size_t)(slot < wpc ? slot : 0) * arena);
+  // the world's arena descriptor heads its shared-memory region (one copy per
+  // world, read by broadcast instead of a per-thread local-memory copy)
+  unsigned char *wbase = smem + (size_t)(slot < wpc ? slot : 0) * arena;
+  Arena<R> &A = *reinterpret_cast<Arena<R> *>(wbase);
+  if (slot < wpc && TID == 0) Arena<R>::layout(m, T, &A, wbase);
+  __syncthreads();
   const Mdl<R> M(m);
   if (act) {
     load_world<R, T>(m, d, A, w);
@@ -2179,13 +2285,15 @@ __global__ void __launch_bounds__(384, 1) control_step(const B200Model m, const 
 }
 
 template <class R, bool CONVEX, int T>
-__global__ void __launch_bounds__(384, 1) forward_step(const B200Model m, const B200Data d, int bootstrap, const int *mask,
-                                                     int wpc, int arena) {
+__global__ void __launch_bounds__(384, 1) forward_step(const __grid_constant__ B200Model m, const __grid_constant__ B200Data d,
+                                                     int bootstrap, const int *mask, int wpc, int arena) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int slot = threadIdx.x / T, w = blockIdx.x * wpc + slot;
   const bool act = slot < wpc && w < d.nworld && (!mask || mask[w]);
-  Arena<R> A;
-  Arena<R>::layout(m, T, &A, smem + (size_t)(slot < wpc ? slot : 0) * arena);
+  unsigned char *wbase = smem + (size_t)(slot < wpc ? slot : 0) * arena;
+  Arena<R> &A = *reinterpret_cast<Arena<R> *>(wbase);
+  if (slot < wpc && TID == 0) Arena<R>::layout(m, T, &A, wbase);
+  __syncthreads();
   const Mdl<R> M(m);
   if (act) load_world<R, T>(m, d, A, w);
   __syncthreads();
