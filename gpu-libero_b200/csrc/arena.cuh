@@ -63,7 +63,7 @@ template <class R> struct Arena {
                // [11] islands [12] largest island [13] single-dof rows [14] refactor Newton H
                // [15] sum of row widths k_r [16..19] OSC factor flags [20..22] pinv flags
                // [23] sum of k_r^2 [24] factored block work (n^3 + 6 n^2)
-  R *red;    // reduction scratch (one real per warp of the world)
+  R *red;    // reduction scratch: up to 9 values per warp of the world
   long long *prof;  // [0] last stamp, [1..15] per-stage cycle sums (stage profiling only)
   int ubytes;       // size of the stage-scoped union region (H, OSC and kinematics scratch)
 
@@ -72,7 +72,7 @@ template <class R> struct Arena {
   __host__ __device__ static int seg_capacity(const B200Model &m) { return m.nfric + m.nlimited + 2 * m.ncon_max; }
   // colbuf holds the Cholesky column buffers (2 x nv) or one 6 x 6 contact
   // coupling matrix per warp of a world (at most four warps)
-  static constexpr int kColbufWarps = 4, kColbufMin = 160;
+  static constexpr int kColbufWarps = 4, kColbufMin = 160, kRed = 9 * kColbufWarps;
   static_assert(kColbufWarps * 36 <= kColbufMin, "colbuf holds a 6 x 6 matrix per warp");
 
   // Stage-scoped arrays share one region (U): kinematics -> CRB scratch
@@ -108,7 +108,7 @@ template <class R> struct Arena {
     o[k++] = c.take<int>(nt + 1); o[k++] = c.take<unsigned>(seg_capacity(m));
     o[k++] = c.take<R>(nv);
     o[k++] = c.take<R>(2 * nv > kColbufMin ? 2 * nv : kColbufMin);  // colbuf
-    o[k++] = c.take<R>(8); o[k++] = c.take<int>(32); o[k++] = c.take<R>(32);  // red: one real per warp of a world
+    o[k++] = c.take<R>(8); o[k++] = c.take<int>(32); o[k++] = c.take<R>(kRed);
     o[k++] = c.take<long long>(16);
     // union region
     const size_t kin = (size_t)(nb * 3 + nb * 9 + nj * 3 + nj * 3 + nb * 10) * sizeof(R) + 5 * 16;

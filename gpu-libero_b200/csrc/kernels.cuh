@@ -71,6 +71,26 @@ template <class R> __device__ __forceinline__ R warp_sum(R v) {
   return v;
 }
 
+// N sums over the world's threads in one reduction: warp shuffles, then the
+// warps' partials summed in warp order; red: N * T / 32 values of scratch
+template <int T, int N, class V> __device__ __forceinline__ void world_sums(V (&v)[N], V *red) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = warp_sum(v[i]);
+  if (T == 32) return;
+  SYNC();
+  if (LANE == 0) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) red[(TID >> 5) * N + i] = v[i];
+  }
+  SYNC();
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    V s = 0;
+    for (int k = 0; k < T / 32; ++k) s += red[k * N + i];
+    v[i] = s;
+  }
+}
+
 // sum over the world's threads; red: T / 32 reals of scratch
 template <int T, class R> __device__ __forceinline__ R world_sum(R v, R *red) {
   v = warp_sum(v);
@@ -627,9 +647,9 @@ template <class R> __device__ __forceinline__ void set_row_trees(const Mdl<R> &M
 
 // Islands: kinematic trees coupled by a two-tree constraint row share one
 // Newton Hessian block.  Warp 0.  Without coupling rows every tree is its own
-// island and the tree layout is reused (packed blocks at tree_padr).  Otherwise lane
-// 0 unions trees over the coupled contacts; island ids follow the smallest
-// tree index, so the blocks are deterministic.
+// island and the tree layout is reused (packed blocks at tree_padr).
+// Otherwise the coupled contacts join trees into components, numbered by
+// their smallest tree index, so the blocks are deterministic.
 template <class R> __device__ B200_STAGE_ATTR void islands(const Mdl<R> &M, Arena<R> &A, bool coupled) {
   const int nt = M.m.ntree, nv = M.m.nv, lane = LANE;
   if (!coupled) {
@@ -648,35 +668,63 @@ template <class R> __device__ B200_STAGE_ATTR void islands(const Mdl<R> &M, Aren
     __syncwarp();
     return;
   }
+  // lane t < nt: tree t.  Adjacency masks from the contacts that couple two
+  // trees, then components by merging neighbours' masks until stable (each
+  // round doubles the path length covered); a component's root is its
+  // smallest tree, and islands are numbered in root order.
+  const unsigned full = 0xffffffffu;
+  const int ncon = A.iscal[0];
+  unsigned adj = lane < nt ? 1u << lane : 0u;
+  for (int base = 0; base < ncon; base += 32) {
+    const int k = base + lane;
+    int ta = -1, tb = -1;
+    if (k < ncon) {
+      const int r0 = A.con_adr[A.con_order[k]];
+      if (r0 >= 0) { ta = A.row_t[2 * r0]; tb = A.row_t[2 * r0 + 1]; }
+    }
+    unsigned pending = __ballot_sync(full, tb >= 0);
+    while (pending) {
+      const int src = __ffs(pending) - 1;
+      pending &= pending - 1u;
+      const int a = __shfl_sync(full, ta, src), bb = __shfl_sync(full, tb, src);
+      if (lane == a) adj |= 1u << bb;
+      if (lane == bb) adj |= 1u << a;
+    }
+  }
+  unsigned comp = adj;
+  for (bool grew = true; grew;) {
+    unsigned merged = comp;
+    for (int u = 0; u < nt; ++u) {
+      const unsigned mu = __shfl_sync(full, comp, u);
+      if ((comp >> u) & 1u) merged |= mu;
+    }
+    grew = __any_sync(full, merged != comp);
+    comp = merged;
+  }
+  const int dn = lane < nt ? IF(tree_dofnum)[lane] : 0, root = lane < nt ? __ffs(comp) - 1 : 0;
+  const unsigned roots = __ballot_sync(full, lane < nt && root == lane);
+  int n = 0;  // dofs of the component (meaningful at its root)
+  for (int u = 0; u < nt; ++u) {
+    const int v = __shfl_sync(full, dn, u);
+    if ((comp >> u) & 1u) n += v;
+  }
+  const bool is_root = (roots >> lane) & 1u;
+  int at = is_root ? n : 0, off = is_root ? n * (n + 1) / 2 : 0;
+  for (int o = 1; o < 32; o <<= 1) {  // inclusive scans over the roots in tree order
+    const int x = __shfl_up_sync(full, at, o), y = __shfl_up_sync(full, off, o);
+    if (lane >= o) { at += x; off += y; }
+  }
+  const int isl = __popc(roots & ((1u << root) - 1u));
+  if (lane < nt) A.tree_isl[lane] = isl;
+  if (is_root) {
+    A.isl_n[isl] = n;
+    A.isl_dofstart[isl] = at - n;
+    A.isl_off[isl] = off - n * (n + 1) / 2;
+  }
+  const int maxn = __reduce_max_sync(full, is_root ? n : 0);
   if (lane == 0) {
-    int par[32], root_isl[32];
-    for (int t = 0; t < nt; ++t) { par[t] = t; root_isl[t] = -1; }
-    const int nefc = A.iscal[1];
-    for (int r = 0; r < nefc; ++r) {
-      const int a = A.row_t[2 * r], b = A.row_t[2 * r + 1];
-      if (a < 0 || b < 0) continue;
-      int ra = a, rb = b;
-      while (par[ra] != ra) ra = par[ra];
-      while (par[rb] != rb) rb = par[rb];
-      if (ra != rb) par[ra > rb ? ra : rb] = ra < rb ? ra : rb;
-    }
-    int nisl = 0;
-    for (int t = 0; t < nt; ++t) {
-      int r = t;
-      while (par[r] != r) r = par[r];
-      if (root_isl[r] < 0) { root_isl[r] = nisl; A.isl_n[nisl] = 0; ++nisl; }
-      A.tree_isl[t] = root_isl[r];
-      A.isl_n[root_isl[r]] += IF(tree_dofnum)[t];
-    }
-    int at = 0, off = 0, maxn = 0;
-    for (int i = 0; i < nisl; ++i) {
-      A.isl_dofstart[i] = at;
-      A.isl_off[i] = off;
-      at += A.isl_n[i];
-      off += A.isl_n[i] * (A.isl_n[i] + 1) / 2;
-      maxn = A.isl_n[i] > maxn ? A.isl_n[i] : maxn;
-    }
-    A.isl_dofstart[nisl] = at;
+    const int nisl = __popc(roots);
+    A.isl_dofstart[nisl] = nv;
     A.iscal[11] = nisl;
     A.iscal[12] = maxn;
   }
@@ -947,9 +995,9 @@ template <class R, int T> __device__ B200_STAGE_ATTR void constraints(const Mdl<
       }
     }
   }
-  ksum = world_sum<T>(ksum, (int *)A.red);
-  k2sum = world_sum<T>(k2sum, (int *)A.red);
-  if (TID == 0) { A.iscal[15] = ksum; A.iscal[23] = k2sum; }
+  int ks[2] = {ksum, k2sum};
+  world_sums<T>(ks, (int *)A.red);
+  if (TID == 0) { A.iscal[15] = ks[0]; A.iscal[23] = ks[1]; }
   SYNC();
 }
 
@@ -1691,9 +1739,9 @@ template <class R, int T> __device__ B200_STAGE_ATTR void direction(const Mdl<R>
       sq += x[p] * x[p];
       dec += A.grad[d] * x[p];
     }
-  sq = world_sum<T>(sq, A.red);
-  dec = world_sum<T>(dec, A.red);
-  if (TID == 0) { A.scal[2] = sq; A.scal[4] = dec; }
+  R sd[2] = {sq, dec};
+  world_sums<T>(sd, A.red);
+  if (TID == 0) { A.scal[2] = sd[0]; A.scal[4] = sd[1]; }
   SYNC();
   if (TID == 0) A.iscal[14] = 0;  // H holds the factor of the current states
 }
@@ -1867,11 +1915,13 @@ template <class R, int T> __device__ B200_STAGE_ATTR void linesearch(const Mdl<R
       g1 += A.search[i] * (A.Ma[i] - A.qfrc_smooth[i]);
       g2 += R(0.5) * A.search[i] * A.Mv[i];
     }
-    g1 = world_sum<T>(g1, A.red);
-    g2 = world_sum<T>(g2, A.red);
     Pt<R> loc = {0, 0, 0};
     FOR(r, nefc) loc = padd(loc, eval_zero(load_row(M, A, r, nf)));
-    const Pt<R> rows = world_pt<T>(loc, A.red);
+    R v5[5] = {g1, g2, loc.cost, loc.slope, loc.curv};
+    world_sums<T>(v5, A.red);
+    g1 = v5[0];
+    g2 = v5[1];
+    const Pt<R> rows = {v5[2], v5[3], v5[4]};
     int evals = 1;
     const Pt<R> p0 = {rows.cost, g1 + rows.slope, R(2) * g2 + rows.curv};
     const Pt<R> delta = {0, p0.slope, p0.curv};
@@ -1902,9 +1952,11 @@ template <class R, int T> __device__ B200_STAGE_ATTR void linesearch(const Mdl<R
           sh = padd(sh, eval_shift(row, hn));
           sm = padd(sm, eval_shift(row, ma));
         }
-        const Pt<R> nl = padd(quadratic(g1, g2, ln), world_pt<T>(sl, A.red));
-        const Pt<R> nh = padd(quadratic(g1, g2, hn), world_pt<T>(sh, A.red));
-        const Pt<R> mid = padd(quadratic(g1, g2, ma), world_pt<T>(sm, A.red));
+        R v9[9] = {sl.cost, sl.slope, sl.curv, sh.cost, sh.slope, sh.curv, sm.cost, sm.slope, sm.curv};
+        world_sums<T>(v9, A.red);
+        const Pt<R> nl = padd(quadratic(g1, g2, ln), Pt<R>{v9[0], v9[1], v9[2]});
+        const Pt<R> nh = padd(quadratic(g1, g2, hn), Pt<R>{v9[3], v9[4], v9[5]});
+        const Pt<R> mid = padd(quadratic(g1, g2, ma), Pt<R>{v9[6], v9[7], v9[8]});
         evals += 3;
         const bool cl = mabs(nl.slope) < gacc && nl.cost < R(0), ch = mabs(nh.slope) < gacc && nh.cost < R(0);
         const bool cm = mabs(mid.slope) < gacc && mid.cost < R(0);
