@@ -368,19 +368,18 @@ __device__ void chol_blocks_reg(R *H, const BlockRows &b, int maxn, R *colbuf, i
       if (j == k) rk = row[j];
     if (n > k && a == k) {
       const R d = msqrt(rk);
-      col[b.start[0] + k] = d;  // pivot, read by the rows below
+      col[b.start[0] + k] = R(1) / d;  // the pivot's reciprocal, read by the rows below
+#pragma unroll
+      for (int j = 0; j < MAXN; ++j)
+        if (j == k) row[j] = d;
     }
     __syncwarp();
     if (n > k && a > k) {
-      const R l = rk / col[b.start[0] + k];
+      const R l = rk * col[b.start[0] + k];
       col[b.start[0] + a] = l;
 #pragma unroll
       for (int j = 0; j < MAXN; ++j)
         if (j == k) row[j] = l;
-    } else if (n > k && a == k) {
-#pragma unroll
-      for (int j = 0; j < MAXN; ++j)
-        if (j == k) row[j] = col[b.start[0] + k];
     }
     __syncwarp();
     if (n > k && a > k) {
@@ -401,9 +400,10 @@ __device__ void chol_blocks_reg(R *H, const BlockRows &b, int maxn, R *colbuf, i
 // Factor (optional) and solve L L^T x = x of a warp's blocks when each lane
 // owns at most one row (b.rows <= 32, blocks of at most MAXN): the lane's
 // row of L stays in registers, so the substitutions exchange the solved
-// entries by shuffles instead of shared memory and warp barriers.  The
-// operations and their order match chol_blocks_reg + solve_blocks.  xin: the
-// lane's entry of the right-hand side; returns its entry of the solution.
+// entries by shuffles instead of shared memory and warp barriers.  Each
+// pivot's reciprocal is formed once, so the serial chains multiply instead
+// of divide.  xin: the lane's entry of the right-hand side; returns its
+// entry of the solution.
 template <class R, int MAXN>
 __device__ R chol_solve_reg(R *H, const BlockRows &b, int maxn, R *colbuf, int stride, bool factor, R xin) {
   const int n = b.n[0], a = b.a[0], lane = LANE;
@@ -411,6 +411,7 @@ __device__ R chol_solve_reg(R *H, const BlockRows &b, int maxn, R *colbuf, int s
   R row[MAXN];
 #pragma unroll
   for (int j = 0; j < MAXN; ++j) row[j] = (n > 0 && j <= a && j < n) ? H[b.base[0] + tri(a, j)] : R(0);
+  R rinv = 0;  // 1 / the pivot of the lane's row
   if (factor) {
     for (int k = 0; k < maxn; ++k) {
       R *col = colbuf + (k & 1) * stride;
@@ -418,18 +419,21 @@ __device__ R chol_solve_reg(R *H, const BlockRows &b, int maxn, R *colbuf, int s
 #pragma unroll
       for (int j = 0; j < MAXN; ++j)
         if (j == k) rk = row[j];
-      if (n > k && a == k) col[b.start[0] + k] = msqrt(rk);
+      if (n > k && a == k) {
+        const R d = msqrt(rk);
+        rinv = R(1) / d;
+        col[b.start[0] + k] = rinv;
+#pragma unroll
+        for (int j = 0; j < MAXN; ++j)
+          if (j == k) row[j] = d;
+      }
       __syncwarp();
       if (n > k && a > k) {
-        const R l = rk / col[b.start[0] + k];
+        const R l = rk * col[b.start[0] + k];
         col[b.start[0] + a] = l;
 #pragma unroll
         for (int j = 0; j < MAXN; ++j)
           if (j == k) row[j] = l;
-      } else if (n > k && a == k) {
-#pragma unroll
-        for (int j = 0; j < MAXN; ++j)
-          if (j == k) row[j] = col[b.start[0] + k];
       }
       __syncwarp();
       if (n > k && a > k) {
@@ -445,12 +449,17 @@ __device__ R chol_solve_reg(R *H, const BlockRows &b, int maxn, R *colbuf, int s
         if (j <= a && j < n) H[b.base[0] + tri(a, j)] = row[j];
     }
   }
+  else if (n > 0) {
+#pragma unroll
+    for (int j = 0; j < MAXN; ++j)
+      if (j == a) rinv = R(1) / row[j];
+  }
   R x = xin;
   // forward: L y = x
 #pragma unroll
   for (int k = 0; k < MAXN; ++k) {
     if (k >= maxn) break;
-    if (n > k && a == k) x /= row[k];
+    if (n > k && a == k) x *= rinv;
     const R xk = __shfl_sync(full, x, (lane - a + k) & 31);
     if (n > k && a > k) x -= row[k] * xk;
   }
@@ -459,7 +468,7 @@ __device__ R chol_solve_reg(R *H, const BlockRows &b, int maxn, R *colbuf, int s
   for (int k = MAXN - 1; k >= 0; --k) {
     if (k >= maxn) continue;
     const R lka = (n > k && a < k) ? H[b.base[0] + tri(k, a)] : R(0);
-    if (n > k && a == k) x /= row[k];
+    if (n > k && a == k) x *= rinv;
     const R xk = __shfl_sync(full, x, (lane - a + k) & 31);
     if (n > k && a < k) x -= lka * xk;
   }
@@ -1139,10 +1148,10 @@ static __device__ void chol_warp(double *a, int n, int ld, int lane, int *bad) {
     if (!(p > 1e-12 * dmax)) {
       if (lane == 0) *bad = 1;
     }
-    const double d = sqrt(fmax(p, 1e-300));
+    const double d = sqrt(fmax(p, 1e-300)), inv = 1.0 / d;
     __syncwarp();
     if (lane == k) a[k * ld + k] = d;
-    else if (lane > k && lane < n) a[lane * ld + k] /= d;
+    else if (lane > k && lane < n) a[lane * ld + k] *= inv;
     __syncwarp();
     if (lane > k && lane < n)
       for (int j = k + 1; j <= lane; ++j) a[lane * ld + j] -= a[lane * ld + k] * a[j * ld + k];
@@ -1310,16 +1319,20 @@ template <class R, int T> __device__ B200_STAGE_ATTR void osc_control(const Mdl<
     chol_warp(L7, 7, 7, lane, &flags[0]);
     if (lane < 6) {  // column c of M^-1 J^T
       const int c = lane;
-      double y[7];
+      double y[7], id[7];
+#pragma unroll
+      for (int i = 0; i < 7; ++i) id[i] = 1.0 / L7[i * 7 + i];
+#pragma unroll
       for (int i = 0; i < 7; ++i) {
         double v = S[osc::kJ + c * 7 + i];
         for (int k = 0; k < i; ++k) v -= L7[i * 7 + k] * y[k];
-        y[i] = v / L7[i * 7 + i];
+        y[i] = v * id[i];
       }
+#pragma unroll
       for (int i = 6; i >= 0; --i) {
         double v = y[i];
         for (int k = i + 1; k < 7; ++k) v -= L7[k * 7 + i] * y[k];
-        y[i] = v / L7[i * 7 + i];
+        y[i] = v * id[i];
       }
       for (int i = 0; i < 7; ++i) S[osc::kMJT + i * 6 + c] = y[i];
     }
@@ -1343,16 +1356,20 @@ template <class R, int T> __device__ B200_STAGE_ATTR void osc_control(const Mdl<
     // full inverse: lane c solves A x = e_c; 3x3 blocks by the adjugate
     if (lane < 6) {
       const int c = lane;
-      double y[6];
+      double y[6], id[6];
+#pragma unroll
+      for (int i = 0; i < 6; ++i) id[i] = 1.0 / LA[i * 6 + i];
+#pragma unroll
       for (int i = 0; i < 6; ++i) {
         double v = i == c ? 1.0 : 0.0;
         for (int k = 0; k < i; ++k) v -= LA[i * 6 + k] * y[k];
-        y[i] = v / LA[i * 6 + i];
+        y[i] = v * id[i];
       }
+#pragma unroll
       for (int i = 5; i >= 0; --i) {
         double v = y[i];
         for (int k = i + 1; k < 6; ++k) v -= LA[k * 6 + i] * y[k];
-        y[i] = v / LA[i * 6 + i];
+        y[i] = v * id[i];
       }
       for (int i = 0; i < 6; ++i) S[osc::kLf + i * 6 + c] = y[i];
     } else if (lane >= 8 && lane < 26) {
