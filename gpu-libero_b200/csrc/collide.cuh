@@ -659,9 +659,9 @@ __device__ __noinline__ void plane_mesh(const Mdl<R> &M, Arena<R> &A, const Mate
 // The reference's CCD contract (mjwarp_convex_collision.cuh:46-78,
 // mjwarp_convex_epa.cuh gjk_phase): supports inflated by half the pair margin
 // on each shape, sphere / capsule cores first, GJK distance with a separation
-// cutoff, EPA for penetration, one contact at the witness midpoint.  The
-// distance subalgorithm searches the sub-simplices that contain the newest
-// support point; EPA is the expanding polytope method (van den Bergen 2001).  One thread
+// cutoff, EPA for penetration, one contact at the witness midpoint.  GJK's
+// distance subalgorithm is the signed-volume method (mjwarp_convex_simplex.cuh);
+// EPA is the expanding polytope method (van den Bergen 2001).  One thread
 // runs one pair; the polytope lives in the thread's local memory.
 template <class R> struct CShape {
   int type, nvert;
@@ -699,95 +699,133 @@ template <class R> struct Simplex {
   int n;
 };
 
-template <class R> __device__ R det3(const R G[3][3]) {
-  return G[0][0] * (G[1][1] * G[2][2] - G[1][2] * G[2][1]) - G[0][1] * (G[1][0] * G[2][2] - G[1][2] * G[2][0]) +
-         G[0][2] * (G[1][0] * G[2][1] - G[1][1] * G[2][0]);
+// Signed-volume distance sub-algorithm (Montanari, Petrinic and Barbieri,
+// "Improving the GJK algorithm for faster and more reliable distance queries
+// between convex objects", ACM TOG 2017), the method the reference pins
+// (mjwarp_convex_simplex.cuh): barycentric weights of the simplex point
+// nearest the origin.  Vertices keep the caller's order (the newest support
+// point last); a face whose signed volume disagrees with the whole simplex's
+// is searched recursively and the nearest candidate wins.
+template <class R> struct SvWeights { R w[4]; };
+template <class R> __device__ __forceinline__ bool sv_same_sign(R a, R b) {
+  return (a > R(0) && b > R(0)) || (a < R(0) && b < R(0));
+}
+// segment (p, q); when the origin projects outside, the vertex q
+template <class R> __device__ SvWeights<R> sv_segment(V3<R> p, V3<R> q) {
+  const V3<R> e = q - p;
+  const V3<R> o = q + e * (-dot(q, e) / dot(e, e));  // origin projected on the line
+  int k = 0;
+  R mu = p.x - q.x;
+  if (mabs(p.y - q.y) >= mabs(mu)) { mu = p.y - q.y; k = 1; }
+  if (mabs(p.z - q.z) >= mabs(mu)) { mu = p.z - q.z; k = 2; }
+  const R c1 = o[k] - q[k], c2 = p[k] - o[k];
+  if (sv_same_sign(mu, c1) && sv_same_sign(mu, c2)) return {{c1 / mu, c2 / mu, R(0), R(0)}};
+  return {{R(0), R(1), R(0), R(0)}};
+}
+// origin projected on the plane of (a, b, c), trying three normal forms;
+// false when the triangle is degenerate
+template <class R> __device__ bool sv_plane(V3<R> a, V3<R> b, V3<R> c, V3<R> &o) {
+  const V3<R> ab = b - a, ac = c - a, bc = c - b;
+  V3<R> n = cross(bc, ab);
+  R nv = dot(n, b), nn = dot(n, n);
+  if (nn == R(0)) return false;
+  if (nv != R(0) && nn > R(1e-15)) { o = n * (nv / nn); return true; }
+  n = cross(ab, ac); nv = dot(n, a); nn = dot(n, n);
+  if (nn == R(0)) return false;
+  if (nv != R(0) && nn > R(1e-15)) { o = n * (nv / nn); return true; }
+  n = cross(ac, bc); nv = dot(n, c); nn = dot(n, n);
+  o = n * (nv / nn);
+  return true;
+}
+template <class R> __device__ __forceinline__ R sv_area(V3<R> p, V3<R> u, V3<R> v, int i, int j) {
+  const V3<R> a = u - p, b = v - p;
+  return a[i] * b[j] - a[j] * b[i];
+}
+template <class R> __device__ SvWeights<R> sv_triangle(V3<R> a, V3<R> b, V3<R> c) {
+  V3<R> o;
+  if (!sv_plane(a, b, c, o)) return sv_segment(a, b);
+  // the coordinate plane in which the triangle's projection is largest
+  const V3<R> u = b - a, v = c - a;
+  const R myz = u.y * v.z - u.z * v.y, mxz = u.x * v.z - u.z * v.x, mxy = u.x * v.y - u.y * v.x;
+  R m;
+  int i, j;
+  if (mabs(myz) >= mabs(mxz) && mabs(myz) >= mabs(mxy)) { m = myz; i = 1; j = 2; }
+  else if (mabs(mxz) >= mabs(mxy)) { m = mxz; i = 0; j = 2; }
+  else { m = mxy; i = 0; j = 1; }
+  const R s1 = sv_area(o, b, c, i, j), s2 = sv_area(o, c, a, i, j), s3 = sv_area(o, a, b, i, j);
+  const bool in1 = sv_same_sign(m, s1), in2 = sv_same_sign(m, s2), in3 = sv_same_sign(m, s3);
+  if (in1 && in2 && in3) return {{s1 / m, s2 / m, s3 / m, R(0)}};
+  SvWeights<R> out = {{R(0), R(0), R(0), R(0)}};
+  R best = R(1e30);
+  if (!in1) {
+    const SvWeights<R> e = sv_segment(b, c);
+    const V3<R> x = b * e.w[0] + c * e.w[1];
+    out = {{R(0), e.w[0], e.w[1], R(0)}};
+    best = dot(x, x);
+  }
+  if (!in2) {
+    const SvWeights<R> e = sv_segment(a, c);
+    const V3<R> x = a * e.w[0] + c * e.w[1];
+    const R d = dot(x, x);
+    if (d < best) { out = {{e.w[0], R(0), e.w[1], R(0)}}; best = d; }
+  }
+  if (!in3) {
+    const SvWeights<R> e = sv_segment(a, b);
+    const V3<R> x = a * e.w[0] + b * e.w[1];
+    if (dot(x, x) < best) out = {{e.w[0], e.w[1], R(0), R(0)}};
+  }
+  return out;
+}
+template <class R> __device__ SvWeights<R> sv_tetrahedron(V3<R> a, V3<R> b, V3<R> c, V3<R> d) {
+  const R s1 = -dot(b, cross(c, d)), s2 = dot(a, cross(c, d)), s3 = -dot(a, cross(b, d)), s4 = dot(a, cross(b, c));
+  const R vol = s1 + s2 + s3 + s4;
+  const bool in1 = sv_same_sign(vol, s1), in2 = sv_same_sign(vol, s2), in3 = sv_same_sign(vol, s3),
+             in4 = sv_same_sign(vol, s4);
+  if (in1 && in2 && in3 && in4) return {{s1 / vol, s2 / vol, s3 / vol, s4 / vol}};
+  SvWeights<R> out = {{R(0), R(0), R(0), R(0)}};
+  R best = R(1e30);
+  if (!in1) {
+    const SvWeights<R> t = sv_triangle(b, c, d);
+    const V3<R> x = b * t.w[0] + c * t.w[1] + d * t.w[2];
+    out = {{R(0), t.w[0], t.w[1], t.w[2]}};
+    best = dot(x, x);
+  }
+  if (!in2) {
+    const SvWeights<R> t = sv_triangle(a, c, d);
+    const V3<R> x = a * t.w[0] + c * t.w[1] + d * t.w[2];
+    const R dd = dot(x, x);
+    if (dd < best) { out = {{t.w[0], R(0), t.w[1], t.w[2]}}; best = dd; }
+  }
+  if (!in3) {
+    const SvWeights<R> t = sv_triangle(a, b, d);
+    const V3<R> x = a * t.w[0] + b * t.w[1] + d * t.w[2];
+    const R dd = dot(x, x);
+    if (dd < best) { out = {{t.w[0], t.w[1], R(0), t.w[2]}}; best = dd; }
+  }
+  if (!in4) {
+    const SvWeights<R> t = sv_triangle(a, b, c);
+    const V3<R> x = a * t.w[0] + b * t.w[1] + c * t.w[2];
+    if (dot(x, x) < best) out = {{t.w[0], t.w[1], t.w[2], R(0)}};
+  }
+  return out;
 }
 
-// Minimum-norm point of the simplex.  Candidates are the sub-simplices that
-// contain the newest support point (the last vertex; standard GJK), each
-// solved for its affine minimiser; the best one with positive weights wins.
-// Every loop is unrolled over constant vertex masks, so the simplex stays in
-// registers.
+// Reduce the simplex to the vertices with nonzero weight (order kept), the
+// weights becoming the affine coordinates of the nearest point.
 template <class R> __device__ void simplex_reduce(Simplex<R> &s) {
-  const int n = s.n, last = n - 1;
-  R best = R(1e30), lam_best[4] = {0, 0, 0, 0};
-  int mask_best = 1 << last;
-#pragma unroll
-  for (int mask = 1; mask < 16; ++mask) {
-    if (mask >= (1 << n) || !((mask >> last) & 1)) continue;
-    V3<R> p[4];
-    int k = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if ((mask >> i) & 1) p[k++] = s.w[i];
-    R lam[4] = {0, 0, 0, 0};
-    if (k == 1) {
-      lam[0] = 1;
-    } else {
-      V3<R> e[3];
-#pragma unroll
-      for (int j = 1; j < 4; ++j)
-        if (j < k) e[j - 1] = p[j] - p[0];
-      R G[3][3] = {{0, 0, 0}, {0, 0, 0}, {0, 0, 0}}, rhs[3] = {0, 0, 0}, mu[3] = {0, 0, 0};
-#pragma unroll
-      for (int a = 0; a < 3; ++a)
-        if (a < k - 1) {
-          rhs[a] = -dot(e[a], p[0]);
-#pragma unroll
-          for (int b = 0; b < 3; ++b)
-            if (b < k - 1) G[a][b] = dot(e[a], e[b]);
-        }
-      if (k == 2) {
-        if (!(G[0][0] > R(1e-30))) continue;
-        mu[0] = rhs[0] / G[0][0];
-      } else if (k == 3) {
-        const R det = G[0][0] * G[1][1] - G[0][1] * G[1][0];
-        if (!(mabs(det) > R(1e-30))) continue;
-        mu[0] = (rhs[0] * G[1][1] - G[0][1] * rhs[1]) / det;
-        mu[1] = (G[0][0] * rhs[1] - rhs[0] * G[1][0]) / det;
-      } else {
-        const R det = det3(G);
-        if (!(mabs(det) > R(1e-30))) continue;
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-          R M3[3][3];
-#pragma unroll
-          for (int a = 0; a < 3; ++a)
-#pragma unroll
-            for (int b = 0; b < 3; ++b) M3[a][b] = b == c ? rhs[a] : G[a][b];
-          mu[c] = det3(M3) / det;
-        }
-      }
-      R l0 = 1;
-      bool ok = true;
-#pragma unroll
-      for (int j = 0; j < 3; ++j)
-        if (j < k - 1) { lam[j + 1] = mu[j]; l0 -= mu[j]; ok &= mu[j] > R(0); }
-      lam[0] = l0;
-      if (!(ok && l0 > R(0))) continue;
-    }
-    V3<R> x = v3<R>(0, 0, 0);
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if (j < k) x = x + p[j] * lam[j];
-    const R d = dot(x, x);
-    if (d < best) {
-      best = d;
-      mask_best = mask;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) lam_best[j] = lam[j];
-    }
-  }
+  SvWeights<R> W;
+  if (s.n == 4) W = sv_tetrahedron(s.w[0], s.w[1], s.w[2], s.w[3]);
+  else if (s.n == 3) W = sv_triangle(s.w[0], s.w[1], s.w[2]);
+  else if (s.n == 2) W = sv_segment(s.w[0], s.w[1]);
+  else W = {{R(1), R(0), R(0), R(0)}};
   Simplex<R> t;
-  t.n = 0;
   int k = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i)
-    if ((mask_best >> i) & 1) {
+    if (i < s.n && W.w[i] != R(0)) {
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        if (j == k) { t.w[j] = s.w[i]; t.a[j] = s.a[i]; t.b[j] = s.b[i]; t.lam[j] = lam_best[j]; }
+        if (j == k) { t.w[j] = s.w[i]; t.a[j] = s.a[i]; t.b[j] = s.b[i]; t.lam[j] = W.w[i]; }
       ++k;
     }
   t.n = k;
@@ -824,6 +862,7 @@ template <class R> __device__ GjkOut<R> gjk(const CShape<R> &A, const CShape<R> 
       if (i == s.n) { s.w[i] = w; s.a[i] = a; s.b[i] = b; }
     s.n++;
     simplex_reduce(s);
+    if (s.n < 1) break;
     x = v3<R>(0, 0, 0);
 #pragma unroll
     for (int i = 0; i < 4; ++i)

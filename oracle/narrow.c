@@ -193,72 +193,124 @@ static V3 cs_support(const CShape *s, V3 d) {
 
 typedef struct { V3 w[4], a[4], b[4]; real lam[4]; int n; } Simplex;
 
-/* minimum-norm point of the simplex: best sub-simplex with positive affine
- * weights among those containing the newest support point (the last vertex) */
-static void simplex_reduce(Simplex *s) {
-  real best = R(1e30), lam_best[4] = {0, 0, 0, 0};
-  int mask_best = 1 << (s->n - 1);
-  for (int mask = 1; mask < (1 << s->n); ++mask) {
-    if (!((mask >> (s->n - 1)) & 1)) continue;
-    int idx[4], k = 0;
-    for (int i = 0; i < s->n; ++i)
-      if (mask & (1 << i)) idx[k++] = i;
-    real lam[4] = {0, 0, 0, 0}, mu[3] = {0, 0, 0};
-    if (k > 1) { /* minimise |w0 + sum mu_j (w_j - w0)|: normal equations by Cramer's rule */
-      V3 e[3];
-      V3 w0 = s->w[idx[0]];
-      for (int j = 1; j < k; ++j) e[j - 1] = vsub(s->w[idx[j]], w0);
-      int q = k - 1;
-      real G[3][3], rhs[3];
-      for (int i = 0; i < q; ++i) {
-        rhs[i] = -vdot(e[i], w0);
-        for (int j = 0; j < q; ++j) G[i][j] = vdot(e[i], e[j]);
-      }
-      real det;
-      if (q == 1) {
-        det = G[0][0];
-        if (!(det > R(1e-30))) continue;
-        mu[0] = rhs[0] / det;
-      } else if (q == 2) {
-        det = G[0][0] * G[1][1] - G[0][1] * G[1][0];
-        if (!(rabs(det) > R(1e-30))) continue;
-        mu[0] = (rhs[0] * G[1][1] - G[0][1] * rhs[1]) / det;
-        mu[1] = (G[0][0] * rhs[1] - rhs[0] * G[1][0]) / det;
-      } else {
-        det = G[0][0] * (G[1][1] * G[2][2] - G[1][2] * G[2][1]) - G[0][1] * (G[1][0] * G[2][2] - G[1][2] * G[2][0]) +
-              G[0][2] * (G[1][0] * G[2][1] - G[1][1] * G[2][0]);
-        if (!(rabs(det) > R(1e-30))) continue;
-        for (int c = 0; c < 3; ++c) {
-          real M3[3][3];
-          for (int i = 0; i < 3; ++i)
-            for (int j = 0; j < 3; ++j) M3[i][j] = j == c ? rhs[i] : G[i][j];
-          mu[c] = (M3[0][0] * (M3[1][1] * M3[2][2] - M3[1][2] * M3[2][1]) -
-                   M3[0][1] * (M3[1][0] * M3[2][2] - M3[1][2] * M3[2][0]) +
-                   M3[0][2] * (M3[1][0] * M3[2][1] - M3[1][1] * M3[2][0])) / det;
-        }
-      }
-      real l0 = 1;
-      for (int j = 0; j < q; ++j) { lam[j + 1] = mu[j]; l0 -= mu[j]; }
-      lam[0] = l0;
-      int ok = 1;
-      for (int j = 0; j < k; ++j) ok &= lam[j] > 0;
-      if (!ok) continue;
-    } else
-      lam[0] = 1;
-    V3 x = v3(0, 0, 0);
-    for (int j = 0; j < k; ++j) x = vadd(x, vscale(s->w[idx[j]], lam[j]));
-    real d = vdot(x, x);
-    if (d < best) {
-      best = d; mask_best = mask;
-      for (int j = 0; j < 4; ++j) lam_best[j] = lam[j];
-    }
+/* Signed-volume distance sub-algorithm (Montanari, Petrinic and Barbieri,
+ * ACM TOG 2017), the method of the reference's
+ * libero/libero/gpu/cuda/collision/mjwarp_convex_simplex.cuh:17-72: weights of
+ * the simplex point nearest the origin, vertices in the caller's order (the
+ * newest support point last); faces whose signed volume disagrees with the
+ * whole simplex's are searched recursively, the nearest candidate winning. */
+typedef struct { real w[4]; } SvW;
+static int sv_same_sign(real a, real b) { return (a > 0 && b > 0) || (a < 0 && b < 0); }
+static real vcomp(V3 v, int k) { return k == 0 ? v.x : k == 1 ? v.y : v.z; }
+static SvW sv_segment(V3 p, V3 q) {
+  V3 e = vsub(q, p);
+  V3 o = vadd(q, vscale(e, -vdot(q, e) / vdot(e, e)));
+  int k = 0;
+  real mu = p.x - q.x;
+  if (rabs(p.y - q.y) >= rabs(mu)) { mu = p.y - q.y; k = 1; }
+  if (rabs(p.z - q.z) >= rabs(mu)) { mu = p.z - q.z; k = 2; }
+  real c1 = vcomp(o, k) - vcomp(q, k), c2 = vcomp(p, k) - vcomp(o, k);
+  SvW r = {{0, 1, 0, 0}};
+  if (sv_same_sign(mu, c1) && sv_same_sign(mu, c2)) { r.w[0] = c1 / mu; r.w[1] = c2 / mu; }
+  return r;
+}
+static int sv_plane(V3 a, V3 b, V3 c, V3 *o) {
+  V3 ab = vsub(b, a), ac = vsub(c, a), bc = vsub(c, b);
+  V3 n = vcross(bc, ab);
+  real nv = vdot(n, b), nn = vdot(n, n);
+  if (nn == 0) return 0;
+  if (nv != 0 && nn > R(1e-15)) { *o = vscale(n, nv / nn); return 1; }
+  n = vcross(ab, ac); nv = vdot(n, a); nn = vdot(n, n);
+  if (nn == 0) return 0;
+  if (nv != 0 && nn > R(1e-15)) { *o = vscale(n, nv / nn); return 1; }
+  n = vcross(ac, bc); nv = vdot(n, c); nn = vdot(n, n);
+  *o = vscale(n, nv / nn);
+  return 1;
+}
+static real sv_area(V3 p, V3 u, V3 v, int i, int j) {
+  V3 a = vsub(u, p), b = vsub(v, p);
+  return vcomp(a, i) * vcomp(b, j) - vcomp(a, j) * vcomp(b, i);
+}
+static SvW sv_triangle(V3 a, V3 b, V3 c) {
+  V3 o;
+  if (!sv_plane(a, b, c, &o)) return sv_segment(a, b);
+  V3 u = vsub(b, a), v = vsub(c, a);
+  real myz = u.y * v.z - u.z * v.y, mxz = u.x * v.z - u.z * v.x, mxy = u.x * v.y - u.y * v.x, m;
+  int i, j;
+  if (rabs(myz) >= rabs(mxz) && rabs(myz) >= rabs(mxy)) { m = myz; i = 1; j = 2; }
+  else if (rabs(mxz) >= rabs(mxy)) { m = mxz; i = 0; j = 2; }
+  else { m = mxy; i = 0; j = 1; }
+  real s1 = sv_area(o, b, c, i, j), s2 = sv_area(o, c, a, i, j), s3 = sv_area(o, a, b, i, j);
+  int in1 = sv_same_sign(m, s1), in2 = sv_same_sign(m, s2), in3 = sv_same_sign(m, s3);
+  SvW out = {{0, 0, 0, 0}};
+  if (in1 && in2 && in3) { out.w[0] = s1 / m; out.w[1] = s2 / m; out.w[2] = s3 / m; return out; }
+  real best = R(1e30);
+  if (!in1) {
+    SvW e = sv_segment(b, c);
+    V3 x = vadd(vscale(b, e.w[0]), vscale(c, e.w[1]));
+    out.w[0] = 0; out.w[1] = e.w[0]; out.w[2] = e.w[1]; out.w[3] = 0;
+    best = vdot(x, x);
   }
+  if (!in2) {
+    SvW e = sv_segment(a, c);
+    V3 x = vadd(vscale(a, e.w[0]), vscale(c, e.w[1]));
+    real d = vdot(x, x);
+    if (d < best) { out.w[0] = e.w[0]; out.w[1] = 0; out.w[2] = e.w[1]; out.w[3] = 0; best = d; }
+  }
+  if (!in3) {
+    SvW e = sv_segment(a, b);
+    V3 x = vadd(vscale(a, e.w[0]), vscale(b, e.w[1]));
+    if (vdot(x, x) < best) { out.w[0] = e.w[0]; out.w[1] = e.w[1]; out.w[2] = 0; out.w[3] = 0; }
+  }
+  return out;
+}
+static SvW sv_tetrahedron(V3 a, V3 b, V3 c, V3 d) {
+  real s1 = -vdot(b, vcross(c, d)), s2 = vdot(a, vcross(c, d)), s3 = -vdot(a, vcross(b, d)), s4 = vdot(a, vcross(b, c));
+  real vol = s1 + s2 + s3 + s4;
+  int in1 = sv_same_sign(vol, s1), in2 = sv_same_sign(vol, s2), in3 = sv_same_sign(vol, s3), in4 = sv_same_sign(vol, s4);
+  SvW out = {{0, 0, 0, 0}};
+  if (in1 && in2 && in3 && in4) {
+    out.w[0] = s1 / vol; out.w[1] = s2 / vol; out.w[2] = s3 / vol; out.w[3] = s4 / vol;
+    return out;
+  }
+  real best = R(1e30);
+  if (!in1) {
+    SvW t = sv_triangle(b, c, d);
+    V3 x = vadd(vadd(vscale(b, t.w[0]), vscale(c, t.w[1])), vscale(d, t.w[2]));
+    out.w[0] = 0; out.w[1] = t.w[0]; out.w[2] = t.w[1]; out.w[3] = t.w[2];
+    best = vdot(x, x);
+  }
+  if (!in2) {
+    SvW t = sv_triangle(a, c, d);
+    V3 x = vadd(vadd(vscale(a, t.w[0]), vscale(c, t.w[1])), vscale(d, t.w[2]));
+    real dd = vdot(x, x);
+    if (dd < best) { out.w[0] = t.w[0]; out.w[1] = 0; out.w[2] = t.w[1]; out.w[3] = t.w[2]; best = dd; }
+  }
+  if (!in3) {
+    SvW t = sv_triangle(a, b, d);
+    V3 x = vadd(vadd(vscale(a, t.w[0]), vscale(b, t.w[1])), vscale(d, t.w[2]));
+    real dd = vdot(x, x);
+    if (dd < best) { out.w[0] = t.w[0]; out.w[1] = t.w[1]; out.w[2] = 0; out.w[3] = t.w[2]; best = dd; }
+  }
+  if (!in4) {
+    SvW t = sv_triangle(a, b, c);
+    V3 x = vadd(vadd(vscale(a, t.w[0]), vscale(b, t.w[1])), vscale(c, t.w[2]));
+    if (vdot(x, x) < best) { out.w[0] = t.w[0]; out.w[1] = t.w[1]; out.w[2] = t.w[2]; out.w[3] = 0; }
+  }
+  return out;
+}
+
+/* keep the vertices with nonzero weight (order kept); the weights become the
+ * affine coordinates of the nearest point (mjwarp_convex_gjk.cuh:71-75) */
+static void simplex_reduce(Simplex *s) {
+  SvW W = {{1, 0, 0, 0}};
+  if (s->n == 4) W = sv_tetrahedron(s->w[0], s->w[1], s->w[2], s->w[3]);
+  else if (s->n == 3) W = sv_triangle(s->w[0], s->w[1], s->w[2]);
+  else if (s->n == 2) W = sv_segment(s->w[0], s->w[1]);
   Simplex t;
   int k = 0;
   for (int i = 0; i < s->n; ++i)
-    if (mask_best & (1 << i)) {
-      t.w[k] = s->w[i]; t.a[k] = s->a[i]; t.b[k] = s->b[i]; t.lam[k] = lam_best[k]; ++k;
-    }
+    if (W.w[i] != 0) { t.w[k] = s->w[i]; t.a[k] = s->a[i]; t.b[k] = s->b[i]; t.lam[k] = W.w[i]; ++k; }
   t.n = k;
   *s = t;
 }
@@ -286,6 +338,7 @@ static GjkOut gjk(const CShape *A, const CShape *B, real tol, int iterations, re
     }
     s->w[s->n] = w; s->a[s->n] = a; s->b[s->n] = b; s->n++;
     simplex_reduce(s);
+    if (s->n < 1) break;
     x = v3(0, 0, 0);
     for (int i = 0; i < s->n; ++i) x = vadd(x, vscale(s->w[i], s->lam[i]));
     prev = norm;
