@@ -201,14 +201,14 @@ typedef struct { V3 w[4], a[4], b[4]; real lam[4]; int n; } Simplex;
  * whole simplex's are searched recursively, the nearest candidate winning. */
 typedef struct { real w[4]; } SvW;
 static int sv_same_sign(real a, real b) { return (a > 0 && b > 0) || (a < 0 && b < 0); }
-static real vcomp(V3 v, int k) { return k == 0 ? v.x : k == 1 ? v.y : v.z; }
+static real vcomp(V3 v, int k) { return v.v[k]; }
 static SvW sv_segment(V3 p, V3 q) {
   V3 e = vsub(q, p);
   V3 o = vadd(q, vscale(e, -vdot(q, e) / vdot(e, e)));
   int k = 0;
-  real mu = p.x - q.x;
-  if (rabs(p.y - q.y) >= rabs(mu)) { mu = p.y - q.y; k = 1; }
-  if (rabs(p.z - q.z) >= rabs(mu)) { mu = p.z - q.z; k = 2; }
+  real mu = p.v[0] - q.v[0];
+  if (rabs(p.v[1] - q.v[1]) >= rabs(mu)) { mu = p.v[1] - q.v[1]; k = 1; }
+  if (rabs(p.v[2] - q.v[2]) >= rabs(mu)) { mu = p.v[2] - q.v[2]; k = 2; }
   real c1 = vcomp(o, k) - vcomp(q, k), c2 = vcomp(p, k) - vcomp(o, k);
   SvW r = {{0, 1, 0, 0}};
   if (sv_same_sign(mu, c1) && sv_same_sign(mu, c2)) { r.w[0] = c1 / mu; r.w[1] = c2 / mu; }
@@ -235,7 +235,7 @@ static SvW sv_triangle(V3 a, V3 b, V3 c) {
   V3 o;
   if (!sv_plane(a, b, c, &o)) return sv_segment(a, b);
   V3 u = vsub(b, a), v = vsub(c, a);
-  real myz = u.y * v.z - u.z * v.y, mxz = u.x * v.z - u.z * v.x, mxy = u.x * v.y - u.y * v.x, m;
+  real myz = u.v[1] * v.v[2] - u.v[2] * v.v[1], mxz = u.v[0] * v.v[2] - u.v[2] * v.v[0], mxy = u.v[0] * v.v[1] - u.v[1] * v.v[0], m;
   int i, j;
   if (rabs(myz) >= rabs(mxz) && rabs(myz) >= rabs(mxy)) { m = myz; i = 1; j = 2; }
   else if (rabs(mxz) >= rabs(mxy)) { m = mxz; i = 0; j = 2; }
