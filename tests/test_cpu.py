@@ -206,3 +206,14 @@ def test_flop_count_block_sparse_reduces_to_dense():
     sparse = dict(base, efc_k=np.full(W, nefc * 7), efc_k2=np.full(W, nefc * 49),
                   fact_blk=np.full(W, 7 * 7 * (7 + 6) + 2 * 7 * 7 * 6))
     assert flops.substep_flops(s.sizes, td, sparse, 1) < 0.5 * b
+
+
+def test_reference_leaf_checker_abi():
+    """The checker library built from the reference's own collision leaves (when
+    present) agrees with its loader and with the leaves' own argument-pack sizes."""
+    import sys
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / 'oracle'))
+    import ref_contacts
+    if not ref_contacts.available():
+        pytest.skip('oracle/_ref/libref_contacts.so not built')
+    ref_contacts.RefCollision()
