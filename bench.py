@@ -32,7 +32,14 @@ import __graft_entry__ as entry  # noqa: E402
 
 METRIC = 'env control steps/sec (whole box) at 16K worlds/GPU; physics substeps/sec'
 UNIT = 'env control steps/s'
-TRAFFIC_BYTES_PER_WORLD = 1601
+# DRAM read + write bytes per world and control step (FP32), from one ncu
+# capture of control_step per scene, scaled by worlds (per-world state is
+# independent): scene A at 2368 worlds (profiles/control_step_scene_a_2368w_full.md),
+# scene B at 444 worlds (profiles/control_step_scene_b_444w_full.md)
+TRAFFIC_BYTES_PER_WORLD = {'scene_a': 1601, 'scene_b': 8433}
+# control-step stages the kernel stamps with clock64 (data.stage_cycles slots 1..15)
+STAGES = ('kinematics', 'com_crb', 'mass_factor', 'collision', 'constraints', 'velocity', 'osc', 'actuation',
+          'newton_init', 'linesearch', 'gradient', 'hessian', 'direction', 'euler', 'barrier_wait')
 WORKLOADS = {
     'scene_a': 'scene_a: Franka-like arm + gripper + plane + 3 free boxes, elliptic cones, 25 substeps/control step',
     'scene_b': 'scene_b: scene A arm + 12 dropped objects (4 boxes, 4 capsules, 2 spheres, 2 convex hulls), '
@@ -221,7 +228,7 @@ def main():
         gather.wait()
     torch.cuda.synchronize(dev)
     counters0 = {k: rt.buffers[k].clone() for k in ('efc_total', 'con_total', 'newton_rows', 'ls_rows',
-                                                     'newton_total', 'efc_k', 'efc_k2', 'fact_blk')}
+                                                     'newton_total', 'efc_k', 'efc_k2', 'fact_blk', 'stage_cycles')}
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     clocks = ClockSampler(local)
     if world_size > 1:
@@ -256,6 +263,10 @@ def main():
     # that wraps during the interval still gives its delta
     deltas = {k: (rt.buffers[k].long() - counters0[k].long()).remainder(1 << 32).cpu().numpy()
               for k in counters0}
+    # wall cycles of each stage per world and substep (lane 0 of each world stamps clock64;
+    # barrier_wait is the time a world waits at CTA barriers for the other worlds of its CTA)
+    stage = deltas.pop('stage_cycles').astype(np.float64).mean(0)[1:] / (args.steps * scene.substeps)
+    stage_cycles = {name: round(float(c)) for name, c in zip(STAGES, stage)}
     fl = flops.substep_flops(scene.sizes, scene.ints['tree_dofnum'], deltas, scene.substeps)
     fl_dense = flops.dense_substep_flops(scene.sizes, scene.ints['tree_dofnum'], deltas, scene.substeps)
     kernel_s = elapsed / args.steps  # one kernel per graph replay
@@ -279,7 +290,7 @@ def main():
     # DRAM read+write per world per control step from one ncu capture of the
     # same kernel at 2368 worlds, scaled by worlds (per-world state is
     # independent): profiles/control_step_scene_a_2368w_full.md
-    traffic = TRAFFIC_BYTES_PER_WORLD * W if args.precision == 'fp32' and args.scene == 'scene_a' else None
+    traffic = TRAFFIC_BYTES_PER_WORLD[args.scene] * W if args.precision == 'fp32' else None
 
     # e2e through the public API (pinned H2D actions, D2H observations)
     env = B200BatchEnv(scene, W, device=dev, precision=args.precision, seed=args.seed, world_offset=offset)
@@ -334,6 +345,7 @@ def main():
                               frac=bytes_per_world * W / kernel_s / 1e9 / hbm_gbs, peak_source=peak_src,
                               bytes_per_world=bytes_per_world, traffic=traffic),
             kernel_ms=dict(mean=float(step_ms.mean()), min=float(step_ms.min()), max=float(step_ms.max())),
+            stage_cycles_per_world_substep=stage_cycles,
             cpu_baseline=base, clocks=clock, gpu_launches=args.steps)
         print(json.dumps(line), flush=True)
     env.close()
