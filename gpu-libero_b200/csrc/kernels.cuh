@@ -582,7 +582,13 @@ template <class R, int T, bool CONVEX> __device__ B200_STAGE_ATTR void collision
         if (f >= 0) list[off[f] + atomicAdd(&fill[f], 1)] = p;
       }
       SYNC();
-      FOR(i, total) narrow_pair<R, CONVEX>(M, A, list[i], fam[list[i]]);
+      // families dealt to the world's warps (convex alone on the first), so that
+      // a warp runs one or two collider code paths instead of all of them
+      constexpr int kFamWarp[kFam] = {3, 1, 3, 2, 0};
+      const int nw = T / 32, wid = TID / 32;
+      for (int f = 0; f < kFam; ++f)
+        if (kFamWarp[f] % nw == wid)
+          for (int i = LANE; i < cnt[f]; i += 32) narrow_pair<R, CONVEX>(M, A, list[off[f] + i], f);
     } else {
       FOR(p, m.npair) {
         const int f = pair_family<R, CONVEX>(M, A, p);
