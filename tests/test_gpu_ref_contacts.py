@@ -10,7 +10,7 @@ arrays.  Compared over the pair families the reference's FP32 engine covers
 box; capsule, box and mesh against mesh):
 
 - contact counts per world and the contact pair list (geom order included)
-  are bit-exact;
+  are bit-exact, from the initial drop to settled piles (25 control steps);
 - contact distances agree within 2e-5 m for the closed-form families and
   within the CCD tolerance band (2e-4 m) for GJK/EPA pairs, and contact normals
   within 1e-3 (convex: 2e-2, where EPA's polytope stops on a face near the
@@ -126,7 +126,7 @@ def test_scene_a_contacts_match_reference_leaves(ref, steps):
     assert s['contacts'] > 0
 
 
-@pytest.mark.parametrize('steps', [0, 4, 10])
+@pytest.mark.parametrize('steps', [0, 4, 10, 25])
 def test_scene_b_contacts_match_reference_leaves(ref, steps):
-    s = compare(scenes.scene_b(), ref, 48, steps, seed=7)
+    s = compare(scenes.scene_b(), ref, 96 if steps == 25 else 48, steps, seed=7)
     assert s['contacts'] > 0 or steps == 0  # objects start in the air
