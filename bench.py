@@ -36,7 +36,7 @@ UNIT = 'env control steps/s'
 # capture of control_step per scene, scaled by worlds (per-world state is
 # independent): scene A at 2368 worlds (profiles/control_step_scene_a_2368w_full.md),
 # scene B at 444 worlds (profiles/control_step_scene_b_444w_full.md)
-TRAFFIC_BYTES_PER_WORLD = {'scene_a': 1007, 'scene_b': 9188}
+TRAFFIC_BYTES_PER_WORLD = {'scene_a': 1032, 'scene_b': 9188}
 # control-step stages the kernel stamps with clock64 (data.stage_cycles slots 1..15)
 STAGES = ('kinematics', 'com_crb', 'mass_factor', 'collision', 'constraints', 'velocity', 'osc', 'actuation',
           'newton_init', 'linesearch', 'gradient', 'hessian', 'direction', 'euler', 'barrier_wait')

@@ -36,14 +36,22 @@ int max_optin_smem() {
   }
   return v;
 }
-// Worlds per CTA.  Two CTAs per SM (each holding half of the SM's shared
-// memory) measured faster than one large CTA: worlds of a CTA wait for its
-// slowest world at stage barriers, and the second CTA fills those gaps.
+// Worlds per CTA: one CTA fills the SM's shared memory.  The worlds of a CTA
+// advance through the stages in lockstep, so every warp of the SM runs the
+// same stage's code and the instruction caches serve them all.  Two CTAs per
+// SM run different stages at a time: on scene A (one-warp worlds) that made
+// instruction fetch the largest stall, and eight worlds in one CTA measured
+// 79.5 ms per control step against 95.9 ms for two CTAs of four.
 int worlds_per_cta(const B200Model *m, int limit) {
   const size_t arena = arena_for(m);
   if (arena == 0 || (int)arena > limit) return 0;
   const int half = (228 * 1024) / 2 - 1024;  // per-SM capacity shared by two CTAs
-  int wpc = half / (int)arena >= 3 ? half / (int)arena : limit / (int)arena;
+  static int two = -1;  // B200PHYS_TWO_CTAS=1: two CTAs per SM (when each holds 3+ worlds), for tuning
+  if (two < 0) {
+    const char *e = getenv("B200PHYS_TWO_CTAS");
+    two = e && atoi(e) == 1;
+  }
+  int wpc = two && half / (int)arena >= 3 ? half / (int)arena : limit / (int)arena;
   static int cap = -1;  // B200PHYS_WPC: smaller CTAs (more CTAs per SM), for tuning
   if (cap < 0) {
     const char *e = getenv("B200PHYS_WPC");
