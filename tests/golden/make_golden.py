@@ -19,6 +19,7 @@ Reference modules used (paths inside the reference checkout):
   tests/fixtures/boxbox_task5.json, boxbox_edge_projection.json,
   boxbox_first_face_vertex.csv, boxbox_sat_face_tie.csv, and the unit-box
   cases of tests/cuda/precision_boxbox_test.cu:76-82.
+  tests/data/gjk_tuned_direction.json (a recorded LIBERO box-box overlap).
 """
 import csv
 import importlib
@@ -361,6 +362,24 @@ def make_box_fixtures(mods, path):
     (HERE / 'box_fixtures.json').write_text(json.dumps(out, indent=1))
 
 
+def make_gjk_direction(mods, path):
+    """The reference's recorded zero-margin box-box overlap (libero_spatial task 5,
+    tests/data/gjk_tuned_direction.json, used by tests/test_mjwarp_convex_gjk.py:42-52)
+    whose previously tuned GJK direction wrongly claimed separation; the expected
+    depth is the reference's independent SAT separation of the two boxes."""
+    f = json.loads((Path(path) / 'tests' / 'data' / 'gjk_tuned_direction.json').read_text())
+    a, b = np.asarray(f['position1'], float), np.asarray(f['position2'], float)
+    rot, size = np.asarray(f['rotations'], float), np.asarray(f['sizes'], float)
+    sep = float(mods['box'].box_separation(a, b, rot[0], rot[1], size[0], size[1]))
+    assert sep < -f['tolerance']
+    out = dict(pos=[a.tolist(), b.tolist()], mat=rot.tolist(), size=size.tolist(), separation=sep,
+               tolerance=f['tolerance'], iterations=f['iterations'], epa_iterations=f['epa_iterations'],
+               provenance=f['provenance'],
+               note='penetrating boxes a tuned GJK direction once declared separated; '
+                    'the convex path must report the SAT depth')
+    (HERE / 'gjk_tuned_direction.json').write_text(json.dumps(out, indent=1))
+
+
 def main():
     if len(sys.argv) != 2:
         raise SystemExit(__doc__)
@@ -372,6 +391,7 @@ def main():
     make_euler(mods, s, native, oracle)
     make_box_pairs(mods, oracle)
     make_box_fixtures(mods, sys.argv[1])
+    make_gjk_direction(mods, sys.argv[1])
     print('golden vectors written to', HERE)
 
 

@@ -8,6 +8,7 @@ FP64 validation oracles and shipped box-box fixtures):
   euler_position_scene_a.npz   mjwarp_euler_reference.reference(c, 'position')
   box_pairs.npz                mjwarp_box_reference.pair_math (SAT separation, segment-box distance)
   box_fixtures.json            tests/fixtures/boxbox_* and tests/cuda/precision_boxbox_test.cu cases
+  gjk_tuned_direction.json     tests/data/gjk_tuned_direction.json with its SAT depth (box_separation)
 
 Tolerances: FP64 oracle within 1e-12 absolute of the reference's FP64 values
 (bit-level agreement up to summation order); FP32 oracle within 8x the
@@ -220,3 +221,20 @@ def test_convex_path_against_reference_box_geometry(oracle):
         elif want > max(tol, 1e-9):
             assert got is None
     assert min(checked.values()) >= 20
+
+
+def test_recorded_boxbox_overlap_is_not_declared_separated(oracle):
+    """The reference's recorded LIBERO overlap (gjk_tuned_direction.json: two
+    boxes 39 µm deep that a tuned GJK direction once declared separated).
+    GJK/EPA, on the boxes as primitives against hulls and as two hulls, must
+    report the contact at the reference's SAT depth, within the CCD tolerance
+    in FP32."""
+    precision, orc, _ = oracle
+    f = load('gjk_tuned_direction.json')
+    p, R, s = (np.asarray(f[k], float) for k in ('pos', 'mat', 'size'))
+    tol = 1e-12 if precision == 'fp64' else 2 * f['tolerance']
+    kw = dict(tol=f['tolerance'], iterations=f['iterations'], epa_iterations=f['epa_iterations'])
+    for kind1, v1 in ((6, None), (7, box_corners(s[0]))):
+        got = orc.convex(kind1, p[0], R[0], s[0], v1, 7, p[1], R[1], s[1], box_corners(s[1]), **kw)
+        assert got is not None, (precision, kind1)
+        assert abs(got[0] - f['separation']) <= tol, (precision, kind1, got[0], f['separation'])
