@@ -202,6 +202,9 @@ def main():
     dev = torch.device('cuda', local)
     if world_size > 1:
         from datetime import timedelta
+        # NCCL's own log lines (its version banner among them) go to stderr, so that
+        # rank 0's stdout carries the one JSON line
+        os.environ.setdefault('NCCL_DEBUG_FILE', '/dev/stderr')
         dist.init_process_group('nccl', device_id=dev, timeout=timedelta(seconds=120))
     W = args.worlds
     offset = rank * W
