@@ -198,13 +198,16 @@ def main():
     world_size = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
     local = int(os.environ.get('LOCAL_RANK', '0'))
+    # stdout carries exactly one JSON line: whatever the libraries print on file
+    # descriptor 1 (NCCL's version banner, for one) is sent to stderr, and the
+    # result is written to a duplicate of the original stdout
+    sys.stdout.flush()
+    result_out = os.fdopen(os.dup(1), 'w')
+    os.dup2(2, 1)
     torch.cuda.set_device(local)
     dev = torch.device('cuda', local)
     if world_size > 1:
         from datetime import timedelta
-        # NCCL's own log lines (its version banner among them) go to stderr, so that
-        # rank 0's stdout carries the one JSON line
-        os.environ.setdefault('NCCL_DEBUG_FILE', '/dev/stderr')
         dist.init_process_group('nccl', device_id=dev, timeout=timedelta(seconds=120))
     W = args.worlds
     offset = rank * W
@@ -350,7 +353,7 @@ def main():
             kernel_ms=dict(mean=float(step_ms.mean()), min=float(step_ms.min()), max=float(step_ms.max())),
             stage_cycles_per_world_substep=stage_cycles,
             cpu_baseline=base, clocks=clock, gpu_launches=args.steps)
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=result_out, flush=True)
     env.close()
     rt.close()
     if world_size > 1:
