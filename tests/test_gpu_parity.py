@@ -252,3 +252,32 @@ def test_scene_b_control_steps_parity(scene_b_state, oracle_module, precision, t
     nv = b.sizes['nv']
     assert np.all(gpu['fact_blk'][:, 0] > 0)
     assert np.all(gpu['fact_blk'][:, 0] <= gpu['newton_total'][:, 0].astype(np.int64) * nv * nv * (nv + 6))
+
+
+@pytest.mark.parametrize('precision,tol', [('fp32', 2e-4), ('fp64', 2e-6)])
+def test_hundred_control_steps_track_the_oracle(scene, oracle_module, precision, tol):
+    """BASELINE's trajectory horizon: 100 control steps (2500 substeps) of scene A.
+    Measured on a B200: max |dqpos| 9.7e-5 (FP32) and 6.8e-7 (FP64) over the
+    run; the FP64 gap is the Newton stop rule (tolerance 1e-8), under which the
+    two implementations may stop one iteration apart.  Contact counts stay
+    equal at every checkpoint."""
+    n = 4
+    from gpu_libero_b200.runtime import Runtime
+    rt = Runtime(scene, n, precision=precision)
+    q, v = scene.initial_state(n, seed=5)
+    rt.set_state(np.concatenate([np.zeros((n, 1)), q, v], axis=1))
+    torch.cuda.synchronize()
+    ref = host_copy(rt, n)
+    orc = oracle_module.Oracle(precision)
+    for step in range(100):
+        a = scene.actions(n, step, seed=5)
+        rt.enqueue_action(a)
+        ref['action'][:] = a
+        orc.step(rt.packed.host_struct(), native.data_struct(ref, n), 0, n, rt.substeps, 1)
+        if step % 25 == 24:
+            torch.cuda.synchronize()
+            assert np.max(np.abs(rt.buffers['qpos'].cpu().numpy() - ref['qpos'])) < tol, step
+            assert np.array_equal(rt.buffers['ncon'].cpu().numpy(), ref['ncon']), step
+    gpu = {k: t.cpu().numpy() for k, t in rt.buffers.items()}
+    assert np.all(gpu['integration_count'] == 2500)
+    assert not np.any(gpu['overflow'] & ~0x600) and not np.any(gpu['error'])
