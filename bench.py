@@ -33,9 +33,10 @@ import __graft_entry__ as entry  # noqa: E402
 METRIC = 'env control steps/sec (whole box) at 16K worlds/GPU; physics substeps/sec'
 UNIT = 'env control steps/s'
 # DRAM read + write bytes per world and control step (FP32), from one ncu
-# capture of control_step per scene, scaled by worlds (per-world state is
-# independent): scene A at 2368 worlds (profiles/control_step_scene_a_2368w_full.md),
-# scene B at 444 worlds (profiles/control_step_scene_b_444w_full.md)
+# capture of control_step per scene (dram__bytes_read.sum + dram__bytes_write.sum
+# of one launch divided by its worlds; per-world state is independent, so the
+# traffic scales with the worlds of a launch): scene A captured at 2368 worlds,
+# scene B at 444 worlds
 TRAFFIC_BYTES_PER_WORLD = {'scene_a': 1032, 'scene_b': 9188}
 # control-step stages the kernel stamps with clock64 (data.stage_cycles slots 1..15)
 STAGES = ('kinematics', 'com_crb', 'mass_factor', 'collision', 'constraints', 'velocity', 'osc', 'actuation',
@@ -293,9 +294,6 @@ def main():
         hbm_gbs, peak_src = float(peaks['hbm_gbs']), 'measured'
     except (OSError, ValueError, KeyError):
         hbm_gbs, peak_src = 6650.0, 'fallback'
-    # DRAM read+write per world per control step from one ncu capture of the
-    # same kernel at 2368 worlds, scaled by worlds (per-world state is
-    # independent): profiles/control_step_scene_a_2368w_full.md
     traffic = TRAFFIC_BYTES_PER_WORLD[args.scene] * W if args.precision == 'fp32' else None
 
     # e2e through the public API (pinned H2D actions, D2H observations)

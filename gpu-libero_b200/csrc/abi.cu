@@ -1,7 +1,6 @@
 // C ABI of the B200 physics step: argument checks, launch shape, dispatch
 // to the kernel instances (inst.cu).
 #include <cuda_runtime.h>
-#include <cstdlib>
 #include "b200phys.h"
 #include "arena.cuh"
 #include "launch.h"
@@ -13,6 +12,9 @@
 // ============================================================ C ABI
 namespace {
 constexpr int kMaxWorldsPerCta = 8;
+
+// Largest dynamic shared memory a CTA may opt into on sm_100 (227 KB).
+constexpr size_t kSm100OptinSmem = 227 * 1024;
 
 bool model_ok(const B200Model *m) {
   return m && m->real && m->ints && (m->real_bytes == 4 || m->real_bytes == 8) && m->nv >= 1 && m->nv <= 128 &&
@@ -27,13 +29,12 @@ size_t arena_for(const B200Model *m) {
   return m->real_bytes == 4 ? b200::Arena<float>::layout(*m, 32, nullptr, nullptr)
                             : b200::Arena<double>::layout(*m, 32, nullptr, nullptr);
 }
+// Opt-in shared memory per block of the current device, queried on every
+// call (a cheap attribute read), so that each device and thread sees its own.
 int max_optin_smem() {
-  static int v = -1;
-  if (v < 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) v = 0;
-  }
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return 0;
   return v;
 }
 // Worlds per CTA: one CTA fills the SM's shared memory.  The worlds of a CTA
@@ -45,20 +46,8 @@ int max_optin_smem() {
 int worlds_per_cta(const B200Model *m, int limit) {
   const size_t arena = arena_for(m);
   if (arena == 0 || (int)arena > limit) return 0;
-  const int half = (228 * 1024) / 2 - 1024;  // per-SM capacity shared by two CTAs
-  static int two = -1;  // B200PHYS_TWO_CTAS=1: two CTAs per SM (when each holds 3+ worlds), for tuning
-  if (two < 0) {
-    const char *e = getenv("B200PHYS_TWO_CTAS");
-    two = e && atoi(e) == 1;
-  }
-  int wpc = two && half / (int)arena >= 3 ? half / (int)arena : limit / (int)arena;
-  static int cap = -1;  // B200PHYS_WPC: smaller CTAs (more CTAs per SM), for tuning
-  if (cap < 0) {
-    const char *e = getenv("B200PHYS_WPC");
-    cap = e ? atoi(e) : kMaxWorldsPerCta;
-    if (cap < 1 || cap > kMaxWorldsPerCta) cap = kMaxWorldsPerCta;
-  }
-  return wpc > cap ? cap : wpc;
+  const int wpc = limit / (int)arena;
+  return wpc > kMaxWorldsPerCta ? kMaxWorldsPerCta : wpc;
 }
 // Launch shape: worlds per CTA and threads per world.  A world is one warp,
 // or four warps when at most three worlds fit on an SM (large models), so
@@ -77,12 +66,6 @@ int launch_shape(const B200Model *m, Shape *sh) {
   const int arena = (int)arena_for(m);
   const int per_sm = ((228 * 1024) / (sh->wpc * arena + 1024)) * sh->wpc;
   sh->T = per_sm <= 3 ? 128 : 32;
-  static int force = -1;  // B200PHYS_THREADS: 32 or 128 threads per world, for tuning
-  if (force < 0) {
-    const char *e = getenv("B200PHYS_THREADS");
-    force = e ? atoi(e) : 0;
-  }
-  if (force == 32 || force == 128) sh->T = force;
   if (sh->T * sh->wpc > 384) sh->wpc = 384 / sh->T;  // the kernels' launch bound
   const bool convex = m->nmesh > 0;
   if (m->real_bytes == 4) return convex ? prepare_rc<float, true>(m, *sh) : prepare_rc<float, false>(m, *sh);
@@ -112,7 +95,11 @@ const char *b200phys_source_id(void) { return B200PHYS_SOURCE_ID; }
 int b200phys_arch(void) { return 100; }
 size_t b200phys_model_bytes(void) { return sizeof(B200Model); }
 size_t b200phys_data_bytes(void) { return sizeof(B200Data); }
-size_t b200phys_world_smem_bytes(const B200Model *m) { return model_ok(m) ? arena_for(m) : 0; }
+size_t b200phys_world_smem_bytes(const B200Model *m) {
+  if (!model_ok(m)) return 0;
+  const size_t arena = arena_for(m);
+  return arena <= kSm100OptinSmem ? arena : 0;
+}
 
 int b200phys_prepare(const B200Model *m) {
   if (!model_ok(m)) return (int)cudaErrorInvalidValue;

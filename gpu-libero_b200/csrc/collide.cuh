@@ -1,3 +1,6 @@
+// Portions (sphere_box, capsule_box, box_box, clip_poly) restate MuJoCo Warp's
+// primitive contact geometry: Copyright 2025 The Newton Developers,
+// SPDX-License-Identifier: Apache-2.0 (see NOTICE).
 // Per-pair collision for one world: broadphase filters and primitive
 // narrowphase.  One thread owns one candidate pair; contacts are appended to
 // the world's shared-memory contact table and later ordered by
@@ -889,8 +892,26 @@ template <class R> struct Polytope {
   bool alive[kEpaMaxF];
 };
 
+// Drop the dead faces, keeping the live ones in their order (the best-face
+// search breaks ties by the lower index, so the order is part of the result).
+template <class R> __device__ void epa_compact(Polytope<R> &P) {
+  int k = 0;
+  for (int f = 0; f < P.nf; ++f) {
+    if (!P.alive[f]) continue;
+    if (k != f) {
+      P.face[k][0] = P.face[f][0]; P.face[k][1] = P.face[f][1]; P.face[k][2] = P.face[f][2];
+      P.n[k] = P.n[f]; P.d[k] = P.d[f]; P.alive[k] = true;
+    }
+    ++k;
+  }
+  P.nf = k;
+}
+
+// New face (i, j, l): its index, -1 for a degenerate triangle, -2 when the
+// face pool is full even after compaction.
 template <class R> __device__ int epa_add_face(Polytope<R> &P, int i, int j, int l) {
-  if (P.nf >= kEpaMaxF) return -1;
+  if (P.nf >= kEpaMaxF) epa_compact(P);
+  if (P.nf >= kEpaMaxF) return -2;
   V3<R> n = cross(P.w[j] - P.w[i], P.w[l] - P.w[i]);
   const R len = msqrt(dot(n, n));
   if (!(len > R(1e-30))) return -1;
@@ -918,6 +939,7 @@ template <class R> __device__ bool epa_seed(Polytope<R> &P, const CShape<R> &A, 
     V3<R> ax = v3<R>(0, 0, 0);
     ax[k / 2] = k % 2 ? R(-1) : R(1);
     const int v = epa_push(P, A, B, ax);
+    if (v == 0) continue;  // an empty simplex (coincident centres): the first vertex seeds
     const V3<R> e = P.w[v] - P.w[0];
     if (dot(e, e) < R(1e-20)) P.nv--;
   }
@@ -958,8 +980,10 @@ template <class R> __device__ bool epa_seed(Polytope<R> &P, const CShape<R> &A, 
   return true;
 }
 
+// ok: a penetration depth was found; overflow: a vertex, face or horizon
+// pool filled before EPA converged (the reference's EPA_HORIZON status).
 template <class R> struct EpaOut {
-  bool ok;
+  bool ok, overflow;
   R depth;
   V3<R> x1, x2;
 };
@@ -968,6 +992,7 @@ template <class R>
 __device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R> &s, R tol, int iterations) {
   EpaOut<R> o;
   o.ok = false;
+  o.overflow = false;
   Polytope<R> P;
   if (!epa_seed(P, A, B, s)) return o;
   int best = -1;
@@ -979,7 +1004,7 @@ __device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R
     if (it == iterations) break;
     const V3<R> n = P.n[best];
     const int v = epa_push(P, A, B, n);
-    if (v < 0) break;
+    if (v < 0) { o.overflow = true; break; }
     if (dot(P.w[v], n) - P.d[best] < tol) { P.nv--; break; }
     int edges[3 * kEpaMaxF][2], ne = 0;
     for (int f = 0; f < P.nf; ++f) {
@@ -992,12 +1017,15 @@ __device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R
           if (edges[q][0] == j && edges[q][1] == i) { dup = q; break; }
         if (dup >= 0) { edges[dup][0] = edges[ne - 1][0]; edges[dup][1] = edges[ne - 1][1]; --ne; }
         else if (ne < 3 * kEpaMaxF) { edges[ne][0] = i; edges[ne][1] = j; ++ne; }
+        else o.overflow = true;
       }
     }
     bool full = false;
-    for (int q = 0; q < ne; ++q)
-      if (epa_add_face(P, edges[q][0], edges[q][1], v) < 0) { full = true; break; }
-    if (full) break;
+    for (int q = 0; q < ne; ++q) {
+      const int f = epa_add_face(P, edges[q][0], edges[q][1], v);
+      if (f < 0) { full = true; o.overflow |= f == -2; break; }
+    }
+    if (full || o.overflow) break;
   }
   if (best < 0) return o;
   const int i = P.face[best][0], j = P.face[best][1], l = P.face[best][2];
@@ -1063,6 +1091,7 @@ __device__ __noinline__ void convex_pair(const Mdl<R> &M, Arena<R> &A, int pair,
     if (r.dist > tol) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
     else {
       const EpaOut<R> e = epa(S1, S2, r.s, tol, M.m.epa_iterations);
+      if (e.overflow) atomicOr(&A.iscal[3], B200_OVERFLOW_EPA_HORIZON);
       if (!e.ok) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
       else { dist = -e.depth; x1 = e.x1; x2 = e.x2; }
     }

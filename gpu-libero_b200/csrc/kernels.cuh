@@ -1,3 +1,6 @@
+// Portions (impedance, row_params; the line-search row model Pt .. eval_shift)
+// restate MuJoCo Warp's constraint and line-search formulas: Copyright 2025
+// The Newton Developers, SPDX-License-Identifier: Apache-2.0 (see NOTICE).
 // B200-native batched rigid-body physics step (sm_100a): device code.
 // Included by inst.cu, which instantiates the kernels per precision and
 // mesh support; abi.cu holds the C ABI and the launch shape.
@@ -61,10 +64,6 @@ template <int T, class R> __device__ __forceinline__ void mark(Arena<R> &A, int 
     A.prof[0] = t;
   }
 }
-
-#ifndef B200_STAGE_ATTR
-#define B200_STAGE_ATTR
-#endif
 
 template <class R> __device__ __forceinline__ R warp_sum(R v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -134,7 +133,7 @@ template <class R> __device__ __forceinline__ R jdot(const Mdl<R> &M, const Aren
 
 // ============================================================ position stage
 // forward kinematics, level by level (mjwarp_kinematics.cu:95-212 semantics)
-template <class R, int T> __device__ B200_STAGE_ATTR void kinematics(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ void kinematics(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   if (TID == 0) {
     A.xpos[0] = A.xpos[1] = A.xpos[2] = 0;
@@ -213,7 +212,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void kinematics(const Mdl<R
 // subtree com, centred inertia, motion axes, CRB and the mass matrix
 // (mjwarp_com_pos.cu:7-88, mjwarp_mass_matrix.cu:52-104).  Subtrees are
 // contiguous body intervals, so each sum has one owner and no barrier chain.
-template <class R, int T> __device__ B200_STAGE_ATTR void com_crb_mass(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ void com_crb_mass(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int nb = m.nbody;
   const R *mass = RF(body_mass);
@@ -477,16 +476,13 @@ __device__ R chol_solve_reg(R *H, const BlockRows &b, int maxn, R *colbuf, int s
 }
 
 // colbuf: 2 x nv reals (the register variant's double-buffered column, indexed by position)
-template <class R> __device__ B200_STAGE_ATTR void chol_blocks(R *H, const BlockRows &b, int maxn, int nv, R *colbuf) {
-#ifndef B200_CHOL_SMEM
+template <class R> __device__ void chol_blocks(R *H, const BlockRows &b, int maxn, int nv, R *colbuf) {
   if (b.rows <= 32 && maxn <= 16) chol_blocks_reg<R, 16>(H, b, maxn, colbuf, nv);
-  else
-#endif
-    chol_blocks_smem(H, b, maxn);
+  else chol_blocks_smem(H, b, maxn);
 }
 
 // solve L L^T x = x in place over a warp's blocks (x indexed by position)
-template <class R> __device__ B200_STAGE_ATTR void solve_blocks(const R *H, const BlockRows &b, R *x, int maxn, int lane) {
+template <class R> __device__ void solve_blocks(const R *H, const BlockRows &b, R *x, int maxn, int lane) {
   for (int k = 0; k < maxn; ++k) {
 #pragma unroll
     for (int s = 0; s < 4; ++s)
@@ -514,7 +510,6 @@ template <class R> __device__ B200_STAGE_ATTR void solve_blocks(const R *H, cons
 template <class R, int T> __device__ void tree_solve(const Mdl<R> &M, R *L, R *x, R *colbuf, bool factor) {
   const BlockRows b = TREE_ROWS(T);
   const int maxn = M.m.max_tree_dofs;
-#ifndef B200_CHOL_SMEM
   if (b.rows <= 32 && maxn <= 16) {
     const int p = b.start[0] + b.a[0];
     const R v = chol_solve_reg<R, 16>(L, b, maxn, colbuf, M.m.nv, factor, b.n[0] > 0 ? x[p] : R(0));
@@ -522,7 +517,6 @@ template <class R, int T> __device__ void tree_solve(const Mdl<R> &M, R *L, R *x
     __syncwarp();
     return;
   }
-#endif
   if (factor) chol_blocks_smem(L, b, maxn);
   solve_blocks(L, b, x, maxn, LANE);
 }
@@ -541,7 +535,7 @@ template <class R, int T> __device__ void pack_tree_blocks(const Mdl<R> &M, cons
 }
 
 // y = M x with the dense tree blocks (one thread per dof)
-template <class R, int T> __device__ B200_STAGE_ATTR void mass_mul(const Mdl<R> &M, const R *Mb, const R *x, R *y) {
+template <class R, int T> __device__ void mass_mul(const Mdl<R> &M, const R *Mb, const R *x, R *y) {
   FOR(i, M.m.nv) {
     const int t = IF(dof_treeid)[i], a = IF(tree_dofadr)[t], n = IF(tree_dofnum)[t];
     const R *row = Mb + IF(tree_madr)[t] + (i - a) * n;
@@ -554,7 +548,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void mass_mul(const Mdl<R> 
 // ============================================================ collision
 // CONVEX: the kernel variant for models with mesh geoms (plane-mesh and the
 // GJK/EPA pairs); models without meshes run the smaller variant.
-template <class R, int T, bool CONVEX> __device__ B200_STAGE_ATTR void collision(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T, bool CONVEX> __device__ void collision(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   // Broadphase first, then the narrowphase over the surviving pairs grouped
   // by family, so that the threads of a warp run the same collider.  The
@@ -621,7 +615,7 @@ template <class R> __device__ __forceinline__ R ipow(R a, R b) {
 }
 
 template <class R> struct KBI { R k, b, imp; };
-template <class R> __device__ B200_STAGE_ATTR KBI<R> impedance(const B200Model &m, const R *ref, const R *imp, R position) {
+template <class R> __device__ KBI<R> impedance(const B200Model &m, const R *ref, const R *imp, R position) {
   const R minval = R(1e-15), minimp = R(0.0001), maximp = R(0.9999);
   const bool refsafe = !(m.disable_flags & B200_DSBL_REFSAFE);
   const R ts = R(m.timestep);
@@ -665,7 +659,7 @@ template <class R> __device__ __forceinline__ void set_row_trees(const Mdl<R> &M
 // island and the tree layout is reused (packed blocks at tree_padr).
 // Otherwise the coupled contacts join trees into components, numbered by
 // their smallest tree index, so the blocks are deterministic.
-template <class R> __device__ B200_STAGE_ATTR void islands(const Mdl<R> &M, Arena<R> &A, bool coupled) {
+template <class R> __device__ void islands(const Mdl<R> &M, Arena<R> &A, bool coupled) {
   const int nt = M.m.ntree, nv = M.m.nv, lane = LANE;
   if (!coupled) {
     for (int t = lane; t < nt; t += 32) {
@@ -813,7 +807,7 @@ template <class R> __device__ void tree_segments(const Mdl<R> &M, Arena<R> &A, i
   __syncwarp();
 }
 
-template <class R, int T> __device__ B200_STAGE_ATTR void constraints(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ void constraints(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int cap = m.nefc_max, kmax = m.kmax_dof;
   const bool off = m.disable_flags & B200_DSBL_CONSTRAINT;
@@ -1035,7 +1029,7 @@ template <class R> __device__ __forceinline__ void force_cross(const R *v, const
   o[5] = -v[1] * f[3] + v[0] * f[4];
 }
 
-template <class R, int T> __device__ B200_STAGE_ATTR void velocity(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ void velocity(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   if (TID < 6) {
     const int c = TID;
@@ -1246,7 +1240,7 @@ template <class R> __device__ R action_component(const Mdl<R> &M, R action, int 
   return (a - (p[6 + axis] + p[axis]) * R(0.5)) * scale + (p[18 + axis] + p[12 + axis]) * R(0.5);
 }
 
-template <class R> __device__ B200_STAGE_ATTR void rotation_delta(R x, R y, R z, double *r) {
+template <class R> __device__ void rotation_delta(R x, R y, R z, double *r) {
   const R angle = msqrt(x * x + y * y + z * z);
   const R f = angle == R(0) ? R(0) : msin(angle * R(0.5)) / angle;
   const R raw[4] = {x * f, y * f, z * f, angle == R(0) ? R(1) : mcos(angle * R(0.5))};
@@ -1267,7 +1261,7 @@ template <class R> __device__ B200_STAGE_ATTR void rotation_delta(R x, R y, R z,
   r[7] = (double)(R)(q[2] * q[3] + q[1] * q[0]);
 }
 
-template <class R, int T> __device__ B200_STAGE_ATTR void osc_control(const Mdl<R> &M, Arena<R> &A, bool policy) {
+template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> &A, bool policy) {
   const B200Model &m = M.m;
   const int nv = m.nv, site = m.ee_site, body = IF(site_bodyid)[site];
   const int *vi = IF(osc_dofadr), *qi = IF(osc_qposadr), *ids = IF(osc_actuator);
@@ -1505,7 +1499,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void osc_control(const Mdl<
 }
 
 // ============================================================ actuation
-template <class R, int T> __device__ B200_STAGE_ATTR void actuation(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ void actuation(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   FOR(d, m.nv) {
     R f = 0;
@@ -1542,7 +1536,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void actuation(const Mdl<R>
 // ============================================================ Newton
 // mjwarp_solver_state.cu, mjwarp_constraint.cu, mjwarp_hessian.cu,
 // mjwarp_direction.cu, mjwarp_linesearch.cu
-template <class R, int T> __device__ B200_STAGE_ATTR void eval_gradient(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ void eval_gradient(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int nefc = A.iscal[1], nf = A.iscal[2], nv = m.nv;
   const R impratio = R(m.impratio_invsqrt);
@@ -1613,7 +1607,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void eval_gradient(const Md
 // pair, larger index first, so every entry's sum is deterministic.  The cone
 // matrices' scalars are staged per contact in efc_quad, which the line search
 // rewrites before its next use.
-template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ void hessian(const Mdl<R> &M, Arena<R> &A) {
   // unchanged constraint states and no cone-state contact: H, and its factor
   // still held in A.H, are exactly what this assembly would produce again
   if (!A.iscal[14]) return;
@@ -1719,17 +1713,13 @@ template <class R, int T> __device__ B200_STAGE_ATTR void hessian(const Mdl<R> &
 
 // Cholesky of every island block (islands dealt to the world's warps),
 // H x = grad, search = -x (mjwarp_direction.cu:80-160)
-template <class R, int T> __device__ B200_STAGE_ATTR void direction(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ void direction(const Mdl<R> &M, Arena<R> &A) {
   const int nv = M.m.nv;
   R *x = A.xs;
   const int lane = LANE, maxn = A.iscal[12];
   const bool refactor = A.iscal[14];
   const BlockRows b = ISLAND_ROWS(T);
-#ifndef B200_CHOL_SMEM
   const bool reg = b.rows <= 32 && maxn <= 16;
-#else
-  const bool reg = false;
-#endif
   if (reg) {  // one row per lane: factor and solve in registers
     const int p = b.start[0] + b.a[0];
     const R xv = chol_solve_reg<R, 16>(A.H, b, maxn, A.colbuf, nv, refactor, b.n[0] > 0 ? A.grad[A.isl_dof[p]] : R(0));
@@ -1786,7 +1776,7 @@ template <class R> struct LsRow {
   int kind, state0;
   R x, v, d, loss, q0, q1, q2, u0, v0, uu, uv, vv, dm, mu, cost0, t0, r0;
 };
-template <class R> __device__ B200_STAGE_ATTR LsRow<R> load_row(const Mdl<R> &M, const Arena<R> &A, int r, int nf) {
+template <class R> __device__ LsRow<R> load_row(const Mdl<R> &M, const Arena<R> &A, int r, int nf) {
   LsRow<R> o;
   o.kind = 0; o.state0 = 0;
   o.x = o.v = o.d = o.loss = o.q0 = o.q1 = o.q2 = o.u0 = o.v0 = o.uu = o.uv = o.vv = o.dm = o.mu = o.cost0 = o.t0 = o.r0 = 0;
@@ -1816,7 +1806,7 @@ template <class R> __device__ B200_STAGE_ATTR LsRow<R> load_row(const Mdl<R> &M,
   if (o.kind == 1) o.loss = A.efc_floss[r];
   return o;
 }
-template <class R> __device__ B200_STAGE_ATTR Pt<R> friction_point(const LsRow<R> &r, R x) {
+template <class R> __device__ Pt<R> friction_point(const LsRow<R> &r, R x) {
   const R rf = safe_div(r.loss, r.d);
   if (-rf < x && x < rf) {
     const R vd = r.v * r.d;
@@ -1825,7 +1815,7 @@ template <class R> __device__ B200_STAGE_ATTR Pt<R> friction_point(const LsRow<R
   if (x <= -rf) return {r.loss * (R(-0.5) * rf - x), -r.loss * r.v, R(0)};
   return {r.loss * (R(-0.5) * rf + x), r.loss * r.v, R(0)};
 }
-template <class R> __device__ B200_STAGE_ATTR Pt<R> eval_zero(const LsRow<R> &r) {
+template <class R> __device__ Pt<R> eval_zero(const LsRow<R> &r) {
   if (r.kind == 4) return {0, 0, 0};
   if (r.kind == 3) {
     if (r.state0 == 1) return {r.q0, r.q1, R(2) * r.q2};
@@ -1840,7 +1830,7 @@ template <class R> __device__ B200_STAGE_ATTR Pt<R> eval_zero(const LsRow<R> &r)
   const R vd = r.v * r.d;
   return {R(0.5) * r.d * r.x * r.x, vd * r.x, r.v * vd};
 }
-template <class R> __device__ B200_STAGE_ATTR Pt<R> cone_quad_shift(const LsRow<R> &r, R alpha, R n, R tsqr) {
+template <class R> __device__ Pt<R> cone_quad_shift(const LsRow<R> &r, R alpha, R n, R tsqr) {
   const R aq2 = alpha * r.q2;
   R cost = alpha * (aq2 + r.q1);
   if (r.state0 == 4) {
@@ -1849,7 +1839,7 @@ template <class R> __device__ B200_STAGE_ATTR Pt<R> cone_quad_shift(const LsRow<
   } else if (r.state0 == 0) cost = R(0.5) * r.dm * (R(1) + r.mu * r.mu) * (n * n + mmax(tsqr, R(0)));
   return {cost, R(2) * aq2 + r.q1, R(2) * r.q2};
 }
-template <class R> __device__ B200_STAGE_ATTR Pt<R> eval_shift(const LsRow<R> &r, R alpha) {
+template <class R> __device__ Pt<R> eval_shift(const LsRow<R> &r, R alpha) {
   if (r.kind == 4) return {0, 0, 0};
   if (r.kind == 3) {
     const R n = r.u0 + alpha * r.v0, tsd = alpha * (R(2) * r.uv + alpha * r.vv), tsqr = r.uu + tsd;
@@ -1899,7 +1889,7 @@ template <int T, class R> __device__ __forceinline__ Pt<R> world_pt(Pt<R> p, R *
   return s;
 }
 
-template <class R, int T> __device__ B200_STAGE_ATTR void linesearch(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ void linesearch(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int nv = m.nv, nefc = A.iscal[1], nf = A.iscal[2];
   mass_mul<R, T>(M, A.M, A.search, A.Mv);
@@ -2031,7 +2021,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void linesearch(const Mdl<R
 
 // Newton solve (mjwarp_solver_state.cu, physics.py:47-70): initial
 // gradient/Hessian/direction, then iterations until the world's stop rule.
-template <class R, int T> __device__ B200_STAGE_ATTR void newton_init(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ void newton_init(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int nv = m.nv, nefc = A.iscal[1];
   const bool warm = !(m.disable_flags & B200_DSBL_WARMSTART);
@@ -2047,7 +2037,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void newton_init(const Mdl<
   mark<T>(A, 9);
 }
 
-template <class R, int T> __device__ B200_STAGE_ATTR void newton_iteration(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ void newton_iteration(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const R tol = R(m.tolerance), scale = R(m.meaninertia) * R(m.nv);
   linesearch<R, T>(M, A);
@@ -2071,7 +2061,7 @@ template <class R, int T> __device__ B200_STAGE_ATTR void newton_iteration(const
 }
 
 // ============================================================ Euler
-template <class R, int T> __device__ B200_STAGE_ATTR void euler(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ void euler(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int nv = m.nv;
   const R dt = R(m.timestep);
@@ -2115,6 +2105,11 @@ template <class R, int T> __device__ B200_STAGE_ATTR void euler(const Mdl<R> &M,
   }
   if (TID == 0) A.scal[5] += dt;
   SYNC();
+  // state check (MuJoCo mj_checkPos / mj_checkVel): non-finite or beyond 1e10
+  bool bad = false;
+  FOR(i, m.nq) bad |= !(mabs(A.qpos[i]) <= R(1e10));
+  FOR(i, nv) bad |= !(mabs(A.qvel[i]) <= R(1e10));
+  if (bad) atomicOr(&A.iscal[3], B200_STATUS_BADSTATE);
 }
 
 // ============================================================ driver
@@ -2125,7 +2120,7 @@ __device__ __forceinline__ int *irow_of(int *p, int w, int width) {
   return p ? p + (size_t)w * width : nullptr;
 }
 
-template <class R, int T> __device__ B200_STAGE_ATTR void load_world(const B200Model &m, const B200Data &d, Arena<R> &A, int w) {
+template <class R, int T> __device__ void load_world(const B200Model &m, const B200Data &d, Arena<R> &A, int w) {
   const R *src;
   src = row_of<R>(d.qpos, w, m.nq); FOR(i, m.nq) A.qpos[i] = src[i];
   src = row_of<R>(d.qvel, w, m.nv); FOR(i, m.nv) A.qvel[i] = src[i];
@@ -2143,9 +2138,18 @@ template <class R, int T> __device__ B200_STAGE_ATTR void load_world(const B200M
     A.iscal[6] = irow_of(d.error, w, 1)[0];
   }
   SYNC();
+  // a world handed in with a bad state (MuJoCo mj_checkPos / mj_checkVel) is not stepped
+  bool bad = false;
+  FOR(i, m.nq) bad |= !(mabs(A.qpos[i]) <= R(1e10));
+  FOR(i, m.nv) bad |= !(mabs(A.qvel[i]) <= R(1e10));
+  if (bad) atomicOr(&A.iscal[3], B200_STATUS_BADSTATE);
+  SYNC();
 }
 
-template <class R, int T> __device__ __noinline__ void store_state(const B200Model &m, const B200Data &d, Arena<R> &A, int w) {
+// obs: write the observation slab (it needs this launch's kinematics, which a
+// world that did not step has not computed)
+template <class R, int T>
+__device__ __noinline__ void store_state(const B200Model &m, const B200Data &d, Arena<R> &A, int w, bool obs) {
   R *dst;
   dst = row_of<R>(d.qpos, w, m.nq); FOR(i, m.nq) dst[i] = A.qpos[i];
   dst = row_of<R>(d.qvel, w, m.nv); FOR(i, m.nv) dst[i] = A.qvel[i];
@@ -2157,7 +2161,7 @@ template <class R, int T> __device__ __noinline__ void store_state(const B200Mod
   if ((dst = row_of<R>(d.qacc, w, m.nv))) FOR(i, m.nv) dst[i] = A.qacc[i];
   // observation slab: arm+gripper qpos/qvel (current), end-effector pose and
   // free-body poses (last substep's kinematics, as MuJoCo publishes them)
-  if ((dst = row_of<R>(d.obs, w, m.nobs))) {
+  if (obs && (dst = row_of<R>(d.obs, w, m.nobs))) {
     const Mdl<R> M(m);
     FOR(e, m.nobs) {
       R v = 0;
@@ -2175,8 +2179,11 @@ template <class R, int T> __device__ __noinline__ void store_state(const B200Mod
       } else if (e < 25 + 7 * m.nfree) {
         const int f = (e - 25) / 7, c = (e - 25) % 7, b = IF(free_bodyid)[f];
         v = c < 3 ? A.xpos[3 * b + c] : A.xquat[4 * b + c - 3];
+      } else if (m.task_body >= 0 && m.task_body < m.nfree) {
+        // reward, then done: the task body lifted above task_lift_z (sparse success)
+        v = R(A.xpos[3 * IF(free_bodyid)[m.task_body] + 2] > R(m.task_lift_z));
       }
-      dst[e] = v;  // reward and done are 0: synthetic scenes carry no task predicates
+      dst[e] = v;
     }
   }
   if (TID == 0) {
@@ -2209,7 +2216,20 @@ template <class R, int T> __device__ __noinline__ void store_outputs(const B200M
   if ((dst = row_of<R>(d.con_frame, w, nc * 9)))
     FOR(e, ncon * 9) dst[e] = A.con[(size_t)A.con_order[e / 9] * kCWidth + kCFrame + e % 9];
   if ((dst = row_of<R>(d.efc_force, w, m.nefc_max))) FOR(r, nefc) dst[r] = A.efc_force[r];
+  if ((dst = row_of<R>(d.efc_D, w, m.nefc_max))) FOR(r, nefc) dst[r] = A.efc_D[r];
+  if ((dst = row_of<R>(d.efc_aref, w, m.nefc_max))) FOR(r, nefc) dst[r] = A.efc_aref[r];
+  if ((dst = row_of<R>(d.efc_J, w, m.nefc_max * nv))) {
+    const Mdl<R> M(m);
+    FOR(e, nefc * nv) {  // rows expanded to dense dof order
+      const int r = e / nv, dof = e % nv, t0 = A.row_t[2 * r], t1 = A.row_t[2 * r + 1];
+      const int n0 = t0 >= 0 ? IF(tree_dofnum)[t0] : 0, td = IF(dof_treeid)[dof], off = dof - IF(tree_dofadr)[td];
+      const R *row = A.J + (size_t)r * m.kmax_dof;
+      dst[e] = td == t0 ? row[off] : td == t1 ? row[n0 + off] : R(0);
+    }
+  }
   int *idst;
+  if ((idst = irow_of(d.efc_type, w, m.nefc_max))) FOR(r, nefc) idst[r] = A.efc_type[r];
+  if ((idst = irow_of(d.efc_id, w, m.nefc_max))) FOR(r, nefc) idst[r] = A.efc_id[r];
   if ((idst = irow_of(d.con_geom, w, nc * 2)))
     FOR(e, ncon * 2) idst[e] = e & 1 ? A.con_g2[A.con_order[e >> 1]] : A.con_g1[A.con_order[e >> 1]];
   if (TID == 0) {
@@ -2219,52 +2239,24 @@ template <class R, int T> __device__ __noinline__ void store_outputs(const B200M
 }
 
 
-// A CTA holds `wpc` worlds, one warp each, in consecutive shared-memory
-// arenas.  The worlds advance through the stages of a substep together
-// (CTA barrier between stages) so that co-resident warps execute the same
-// code region; the Newton loop runs until every world of the CTA has met its
-// stop rule, worlds already done idle.  Warps past the last world take part
-// in the barriers only.
-// B200_SYNC_LEVEL: 2 = CTA barrier after every stage (lockstep worlds),
-// 1 = one CTA barrier per substep, 0 = worlds run free (warp syncs only).
-// B200_SYNC_LEVEL 3: the CTA barrier follows every stage from collision to
-// actuation; the Newton loop, Euler and the next substep's kinematics, CoM /
-// CRB and mass factor run per world, so worlds that meet the Newton stop
-// rule early continue instead of idling.
-#ifndef B200_SYNC_LEVEL
-#define B200_SYNC_LEVEL 2
-#endif
-#if B200_SYNC_LEVEL >= 2
-#define STAGE_SYNC() __syncthreads()
-#else
-#define STAGE_SYNC() SYNC()
-#endif
-#define STAGE(call, k)  \
-  do {                  \
-    if (act) {          \
-      call;             \
-      mark<T>(A, k);       \
-    }                   \
-    STAGE_SYNC();       \
+// A CTA holds `wpc` worlds in consecutive shared-memory arenas.  The worlds
+// advance through the stages of a substep together (CTA barrier after every
+// stage) so that co-resident warps execute the same code region and the
+// instruction caches serve them all; the Newton loop runs until every world of
+// the CTA has met its stop rule, worlds already done idle.  Warps past the last
+// world take part in the barriers only.
+#define STAGE(call, k)       \
+  do {                       \
+    if (act) {               \
+      call;                  \
+      mark<T>(A, k);         \
+    }                        \
+    __syncthreads();         \
     if (act) mark<T>(A, 15); \
   } while (0)
-// a stage that level 3 runs without the CTA barrier (world barrier only)
-#if B200_SYNC_LEVEL == 3
-#define STAGE_FREE(call, k) \
-  do {                      \
-    if (act) {              \
-      call;                 \
-      mark<T>(A, k);        \
-      SYNC();               \
-      mark<T>(A, 15);       \
-    }                       \
-  } while (0)
-#else
-#define STAGE_FREE(call, k) STAGE(call, k)
-#endif
 
 // factor of the mass matrix, one block per kinematic tree (mjwarp_mass_factor.cu)
-template <class R, int T> __device__ B200_STAGE_ATTR void mass_factor(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T> __device__ void mass_factor(const Mdl<R> &M, Arena<R> &A) {
   pack_tree_blocks<R, T>(M, A.M, A.L);
   SYNC();
   chol_blocks(A.L, TREE_ROWS(T), M.m.max_tree_dofs, M.m.nv, A.colbuf);
@@ -2272,29 +2264,20 @@ template <class R, int T> __device__ B200_STAGE_ATTR void mass_factor(const Mdl<
 }
 
 template <class R, bool CONVEX, int T> __device__ void step1_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
-  STAGE_FREE((kinematics<R, T>(M, A)), 1);
-  STAGE_FREE((com_crb_mass<R, T>(M, A)), 2);
-  STAGE_FREE((mass_factor<R, T>(M, A)), 3);
-#if B200_SYNC_LEVEL == 3
-  __syncthreads();  // worlds meet again before the collision code
-  if (act) mark<T>(A, 15);
-#endif
+  STAGE((kinematics<R, T>(M, A)), 1);
+  STAGE((com_crb_mass<R, T>(M, A)), 2);
+  STAGE((mass_factor<R, T>(M, A)), 3);
   STAGE((collision<R, T, CONVEX>(M, A)), 4);
   STAGE((constraints<R, T>(M, A)), 5);
   STAGE((velocity<R, T>(M, A)), 6);
 }
 
 template <class R, int T> __device__ void newton_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
-  STAGE_FREE((newton_init<R, T>(M, A)), 0);
-#if B200_SYNC_LEVEL == 2
+  STAGE((newton_init<R, T>(M, A)), 0);
   while (__syncthreads_or(act && !A.iscal[5])) {
     if (act) mark<T>(A, 15);  // barrier wait and idle iterations of worlds already done
     if (act && !A.iscal[5]) newton_iteration<R, T>(M, A);
   }
-#else
-  if (act)
-    while (!A.iscal[5]) newton_iteration<R, T>(M, A);  // world-uniform: iscal[5] is read after a world sync
-#endif
   if (act) mark<T>(A, 15);
 }
 
@@ -2304,7 +2287,8 @@ __global__ void __launch_bounds__(384, 1) control_step(const __grid_constant__ B
   static_assert(T % 32 == 0 && T / 32 <= Arena<R>::kColbufWarps, "per-warp scratch covers at most four warps");
   extern __shared__ __align__(16) unsigned char smem[];
   const int slot = threadIdx.x / T, w = blockIdx.x * wpc + slot;
-  const bool act = slot < wpc && w < d.nworld;
+  const bool in = slot < wpc && w < d.nworld;
+  bool act = in;  // the world steps; false once its state went bad (B200_STATUS_BADSTATE)
   // the world's arena descriptor heads its shared-memory region (one copy per
   // world, read by broadcast instead of a per-thread local-memory copy)
   unsigned char *wbase = smem + (size_t)(slot < wpc ? slot : 0) * arena;
@@ -2322,10 +2306,10 @@ __global__ void __launch_bounds__(384, 1) control_step(const __grid_constant__ B
     SYNC();
   }
   __syncthreads();
+  int stepped = 0;
   for (int s = 0; s < substeps; ++s) {
-#if B200_SYNC_LEVEL == 1
-    __syncthreads();
-#endif
+    // world-uniform: the status word is read after a CTA barrier
+    if (act && (A.iscal[3] & B200_STATUS_BADSTATE)) act = false;
     step1_stages<R, CONVEX, T>(M, A, act);
     STAGE((osc_control<R, T>(M, A, policy && s == 0)), 7);
     STAGE((actuation<R, T>(M, A)), 8);
@@ -2343,16 +2327,19 @@ __global__ void __launch_bounds__(384, 1) control_step(const __grid_constant__ B
       if (d.efc_k2) irow_of(d.efc_k2, w, 1)[0] += A.iscal[23];
       if (d.fact_blk) irow_of(d.fact_blk, w, 1)[0] += A.iscal[24];
       A.iscal[24] = 0;
+      if (s < 32 && d.niter_trace) irow_of(d.niter_trace, w, 32)[s] = it;
+      if (s < 32 && d.ls_trace) irow_of(d.ls_trace, w, 32)[s] = evals;
     }
     if (act && s == substeps - 1) store_outputs<R, T>(m, d, A, w);
-    STAGE_FREE((euler<R, T>(M, A)), 14);
+    STAGE((euler<R, T>(M, A)), 14);
+    stepped += act;
   }
-  if (!act) return;
+  if (!in) return;
   if (TID == 0) {
     if (d.ls_total) irow_of(d.ls_total, w, 1)[0] += A.iscal[7];
-    if (d.integration_count) irow_of(d.integration_count, w, 1)[0] += substeps;
+    if (d.integration_count) irow_of(d.integration_count, w, 1)[0] += stepped;
   }
-  store_state<R, T>(m, d, A, w);
+  store_state<R, T>(m, d, A, w, stepped > 0);
   if (TID == 0 && d.stage_cycles) {
     int *out = irow_of(d.stage_cycles, w, 16);
     for (int k = 1; k < 16; ++k) out[k] += (int)A.prof[k];
@@ -2384,7 +2371,7 @@ __global__ void __launch_bounds__(384, 1) forward_step(const __grid_constant__ B
   newton_stages<R, T>(M, A, act);
   if (!act) return;
   store_outputs<R, T>(m, d, A, w);
-  store_state<R, T>(m, d, A, w);
+  store_state<R, T>(m, d, A, w, true);
 }
 
 }  // namespace b200

@@ -113,6 +113,10 @@ class PackedModel:
             setattr(m, n, int(self.sizes[n]))
         for n in LAYOUT.real_scalars:
             setattr(m, n, float(self.scene.scalars[n]))
+        # The FP32 engine floors the Newton tolerance at 1e-6
+        # (cuda_fp32/model.py:71); the FP64 engine keeps the model's own.
+        if self.dtype == np.float64:
+            m.tolerance = float(self.scene.options.get('tolerance', m.tolerance))
         for n, _ in LAYOUT.int_arrays + LAYOUT.real_arrays:
             setattr(m, 'off_' + n, self.offsets[n])
         return m

@@ -12,6 +12,7 @@ Device memory is owned by PyTorch tensors (plumbing only); every physics
 computation runs in libb200phys.so.  There is no CPU fallback: without a CUDA
 device or without the built library, construction raises.
 """
+from contextlib import contextmanager
 from threading import RLock
 
 import numpy as np
@@ -21,6 +22,8 @@ from . import native
 from .scene import Scene, scene_a
 
 OVERFLOW_LIMITS = 0x200 | 0x400  # iteration / line-search limits are legal exits
+# inspection outputs that a step never needs: allocated only for debug runtimes
+DEBUG_FIELDS = ('efc_J', 'efc_D', 'efc_aref', 'efc_type', 'efc_id', 'niter_trace', 'ls_trace')
 
 
 def failure_report(overflow, error, limit=16):
@@ -35,7 +38,8 @@ def failure_report(overflow, error, limit=16):
 class Runtime:
     """Owned device buffers plus the control-step graph of one world shard."""
 
-    def __init__(self, scene, num_envs, *, device='cuda:0', precision='fp32', world_offset=0, library=None):
+    def __init__(self, scene, num_envs, *, device='cuda:0', precision='fp32', world_offset=0, library=None,
+                 debug=False):
         if not torch.cuda.is_available():
             raise RuntimeError('the b200 physics engine requires a CUDA device')
         self.device = torch.device(device)
@@ -50,9 +54,11 @@ class Runtime:
             self.model_ints = torch.from_numpy(self.packed.ints).to(self.device)
             self.model = self.packed.struct(self.model_real.data_ptr(), self.model_ints.data_ptr())
             real, ints = self.packed.data_widths()
-            self.buffers = {k: torch.zeros((self.n, w), dtype=self.dtype, device=self.device) for k, w in real.items()}
+            keep = lambda k: debug or k not in DEBUG_FIELDS  # noqa: E731
+            self.buffers = {k: torch.zeros((self.n, w), dtype=self.dtype, device=self.device)
+                            for k, w in real.items() if keep(k)}
             self.buffers.update({k: torch.zeros((self.n, w), dtype=torch.int32, device=self.device)
-                                 for k, w in ints.items()})
+                                 for k, w in ints.items() if keep(k)})
             self.mask = torch.ones(self.n, dtype=torch.int32, device=self.device)
         self.data = native.data_struct(self.buffers, self.n, self.world_offset, pointer=lambda t: t.data_ptr())
         smem = self.lib.smem_bytes(self.model)
@@ -112,16 +118,17 @@ class Runtime:
             self._pinned = dict(
                 action=torch.zeros((self.n, 7), dtype=self.dtype, pin_memory=True),
                 obs=torch.zeros((self.n, nobs), dtype=self.dtype, pin_memory=True),
-                status=torch.zeros((2, self.n), dtype=torch.int32, pin_memory=True))
-            self._status = torch.zeros((2, self.n), dtype=torch.int32, device=self.device)
+                status=torch.zeros((3, self.n), dtype=torch.int32, pin_memory=True))
+            self._status = torch.zeros((3, self.n), dtype=torch.int32, device=self.device)
         return self._pinned
 
     def step_host(self, actions):
         """One control step from host actions to host observations.
 
         H2D copy of the actions (pinned), the control graph, then one D2H copy
-        of the observation slab and one of the status words; returns views of
-        the pinned host buffers after the stream has drained."""
+        of the observation slab and one of the status words (overflow, error,
+        integration count); returns views of the pinned host buffers after the
+        stream has drained."""
         io = self.pinned_io()
         host = io['action']
         host.numpy()[:] = actions
@@ -130,7 +137,8 @@ class Runtime:
             self._graph.replay()
         else:
             self.launch_step(policy=True)
-        torch.stack([self.buffers['overflow'][:, 0], self.buffers['error'][:, 0]], out=self._status)
+        torch.stack([self.buffers['overflow'][:, 0], self.buffers['error'][:, 0],
+                     self.buffers['integration_count'][:, 0]], out=self._status)
         io['obs'].copy_(self.buffers['obs'], non_blocking=True)
         io['status'].copy_(self._status, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
@@ -140,7 +148,7 @@ class Runtime:
         return self.n * 7 * self.buffers['action'].element_size()
 
     def d2h_bytes_per_step(self):
-        return self.buffers['obs'].numel() * self.buffers['obs'].element_size() + 2 * self.n * 4
+        return self.buffers['obs'].numel() * self.buffers['obs'].element_size() + 3 * self.n * 4
 
     def count(self, kind, mask=None):
         """Host counters of reset/epoch events (cuda_fp32 bridges count kinds 2/3)."""
@@ -215,8 +223,26 @@ class B200BatchEnv:
         self._lock = RLock()
         self.runtime = Runtime(self.scene, num_envs, device=device, precision=precision, world_offset=world_offset)
         self.nq, self.nv = self.scene.sizes['nq'], self.scene.sizes['nv']
-        self._closed = False
+        self._closed = self._failed = False
+        self._integrations = np.zeros(num_envs, np.int64)
         self.reset(init_states=init_states)
+
+    # ---- failure quarantine (cuda_fp32/environment.py:126-140, batch_env.py:298-302,376-384)
+    def _open(self):
+        if self._closed:
+            raise RuntimeError('B200 batch environment is closed')
+        if self._failed:
+            raise RuntimeError('B200 batch execution failed; close and rebuild required')
+
+    @contextmanager
+    def _mutation(self):
+        """Any failure while device state changes quarantines the batch: its
+        worlds may be partly advanced, so later calls raise until rebuilt."""
+        try:
+            yield
+        except BaseException:
+            self._failed = True
+            raise
 
     # ---- lifecycle ----------------------------------------------------
     def _initial_rows(self, seed):
@@ -225,34 +251,51 @@ class B200BatchEnv:
 
     def reset(self, init_states=None, ids=None):
         with self._lock:
+            self._open()
             rows = self._initial_rows(self.seed_value) if init_states is None else np.asarray(init_states, np.float64)
             if ids is not None and init_states is None:
                 rows = rows[np.asarray(ids)]
-            self.runtime.set_state(rows, ids=ids, reset=True)
-            self.runtime.check()
+            with self._mutation():
+                self.runtime.set_state(rows, ids=ids, reset=True)
+                self.runtime.check()
+                self._integrations[:] = self.runtime.buffers['integration_count'][:, 0].cpu().numpy()
             return self.observations()
 
     def set_init_state(self, init_states, ids=None):
         """Restore [time, qpos, qvel] rows; controller history is kept (README.md:320-325)."""
         with self._lock:
-            self.runtime.set_state(init_states, ids=ids, reset=False)
-            self.runtime.check()
+            self._open()
+            with self._mutation():
+                self.runtime.set_state(init_states, ids=ids, reset=False)
+                self.runtime.check()
             return self.observations()
 
     def get_sim_state(self):
+        self._open()
         s = self.runtime.download_state()
         return np.concatenate([s['time'], s['qpos'], s['qvel']], axis=1)
 
     def step(self, actions):
+        """One control step of every world: (obs, reward, done, infos).
+
+        reward and done are the synthetic task's sparse success predicate,
+        evaluated on the device.  A fatal status word, or a world that did not
+        commit every substep, raises and quarantines the batch."""
         actions = np.asarray(actions)
-        if actions.shape != (self.num_envs, 7) or not np.all(np.isfinite(actions)):
-            raise ValueError('actions must be finite with shape (num_envs, 7)')
         with self._lock:
-            slab, status = self.runtime.step_host(actions)
-            status = status.numpy()
-            fatal = status[0] & ~OVERFLOW_LIMITS
-            if np.any(fatal) or np.any(status[1]):
-                raise RuntimeError(failure_report(status[0], status[1]))
+            self._open()
+            if actions.shape != (self.num_envs, 7) or not np.all(np.isfinite(actions)):
+                raise ValueError('actions must be finite with shape (num_envs, 7)')
+            with self._mutation():
+                slab, status = self.runtime.step_host(actions)
+                status = status.numpy()
+                fatal = status[0] & ~OVERFLOW_LIMITS
+                if np.any(fatal) or np.any(status[1]):
+                    raise RuntimeError(failure_report(status[0], status[1]))
+                committed = status[2].astype(np.int64) - self._integrations
+                if not np.all(committed == self.runtime.substeps):
+                    raise RuntimeError('B200 batch did not commit every requested physics substep')
+                self._integrations += committed
             slab = slab.numpy().copy()
             nfree = self.scene.sizes['nfree']
             obs = dict(robot0_joint_pos=slab[:, :9], robot0_joint_vel=slab[:, 9:18], robot0_eef_pos=slab[:, 18:21],
@@ -270,9 +313,12 @@ class B200BatchEnv:
                     .cpu().numpy())
 
     def diagnostics(self):
-        overflow, error = self.runtime.check()
+        """Status without raising (a quarantined batch still reports why)."""
         b = self.runtime.buffers
-        return dict(physics_backend='gpu', physics_engine='b200', precision=self.precision,
+        torch.cuda.synchronize(self.runtime.device)
+        overflow = b['overflow'].cpu().numpy().reshape(-1)
+        error = b['error'].cpu().numpy().reshape(-1)
+        return dict(physics_backend='gpu', physics_engine='b200', precision=self.precision, failed=self._failed,
                     actual_integration_count=b['integration_count'].cpu().numpy().reshape(-1).tolist(),
                     first_error=error.tolist(), substeps=self.runtime.substeps,
                     capacities=dict(nconmax=self.scene.sizes['ncon_max'], njmax=self.scene.sizes['nefc_max']),
@@ -284,7 +330,8 @@ class B200BatchEnv:
         g = lambda k: b[k].cpu().numpy().reshape(-1).tolist()  # noqa: E731
         return dict(integration_count=g('integration_count'), state_epoch=self.runtime.state_epoch.tolist(),
                     reset_events=self.runtime.reset_events.tolist(), newton_attempts=g('newton_total'),
-                    first_error=g('error'), upstream_status=g('overflow'), ncon=g('ncon'), nefc=g('nefc'))
+                    first_error=g('error'), upstream_status=g('overflow'), ncon=g('ncon'), nefc=g('nefc'),
+                    newton_iterations=g('niter'), linesearch_evaluations=g('ls_total'))
 
     def close(self):
         with self._lock:

@@ -430,7 +430,8 @@ class Scene:
                           disable_flags=opt.get('disable_flags', 0),
                           ee_site=[s.name for _, s in S].index(self.controller['site']),
                           nvs=nvs, kmax_dof=max(pair_dofs + [1]), max_tree_dofs=int(tree_dofnum.max()),
-                          osc_uncouple=int(self.controller.get('uncouple', True)))
+                          osc_uncouple=int(self.controller.get('uncouple', True)),
+                          task_body=int(opt.get('task_body', 0 if free_bodies else -1)))
         ints.update(
             body_parentid=parent, body_rootid=root, body_weldid=weld,
             body_jntnum=np.array(body_jntnum, np.int32), body_jntadr=np.array(body_jntadr, np.int32),
@@ -505,7 +506,8 @@ class Scene:
         self.scalars = dict(timestep=opt['timestep'], gravity_x=0.0, gravity_y=0.0, gravity_z=-9.81,
                             tolerance=max(opt['tolerance'], 1e-6), ls_tolerance=opt.get('ls_tolerance', 0.01),
                             impratio_invsqrt=1.0 / math.sqrt(max(opt.get('impratio', 1.0), 1e-15)),
-                            meaninertia=1.0, ccd_tolerance=opt.get('ccd_tolerance', 1e-6))
+                            meaninertia=1.0, ccd_tolerance=opt.get('ccd_tolerance', 1e-6),
+                            task_lift_z=opt.get('task_lift_z', 0.2))
         self.geom_names = [g.name for _, g in G]
         self.body_names = [b.name for b in B]
         self._set_const()
@@ -775,7 +777,7 @@ def scene_a(seed=0, cone='elliptic', nconmax=32, njmax=None, iterations=50, ls_i
 
 
 def scene_b(seed=0, cone='elliptic', nconmax=96, njmax=None, iterations=50, ls_iterations=50,
-            tolerance=1e-8):
+            tolerance=1e-8, hull_points=32, epa_iterations=32, ccd_tolerance=1e-6):
     """BASELINE scene B: scene A's arm plus 12 dropped free objects (nq=93, nv=81).
 
     4 boxes (half-extents U[0.02,0.05]), 4 capsules (radius U[0.015,0.04],
@@ -803,7 +805,7 @@ def scene_b(seed=0, cone='elliptic', nconmax=96, njmax=None, iterations=50, ls_i
             radius = size[0]
         else:
             axes = rng.uniform(0.02, 0.06, 3)
-            d = rng.normal(size=(32, 3))
+            d = rng.normal(size=(hull_points, 3))
             d /= np.linalg.norm(d, axis=1, keepdims=True)
             mesh = convex_mesh(d * axes)
             size, margin = tuple(np.ptp(mesh['vert'], axis=0) / 2), 0.001
@@ -816,7 +818,8 @@ def scene_b(seed=0, cone='elliptic', nconmax=96, njmax=None, iterations=50, ls_i
         bodies.append(b)
         objects.append(dict(id=len(bodies) - 1, radius=radius, rest_z=None, drop=(0.05, 0.15), tumble=True))
     opt = dict(timestep=0.002, iterations=iterations, ls_iterations=ls_iterations, tolerance=tolerance,
-               cone=1 if cone == 'elliptic' else 0, impratio=1.0, ls_tolerance=0.01)
+               cone=1 if cone == 'elliptic' else 0, impratio=1.0, ls_tolerance=0.01, epa_iterations=epa_iterations,
+               ccd_tolerance=ccd_tolerance)
     scene = Scene('scene_b', bodies, actuators, opt, dict(nconmax=nconmax, njmax=njmax), controller)
     scene.objects = objects
     scene.object_square = 0.5

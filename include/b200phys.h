@@ -39,8 +39,13 @@ extern "C" {
 /* Overflow bits (reference OverflowType, cuda_fp32/constants.py:89-101). */
 #define B200_OVERFLOW_NEFC (1 << 0)
 #define B200_OVERFLOW_NARROWPHASE (1 << 3)
+#define B200_OVERFLOW_EPA_HORIZON (1 << 8) /* EPA polytope pool full (fatal) */
 #define B200_OVERFLOW_ITERATIONS (1 << 9)
 #define B200_OVERFLOW_LS_ITERATIONS (1 << 10)
+/* Non-finite or huge state (|x| > 1e10, MuJoCo's mjMAXVAL in mj_checkPos /
+ * mj_checkVel): set after the substep that produced it; the world is not
+ * stepped further in that launch (fatal; no reference bit has this value). */
+#define B200_STATUS_BADSTATE (1 << 16)
 
 /* disable_flags bits (MuJoCo 3.x mjtDisableBit positions). */
 #define B200_DSBL_CONSTRAINT (1 << 0)
@@ -106,7 +111,8 @@ size_t b200phys_model_bytes(void); /* sizeof(B200Model), checked by the host */
 size_t b200phys_data_bytes(void);  /* sizeof(B200Data), checked by the host */
 
 /* Dynamic shared memory one world needs for this model, in bytes
- * (0 if the model exceeds the per-block limit). */
+ * (0 if the model is rejected or one world's arena exceeds the 227 KB a
+ * CTA can opt into on sm_100). */
 size_t b200phys_world_smem_bytes(const B200Model *m);
 
 /* Configure the kernels for this model (dynamic shared memory opt-in).

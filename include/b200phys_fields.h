@@ -17,6 +17,16 @@
  *
  * Data fields carry a per-world width expression written in model size names;
  * the host evaluates it to allocate world-major [nworld, width] buffers.
+ * Every output pointer may be NULL (not written).  Inspection outputs that a
+ * step never needs (the dense constraint rows efc_J / efc_D / efc_aref /
+ * efc_type / efc_id of the last substep, and the per-substep Newton and
+ * line-search counts niter_trace / ls_trace of the last control step, first
+ * 32 substeps) are allocated by the host only when it asks for them.
+ *
+ * task_body / task_lift_z: the synthetic scenes' task predicate.  Success is
+ * the free body free_bodyid[task_body] (its centre of mass frame origin) above
+ * task_lift_z; reward = 1 and done = 1 on success, else 0 (LIBERO's sparse
+ * reward, batch_env.py:463-475).  task_body < 0 disables the predicate.
  */
 #ifndef B200PHYS_FIELDS_H
 #define B200PHYS_FIELDS_H
@@ -28,12 +38,12 @@
   X(iterations) X(ls_iterations) X(disable_flags) X(ee_site) X(real_bytes) \
   X(nvs) X(kmax_dof) X(max_tree_dofs) X(osc_uncouple) X(nfree) X(nobs) \
   X(nmesh) X(nmeshvert) X(nmeshpoly) X(nmeshpolyvert) X(nmeshpolymap) \
-  X(ccd_iterations) X(epa_iterations) X(nL)
+  X(ccd_iterations) X(epa_iterations) X(nL) X(task_body)
 
 /* real scalars of the model (stored as double, read as the kernel's real) */
 #define B200_MODEL_REAL_SCALARS(X) \
   X(timestep) X(gravity_x) X(gravity_y) X(gravity_z) X(tolerance) \
-  X(ls_tolerance) X(impratio_invsqrt) X(meaninertia) X(ccd_tolerance)
+  X(ls_tolerance) X(impratio_invsqrt) X(meaninertia) X(ccd_tolerance) X(task_lift_z)
 
 /* int32 arrays: X(name, length-expression) */
 #define B200_MODEL_INT_ARRAYS(X) \
@@ -85,7 +95,8 @@
   X(site_xmat, nsite * 9) X(subtree_com, nbody * 3) X(qfrc_bias, nv) \
   X(qfrc_actuator, nv) X(qfrc_constraint, nv) X(qacc_smooth, nv) \
   X(con_dist, ncon_max) X(con_pos, ncon_max * 3) X(con_frame, ncon_max * 9) \
-  X(efc_force, nefc_max) X(obs, nobs)
+  X(efc_force, nefc_max) X(obs, nobs) \
+  X(efc_J, nefc_max * nv) X(efc_D, nefc_max) X(efc_aref, nefc_max)
 
 /* world-major int32 data: X(name, per-world width) */
 #define B200_DATA_INT(X) \
@@ -93,6 +104,6 @@
   X(error, 1) X(niter, 1) X(newton_total, 1) X(ls_total, 1) \
   X(integration_count, 1) X(efc_total, 1) X(con_total, 1) \
   X(newton_rows, 1) X(ls_rows, 1) X(efc_k, 1) X(efc_k2, 1) X(fact_blk, 1) \
-  X(stage_cycles, 16)
+  X(stage_cycles, 16) X(efc_type, nefc_max) X(efc_id, nefc_max) X(niter_trace, 32) X(ls_trace, 32)
 
 #endif

@@ -1,3 +1,5 @@
+/* Portions restate MuJoCo Warp formulas: Copyright 2025 The Newton Developers,
+ * SPDX-License-Identifier: Apache-2.0 (see NOTICE). */
 /* Narrowphase families beyond plane/box (included by oracle.c; test
  * infrastructure only).
  *
@@ -362,8 +364,25 @@ typedef struct {
   int alive[EPA_MAXF];
 } Polytope;
 
+/* drop dead faces, keeping the live ones in order (ties in the best-face
+ * search go to the lower index) */
+static void epa_compact(Polytope *P) {
+  int k = 0;
+  for (int f = 0; f < P->nf; ++f) {
+    if (!P->alive[f]) continue;
+    if (k != f) {
+      memcpy(P->face[k], P->face[f], sizeof(P->face[f]));
+      P->n[k] = P->n[f]; P->d[k] = P->d[f]; P->alive[k] = 1;
+    }
+    ++k;
+  }
+  P->nf = k;
+}
+
+/* new face: its index, -1 when degenerate, -2 when the pool is full */
 static int epa_add_face(Polytope *P, int i, int j, int l) {
-  if (P->nf >= EPA_MAXF) return -1;
+  if (P->nf >= EPA_MAXF) epa_compact(P);
+  if (P->nf >= EPA_MAXF) return -2;
   V3 n = vcross(vsub(P->w[j], P->w[i]), vsub(P->w[l], P->w[i]));
   real len = rsqrt_(vdot(n, n));
   if (!(len > R(1e-30))) return -1;
@@ -390,6 +409,7 @@ static int epa_seed(Polytope *P, const CShape *A, const CShape *B, const Simplex
   static const real axes[6][3] = {{1, 0, 0}, {-1, 0, 0}, {0, 1, 0}, {0, -1, 0}, {0, 0, 1}, {0, 0, -1}};
   for (int k = 0; P->nv < 2 && k < 6; ++k) {
     int v = epa_push(P, A, B, v3(axes[k][0], axes[k][1], axes[k][2]));
+    if (v == 0) continue; /* an empty simplex (coincident centres): the first vertex seeds */
     V3 e = vsub(P->w[v], P->w[0]);
     if (vdot(e, e) < R(1e-20)) P->nv--;
   }
@@ -430,7 +450,7 @@ static int epa_seed(Polytope *P, const CShape *A, const CShape *B, const Simplex
   return 1;
 }
 
-typedef struct { int ok; real depth; V3 x1, x2; } EpaOut;
+typedef struct { int ok, overflow; real depth; V3 x1, x2; } EpaOut; /* overflow: a pool filled */
 
 static EpaOut epa(const CShape *A, const CShape *B, const Simplex *s, real tol, int iterations) {
   EpaOut o;
@@ -446,7 +466,7 @@ static EpaOut epa(const CShape *A, const CShape *B, const Simplex *s, real tol, 
     if (it == iterations) break;
     V3 n = P.n[best];
     int v = epa_push(&P, A, B, n);
-    if (v < 0) break;
+    if (v < 0) { o.overflow = 1; break; }
     if (vdot(P.w[v], n) - P.d[best] < tol) { P.nv--; break; }
     /* remove the faces that see the new vertex; keep their horizon */
     int edges[3 * EPA_MAXF][2], ne = 0;
@@ -459,12 +479,15 @@ static EpaOut epa(const CShape *A, const CShape *B, const Simplex *s, real tol, 
           if (edges[q][0] == j && edges[q][1] == i) { dup = q; break; }
         if (dup >= 0) { edges[dup][0] = edges[ne - 1][0]; edges[dup][1] = edges[ne - 1][1]; --ne; }
         else if (ne < 3 * EPA_MAXF) { edges[ne][0] = i; edges[ne][1] = j; ++ne; }
+        else o.overflow = 1;
       }
     }
     int full = 0;
-    for (int q = 0; q < ne; ++q)
-      if (epa_add_face(&P, edges[q][0], edges[q][1], v) < 0) { full = 1; break; }
-    if (full) break;
+    for (int q = 0; q < ne; ++q) {
+      int f = epa_add_face(&P, edges[q][0], edges[q][1], v);
+      if (f < 0) { full = 1; o.overflow |= f == -2; break; }
+    }
+    if (full || o.overflow) break;
   }
   if (best < 0) return o;
   /* witness points: barycentric coordinates of the origin's projection */
@@ -531,6 +554,7 @@ static void convex_collide(Work *k, const B200Model *m, int g1, int g2) {
     if (r.dist > tol) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
     else {
       EpaOut e = epa(&A, &B, &r.s, tol, m->epa_iterations);
+      if (e.overflow) k->overflow |= B200_OVERFLOW_EPA_HORIZON;
       if (!e.ok) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
       else { dist = -e.depth; x1 = e.x1; x2 = e.x2; }
     }

@@ -1,3 +1,5 @@
+/* Portions restate MuJoCo Warp formulas: Copyright 2025 The Newton Developers,
+ * SPDX-License-Identifier: Apache-2.0 (see NOTICE). */
 /*
  * CPU ORACLE — test infrastructure only.
  *
@@ -1755,14 +1757,21 @@ static void publish_outputs(const B200Model *m, const B200Data *d, Work *k, int 
   if ((p = DR(con_pos, w, nc * 3))) for (int c = 0; c < k->ncon; ++c) memcpy(p + 3 * c, k->con[c].pos, sizeof(real) * 3);
   if ((p = DR(con_frame, w, nc * 9))) for (int c = 0; c < k->ncon; ++c) memcpy(p + 9 * c, k->con[c].frame, sizeof(real) * 9);
   if ((p = DR(efc_force, w, ne))) for (int r = 0; r < k->nefc; ++r) p[r] = k->efc_force[r];
+  if ((p = DR(efc_D, w, ne))) for (int r = 0; r < k->nefc; ++r) p[r] = k->efc_D[r];
+  if ((p = DR(efc_aref, w, ne))) for (int r = 0; r < k->nefc; ++r) p[r] = k->efc_aref[r];
+  if ((p = DR(efc_J, w, ne * nv))) for (int r = 0; r < k->nefc; ++r) memcpy(p + r * nv, k->J[r], sizeof(real) * nv);
   int *ip;
+  if ((ip = DI(efc_type, w, ne))) for (int r = 0; r < k->nefc; ++r) ip[r] = k->efc_type[r];
+  if ((ip = DI(efc_id, w, ne))) for (int r = 0; r < k->nefc; ++r) ip[r] = k->efc_id[r];
   if ((ip = DI(ncon, w, 1))) *ip = k->ncon;
   if ((ip = DI(nefc, w, 1))) *ip = k->nefc;
   if ((ip = DI(con_geom, w, nc * 2))) for (int c = 0; c < k->ncon; ++c) { ip[2 * c] = k->con[c].g1; ip[2 * c + 1] = k->con[c].g2; }
 }
 
 /* observation slab: arm+gripper qpos/qvel (current), end-effector pose and
- * free-body poses from the last substep's kinematics; reward/done are 0 */
+ * free-body poses from the last substep's kinematics, then reward and done:
+ * the task body's origin above task_lift_z (the synthetic scenes' sparse
+ * success predicate) */
 static void publish_obs(const B200Model *m, const B200Data *d, const Work *k, int w, const real *qpos,
                         const real *qvel) {
   real *o = DR(obs, w, m->nobs);
@@ -1787,6 +1796,18 @@ static void publish_obs(const B200Model *m, const B200Data *d, const Work *k, in
     for (int c = 0; c < 3; ++c) o[25 + 7 * f + c] = k->xpos[fb][c];
     for (int c = 0; c < 4; ++c) o[25 + 7 * f + 3 + c] = k->xquat[fb][c];
   }
+  if (m->task_body >= 0 && m->task_body < m->nfree) {
+    real success = k->xpos[MI(free_bodyid)[m->task_body]][2] > (real)m->task_lift_z ? R(1) : R(0);
+    o[25 + 7 * m->nfree] = success;
+    o[25 + 7 * m->nfree + 1] = success;
+  }
+}
+
+/* MuJoCo mj_checkPos / mj_checkVel: a non-finite or huge (> 1e10) entry */
+static int bad_state(const B200Model *m, const real *qpos, const real *qvel) {
+  for (int i = 0; i < m->nq; ++i) if (!(rabs(qpos[i]) <= R(1e10))) return 1;
+  for (int i = 0; i < m->nv; ++i) if (!(rabs(qvel[i]) <= R(1e10))) return 1;
+  return 0;
 }
 
 /* position + velocity stage (reference Physics.step1, physics.py:185) */
@@ -1814,7 +1835,10 @@ int oracle_step(const B200Model *m, const B200Data *d, int w0, int w1, int subst
   for (int w = w0; w < w1; ++w) {
     real *qpos = DR(qpos, w, nq), *qvel = DR(qvel, w, nv), *warm = DR(qacc_warmstart, w, nv);
     int *overflow = DI(overflow, w, 1), *error = DI(error, w, 1);
+    if (bad_state(m, qpos, qvel)) *overflow |= B200_STATUS_BADSTATE;
+    int stepped = 0;
     for (int s = 0; s < substeps; ++s) {
+      if (*overflow & B200_STATUS_BADSTATE) break; /* a bad world is not stepped (further) */
       k->overflow = 0;
       step1(m, k, qpos, qvel);
       OscState os = {DR(goal_pos, w, 3), DR(goal_rot, w, 9), DR(gripper, w, 2), DR(ctrl, w, nu), DR(action, w, 7), error};
@@ -1830,13 +1854,17 @@ int oracle_step(const B200Model *m, const B200Data *d, int w0, int w1, int subst
       if (d->con_total) *DI(con_total, w, 1) += k->ncon;
       if (d->newton_rows) *DI(newton_rows, w, 1) += k->niter * k->nefc;
       if (d->ls_rows) *DI(ls_rows, w, 1) += k->ls_evals * k->nefc;
+      if (s < 32 && d->niter_trace) DI(niter_trace, w, 32)[s] = k->niter;
+      if (s < 32 && d->ls_trace) DI(ls_trace, w, 32)[s] = k->ls_evals;
       k->ls_evals = 0;
       if (s == substeps - 1) publish_outputs(m, d, k, w);
       euler(m, k, qpos, qvel, DR(qacc, w, nv), warm);
       *DR(time, w, 1) += (real)m->timestep;
       if (d->integration_count) *DI(integration_count, w, 1) += 1;
+      if (bad_state(m, qpos, qvel)) *overflow |= B200_STATUS_BADSTATE;
+      ++stepped;
     }
-    if (substeps > 0) publish_obs(m, d, k, w, qpos, qvel);
+    if (stepped > 0) publish_obs(m, d, k, w, qpos, qvel);
   }
   free(k);
   return 0;
@@ -1850,6 +1878,7 @@ int oracle_forward(const B200Model *m, const B200Data *d, int w0, int w1, int bo
   int nq = m->nq, nv = m->nv, nu = m->nu;
   for (int w = w0; w < w1; ++w) {
     real *qpos = DR(qpos, w, nq), *qvel = DR(qvel, w, nv), *warm = DR(qacc_warmstart, w, nv);
+    if (bad_state(m, qpos, qvel)) *DI(overflow, w, 1) |= B200_STATUS_BADSTATE;
     step1(m, k, qpos, qvel);
     if (bootstrap) {
       int site = m->ee_site;
@@ -1864,6 +1893,7 @@ int oracle_forward(const B200Model *m, const B200Data *d, int w0, int w1, int bo
     newton(m, k, warm, &of);
     *DI(overflow, w, 1) |= of;
     publish_outputs(m, d, k, w);
+    publish_obs(m, d, k, w, qpos, qvel);
     real *qa = DR(qacc, w, nv);
     if (qa) memcpy(qa, k->qacc, sizeof(real) * nv);
     k->ls_evals = 0;
@@ -1965,7 +1995,7 @@ int oracle_leaf_convex(int type1, const real *p1, const real *R1, const real *s1
   CShape B = {type2, vsub(vload(p2), origin), vload(s2), R2, vert2, nvert2, margin};
   real full1 = 0, full2 = 0, d;
   V3 x1, x2;
-  int found = 0;
+  int found = 0, flags = 0; /* return: bit 0 a contact, bit 1 an EPA pool overflow */
   CShape Ac = A, Bc = B;
   if (A.type == B200_GEOM_SPHERE || A.type == B200_GEOM_CAPSULE) { full1 = A.size.v[0] + R(0.5) * margin; Ac.size.v[0] = 0; Ac.margin = 0; }
   if (B.type == B200_GEOM_SPHERE || B.type == B200_GEOM_CAPSULE) { full2 = B.size.v[0] + R(0.5) * margin; Bc.size.v[0] = 0; Bc.margin = 0; }
@@ -1984,13 +2014,14 @@ int oracle_leaf_convex(int type1, const real *p1, const real *R1, const real *s1
     if (r.dist > tol) { d = r.dist; x1 = r.x1; x2 = r.x2; }
     else {
       EpaOut e = epa(&A, &B, &r.s, tol, epa_iterations);
+      if (e.overflow) flags = 2;
       if (!e.ok) { d = r.dist; x1 = r.x1; x2 = r.x2; }
       else { d = -e.depth; x1 = e.x1; x2 = e.x2; }
     }
   }
-  if (!(d < 0)) return 0;
+  if (!(d < 0)) return flags;
   *dist = d + margin;
   vstore(pos, vadd(vscale(vadd(x1, x2), R(0.5)), origin));
   vstore(normal, vnormalize(*dist <= margin ? vsub(x1, x2) : vsub(x2, x1)));
-  return 1;
+  return 1 | flags;
 }

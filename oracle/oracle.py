@@ -113,7 +113,8 @@ class Oracle:
     def convex(self, kind1, p1, R1, s1, v1, kind2, p2, R2, s2, v2, margin=0.0, tol=1e-6, iterations=50,
                epa_iterations=32):
         """Convex narrowphase of two shapes on raw poses; v1 / v2 are local
-        mesh vertices (None for primitives).  Returns (dist, pos, normal) or None."""
+        mesh vertices (None for primitives).  Returns (dist, pos, normal) or
+        None; `self.epa_overflow` tells whether EPA's pools filled."""
         def arr(x, n):
             return np.ascontiguousarray(np.zeros(n) if x is None else np.asarray(x, float).ravel(), self.dtype)
         a = [arr(p1, 3), arr(R1, 9), arr(s1, 3), arr(v1, 3), arr(p2, 3), arr(R2, 9), arr(s2, 3), arr(v2, 3)]
@@ -123,4 +124,5 @@ class Oracle:
         n = self.lib.oracle_leaf_convex(kind1, *[self._ptr(x) for x in a[:4]], n1, kind2,
                                         *[self._ptr(x) for x in a[4:]], n2, margin, tol, iterations,
                                         epa_iterations, self._ptr(dist), self._ptr(pos), self._ptr(nrm))
-        return (float(dist[0]), pos.astype(float), nrm.astype(float)) if n else None
+        self.epa_overflow = bool(n & 2)
+        return (float(dist[0]), pos.astype(float), nrm.astype(float)) if n & 1 else None

@@ -39,8 +39,10 @@ class RefContacts(ct.Structure):
 
 
 def build(reference=None):
-    reference = reference or os.environ.get('GPU_LIBERO_REFERENCE', '/root/reference')
-    if not Path(reference, 'libero', 'libero', 'gpu', 'cuda', 'collision').is_dir():
+    """Compile the leaves from the reference checkout given as `reference` or
+    by the GPU_LIBERO_REFERENCE environment variable; False without one."""
+    reference = reference or os.environ.get('GPU_LIBERO_REFERENCE')
+    if not reference or not Path(reference, 'libero', 'libero', 'gpu', 'cuda', 'collision').is_dir():
         return False
     subprocess.run(['make', '-s', '-C', str(HERE), 'ref', 'REFERENCE=' + str(reference)], check=True)
     return LIB.is_file()
