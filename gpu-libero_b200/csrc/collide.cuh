@@ -980,10 +980,11 @@ template <class R> __device__ bool epa_seed(Polytope<R> &P, const CShape<R> &A, 
   return true;
 }
 
-// ok: a penetration depth was found; overflow: a vertex, face or horizon
-// pool filled before EPA converged (the reference's EPA_HORIZON status).
+// ok: a penetration depth was found; budget: the vertex or face pool filled
+// before EPA converged (it ends with its best face, as at its iteration
+// limit); horizon: the horizon edge list filled (the reference's EPA_HORIZON)
 template <class R> struct EpaOut {
-  bool ok, overflow;
+  bool ok, budget, horizon;
   R depth;
   V3<R> x1, x2;
 };
@@ -992,7 +993,7 @@ template <class R>
 __device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R> &s, R tol, int iterations) {
   EpaOut<R> o;
   o.ok = false;
-  o.overflow = false;
+  o.budget = o.horizon = false;
   Polytope<R> P;
   if (!epa_seed(P, A, B, s)) return o;
   int best = -1;
@@ -1004,7 +1005,7 @@ __device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R
     if (it == iterations) break;
     const V3<R> n = P.n[best];
     const int v = epa_push(P, A, B, n);
-    if (v < 0) { o.overflow = true; break; }
+    if (v < 0) { o.budget = true; break; }
     if (dot(P.w[v], n) - P.d[best] < tol) { P.nv--; break; }
     int edges[3 * kEpaMaxF][2], ne = 0;
     for (int f = 0; f < P.nf; ++f) {
@@ -1017,15 +1018,15 @@ __device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R
           if (edges[q][0] == j && edges[q][1] == i) { dup = q; break; }
         if (dup >= 0) { edges[dup][0] = edges[ne - 1][0]; edges[dup][1] = edges[ne - 1][1]; --ne; }
         else if (ne < 3 * kEpaMaxF) { edges[ne][0] = i; edges[ne][1] = j; ++ne; }
-        else o.overflow = true;
+        else o.horizon = true;
       }
     }
     bool full = false;
     for (int q = 0; q < ne; ++q) {
       const int f = epa_add_face(P, edges[q][0], edges[q][1], v);
-      if (f < 0) { full = true; o.overflow |= f == -2; break; }
+      if (f < 0) { full = true; o.budget |= f == -2; break; }
     }
-    if (full || o.overflow) break;
+    if (full || o.horizon) break;
   }
   if (best < 0) return o;
   const int i = P.face[best][0], j = P.face[best][1], l = P.face[best][2];
@@ -1091,7 +1092,8 @@ __device__ __noinline__ void convex_pair(const Mdl<R> &M, Arena<R> &A, int pair,
     if (r.dist > tol) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
     else {
       const EpaOut<R> e = epa(S1, S2, r.s, tol, M.m.epa_iterations);
-      if (e.overflow) atomicOr(&A.iscal[3], B200_OVERFLOW_EPA_HORIZON);
+      if (e.budget) atomicOr(&A.iscal[3], B200_WARN_EPA_BUDGET);
+      if (e.horizon) atomicOr(&A.iscal[3], B200_OVERFLOW_EPA_HORIZON);
       if (!e.ok) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
       else { dist = -e.depth; x1 = e.x1; x2 = e.x2; }
     }

@@ -1244,21 +1244,27 @@ template <class R> __device__ void rotation_delta(R x, R y, R z, double *r) {
   const R angle = msqrt(x * x + y * y + z * z);
   const R f = angle == R(0) ? R(0) : msin(angle * R(0.5)) / angle;
   const R raw[4] = {x * f, y * f, z * f, angle == R(0) ? R(1) : mcos(angle * R(0.5))};
+  // robosuite's float32 quaternion convention; every float product and sum is
+  // rounded on its own (no fused multiply-add), so that the goal does not
+  // depend on the compiler's contraction choices
   float q[4] = {(float)raw[3], (float)raw[0], (float)raw[1], (float)raw[2]};
   R acc = 0;
-  for (int i = 0; i < 4; ++i) acc += (R)(q[i] * q[i]);
+  for (int i = 0; i < 4; ++i) acc += (R)__fmul_rn(q[i], q[i]);
   const float norm = (float)acc;
   const R factor = msqrt(R(2) / (R)norm);
   for (int i = 0; i < 4; ++i) q[i] = (float)((R)q[i] * factor);
-  r[0] = (double)(R(1) - (R)(q[2] * q[2]) - (R)(q[3] * q[3]));
-  r[4] = (double)(R(1) - (R)(q[1] * q[1]) - (R)(q[3] * q[3]));
-  r[8] = (double)(R(1) - (R)(q[1] * q[1]) - (R)(q[2] * q[2]));
-  r[1] = (double)(R)(q[1] * q[2] - q[3] * q[0]);
-  r[2] = (double)(R)(q[1] * q[3] + q[2] * q[0]);
-  r[3] = (double)(R)(q[1] * q[2] + q[3] * q[0]);
-  r[5] = (double)(R)(q[2] * q[3] - q[1] * q[0]);
-  r[6] = (double)(R)(q[1] * q[3] - q[2] * q[0]);
-  r[7] = (double)(R)(q[2] * q[3] + q[1] * q[0]);
+  auto sq = [&](int i) { return (R)__fmul_rn(q[i], q[i]); };
+  auto sum = [&](int a, int b, int c, int d) { return (R)__fadd_rn(__fmul_rn(q[a], q[b]), __fmul_rn(q[c], q[d])); };
+  auto dif = [&](int a, int b, int c, int d) { return (R)__fsub_rn(__fmul_rn(q[a], q[b]), __fmul_rn(q[c], q[d])); };
+  r[0] = (double)(R(1) - sq(2) - sq(3));
+  r[4] = (double)(R(1) - sq(1) - sq(3));
+  r[8] = (double)(R(1) - sq(1) - sq(2));
+  r[1] = (double)dif(1, 2, 3, 0);
+  r[2] = (double)sum(1, 3, 2, 0);
+  r[3] = (double)sum(1, 2, 3, 0);
+  r[5] = (double)dif(2, 3, 1, 0);
+  r[6] = (double)dif(1, 3, 2, 0);
+  r[7] = (double)sum(2, 3, 1, 0);
 }
 
 template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> &A, bool policy) {
@@ -2229,7 +2235,13 @@ template <class R, int T> __device__ __noinline__ void store_outputs(const B200M
   }
   int *idst;
   if ((idst = irow_of(d.efc_type, w, m.nefc_max))) FOR(r, nefc) idst[r] = A.efc_type[r];
-  if ((idst = irow_of(d.efc_id, w, m.nefc_max))) FOR(r, nefc) idst[r] = A.efc_id[r];
+  if ((idst = irow_of(d.efc_id, w, m.nefc_max))) FOR(r, nefc) {
+    int id = A.efc_id[r];  // contact rows: the contact's slot, published as its sorted index
+    if (A.efc_type[r] >= 5)
+      for (int k = 0; k < ncon; ++k)
+        if (A.con_order[k] == id) { id = k; break; }
+    idst[r] = id;
+  }
   if ((idst = irow_of(d.con_geom, w, nc * 2)))
     FOR(e, ncon * 2) idst[e] = e & 1 ? A.con_g2[A.con_order[e >> 1]] : A.con_g1[A.con_order[e >> 1]];
   if (TID == 0) {

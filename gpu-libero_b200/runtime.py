@@ -21,7 +21,9 @@ import torch
 from . import native
 from .scene import Scene, scene_a
 
-OVERFLOW_LIMITS = 0x200 | 0x400  # iteration / line-search limits are legal exits
+# legal exits: the Newton iteration and line-search limits, and EPA's pool
+# budget (it ends with its best face, as at its iteration limit)
+OVERFLOW_LIMITS = 0x200 | 0x400 | 0x20000
 # inspection outputs that a step never needs: allocated only for debug runtimes
 DEBUG_FIELDS = ('efc_J', 'efc_D', 'efc_aref', 'efc_type', 'efc_id', 'niter_trace', 'ls_trace')
 
@@ -54,7 +56,9 @@ class Runtime:
             self.model_ints = torch.from_numpy(self.packed.ints).to(self.device)
             self.model = self.packed.struct(self.model_real.data_ptr(), self.model_ints.data_ptr())
             real, ints = self.packed.data_widths()
-            keep = lambda k: debug or k not in DEBUG_FIELDS  # noqa: E731
+            # debug: True for every inspection output, or an iterable of their names
+            wanted = set(DEBUG_FIELDS) if debug is True else set(debug or ())
+            keep = lambda k: k not in DEBUG_FIELDS or k in wanted  # noqa: E731
             self.buffers = {k: torch.zeros((self.n, w), dtype=self.dtype, device=self.device)
                             for k, w in real.items() if keep(k)}
             self.buffers.update({k: torch.zeros((self.n, w), dtype=torch.int32, device=self.device)

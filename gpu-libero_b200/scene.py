@@ -75,6 +75,22 @@ def mat_quat(r):
     return q if q[0] >= 0 else -q
 
 
+def _qmul_b(a, b):
+    """Quaternion products of two batches [W, 4] (w, x, y, z)."""
+    aw, ax, ay, az = a[:, 0], a[:, 1], a[:, 2], a[:, 3]
+    bw, bx, by, bz = b[:, 0], b[:, 1], b[:, 2], b[:, 3]
+    return np.stack([aw * bw - ax * bx - ay * by - az * bz, aw * bx + ax * bw + ay * bz - az * by,
+                     aw * by - ax * bz + ay * bw + az * bx, aw * bz + ax * by - ay * bx + az * bw], axis=1)
+
+
+def _qrot_b(q, v):
+    """A vector [3] (or batch [W, 3]) rotated by a batch of quaternions [W, 4]."""
+    u, w = q[:, 1:], q[:, :1]
+    v = np.broadcast_to(v, u.shape)
+    return 2 * np.sum(u * v, axis=1, keepdims=True) * u + (w * w - np.sum(u * u, axis=1, keepdims=True)) * v + \
+        2 * w * np.cross(u, v)
+
+
 def axis_quat(axis, angle):
     axis = np.asarray(axis, float) / np.linalg.norm(axis)
     return np.r_[math.cos(angle / 2), axis * math.sin(angle / 2)]
@@ -543,40 +559,151 @@ class Scene:
         self.reals['dof_invweight0'] = dofw
 
     # ---------------------------------------------------------------- states
+    PLACEMENT_ATTEMPTS = 160
+    CLEARANCE = 0.002      # object-object and object-floor gap at placement
+    ARM_CLEARANCE = 0.005  # object-arm gap at placement
+
     def initial_state(self, nworld, seed=0, world_offset=0):
         """Per-world initial qpos/qvel, seeded per global world index.
 
         Worlds draw from ``SeedSequence(seed).spawn`` indexed by their global
-        world number, so a shard's worlds do not depend on the GPU count."""
+        world number, so a shard's worlds do not depend on the GPU count.  A
+        world's arm joints are its nominal pose plus N(0, 0.05^2) noise; its
+        objects are then placed one after another by rejection sampling, each
+        candidate drawn from the world's own stream, so that no object starts
+        inside the floor, another object or any arm collision geom (the arm
+        taken at that world's own joint angles).  Dropped objects fall from a
+        centre height U[0.05, 0.15] m, raised where needed until their
+        bounding sphere clears the floor."""
         nq, nv = self.sizes['nq'], self.sizes['nv']
         qpos = np.tile(self.reals['qpos0'], (nworld, 1))
         children = np.random.SeedSequence(seed).spawn(world_offset + nworld)[world_offset:]
-        for w, child in enumerate(children):
-            rng = np.random.default_rng(child)
-            self.sample_world(rng, qpos[w])
+        rngs = [np.random.default_rng(child) for child in children]
+        c = self.controller
+        adr = self.ints['jnt_qposadr']
+        noise = np.stack([r.normal(0.0, 0.05, len(c['joints'])) for r in rngs]) if nworld else np.zeros((0, 7))
+        for k, j in enumerate(c['joints']):
+            qpos[:, adr[j]] = c['q0'][k] + noise[:, k]
+        for j, value in zip(c['gripper_joints'], GRIPPER_INIT):
+            qpos[:, adr[j]] = value
+        nobj = len(self.objects)
+        if nworld and nobj:
+            draws = np.stack([r.random((nobj, self.PLACEMENT_ATTEMPTS, 6)) for r in rngs])
+            for a in range(0, nworld, 4096):
+                self._place_objects(qpos[a:a + 4096], draws[a:a + 4096])
         return qpos, np.zeros((nworld, nv))
 
-    def sample_world(self, rng, qpos):
-        c = self.controller
-        for k, j in enumerate(c['joints']):
-            qpos[self.ints['jnt_qposadr'][j]] = c['q0'][k] + rng.normal(0.0, 0.05)
-        for k, (j, value) in enumerate(zip(c['gripper_joints'], GRIPPER_INIT)):
-            qpos[self.ints['jnt_qposadr'][j]] = value
-        placed = []
-        for body in self.objects:
-            adr = self.ints['jnt_qposadr'][self.ints['body_jntadr'][body['id']]]
-            for _ in range(1000):
-                x, y = rng.uniform(-0.5, 0.5, 2) * self.object_square + self.object_center
-                if all((x - px) ** 2 + (y - py) ** 2 > (body['radius'] + pr) ** 2 for px, py, pr in placed):
-                    break
-            placed.append((x, y, body['radius']))
-            z = body['rest_z'] if body['drop'] is None else rng.uniform(*body['drop'])
-            qpos[adr:adr + 3] = [x, y, z]
-            if body.get('tumble'):  # dropped objects: uniformly random orientation
-                q = rng.normal(size=4)
-                qpos[adr + 3:adr + 7] = q / np.linalg.norm(q)
+    def _arm_segments(self, qpos):
+        """Collision geoms of the non-free bodies (arm, hand, fingers) as
+        capsule segments (p0, p1, radius) in world frame, for a batch of
+        states: [W, ngeom_arm, 2, 3] end points and [ngeom_arm] radii (boxes
+        and spheres as zero-length segments of their bounding radius)."""
+        I, R = self.ints, self.reals
+        W, nb = len(qpos), self.sizes['nbody']
+        xpos = np.zeros((W, nb, 3))
+        xquat = np.zeros((W, nb, 4))
+        xquat[:, 0, 0] = 1
+        free = np.zeros(nb, bool)
+        for b in range(1, nb):
+            first, count = I['body_jntadr'][b], I['body_jntnum'][b]
+            if count == 1 and I['jnt_type'][first] == FREE:
+                free[b] = True
+                continue
+            p = I['body_parentid'][b]
+            pos = _qrot_b(xquat[:, p], R['body_pos'][b]) + xpos[:, p]
+            quat = _qmul_b(xquat[:, p], np.broadcast_to(R['body_quat'][b], (W, 4)))
+            for j in range(first, first + count):
+                a, kind = I['jnt_qposadr'][j], I['jnt_type'][j]
+                lpos, lax = R['jnt_pos'][j], R['jnt_axis'][j]
+                anchor = _qrot_b(quat, lpos) + pos
+                if kind == SLIDE:
+                    pos = pos + _qrot_b(quat, lax) * (qpos[:, a] - R['qpos0'][a])[:, None]
+                elif kind == HINGE:
+                    half = 0.5 * (qpos[:, a] - R['qpos0'][a])
+                    rq = np.concatenate([np.cos(half)[:, None], np.sin(half)[:, None] * lax], axis=1)
+                    quat = _qmul_b(quat, rq)
+                    pos = anchor - _qrot_b(quat, lpos)
+            xpos[:, b], xquat[:, b] = pos, quat
+        segs, radii = [], []
+        for g in range(self.sizes['ngeom']):
+            b = I['geom_bodyid'][g]
+            if b == 0 or free[b]:
+                continue
+            kind, size = I['geom_type'][g], np.reshape(R['geom_size'], (-1, 3))[g]
+            centre = _qrot_b(xquat[:, b], np.reshape(R['geom_pos'], (-1, 3))[g]) + xpos[:, b]
+            if kind == CAPSULE:
+                gq = _qmul_b(xquat[:, b], np.broadcast_to(np.reshape(R['geom_quat'], (-1, 4))[g], (W, 4)))
+                axis = _qrot_b(gq, np.array([0.0, 0.0, 1.0])) * size[1]
+                segs.append(np.stack([centre - axis, centre + axis], axis=1))
+                radii.append(size[0])
             else:
-                qpos[adr + 3:adr + 7] = axis_quat((0, 0, 1), rng.uniform(-math.pi, math.pi))
+                segs.append(np.stack([centre, centre], axis=1))
+                radii.append(float(np.linalg.norm(size)) if kind == BOX else size[0])
+        return np.stack(segs, axis=1), np.array(radii)
+
+    def _place_objects(self, qpos, draws):
+        """Rejection placement of the free objects for a batch of worlds;
+        draws[w, object, attempt] holds six uniforms of world w's stream.  A
+        world takes its first candidate that clears everything, else (all
+        candidates failing) the one with the smallest overlap; candidates are
+        examined in blocks, each block only for the worlds still looking."""
+        W, A = len(qpos), draws.shape[2]
+        segs, radii = self._arm_segments(qpos)
+        p0, d = segs[:, :, 0], segs[:, :, 1] - segs[:, :, 0]          # [W, S, 3]
+        dd = np.maximum(np.einsum('wsk,wsk->ws', d, d), 1e-30)
+        placed = []  # (centre [W, 3], radius)
+        for k, body in enumerate(self.objects):
+            rbound = body.get('rbound', body['radius'])
+
+            def candidates(u):
+                xy = (u[..., 0:2] - 0.5) * self.object_square + self.object_center
+                if body['drop'] is None:
+                    z = np.full(u.shape[:-1], body['rest_z'])
+                else:
+                    lo, hi = body['drop']
+                    z = np.maximum(lo + (hi - lo) * u[..., 2], rbound + self.CLEARANCE)
+                return np.concatenate([xy, z[..., None]], axis=-1)
+
+            def overlap(ws, cand):  # worst violation of each candidate of worlds ws
+                short = np.full(cand.shape[:2], -np.inf)
+                for centre, r in placed:
+                    dist = np.linalg.norm(cand - centre[ws, None], axis=-1)
+                    short = np.maximum(short, body['radius'] + r + self.CLEARANCE - dist)
+                rel = cand[:, :, None, :] - p0[ws, None]
+                tt = np.clip(np.einsum('wask,wsk->was', rel, d[ws]) / dd[ws, None], 0.0, 1.0)
+                arm = np.linalg.norm(rel - tt[..., None] * d[ws, None], axis=-1)
+                return np.maximum(short, np.max(rbound + radii + self.ARM_CLEARANCE - arm, axis=-1))
+
+            pick = np.full(W, -1)
+            best = np.full(W, np.inf)
+            fallback = np.zeros(W, int)
+            pending = np.arange(W)
+            for a0 in range(0, A, 16):
+                if not len(pending):
+                    break
+                short = overlap(pending, candidates(draws[pending, k, a0:a0 + 16]))
+                ok = short <= 0
+                hit = ok.any(axis=1)
+                pick[pending[hit]] = a0 + ok[hit].argmax(axis=1)
+                low = short.min(axis=1)
+                better = low < best[pending]
+                fallback[pending[better]] = a0 + short[better].argmin(axis=1)
+                best[pending[better]] = low[better]
+                pending = pending[~hit]
+            pick[pending] = fallback[pending]
+            ua = draws[np.arange(W), k, pick]
+            centre = candidates(ua[:, None])[:, 0]
+            placed.append((centre, body['radius']))
+            a = self.ints['jnt_qposadr'][self.ints['body_jntadr'][body['id']]]
+            qpos[:, a:a + 3] = centre
+            if body.get('tumble'):  # dropped objects: uniformly random orientation (Shoemake)
+                s1, s2 = np.sqrt(1.0 - ua[:, 3]), np.sqrt(ua[:, 3])
+                th1, th2 = 2 * math.pi * ua[:, 4], 2 * math.pi * ua[:, 5]
+                qpos[:, a + 3:a + 7] = np.stack([s2 * np.cos(th2), s1 * np.sin(th1), s1 * np.cos(th1),
+                                                 s2 * np.sin(th2)], axis=1)
+            else:
+                yaw = (2 * ua[:, 3] - 1) * math.pi
+                qpos[:, a + 3:a + 7] = np.stack([np.cos(yaw / 2), 0 * yaw, 0 * yaw, np.sin(yaw / 2)], axis=1)
 
     def actions(self, nworld, step, seed=0, world_offset=0):
         """Seeded OSC_POSE actions: U[-1,1]^6 plus a gripper sign in {-1,1}.
@@ -764,7 +891,8 @@ def scene_a(seed=0, cone='elliptic', nconmax=32, njmax=None, iterations=50, ls_i
         b.geoms.append(Geom('box%d_geom' % k, BOX, tuple(half), contype=1, conaffinity=3,
                             friction=(1.0, 0.005, 0.0001), margin=0.001, mass=mass))
         bodies.append(b)
-        objects.append(dict(id=len(bodies) - 1, radius=float(np.linalg.norm(half[:2])), rest_z=float(half[2]),
+        objects.append(dict(id=len(bodies) - 1, radius=float(np.linalg.norm(half[:2])), rbound=float(np.linalg.norm(half)),
+                            rest_z=float(half[2]),
                             drop=None))
     opt = dict(timestep=0.002, iterations=iterations, ls_iterations=ls_iterations, tolerance=tolerance,
                cone=1 if cone == 'elliptic' else 0, impratio=1.0, ls_tolerance=0.01)

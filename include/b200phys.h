@@ -39,13 +39,18 @@ extern "C" {
 /* Overflow bits (reference OverflowType, cuda_fp32/constants.py:89-101). */
 #define B200_OVERFLOW_NEFC (1 << 0)
 #define B200_OVERFLOW_NARROWPHASE (1 << 3)
-#define B200_OVERFLOW_EPA_HORIZON (1 << 8) /* EPA polytope pool full (fatal) */
+#define B200_OVERFLOW_EPA_HORIZON (1 << 8) /* EPA horizon edge list full (fatal) */
 #define B200_OVERFLOW_ITERATIONS (1 << 9)
 #define B200_OVERFLOW_LS_ITERATIONS (1 << 10)
 /* Non-finite or huge state (|x| > 1e10, MuJoCo's mjMAXVAL in mj_checkPos /
  * mj_checkVel): set after the substep that produced it; the world is not
  * stepped further in that launch (fatal; no reference bit has this value). */
 #define B200_STATUS_BADSTATE (1 << 16)
+/* EPA's vertex or face pool filled before it converged: EPA ends with the best
+ * face found, as at its iteration limit (a legal exit, not fatal; the
+ * reference's full face pool also ends its EPA without a status,
+ * mjwarp_convex_epa.cuh:89,219). */
+#define B200_WARN_EPA_BUDGET (1 << 17)
 
 /* disable_flags bits (MuJoCo 3.x mjtDisableBit positions). */
 #define B200_DSBL_CONSTRAINT (1 << 0)

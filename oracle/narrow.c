@@ -450,7 +450,7 @@ static int epa_seed(Polytope *P, const CShape *A, const CShape *B, const Simplex
   return 1;
 }
 
-typedef struct { int ok, overflow; real depth; V3 x1, x2; } EpaOut; /* overflow: a pool filled */
+typedef struct { int ok, budget, horizon; real depth; V3 x1, x2; } EpaOut; /* budget: a vertex/face pool filled; horizon: the edge list did */
 
 static EpaOut epa(const CShape *A, const CShape *B, const Simplex *s, real tol, int iterations) {
   EpaOut o;
@@ -466,7 +466,7 @@ static EpaOut epa(const CShape *A, const CShape *B, const Simplex *s, real tol, 
     if (it == iterations) break;
     V3 n = P.n[best];
     int v = epa_push(&P, A, B, n);
-    if (v < 0) { o.overflow = 1; break; }
+    if (v < 0) { o.budget = 1; break; }
     if (vdot(P.w[v], n) - P.d[best] < tol) { P.nv--; break; }
     /* remove the faces that see the new vertex; keep their horizon */
     int edges[3 * EPA_MAXF][2], ne = 0;
@@ -479,15 +479,15 @@ static EpaOut epa(const CShape *A, const CShape *B, const Simplex *s, real tol, 
           if (edges[q][0] == j && edges[q][1] == i) { dup = q; break; }
         if (dup >= 0) { edges[dup][0] = edges[ne - 1][0]; edges[dup][1] = edges[ne - 1][1]; --ne; }
         else if (ne < 3 * EPA_MAXF) { edges[ne][0] = i; edges[ne][1] = j; ++ne; }
-        else o.overflow = 1;
+        else o.horizon = 1;
       }
     }
     int full = 0;
     for (int q = 0; q < ne; ++q) {
       int f = epa_add_face(&P, edges[q][0], edges[q][1], v);
-      if (f < 0) { full = 1; o.overflow |= f == -2; break; }
+      if (f < 0) { full = 1; o.budget |= f == -2; break; }
     }
-    if (full || o.overflow) break;
+    if (full || o.horizon) break;
   }
   if (best < 0) return o;
   /* witness points: barycentric coordinates of the origin's projection */
@@ -554,7 +554,8 @@ static void convex_collide(Work *k, const B200Model *m, int g1, int g2) {
     if (r.dist > tol) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
     else {
       EpaOut e = epa(&A, &B, &r.s, tol, m->epa_iterations);
-      if (e.overflow) k->overflow |= B200_OVERFLOW_EPA_HORIZON;
+      if (e.budget) k->overflow |= B200_WARN_EPA_BUDGET;
+      if (e.horizon) k->overflow |= B200_OVERFLOW_EPA_HORIZON;
       if (!e.ok) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
       else { dist = -e.depth; x1 = e.x1; x2 = e.x2; }
     }

@@ -1995,7 +1995,7 @@ int oracle_leaf_convex(int type1, const real *p1, const real *R1, const real *s1
   CShape B = {type2, vsub(vload(p2), origin), vload(s2), R2, vert2, nvert2, margin};
   real full1 = 0, full2 = 0, d;
   V3 x1, x2;
-  int found = 0, flags = 0; /* return: bit 0 a contact, bit 1 an EPA pool overflow */
+  int found = 0, flags = 0; /* return: bit 0 a contact, bit 1 an EPA pool filled */
   CShape Ac = A, Bc = B;
   if (A.type == B200_GEOM_SPHERE || A.type == B200_GEOM_CAPSULE) { full1 = A.size.v[0] + R(0.5) * margin; Ac.size.v[0] = 0; Ac.margin = 0; }
   if (B.type == B200_GEOM_SPHERE || B.type == B200_GEOM_CAPSULE) { full2 = B.size.v[0] + R(0.5) * margin; Bc.size.v[0] = 0; Bc.margin = 0; }
@@ -2014,7 +2014,7 @@ int oracle_leaf_convex(int type1, const real *p1, const real *R1, const real *s1
     if (r.dist > tol) { d = r.dist; x1 = r.x1; x2 = r.x2; }
     else {
       EpaOut e = epa(&A, &B, &r.s, tol, epa_iterations);
-      if (e.overflow) flags = 2;
+      if (e.budget || e.horizon) flags = 2;
       if (!e.ok) { d = r.dist; x1 = r.x1; x2 = r.x2; }
       else { d = -e.depth; x1 = e.x1; x2 = e.x2; }
     }

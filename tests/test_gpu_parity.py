@@ -2,9 +2,12 @@
 
 Tolerances: forward quantities agree to FP32 rounding (|d| <= 1e-4 relative to
 the field's scale); contact pair lists and counts are bit-exact; after 5
-control steps (125 substeps) qpos agrees within 1e-4 absolute in FP32 and
-1e-7 in FP64 (contact dynamics amplify reduction-order rounding; the
-reference itself is not bit-reproducible, its pooled atomics reorder sums).
+control steps (125 substeps) qpos agrees within 1e-4 in FP32 and 1e-9 in
+FP64, and qvel, ctrl and qfrc_actuator within 1e-3 (FP32) and 1e-8 (FP64)
+relative to max(1, |value|).  Contact dynamics amplify reduction-order
+rounding over many substeps; the frozen-input single-substep checks at
+BASELINE's sizes (test_gpu_parity_headline.py) hold every solver output to
+north_star's 1e-4 / 1e-9.
 """
 import numpy as np
 import pytest
@@ -71,12 +74,12 @@ def pyramidal():
     return scenes.scene_a(cone='pyramidal')
 
 
-@pytest.mark.parametrize('precision,tol', [('fp32', 1e-4), ('fp64', 1e-7)])
+@pytest.mark.parametrize('precision,tol', [('fp32', 1e-4), ('fp64', 1e-9)])
 def test_control_steps_parity(scene, oracle_module, precision, tol):
     control_steps_parity(scene, oracle_module, precision, tol)
 
 
-@pytest.mark.parametrize('precision,tol', [('fp32', 1e-4), ('fp64', 1e-7)])
+@pytest.mark.parametrize('precision,tol', [('fp32', 1e-4), ('fp64', 1e-9)])
 def test_pyramidal_control_steps_parity(pyramidal, oracle_module, precision, tol):
     """Pyramidal friction cones: 2(condim-1) rows per contact, each an
     independent inequality row (mjwarp_constraint_build.cu row counts)."""
@@ -95,12 +98,14 @@ def control_steps_parity(scene, oracle_module, precision, tol):
         orc.step(rt.packed.host_struct(), native.data_struct(ref, n), 0, n, rt.substeps, 1)
     torch.cuda.synchronize()
     gpu = {k: t.cpu().numpy() for k, t in rt.buffers.items()}
+    rel = 1e-3 if precision == 'fp32' else 1e-8
     assert np.max(np.abs(gpu['qpos'] - ref['qpos'])) < tol
-    assert np.max(np.abs(gpu['qvel'] - ref['qvel'])) < 100 * tol
     assert np.array_equal(gpu['ncon'], ref['ncon'])
     assert np.array_equal(gpu['integration_count'], ref['integration_count'])
     assert np.max(np.abs(gpu['obs'] - ref['obs'])) < 10 * tol
-    assert np.max(np.abs(gpu['ctrl'] - ref['ctrl'])) < 1e4 * tol
+    for f in ('qvel', 'ctrl', 'qfrc_actuator', 'goal_pos', 'goal_rot'):
+        err = np.abs(gpu[f] - ref[f]) / np.maximum(1.0, np.abs(ref[f]))
+        assert np.max(err) < rel, (f, float(np.max(err)))
     assert not np.any(gpu['overflow'] & ~0x600) and not np.any(gpu['error'])
 
 
@@ -223,7 +228,7 @@ def test_scene_b_forward_parity(scene_b_state, oracle_module, precision, rel):
     assert close(gpu['qacc'], ref['qacc'], 1000 * rel)
 
 
-@pytest.mark.parametrize('precision,tol', [('fp32', 1e-3), ('fp64', 1e-6)])
+@pytest.mark.parametrize('precision,tol', [('fp32', 1e-3), ('fp64', 1e-9)])
 def test_scene_b_control_steps_parity(scene_b_state, oracle_module, precision, tol):
     from gpu_libero_b200.runtime import Runtime
     b, state = scene_b_state
@@ -254,13 +259,11 @@ def test_scene_b_control_steps_parity(scene_b_state, oracle_module, precision, t
     assert np.all(gpu['fact_blk'][:, 0] <= gpu['newton_total'][:, 0].astype(np.int64) * nv * nv * (nv + 6))
 
 
-@pytest.mark.parametrize('precision,tol', [('fp32', 2e-4), ('fp64', 2e-6)])
+@pytest.mark.parametrize('precision,tol', [('fp32', 1e-4), ('fp64', 1e-9)])
 def test_hundred_control_steps_track_the_oracle(scene, oracle_module, precision, tol):
-    """BASELINE's trajectory horizon: 100 control steps (2500 substeps) of scene A.
-    Measured on a B200: max |dqpos| 9.7e-5 (FP32) and 6.8e-7 (FP64) over the
-    run; the FP64 gap is the Newton stop rule (tolerance 1e-8), under which the
-    two implementations may stop one iteration apart.  Contact counts stay
-    equal at every checkpoint."""
+    """BASELINE's trajectory horizon: 100 control steps (2500 substeps) of
+    scene A, within north_star's bounds (1e-4 FP32, 1e-9 FP64) at every 25th
+    step.  Contact counts stay equal at every checkpoint."""
     n = 4
     from gpu_libero_b200.runtime import Runtime
     rt = Runtime(scene, n, precision=precision)

@@ -1,0 +1,195 @@
+"""GPU parity at BASELINE's configurations, on worlds sampled from the full batch.
+
+Configurations (BASELINE.json `configs`):
+  b32  scene B, FP32, 16384 worlds (the configuration the headline metric is quoted on)
+  b64  scene B, FP64, 16384 worlds
+  a32  scene A, FP32, 4096 worlds (config 2)
+  a64  scene A, FP64, 8192 worlds (config 4)
+The whole batch runs 100 control steps (2500 substeps) through the captured
+control graph.  32 worlds sampled across the batch are compared with the CPU
+oracle in three ways:
+
+1. frozen input, one substep: at 10 checkpoints the oracle and the CUDA kernel
+   (a 32-world launch) each take the policy substep from the batch's own state.
+   ctrl, qfrc_actuator, qfrc_constraint, efc_force, qacc and qvel agree within
+   north_star's bound (1e-4 in FP32, 1e-9 in FP64, relative to max(1, |value|));
+   ncon and nefc are equal, and so are the Newton iteration and line-search
+   evaluation counts (FP64: always; FP32: the stop rule and the line search's
+   bracket tests compare quantities at the FP32 tolerance floor, so a rounding
+   difference may move a decision by one iteration in a small fraction of
+   substeps; those samples are counted and bounded, and their fields are held
+   to a looser bound);
+2. teacher-forced: every control step, the oracle advances each sampled world
+   one control step (25 substeps) from the batch's state;
+3. free-running: the oracle runs the sampled worlds alone for all 100 control
+   steps.  Contact dynamics amplify any rounding difference, so the distance to
+   the batch is compared with the trajectories' own sensitivity: the same
+   worlds run again on the GPU from a qpos perturbed by one ulp.
+
+The kernel is bit-reproducible and a world's result does not depend on the
+batch it runs in (checked here: the 32-world runs equal the batch's rows).
+Measured values are printed (pytest -s shows them).
+"""
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip('torch')
+pytestmark = pytest.mark.gpu
+
+from gpu_libero_b200 import native, scene as scenes  # noqa: E402
+from gpu_libero_b200.runtime import Runtime  # noqa: E402
+
+CONFIGS = {'b32': ('scene_b', 'fp32', 16384), 'b64': ('scene_b', 'fp64', 16384),
+           'a32': ('scene_a', 'fp32', 4096), 'a64': ('scene_a', 'fp64', 8192)}
+STEPS, SAMPLE, CHECKPOINTS = 100, 32, tuple(range(0, 100, 10))
+FIELDS = ('ctrl', 'qfrc_actuator', 'qfrc_constraint', 'qacc', 'qvel')
+TRACES = ('niter_trace', 'ls_trace')
+
+
+def rel(a, b):
+    a, b = np.asarray(a, float), np.asarray(b, float)
+    return np.abs(a - b) / np.maximum(1.0, np.abs(b))
+
+
+def rows(rt, idx):
+    ii = torch.as_tensor(idx, device=rt.device)
+    return {k: t.index_select(0, ii).cpu().numpy().copy() for k, t in rt.buffers.items()}
+
+
+def load_rows(rt, src):
+    for k, t in rt.buffers.items():
+        if k in src:
+            t.copy_(torch.as_tensor(src[k]))
+
+
+@pytest.fixture(scope='module', params=list(CONFIGS))
+def run(request, oracle_module):
+    name, precision, W = CONFIGS[request.param]
+    scene = scenes.scene_b() if name == 'scene_b' else scenes.scene_a()
+    idx = np.sort(np.random.default_rng(0).choice(W, SAMPLE, replace=False))
+    big = Runtime(scene, W, precision=precision, debug=TRACES)
+    q, v = scene.initial_state(W, seed=0)
+    big.set_state(np.concatenate([np.zeros((W, 1)), q, v], axis=1))
+    big.prepare_control_graph()
+    small = Runtime(scene, SAMPLE, precision=precision, debug=True)
+    orc = oracle_module.Oracle(precision)
+    ms = big.packed.host_struct()
+    threads = max(1, len(os.sched_getaffinity(0)))
+    torch.cuda.synchronize()
+    init = rows(big, idx)
+    free = {k: v.copy() for k, v in init.items()}
+    frozen, forced = [], []
+    for k in range(STEPS):
+        a = scene.actions(W, k, seed=0)
+        pre = rows(big, idx)
+        if k in CHECKPOINTS:  # one substep from the batch's state, GPU and oracle
+            load_rows(small, pre)
+            small.buffers['action'].copy_(torch.as_tensor(a[idx]))
+            small.launch_step(policy=True, substeps=1)
+            ref = {kk: vv.copy() for kk, vv in pre.items()}
+            ref['action'][:] = a[idx]
+            orc.step_parallel(ms, native.data_struct(ref, SAMPLE), SAMPLE, 1, 1, threads)
+            torch.cuda.synchronize()
+            frozen.append((rows(small, np.arange(SAMPLE)), ref))
+        big.enqueue_action(a)
+        torch.cuda.synchronize()
+        post = rows(big, idx)
+        ref = pre
+        ref['action'][:] = a[idx]
+        for t in TRACES:
+            ref[t][:] = 0
+        orc.step_parallel(ms, native.data_struct(ref, SAMPLE), SAMPLE, scene.substeps, 1, threads)
+        free['action'][:] = a[idx]
+        orc.step_parallel(ms, native.data_struct(free, SAMPLE), SAMPLE, scene.substeps, 1, threads)
+        forced.append((post, ref))
+    final = rows(big, idx)
+    # the trajectories' sensitivity: the sampled worlds alone, from qpos and from qpos + 1 ulp
+    base = Runtime(scene, SAMPLE, precision=precision)
+    pert = Runtime(scene, SAMPLE, precision=precision)
+    for r in (base, pert):
+        load_rows(r, init)
+    qq = pert.buffers['qpos']
+    qq.copy_(torch.nextafter(qq, torch.full_like(qq, np.inf)))
+    for k in range(STEPS):
+        a = scene.actions(W, k, seed=0)[idx]
+        base.enqueue_action(a)
+        pert.enqueue_action(a)
+    torch.cuda.synchronize()
+    out = dict(tag=request.param, precision=precision, frozen=frozen, forced=forced, final=final, free=free,
+               base=base.buffers['qpos'].cpu().numpy(), pert=pert.buffers['qpos'].cpu().numpy(),
+               overflow=big.buffers['overflow'].cpu().numpy())
+    for r in (big, small, base, pert):
+        r.close()
+    return out
+
+
+def test_frozen_substep(run):
+    fp64 = run['precision'] == 'fp64'
+    bound = 1e-9 if fp64 else 1e-4
+    worst, worst_mis, mismatched, samples, count_diff = {}, 0.0, 0, 0, 0
+    for gpu, ref in run['frozen']:
+        assert np.array_equal(gpu['ncon'], ref['ncon'])
+        assert np.array_equal(gpu['nefc'], ref['nefc'])
+        same = (gpu['niter_trace'][:, 0] == ref['niter_trace'][:, 0]) & (gpu['ls_trace'][:, 0] == ref['ls_trace'][:, 0])
+        samples += len(same)
+        mismatched += int(np.sum(~same))
+        count_diff = max(count_diff, int(np.max(np.abs(gpu['niter_trace'][:, 0] - ref['niter_trace'][:, 0]))))
+        for w in range(SAMPLE):
+            n = int(ref['nefc'][w, 0])
+            errs = {f: float(rel(gpu[f][w], ref[f][w]).max()) for f in FIELDS}
+            errs['efc_force'] = float(rel(gpu['efc_force'][w, :n], ref['efc_force'][w, :n]).max(initial=0.0))
+            if same[w]:
+                for f, e in errs.items():
+                    worst[f] = max(worst.get(f, 0.0), e)
+            else:
+                worst_mis = max(worst_mis, max(errs.values()))
+    print('\n[%s] frozen substep: worst %s; count mismatches %d/%d (max |dniter| %d, worst field there %.2e)'
+          % (run['tag'], {f: '%.1e' % e for f, e in worst.items()}, mismatched, samples, count_diff, worst_mis))
+    for f, e in worst.items():
+        assert e <= bound, (f, e)
+    if fp64:
+        assert mismatched == 0
+    else:
+        assert mismatched <= 0.02 * samples and count_diff <= 2
+        assert worst_mis <= 1e-2
+
+
+def test_teacher_forced_control_steps(run):
+    fp64 = run['precision'] == 'fp64'
+    per_step = []
+    n_eq = niter_eq = ls_eq = total = subs = 0
+    for post, ref in run['forced']:
+        per_step.append(float(rel(post['qpos'], ref['qpos']).max()))
+        n_eq += int(np.sum((post['ncon'] == ref['ncon']) & (post['nefc'] == ref['nefc'])))
+        total += SAMPLE
+        niter_eq += int(np.sum(post['niter_trace'][:, :25] == ref['niter_trace'][:, :25]))
+        ls_eq += int(np.sum(post['ls_trace'][:, :25] == ref['ls_trace'][:, :25]))
+        subs += SAMPLE * 25
+    e = np.array(per_step)
+    print('\n[%s] teacher-forced control step: qpos rel median %.1e p90 %.1e max %.1e; ncon/nefc equal %.4f; '
+          'Newton iterations equal %.5f, line-search evaluations equal %.5f'
+          % (run['tag'], np.median(e), np.percentile(e, 90), e.max(), n_eq / total, niter_eq / subs, ls_eq / subs))
+    if fp64:
+        assert e.max() <= 1e-9
+        assert n_eq == total and niter_eq == subs and ls_eq == subs
+    else:
+        assert np.median(e) <= 1e-4
+        assert niter_eq >= 0.995 * subs and n_eq >= 0.99 * total
+
+
+def test_free_running_hundred_control_steps(run):
+    """BASELINE's horizon: 100 control steps from the initial state."""
+    final, free = run['final'], run['free']
+    assert np.array_equal(run['base'], final['qpos'])  # a world's result does not depend on its batch
+    err = np.abs(final['qpos'] - free['qpos']).max(axis=1)
+    chaos = np.abs(run['pert'] - run['base']).max(axis=1)
+    print('\n[%s] free-running 100 control steps: |dqpos| max %.2e median %.2e; one-ulp sensitivity max %.2e '
+          'median %.2e' % (run['tag'], err.max(), np.median(err), chaos.max(), np.median(chaos)))
+    assert np.all(np.isfinite(free['qpos']))
+    if run['tag'] == 'a64':
+        assert err.max() <= 1e-9  # north_star's FP64 bound
+    assert np.median(err) <= 10 * max(np.median(chaos), 1e-12 if run['precision'] == 'fp64' else 1e-6)
+    fatal = run['overflow'] & ~(0x200 | 0x400 | 0x20000)
+    assert not np.any(fatal)

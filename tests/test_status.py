@@ -4,8 +4,11 @@ The CPU oracle carries the same status rules as the CUDA kernel (the GPU
 tests compare the two world by world):
   - a world whose qpos / qvel is non-finite or beyond 1e10 (MuJoCo
     mj_checkPos / mj_checkVel) gets B200_STATUS_BADSTATE and is not stepped;
-  - an EPA whose vertex, face or horizon pool fills reports EPA_HORIZON
-    (reference OverflowType, cuda_fp32/constants.py:89-101);
+  - an EPA whose vertex or face pool fills ends with its best face and
+    reports the non-fatal B200_WARN_EPA_BUDGET, like its iteration limit (the
+    reference's full face pool also ends its EPA without a status,
+    mjwarp_convex_epa.cuh:89,219; EPA_HORIZON stays the fatal horizon-list
+    overflow of the reference's OverflowType, cuda_fp32/constants.py:89-101);
   - reward and done are the synthetic task's sparse success predicate.
 Batch quarantine follows the reference env (cuda_fp32/environment.py:126-140,
 batch_env.py:298-302,376-384; tests/test_gpu_batch_env.py:123): a failed
@@ -23,7 +26,7 @@ import pytest
 from gpu_libero_b200 import native, scene as scenes
 
 ROOT = Path(__file__).resolve().parents[1]
-BADSTATE, EPA_HORIZON = 1 << 16, 1 << 8
+BADSTATE, EPA_BUDGET = 1 << 16, 1 << 17
 
 
 def oracle_world_state(oracle_module, scene, n, seed=3):
@@ -71,9 +74,8 @@ def test_task_predicate_is_the_lifted_task_body(oracle_module):
 def test_epa_pool_overflow_is_reported(oracle_module):
     """A sphere inside a finely tessellated hull (2000 points on a sphere):
     EPA needs more than 44 expansions to resolve the nearest facet, so with a
-    budget of 200 its 48-vertex pool fills and the status is raised; the
-    scenes' 32 expansions never fill it (dead faces are compacted, and 36
-    vertices bound 68 live faces)."""
+    budget of 200 its 48-vertex pool fills and the budget status is raised;
+    32 expansions (the scenes' setting) leave 36 vertices, below the pool."""
     orc = oracle_module.Oracle('fp64')
     rng = np.random.default_rng(1)
     d = rng.normal(size=(2000, 3))
