@@ -128,8 +128,9 @@ typedef struct {
   real cvel[MAXB][6], cdof_dot[MAXV][6], qfrc_bias[MAXV], qfrc_passive[MAXV];
   real act_length[16], act_moment[16], act_force[16], qfrc_actuator[MAXV];
   real qfrc_smooth[MAXV], qacc_smooth[MAXV];
-  /* collision / constraints */
-  int ncon, nefc, nf, overflow;
+  /* collision / constraints: rows [0, ne) are equality rows (none in the
+   * scenes; the Newton-piece leaves use them), [ne, ne + nf) friction loss */
+  int ncon, nefc, ne, nf, overflow;
   Contact con[MAXC];
   int con_adr[MAXC];
   real J[MAXE][MAXV];
@@ -1347,8 +1348,9 @@ static void eval_constraints(const B200Model *m, Work *k) {
   for (int r = 0; r < k->nefc; ++r) {
     real d = k->efc_D[r], res = k->efc_jaref[r], force;
     int state;
-    int friction = r < k->nf;
-    if (friction) {
+    int friction = r >= k->ne && r < k->ne + k->nf;
+    if (r < k->ne) { force = -d * res; state = kQuadratic; }
+    else if (friction) {
       real loss = k->efc_frictionloss[r], radius = safe_div(loss, d);
       if (res <= -radius) { force = loss; state = kLinearNegative; }
       else if (res >= radius) { force = -loss; state = kLinearPositive; }
@@ -1454,7 +1456,8 @@ typedef struct {
 static Row load_row(const B200Model *m, const Work *k, int r) {
   Row o;
   memset(&o, 0, sizeof(o));
-  if (r < k->nf) o.kind = 1;
+  if (r < k->ne) o.kind = 0; /* equality: always quadratic */
+  else if (r < k->ne + k->nf) o.kind = 1;
   else if (k->efc_type[r] != 7) o.kind = 2;
   else {
     int c = k->efc_id[r], head = k->con_adr[c];
@@ -2024,4 +2027,105 @@ int oracle_leaf_convex(int type1, const real *p1, const real *R1, const real *s1
   vstore(pos, vadd(vscale(vadd(x1, x2), R(0.5)), origin));
   vstore(normal, vnormalize(*dist <= margin ? vsub(x1, x2) : vsub(x2, x1)));
   return 1 | flags;
+}
+
+/* ---- Newton-piece leaves (golden-vector tests): one world's constraint rows
+ * given explicitly in the reference's row layout (equality, friction loss,
+ * then limit and contact rows; a contact's rows are contiguous from
+ * con_adr[c], -1 for a contact without rows) and a dense mass matrix. */
+typedef struct {
+  int nv, nefc, ne, nf, ncon, ls_iterations;
+  double impratio_invsqrt, tolerance, ls_tolerance, meaninertia;
+  const real *M, *J, *D, *frictionloss, *qfrc_smooth, *search;
+  const int *type, *id, *state_in, *con_dim, *con_adr;
+  const real *con_friction;
+  real *jaref, *qacc, *Ma, *force, *H, *alpha, *improvement;
+  int *state, *ls_evals, *overflow;
+} NewtonLeaf;
+
+size_t oracle_newton_leaf_bytes(void) { return sizeof(NewtonLeaf); }
+
+/* a model of one kinematic tree holding every dof, so that M is one block */
+static int leaf_setup(const NewtonLeaf *a, B200Model *m, int *ints, Work *k) {
+  int nv = a->nv;
+  if (nv < 1 || nv > MAXV || a->nefc < 0 || a->nefc > MAXE || a->ncon < 0 || a->ncon > MAXC) return 1;
+  memset(m, 0, sizeof(*m));
+  for (int i = 0; i < nv; ++i) ints[i] = 0;
+  ints[nv] = 0; ints[nv + 1] = nv; ints[nv + 2] = 0;
+  m->ints = ints;
+  m->off_dof_treeid = 0; m->off_tree_dofadr = nv; m->off_tree_dofnum = nv + 1; m->off_tree_madr = nv + 2;
+  m->nv = nv; m->ntree = 1; m->cone = 1; m->real_bytes = (int)sizeof(real);
+  m->impratio_invsqrt = a->impratio_invsqrt; m->tolerance = a->tolerance; m->ls_tolerance = a->ls_tolerance;
+  m->meaninertia = a->meaninertia; m->ls_iterations = a->ls_iterations;
+  k->nefc = a->nefc; k->ne = a->ne; k->nf = a->nf; k->ncon = a->ncon;
+  memcpy(k->M, a->M, sizeof(real) * nv * nv);
+  for (int r = 0; r < a->nefc; ++r) {
+    for (int i = 0; i < nv; ++i) k->J[r][i] = a->J[(size_t)r * nv + i];
+    k->efc_D[r] = a->D[r];
+    k->efc_frictionloss[r] = a->frictionloss ? a->frictionloss[r] : 0;
+    k->efc_type[r] = a->type[r];
+    k->efc_id[r] = a->id[r];
+    k->efc_jaref[r] = a->jaref[r];
+    k->efc_state[r] = a->state_in ? a->state_in[r] : 0;
+  }
+  for (int c = 0; c < a->ncon; ++c) {
+    k->con[c].dim = a->con_dim[c];
+    for (int j = 0; j < 5; ++j) k->con[c].friction[j] = a->con_friction[5 * c + j];
+    k->con_adr[c] = a->con_adr[c];
+  }
+  return 0;
+}
+
+/* row forces and states (mjwarp_constraint.cu:27-228) */
+int oracle_leaf_newton_rows(const NewtonLeaf *a) {
+  B200Model m;
+  int ints[MAXV + 3];
+  Work *k = (Work *)calloc(1, sizeof(Work));
+  if (!k) return 2;
+  if (leaf_setup(a, &m, ints, k)) { free(k); return 1; }
+  eval_constraints(&m, k);
+  for (int r = 0; r < a->nefc; ++r) { a->force[r] = k->efc_force[r]; a->state[r] = k->efc_state[r]; }
+  free(k);
+  return 0;
+}
+
+/* H = M + J' D J over quadratic rows + elliptic-cone curvature, from the
+ * given row states (mjwarp_hessian.cu:33-212); dense nv x nv */
+int oracle_leaf_newton_hessian(const NewtonLeaf *a) {
+  B200Model m;
+  int ints[MAXV + 3];
+  Work *k = (Work *)calloc(1, sizeof(Work));
+  if (!k) return 2;
+  if (leaf_setup(a, &m, ints, k)) { free(k); return 1; }
+  hessian(&m, k);
+  memcpy(a->H, k->H, sizeof(real) * a->nv * a->nv);
+  free(k);
+  return 0;
+}
+
+/* one exact line search along `search` from qacc (mjwarp_linesearch.cu:80-365):
+ * alpha, improvement, and qacc / Ma / jaref moved by alpha */
+int oracle_leaf_newton_linesearch(const NewtonLeaf *a) {
+  B200Model m;
+  int ints[MAXV + 3];
+  Work *k = (Work *)calloc(1, sizeof(Work));
+  if (!k) return 2;
+  if (leaf_setup(a, &m, ints, k)) { free(k); return 1; }
+  int nv = a->nv, of = 0;
+  real sd = 0;
+  for (int i = 0; i < nv; ++i) {
+    k->qacc[i] = a->qacc[i]; k->Ma[i] = a->Ma[i]; k->qfrc_smooth[i] = a->qfrc_smooth[i];
+    k->search[i] = a->search[i]; sd += a->search[i] * a->search[i];
+  }
+  k->search_dot = sd;
+  k->ls_evals = 0;
+  linesearch(&m, k, &of);
+  *a->alpha = k->alpha;
+  *a->improvement = k->improvement;
+  *a->ls_evals = k->ls_evals;
+  *a->overflow = of;
+  for (int i = 0; i < nv; ++i) { a->qacc[i] = k->qacc[i]; a->Ma[i] = k->Ma[i]; }
+  for (int r = 0; r < a->nefc; ++r) a->jaref[r] = k->efc_jaref[r];
+  free(k);
+  return 0;
 }

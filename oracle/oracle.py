@@ -19,6 +19,15 @@ def build():
     subprocess.run(['make', '-s', '-C', str(HERE)], check=True)
 
 
+class NewtonLeaf(ct.Structure):
+    """One world's constraint rows for the Newton-piece leaves (oracle.c NewtonLeaf)."""
+    _fields_ = ([(k, ct.c_int) for k in ('nv', 'nefc', 'ne', 'nf', 'ncon', 'ls_iterations')] +
+                [(k, ct.c_double) for k in ('impratio_invsqrt', 'tolerance', 'ls_tolerance', 'meaninertia')] +
+                [(k, ct.c_void_p) for k in ('M', 'J', 'D', 'frictionloss', 'qfrc_smooth', 'search', 'type', 'id',
+                                            'state_in', 'con_dim', 'con_adr', 'con_friction', 'jaref', 'qacc', 'Ma',
+                                            'force', 'H', 'alpha', 'improvement', 'state', 'ls_evals', 'overflow')])
+
+
 class Oracle:
     def __init__(self, precision='fp32'):
         name = 'liboracle_f32.so' if precision in ('fp32', 'float32') else 'liboracle_f64.so'
@@ -39,6 +48,13 @@ class Oracle:
         self.lib.oracle_step.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_int, ct.c_int, ct.c_int, ct.c_int]
         self.lib.oracle_forward.restype = ct.c_int
         self.lib.oracle_forward.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_int, ct.c_int, ct.c_int]
+        for leaf in ('rows', 'hessian', 'linesearch'):
+            fn = getattr(self.lib, 'oracle_leaf_newton_' + leaf)
+            fn.restype = ct.c_int
+            fn.argtypes = [ct.POINTER(NewtonLeaf)]
+        self.lib.oracle_newton_leaf_bytes.restype = ct.c_size_t
+        if self.lib.oracle_newton_leaf_bytes() != ct.sizeof(NewtonLeaf):
+            raise ValueError('NewtonLeaf layout differs between oracle.c and oracle.py')
 
     def step(self, model, data, w0, w1, substeps, policy):
         rc = self.lib.oracle_step(ct.addressof(model), ct.addressof(data), w0, w1, substeps, policy)
@@ -126,3 +142,53 @@ class Oracle:
                                         epa_iterations, self._ptr(dist), self._ptr(pos), self._ptr(nrm))
         self.epa_overflow = bool(n & 2)
         return (float(dist[0]), pos.astype(float), nrm.astype(float)) if n & 1 else None
+
+    # ---- Newton pieces on one world's explicit rows (golden-vector tests)
+    def newton(self, piece, case):
+        """Run one Newton piece ('rows', 'hessian' or 'linesearch') on the rows
+        of `case` (a dict of arrays in the reference's row layout); returns
+        the piece's outputs."""
+        r = self.dtype
+        nv, n = int(case['nv']), len(case['type'])
+        keep = []
+
+        def arr(x, dtype):
+            a = np.ascontiguousarray(np.asarray(x, dtype).reshape(-1))
+            keep.append(a)
+            return a.ctypes.data
+
+        s = NewtonLeaf()
+        s.nv, s.nefc, s.ne, s.nf = nv, n, int(case.get('ne', 0)), int(case.get('nf', 0))
+        s.ncon, s.ls_iterations = len(case['con_dim']), int(case.get('ls_iterations', 0))
+        s.impratio_invsqrt = float(case['impratio'])
+        for k in ('tolerance', 'ls_tolerance', 'meaninertia'):
+            setattr(s, k, float(case.get(k, 0.0)))
+        s.M = arr(case.get('M', np.eye(nv)), r)
+        s.J = arr(case['J'], r)
+        s.D = arr(case['D'], r)
+        s.frictionloss = arr(case.get('frictionloss', np.zeros(n)), r)
+        s.type, s.id = arr(case['type'], np.int32), arr(case['id'], np.int32)
+        s.state_in = arr(case.get('state', np.zeros(n)), np.int32)
+        s.con_dim, s.con_adr = arr(case['con_dim'], np.int32), arr(case['con_adr'], np.int32)
+        s.con_friction = arr(case['con_friction'], r)
+        # in/out arrays: always copies, so the caller's inputs stay untouched
+        jaref = np.array(case['jaref'], r, copy=True, order='C')
+        qacc = np.array(case.get('qacc', np.zeros(nv)), r, copy=True, order='C')
+        Ma = np.array(case.get('Ma', np.zeros(nv)), r, copy=True, order='C')
+        s.jaref, s.qacc, s.Ma = jaref.ctypes.data, qacc.ctypes.data, Ma.ctypes.data
+        s.qfrc_smooth = arr(case.get('qfrc_smooth', np.zeros(nv)), r)
+        s.search = arr(case.get('search', np.zeros(nv)), r)
+        force, H = np.zeros(n, r), np.zeros(nv * nv, r)
+        state, alpha, improvement = np.zeros(n, np.int32), np.zeros(1, r), np.zeros(1, r)
+        evals, overflow = np.zeros(1, np.int32), np.zeros(1, np.int32)
+        s.force, s.H, s.state = force.ctypes.data, H.ctypes.data, state.ctypes.data
+        s.alpha, s.improvement = alpha.ctypes.data, improvement.ctypes.data
+        s.ls_evals, s.overflow = evals.ctypes.data, overflow.ctypes.data
+        if getattr(self.lib, 'oracle_leaf_newton_' + piece)(ct.byref(s)):
+            raise RuntimeError('oracle_leaf_newton_%s rejected the case' % piece)
+        if piece == 'rows':
+            return dict(force=force.astype(float), state=state)
+        if piece == 'hessian':
+            return dict(H=H.reshape(nv, nv).astype(float))
+        return dict(alpha=float(alpha[0]), improvement=float(improvement[0]), ls_evals=int(evals[0]),
+                    overflow=int(overflow[0]), qacc=qacc.astype(float), Ma=Ma.astype(float), jaref=jaref.astype(float))

@@ -10,6 +10,8 @@ run here only to supply contact lists to the constraint-row oracle and to
 assert, before anything is written, that it already agrees.  Tests read the
 written .npz/.json files only.
 
+Usage (one part only): python tests/golden/make_golden.py <reference checkout> newton
+
 Reference modules used (paths inside the reference checkout):
   tools/validation/mjwarp_kinematics_reference.py   reference(c, 'composed')
   tools/validation/mjwarp_plane_reference.py        reference(c), material()
@@ -20,6 +22,14 @@ Reference modules used (paths inside the reference checkout):
   boxbox_first_face_vertex.csv, boxbox_sat_face_tie.csv, and the unit-box
   cases of tests/cuda/precision_boxbox_test.cu:76-82.
   tests/data/gjk_tuned_direction.json (a recorded LIBERO box-box overlap).
+  tools/validation/mjwarp_constraint.py   synthetic(), reference(): FP64 row
+      forces and states of the Newton constraint projection (with the
+      reference's ambiguity flags and error bounds)
+  tools/validation/mjwarp_hessian.py      synthetic_case(), matrix_reference():
+      FP64 H = M + J'DJ plus the elliptic-cone curvature (and its majorant)
+  tools/validation/mjwarp_linesearch.py   synthetic(), matrix(), objective():
+      the FP64 cost along the search ray; its minimiser is found here by
+      golden-section search on the reference's objective
 """
 import csv
 import importlib
@@ -380,7 +390,153 @@ def make_gjk_direction(mods, path):
     (HERE / 'gjk_tuned_direction.json').write_text(json.dumps(out, indent=1))
 
 
+# ------------------------------------------------------------------ Newton pieces
+NEWTON_NV = (9, 27, 39, 57)
+
+
+def world_contacts(type_row, id_row, nefc, dims, friction, address, active=None):
+    """One world's contacts, renumbered 0.. in order of first use by its rows:
+    (row ids remapped, dims, frictions, first-row addresses or -1)."""
+    used = []
+    for r in range(nefc):
+        if type_row[r] == 7 and int(id_row[r]) not in used:
+            used.append(int(id_row[r]))
+    remap = {c: i for i, c in enumerate(used)}
+    ids = np.array([remap.get(int(i), int(i)) if type_row[r] == 7 else int(i) for r, i in enumerate(id_row[:nefc])],
+                   np.int32)
+    dim = np.array([int(dims[c]) for c in used], np.int32)
+    fr = np.array([friction[c] for c in used], np.float64).reshape(-1, 5)
+    adr = np.array([int(address[c][0]) if np.all(np.asarray(address[c][:dims[c]]) >= 0) and
+                    (active is None or active[c]) else -1 for c in used], np.int32)
+    return ids, dim, fr, adr
+
+
+def golden_section(f, hi):
+    """Minimiser of a convex function of alpha on [0, hi] (after widening hi
+    until f rises), to the limit of FP64."""
+    lo, f_hi = 0.0, f(hi)
+    while f_hi < f(0.0) and hi < 1e12:
+        hi *= 2
+        f_hi = f(hi)
+    g = (np.sqrt(5) - 1) / 2
+    a, b = lo, hi
+    c, d = b - g * (b - a), a + g * (b - a)
+    fc, fd = f(c), f(d)
+    for _ in range(200):
+        if fc < fd:
+            b, d, fd = d, c, fc
+            c = b - g * (b - a)
+            fc = f(c)
+        else:
+            a, c, fc = c, d, fd
+            d = a + g * (b - a)
+            fd = f(d)
+    return 0.5 * (a + b)
+
+
+def make_newton(path):
+    sys.path.insert(0, str(Path(path) / 'tools'))
+    sys.path.insert(0, str(path))
+    C = importlib.import_module('validation.mjwarp_constraint')
+    H = importlib.import_module('validation.mjwarp_hessian')
+    L = importlib.import_module('validation.mjwarp_linesearch')
+    out, counts = {}, dict(rows=0, hessian=0, linesearch=0)
+
+    def put(kind, fields):
+        i = counts[kind]
+        counts[kind] += 1
+        for k, v in fields.items():
+            out['%s%d_%s' % (kind, i, k)] = np.asarray(v)
+
+    # row forces and states
+    cases = [C.synthetic(nv) for nv in NEWTON_NV]
+    cases += [C.synthetic(39, v) for v in ('world1-done', 'empty-world0', 'top-boundary', 'bottom-boundary',
+                                           'zero-tangent', 'friction-boundary', 'broadcast-impratio')]
+    for case in cases:
+        a = case['arrays']
+        force, state, ambiguous, held, bound = C.reference(a)
+        nv = int(a['nv'])
+        for w in range(2):
+            n = int(a['nefc'][w])
+            if a['done'][w] or n == 0:
+                continue
+            ids, dim, fr, adr = world_contacts(a['type'][w], a['id'][w], n, a['contact_dim'], a['contact_friction'],
+                                               a['contact_efc_address'])
+            put('rows', dict(nv=nv, ne=a['ne'][w], nf=a['nf'][w], type=a['type'][w, :n], id=ids, D=a['D'][w, :n],
+                             frictionloss=a['frictionloss'][w, :n], jaref=a['jaref'][w, :n],
+                             J=a['J'][w, :n, :nv], impratio=a['impratio'][w % a['impratio'].size],
+                             con_dim=dim, con_friction=fr, con_adr=adr, force=force[w, :n], state=state[w, :n],
+                             compare=~(ambiguous[w, :n] | held[w, :n]), bound=bound[w, :n]))
+    # Hessian
+    cases = [H.synthetic_case(nv) for nv in NEWTON_NV] + [H.synthetic_case(39, variant=v) for v in ('zero-friction',)]
+    for case in cases:
+        a, nv = case['arrays'], case['nv']
+        result, magnitude, _ = H.matrix_reference(case)
+        active = a['contact_distance'] - a['contact_margin'] < 0
+        for w in range(2):
+            n = int(a['nefc'][w])
+            if a['done'][w]:
+                continue
+            M = np.zeros((nv, nv))
+            for e, (r, c) in enumerate(zip(a['mass_row'], a['mass_column'])):
+                M[r, c] = M[c, r] = a['mass'][w, e]
+            mine = [c for c in range(min(int(a['contact_count'][0]), a['contact_world'].size))
+                    if a['contact_world'][c] == w]
+            typ = np.full(n, 3, np.int32)
+            rid = np.zeros(n, np.int32)
+            for k, c in enumerate(mine):
+                ids = a['contact_address'][c, :a['contact_dimension'][c]]
+                for r in ids[ids >= 0]:
+                    if r < n:
+                        typ[r], rid[r] = 7, k
+            adr = np.array([int(a['contact_address'][c, 0]) if a['contact_dimension'][c] > 1 and active[c] and
+                            np.all(a['contact_address'][c, :a['contact_dimension'][c]] >= 0) else -1 for c in mine],
+                           np.int32)
+            up = np.triu(result[w, :nv, :nv])
+            mag = np.triu(magnitude[w, :nv, :nv])
+            put('hessian', dict(nv=nv, type=typ, id=rid, D=a['diagonal'][w, :n], jaref=a['jaref'][w, :n],
+                                J=a['jacobian'][w, :n, :nv], state=a['state'][w, :n], M=M,
+                                impratio=a['impratio'][w % a['impratio'].size],
+                                con_dim=np.array([a['contact_dimension'][c] for c in mine], np.int32),
+                                con_friction=np.array([a['contact_friction'][c] for c in mine]).reshape(-1, 5),
+                                con_adr=adr, H=up + np.triu(up, 1).T, magnitude=mag + np.triu(mag, 1).T))
+    # line search
+    cases = [L.synthetic(nv) for nv in NEWTON_NV]
+    cases += [L.synthetic(39, v) for v in ('top-boundary', 'bottom-boundary', 'zero-tangent', 'friction-boundary',
+                                           'small-search')]
+    for case in cases:
+        a = case['arrays']
+        nv = int(a['nv'])
+        mass = L.matrix(a)
+        jv = np.einsum('wri,wi->wr', a['J'][:, :, :nv].astype(np.float64), a['search'].astype(np.float64))
+        for w in range(2):
+            n = int(a['nefc'][w])
+            if a['done'][w] or not np.any(a['search'][w]):
+                continue
+            f = lambda alpha: L.objective(a, w, alpha, mass, jv)  # noqa: E731
+            best = golden_section(f, 1.0)
+            h = 1e-4 * max(best, 1e-3)
+            curv = (f(best + h) - 2 * f(best) + f(best - h)) / (h * h)
+            ids, dim, fr, adr = world_contacts(a['type'][w], a['id'][w], n, a['contact_dim'], a['contact_friction'],
+                                               a['contact_efc_address'])
+            put('linesearch', dict(nv=nv, ne=a['ne'][w], nf=a['nf'][w], type=a['type'][w, :n], id=ids,
+                                   D=a['D'][w, :n], frictionloss=a['frictionloss'][w, :n], jaref=a['Jaref'][w, :n],
+                                   J=a['J'][w, :n, :nv], M=mass[w], qacc=a['qacc'][w], Ma=a['Ma'][w],
+                                   qfrc_smooth=a['qfrc_smooth'][w], search=a['search'][w],
+                                   impratio=a['impratio_invsqrt'][w % a['impratio_invsqrt'].size],
+                                   tolerance=a['tolerance'][0], ls_tolerance=a['ls_tolerance'][0],
+                                   meaninertia=a['inertia'][0], ls_iterations=int(a['ls_iterations']),
+                                   con_dim=dim, con_friction=fr, con_adr=adr, alpha_min=best, cost0=f(0.0),
+                                   cost_min=f(best), curvature=curv))
+    out.update({'count_' + k: np.array(v) for k, v in counts.items()})
+    np.savez_compressed(HERE / 'newton_pieces.npz', **out)
+    print('newton pieces:', counts)
+
+
 def main():
+    if len(sys.argv) == 3 and sys.argv[2] == 'newton':
+        make_newton(sys.argv[1])
+        return
     if len(sys.argv) != 2:
         raise SystemExit(__doc__)
     mods = load_reference(sys.argv[1])
@@ -392,6 +548,7 @@ def main():
     make_box_pairs(mods, oracle)
     make_box_fixtures(mods, sys.argv[1])
     make_gjk_direction(mods, sys.argv[1])
+    make_newton(sys.argv[1])
     print('golden vectors written to', HERE)
 
 
