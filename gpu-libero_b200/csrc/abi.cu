@@ -82,6 +82,36 @@ template <template <class, bool, int> class F, class... A> void dispatch(const B
     else t ? F<double, false, 128>::run(a...) : F<double, false, 32>::run(a...);
   }
 }
+// Worlds sorted by their last control step's work into 256 buckets, heaviest
+// first (a counting sort in one CTA; worlds within a bucket land in arrival
+// order, which changes only which worlds share a CTA, never their results).
+__global__ void __launch_bounds__(1024) order_worlds(const int *work, int *order, int n) {
+  __shared__ int hist[256];
+  __shared__ int top;
+  const int t = threadIdx.x;
+  if (t == 0) top = 1;
+  if (t < 256) hist[t] = 0;
+  __syncthreads();
+  int mx = 1;
+  for (int i = t; i < n; i += blockDim.x) mx = max(mx, work[i]);
+  atomicMax(&top, mx);
+  __syncthreads();
+  const long long scale = top;
+  auto bucket = [&](int i) { return 255 - (int)((long long)min(max(work[i], 0), top) * 255 / scale); };
+  for (int i = t; i < n; i += blockDim.x) atomicAdd(&hist[bucket(i)], 1);
+  __syncthreads();
+  if (t == 0) {
+    int s = 0;
+    for (int k = 0; k < 256; ++k) {
+      const int c = hist[k];
+      hist[k] = s;
+      s += c;
+    }
+  }
+  __syncthreads();
+  for (int i = t; i < n; i += blockDim.x) order[atomicAdd(&hist[bucket(i)], 1)] = i;
+}
+
 template <class R, bool C, int T> struct StepLaunch {
   template <class... A> static void run(A... a) { b200::launch_step<R, C, T>(a...); }
 };
@@ -116,6 +146,13 @@ int b200phys_step_launch(const B200Model *m, const B200Data *d, int substeps, in
   const int arena = (int)arena_for(m), grid = (d->nworld + sh.wpc - 1) / sh.wpc;
   dispatch<StepLaunch>(m, sh, *m, *d, substeps, policy, sh.wpc, arena, grid, (size_t)sh.wpc * arena,
                        (cudaStream_t)stream);
+  return (int)cudaGetLastError();
+}
+
+int b200phys_order_launch(const B200Model *m, const B200Data *d, void *stream) {
+  if (!model_ok(m) || !data_ok(d) || !d->work || !d->order) return (int)cudaErrorInvalidValue;
+  if (d->nworld == 0) return 0;
+  order_worlds<<<1, 1024, 0, (cudaStream_t)stream>>>(d->work, d->order, d->nworld);
   return (int)cudaGetLastError();
 }
 

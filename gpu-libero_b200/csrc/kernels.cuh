@@ -54,6 +54,15 @@ template <int T> __device__ __forceinline__ void world_sync() {
   if (T == 32) __syncwarp();
   else asm volatile("bar.sync %0, %1;" ::"r"(1 + (int)(threadIdx.x / T)), "r"(T) : "memory");
 }
+// Barrier of G threads of a world that work apart from the rest: the whole
+// world (G == T), its first warp alone (G == 32), or its other warps (named
+// barrier 4 + world slot; used only by worlds of more than one warp, which
+// number at most three per CTA, so the ids stay clear of the world barriers).
+template <int T, int G> __device__ __forceinline__ void group_sync() {
+  if (G == T) world_sync<T>();
+  else if (G == 32) __syncwarp();
+  else asm volatile("bar.sync %0, %1;" ::"r"(4 + (int)(threadIdx.x / T)), "r"(G) : "memory");
+}
 
 // Stage profiling (data.stage_cycles != NULL): lane 0 of each world stamps
 // clock64 at stage boundaries, after a barrier.
@@ -547,60 +556,68 @@ template <class R, int T> __device__ void mass_mul(const Mdl<R> &M, const R *Mb,
 
 // ============================================================ collision
 // CONVEX: the kernel variant for models with mesh geoms (plane-mesh and the
-// GJK/EPA pairs); models without meshes run the smaller variant.
-template <class R, int T, bool CONVEX> __device__ void collision(const Mdl<R> &M, Arena<R> &A) {
+// GJK/EPA pairs); models without meshes run the smaller variant.  The G
+// threads [G0, G0 + G) of the world run it; their pair lists start
+// list_offset bytes into the stage-scoped union region.
+template <class R, int T, bool CONVEX, int G0, int G>
+__device__ void collision(const Mdl<R> &M, Arena<R> &A, int list_offset) {
   const B200Model &m = M.m;
+  const int gt = TID - G0;
   // Broadphase first, then the narrowphase over the surviving pairs grouped
-  // by family, so that the threads of a warp run the same collider.  The
-  // pair lists live in the stage-scoped union region (free between the mass
-  // factor and the RNE).  Contact order is fixed by the key sort below, not
-  // by the order in which pairs are processed.
+  // by family, so that the threads of a warp run the same collider.  Contact
+  // order is fixed by the key sort below, not by the order in which pairs are
+  // processed.
   constexpr int kFam = 5;
-  int *fam = (int *)A.H, *cnt = fam + m.npair, *fill = cnt + kFam, *list = fill + kFam;
-  const bool grouped = (2 * m.npair + 2 * kFam) * (int)sizeof(int) <= A.ubytes;
-  if (TID == 0) A.iscal[8] = 0;
-  if (grouped && TID < 2 * kFam) cnt[TID] = 0;
-  SYNC();
+  int *fam = (int *)((unsigned char *)A.H + list_offset), *cnt = fam + m.npair, *fill = cnt + kFam,
+      *list = fill + kFam;
+  const bool grouped = list_offset + (2 * m.npair + 2 * kFam) * (int)sizeof(int) <= A.ubytes;
+  if (gt == 0) A.iscal[8] = 0;
+  if (grouped && gt < 2 * kFam) cnt[gt] = 0;
+  group_sync<T, G>();
   if (!(m.disable_flags & (B200_DSBL_CONSTRAINT | B200_DSBL_CONTACT))) {
     if (grouped) {
-      FOR(p, m.npair) {
+      for (int p = gt; p < m.npair; p += G) {
         const int f = pair_family<R, CONVEX>(M, A, p);
         fam[p] = f;
         if (f >= 0) atomicAdd(&cnt[f], 1);
       }
-      SYNC();
+      group_sync<T, G>();
       int off[kFam], total = 0;
       for (int f = 0; f < kFam; ++f) { off[f] = total; total += cnt[f]; }
-      FOR(p, m.npair) {
+      for (int p = gt; p < m.npair; p += G) {
         const int f = fam[p];
         if (f >= 0) list[off[f] + atomicAdd(&fill[f], 1)] = p;
       }
-      SYNC();
-      // families dealt to the world's warps (convex alone on the first), so that
-      // a warp runs one or two collider code paths instead of all of them
-      constexpr int kFamWarp[kFam] = {3, 1, 3, 2, 0};
-      const int nw = T / 32, wid = TID / 32;
-      for (int f = 0; f < kFam; ++f)
-        if (kFamWarp[f] % nw == wid)
+      group_sync<T, G>();
+      // families dealt to the group's warps, convex pairs (GJK / EPA, the
+      // slowest) alone on one, so that a warp runs one or two collider code
+      // paths instead of all of them
+      constexpr int nw = G / 32;
+      constexpr int kFamWarp4[kFam] = {3, 1, 3, 2, 0}, kFamWarp3[kFam] = {1, 2, 1, 2, 0};
+      const int wid = gt / 32;
+      for (int f = 0; f < kFam; ++f) {
+        const int owner = nw == 3 ? kFamWarp3[f] : kFamWarp4[f] % nw;
+        if (owner == wid)
           for (int i = LANE; i < cnt[f]; i += 32) narrow_pair<R, CONVEX>(M, A, list[off[f] + i], f);
+      }
     } else {
-      FOR(p, m.npair) {
+      for (int p = gt; p < m.npair; p += G) {
         const int f = pair_family<R, CONVEX>(M, A, p);
         if (f >= 0) narrow_pair<R, CONVEX>(M, A, p, f);
       }
     }
   }
-  SYNC();
+  group_sync<T, G>();
   const int n = mmin(A.iscal[8], m.ncon_max);
   // deterministic order: rank of each contact's (pair, id) key
-  FOR(c, n) {
+  for (int c = gt; c < n; c += G) {
     const int key = A.con_key[c];
     int rank = 0;
     for (int k = 0; k < n; ++k) rank += A.con_key[k] < key;
     A.con_order[rank] = c;
   }
-  if (TID == 0) A.iscal[0] = n;
-  SYNC();
+  if (gt == 0) A.iscal[0] = n;
+  group_sync<T, G>();
 }
 
 // ============================================================ constraints
@@ -1267,7 +1284,9 @@ template <class R> __device__ void rotation_delta(R x, R y, R z, double *r) {
   r[7] = (double)sum(2, 3, 1, 0);
 }
 
-template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> &A, bool policy) {
+// G: the threads that run it (the world's first G threads; 32 when the world's
+// other warps run collision meanwhile)
+template <class R, int T, int G> __device__ void osc_control(const Mdl<R> &M, Arena<R> &A, bool policy) {
   const B200Model &m = M.m;
   const int nv = m.nv, site = m.ee_site, body = IF(site_bodyid)[site];
   const int *vi = IF(osc_dofadr), *qi = IF(osc_qposadr), *ids = IF(osc_actuator);
@@ -1293,8 +1312,8 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
     if (l4 == 0 && ax < 6) A.ee_vel[ax] = v;
   }
   // gathers: arm mass block, 6x7 Jacobian (and its transpose)
-  for (int z = lane; z < 49; z += T) S[osc::kM + z] = (double)mass_at(M, A.M, vi[z / 7], vi[z % 7]);
-  for (int z = lane; z < 42; z += T) {
+  for (int z = lane; z < 49; z += G) S[osc::kM + z] = (double)mass_at(M, A.M, vi[z / 7], vi[z % 7]);
+  for (int z = lane; z < 42; z += G) {
     const int ax = z / 7, d = vi[z % 7];
     double jv = 0;
     if (dof_ancestor(M, body, d)) {
@@ -1307,7 +1326,7 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
     }
     S[osc::kJ + z] = jv;
   }
-  SYNC();
+  group_sync<T, G>();
   int *err = &A.iscal[6];
   if (*err) return;  // block-uniform
   // M^-1 J^T, A = J M^-1 J^T and the task-space inverses.  A is symmetric
@@ -1410,9 +1429,9 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
       if (lane == 0 && !(ok_flags[0] && ok_flags[1] && ok_flags[2])) *err = 4;
     }
   }
-  SYNC();
+  group_sync<T, G>();
   if (*err) return;
-  for (int z = lane; z < 42; z += T) {  // Jbar = MJT Lf (7x6)
+  for (int z = lane; z < 42; z += G) {  // Jbar = MJT Lf (7x6)
     const int r = z / 6, c = z % 6;
     double v = 0;
     for (int k = 0; k < 6; ++k) v += S[osc::kMJT + r * 6 + k] * S[osc::kLf + k * 6 + c];
@@ -1441,8 +1460,8 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
       }
     }
   }
-  SYNC();
-  for (int z = lane; z < 49; z += T) {  // N = I - Jbar J (7x7)
+  group_sync<T, G>();
+  for (int z = lane; z < 49; z += G) {  // N = I - Jbar J (7x7)
     const int r = z / 7, c = z % 7;
     double v = 0;
     for (int k = 0; k < 6; ++k) v += S[osc::kJbar + r * 6 + k] * S[osc::kJ + k * 7 + c];
@@ -1459,8 +1478,8 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
   }
   if (lane < 7)
     pd[lane] = (double)nul[0] * ((double)q0[lane] - (double)A.qpos[qi[lane]]) - (double)nul[1] * (double)A.qvel[vi[lane]];
-  SYNC();
-  FOR(z, 13) {
+  group_sync<T, G>();
+  for (int z = lane; z < 13; z += G) {
     double v = 0;
     if (z < 6) {
       if (m.osc_uncouple) {
@@ -1476,7 +1495,7 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
       opm[r] = v;
     }
   }
-  SYNC();
+  group_sync<T, G>();
   if (lane < 7) {
     const int i = lane;
     double task = 0, post = 0;
@@ -1487,9 +1506,9 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
     const double lim = t != t ? t : fmin((double)rg[1], fmax((double)rg[0], t));
     A.ctrl[ids[i]] = (R)lim;
   }
-  FOR(i, 3) A.goal_pos[i] = (R)gp[i];
-  FOR(i, 9) A.goal_rot[i] = (R)gr[i];
-  if (lane == T - 1) {
+  for (int i = lane; i < 3; i += G) A.goal_pos[i] = (R)gp[i];
+  for (int i = lane; i < 9; i += G) A.goal_rot[i] = (R)gr[i];
+  if (lane == G - 1) {
     const R a6 = A.action[6];
     const R sgn = a6 != a6 ? a6 : (a6 > R(0) ? R(1) : (a6 < R(0) ? R(-1) : R(0)));
     const R speed = RF(osc_action_config)[24];
@@ -1501,7 +1520,7 @@ template <class R, int T> __device__ void osc_control(const Mdl<R> &M, Arena<R> 
       A.ctrl[ids[7 + i]] = (rg[1] + rg[0]) * R(0.5) + (rg[1] - rg[0]) * R(0.5) * v;
     }
   }
-  SYNC();
+  group_sync<T, G>();
 }
 
 // ============================================================ actuation
@@ -2275,13 +2294,31 @@ template <class R, int T> __device__ void mass_factor(const Mdl<R> &M, Arena<R> 
   SYNC();
 }
 
-template <class R, bool CONVEX, int T> __device__ void step1_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
+// Position and velocity stages (reference Physics.step1, physics.py:161-186).
+// RNE (velocity) runs before collision: the two touch disjoint data, and the
+// control step then overlaps the FP64 OSC, which needs RNE's bias forces, with
+// collision.
+template <class R, int T> __device__ void position_velocity_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
   STAGE((kinematics<R, T>(M, A)), 1);
   STAGE((com_crb_mass<R, T>(M, A)), 2);
   STAGE((mass_factor<R, T>(M, A)), 3);
-  STAGE((collision<R, T, CONVEX>(M, A)), 4);
-  STAGE((constraints<R, T>(M, A)), 5);
   STAGE((velocity<R, T>(M, A)), 6);
+}
+
+// Collision and the FP64 OSC.  A world of several warps runs the OSC on its
+// first warp while its other warps run the broadphase and narrowphase (the
+// collision lists then start after the OSC's scratch in the union region); a
+// one-warp world runs them one after the other.
+template <class R, int T, bool CONVEX> __device__ void collide_and_control(const Mdl<R> &M, Arena<R> &A, bool policy) {
+  if constexpr (T >= 64) {
+    if (TID < 32) osc_control<R, T, 32>(M, A, policy);
+    else collision<R, T, CONVEX, 32, T - 32>(M, A, Arena<R>::kOscDoubles * (int)sizeof(double));
+    SYNC();
+  } else {
+    collision<R, T, CONVEX, 0, T>(M, A, 0);
+    mark<T>(A, 4);
+    osc_control<R, T, T>(M, A, policy);
+  }
 }
 
 template <class R, int T> __device__ void newton_stages(const Mdl<R> &M, Arena<R> &A, bool act) {
@@ -2298,8 +2335,14 @@ __global__ void __launch_bounds__(384, 1) control_step(const __grid_constant__ B
                                                      int substeps, int policy, int wpc, int arena) {
   static_assert(T % 32 == 0 && T / 32 <= Arena<R>::kColbufWarps, "per-warp scratch covers at most four warps");
   extern __shared__ __align__(16) unsigned char smem[];
-  const int slot = threadIdx.x / T, w = blockIdx.x * wpc + slot;
-  const bool in = slot < wpc && w < d.nworld;
+  const int slot = threadIdx.x / T, i = blockIdx.x * wpc + slot;
+  const bool in = slot < wpc && i < d.nworld;
+  // the world of this slot: d.order[i] when a grouping is given (a permutation)
+  int w = i;
+  if (in && d.order) {
+    const int o = d.order[i];
+    w = o >= 0 && o < d.nworld ? o : i;
+  }
   bool act = in;  // the world steps; false once its state went bad (B200_STATUS_BADSTATE)
   // the world's arena descriptor heads its shared-memory region (one copy per
   // world, read by broadcast instead of a per-thread local-memory copy)
@@ -2318,12 +2361,13 @@ __global__ void __launch_bounds__(384, 1) control_step(const __grid_constant__ B
     SYNC();
   }
   __syncthreads();
-  int stepped = 0;
+  int stepped = 0, work = 0;  // work: kept by the world's thread 0
   for (int s = 0; s < substeps; ++s) {
     // world-uniform: the status word is read after a CTA barrier
     if (act && (A.iscal[3] & B200_STATUS_BADSTATE)) act = false;
-    step1_stages<R, CONVEX, T>(M, A, act);
-    STAGE((osc_control<R, T>(M, A, policy && s == 0)), 7);
+    position_velocity_stages<R, T>(M, A, act);
+    STAGE((collide_and_control<R, T, CONVEX>(M, A, policy && s == 0)), 7);
+    STAGE((constraints<R, T>(M, A)), 5);
     STAGE((actuation<R, T>(M, A)), 8);
     newton_stages<R, T>(M, A, act);
     if (act && TID == 0) {
@@ -2341,6 +2385,7 @@ __global__ void __launch_bounds__(384, 1) control_step(const __grid_constant__ B
       A.iscal[24] = 0;
       if (s < 32 && d.niter_trace) irow_of(d.niter_trace, w, 32)[s] = it;
       if (s < 32 && d.ls_trace) irow_of(d.ls_trace, w, 32)[s] = evals;
+      work += (it + 1) * (nefc + 32) + 4 * A.iscal[0];
     }
     if (act && s == substeps - 1) store_outputs<R, T>(m, d, A, w);
     STAGE((euler<R, T>(M, A)), 14);
@@ -2350,6 +2395,7 @@ __global__ void __launch_bounds__(384, 1) control_step(const __grid_constant__ B
   if (TID == 0) {
     if (d.ls_total) irow_of(d.ls_total, w, 1)[0] += A.iscal[7];
     if (d.integration_count) irow_of(d.integration_count, w, 1)[0] += stepped;
+    if (d.work) irow_of(d.work, w, 1)[0] = work;
   }
   store_state<R, T>(m, d, A, w, stepped > 0);
   if (TID == 0 && d.stage_cycles) {
@@ -2371,7 +2417,9 @@ __global__ void __launch_bounds__(384, 1) forward_step(const __grid_constant__ B
   const Mdl<R> M(m);
   if (act) load_world<R, T>(m, d, A, w);
   __syncthreads();
-  step1_stages<R, CONVEX, T>(M, A, act);
+  position_velocity_stages<R, T>(M, A, act);
+  STAGE((collision<R, T, CONVEX, 0, T>(M, A, 0)), 4);
+  STAGE((constraints<R, T>(M, A)), 5);
   if (act && bootstrap) {
     FOR(i, 3) A.goal_pos[i] = A.sxpos[3 * m.ee_site + i];
     FOR(i, 9) A.goal_rot[i] = A.sxmat[9 * m.ee_site + i];

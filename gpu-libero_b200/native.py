@@ -166,6 +166,8 @@ class Library:
         lib.b200phys_step_launch.restype = ct.c_int
         lib.b200phys_step_launch.argtypes = [ct.POINTER(B200Model), ct.POINTER(B200Data), ct.c_int, ct.c_int,
                                              ct.c_void_p]
+        lib.b200phys_order_launch.restype = ct.c_int
+        lib.b200phys_order_launch.argtypes = [ct.POINTER(B200Model), ct.POINTER(B200Data), ct.c_void_p]
         lib.b200phys_forward_launch.restype = ct.c_int
         lib.b200phys_forward_launch.argtypes = [ct.POINTER(B200Model), ct.POINTER(B200Data), ct.c_int,
                                                 ct.c_void_p, ct.c_void_p]
@@ -197,6 +199,11 @@ class Library:
         if rc:
             raise RuntimeError('b200phys_step_launch failed: CUDA error %d' % rc)
 
+    def order(self, model, data, stream):
+        rc = self.lib.b200phys_order_launch(ct.byref(model), ct.byref(data), ct.c_void_p(stream))
+        if rc:
+            raise RuntimeError('b200phys_order_launch failed: CUDA error %d' % rc)
+
     def forward(self, model, data, bootstrap, mask_ptr, stream):
         rc = self.lib.b200phys_forward_launch(ct.byref(model), ct.byref(data), int(bootstrap),
                                               ct.c_void_p(mask_ptr or 0), ct.c_void_p(stream))
@@ -205,7 +212,8 @@ class Library:
 
 
 EXPORTS = ('b200phys_source_id', 'b200phys_arch', 'b200phys_model_bytes', 'b200phys_data_bytes',
-           'b200phys_world_smem_bytes', 'b200phys_prepare', 'b200phys_step_launch', 'b200phys_forward_launch')
+           'b200phys_world_smem_bytes', 'b200phys_prepare', 'b200phys_step_launch', 'b200phys_forward_launch',
+           'b200phys_order_launch')
 
 
 def alloc_numpy(packed, nworld):

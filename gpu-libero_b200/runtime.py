@@ -41,7 +41,7 @@ class Runtime:
     """Owned device buffers plus the control-step graph of one world shard."""
 
     def __init__(self, scene, num_envs, *, device='cuda:0', precision='fp32', world_offset=0, library=None,
-                 debug=False):
+                 debug=False, regroup=True):
         if not torch.cuda.is_available():
             raise RuntimeError('the b200 physics engine requires a CUDA device')
         self.device = torch.device(device)
@@ -64,6 +64,10 @@ class Runtime:
             self.buffers.update({k: torch.zeros((self.n, w), dtype=torch.int32, device=self.device)
                                  for k, w in ints.items() if keep(k)})
             self.mask = torch.ones(self.n, dtype=torch.int32, device=self.device)
+            # worlds-to-CTA grouping of the step kernel: the identity, then (with
+            # `regroup`) the worlds sorted by their last control step's work
+            self.buffers['order'][:, 0] = torch.arange(self.n, dtype=torch.int32, device=self.device)
+        self.regroup = bool(regroup)
         self.data = native.data_struct(self.buffers, self.n, self.world_offset, pointer=lambda t: t.data_ptr())
         smem = self.lib.smem_bytes(self.model)
         if smem == 0:
@@ -85,19 +89,26 @@ class Runtime:
         self.lib.step(self.model, self.data, self.substeps if substeps is None else substeps, int(policy),
                       self._stream())
 
+    def _control_step(self, stream):
+        """One control step: the step kernel, then the regrouping of worlds by work."""
+        self.lib.step(self.model, self.data, self.substeps, 1, stream)
+        if self.regroup:
+            self.lib.order(self.model, self.data, stream)
+
     def forward(self, bootstrap=False, mask=None):
         ptr = mask.data_ptr() if mask is not None else 0
         self.lib.forward(self.model, self.data, int(bootstrap), ptr, self._stream())
 
     def prepare_control_graph(self):
-        """Capture one control step (all substeps, one kernel) in a CUDA graph."""
+        """Capture one control step (all substeps in one kernel, then the
+        regrouping of worlds) in a CUDA graph."""
         if self._graph is None:
             stream = torch.cuda.Stream(self.device)
             stream.wait_stream(torch.cuda.current_stream(self.device))
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.stream(stream):
                 with torch.cuda.graph(graph, stream=stream):
-                    self.lib.step(self.model, self.data, self.substeps, 1, stream.cuda_stream)
+                    self._control_step(stream.cuda_stream)
             torch.cuda.current_stream(self.device).wait_stream(stream)
             self._graph = graph
         return self
@@ -112,7 +123,7 @@ class Runtime:
         if self._graph is not None:
             self._graph.replay()
         else:
-            self.launch_step(policy=True)
+            self._control_step(self._stream())
 
     def pinned_io(self):
         """Pinned host staging for actions (in) and the observation slab plus
@@ -140,7 +151,7 @@ class Runtime:
         if self._graph is not None:
             self._graph.replay()
         else:
-            self.launch_step(policy=True)
+            self._control_step(self._stream())
         torch.stack([self.buffers['overflow'][:, 0], self.buffers['error'][:, 0],
                      self.buffers['integration_count'][:, 0]], out=self._status)
         io['obs'].copy_(self.buffers['obs'], non_blocking=True)

@@ -147,6 +147,17 @@ int b200phys_step_launch(const B200Model *m, const B200Data *d, int substeps,
 int b200phys_forward_launch(const B200Model *m, const B200Data *d,
                             int bootstrap, const int *mask, void *stream);
 
+/* Regroup the worlds for the next control step: fill d->order with the worlds
+ * sorted by d->work (their solver work in the last control step, written by
+ * b200phys_step_launch), so that the worlds sharing a CTA, which advance
+ * through the stages in lockstep, have similar work and wait less for each
+ * other.  World results do not depend on the grouping.  One small kernel;
+ * graph-capturable; allocates nothing.  This is the reference's world-to-CTA
+ * mapping made adaptive (the reference launches one CTA per world,
+ * cuda_fp32/fused_*.cu); it has no counterpart call in the reference.
+ * Returns a cudaError_t value (cudaErrorInvalidValue without work or order). */
+int b200phys_order_launch(const B200Model *m, const B200Data *d, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

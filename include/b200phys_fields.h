@@ -23,6 +23,12 @@
  * line-search counts niter_trace / ls_trace of the last control step, first
  * 32 substeps) are allocated by the host only when it asks for them.
  *
+ * work / order: `work` is each world's solver work in its last control step
+ * (sum over substeps of (Newton iterations + 1) x (rows + 32) + 4 contacts);
+ * `order`, when given, is the permutation that assigns worlds to the step
+ * kernel's CTA slots (slot i runs world order[i]).  b200phys_order_launch
+ * refills it from `work`, so that worlds of similar work share a CTA.
+ *
  * task_body / task_lift_z: the synthetic scenes' task predicate.  Success is
  * the free body free_bodyid[task_body] (its centre of mass frame origin) above
  * task_lift_z; reward = 1 and done = 1 on success, else 0 (LIBERO's sparse
@@ -104,6 +110,7 @@
   X(error, 1) X(niter, 1) X(newton_total, 1) X(ls_total, 1) \
   X(integration_count, 1) X(efc_total, 1) X(con_total, 1) \
   X(newton_rows, 1) X(ls_rows, 1) X(efc_k, 1) X(efc_k2, 1) X(fact_blk, 1) \
-  X(stage_cycles, 16) X(efc_type, nefc_max) X(efc_id, nefc_max) X(niter_trace, 32) X(ls_trace, 32)
+  X(stage_cycles, 16) X(efc_type, nefc_max) X(efc_id, nefc_max) X(niter_trace, 32) X(ls_trace, 32) \
+  X(work, 1) X(order, 1)
 
 #endif

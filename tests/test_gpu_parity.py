@@ -290,3 +290,36 @@ def test_hundred_control_steps_track_the_oracle(scene, oracle_module, precision,
     gpu = {k: t.cpu().numpy() for k, t in rt.buffers.items()}
     assert np.all(gpu['integration_count'] == 2500)
     assert not np.any(gpu['overflow'] & ~0x600) and not np.any(gpu['error'])
+
+
+def test_regrouping_worlds_changes_no_result():
+    """The step kernel runs the worlds in the CTA grouping of data.order, which
+    b200phys_order_launch refills from each world's work; a world's
+    trajectory is bit-identical whatever worlds share its CTA."""
+    from gpu_libero_b200.runtime import Runtime
+    b = scenes.scene_b()
+    n = 96
+    q, v = b.initial_state(n, seed=17)
+    outs = []
+    for regroup in (True, False):
+        rt = Runtime(b, n, regroup=regroup)
+        rt.set_state(np.concatenate([np.zeros((n, 1)), q, v], axis=1))
+        rt.prepare_control_graph()
+        for k in range(4):
+            rt.enqueue_action(b.actions(n, k, seed=17))
+        torch.cuda.synchronize()
+        order = rt.buffers['order'][:, 0].cpu().numpy()
+        work = rt.buffers['work'][:, 0].cpu().numpy()
+        if regroup:
+            assert sorted(order.tolist()) == list(range(n))   # a permutation
+            top = max(int(work.max()), 1)  # the kernel's 256 buckets, heaviest first
+            bucket = 255 - (np.minimum(np.maximum(work, 0), top).astype(np.int64) * 255 // top)
+            assert np.all(np.diff(bucket[order]) >= 0)
+            assert not np.array_equal(order, np.arange(n))
+        else:
+            assert np.array_equal(order, np.arange(n))
+        assert np.all(work > 0)
+        outs.append({k: rt.buffers[k].cpu().numpy().copy() for k in ('qpos', 'qvel', 'obs', 'ncon', 'niter')})
+        rt.close()
+    for k in outs[0]:
+        assert np.array_equal(outs[0][k], outs[1][k]), k
