@@ -121,17 +121,18 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU path
-def cpu_run(scene, worlds, steps, warmup, seed, threads):
-    """The reference's CPU path restated (C oracle port), threads over worlds."""
+def cpu_run(scene, worlds, steps, warmup, seed, threads, precision='fp64'):
+    """The reference's CPU path restated (C oracle port), threads over worlds.
+    FP64 by default: the reference's own CPU path is FP64 CPU MuJoCo."""
     from gpu_libero_b200 import native
     Oracle = entry.load_oracle().Oracle
-    packed = native.PackedModel(scene, 'fp32')
+    packed = native.PackedModel(scene, precision)
     host = native.alloc_numpy(packed, worlds)
     q, v = scene.initial_state(worlds, seed=seed)
     host['qpos'][:] = q
     host['qvel'][:] = v
     ms, ds = packed.host_struct(), native.data_struct(host, worlds)
-    orc = Oracle('fp32')
+    orc = Oracle(precision)
     orc.forward(ms, ds, 0, worlds, 1)
     times = []
     for k in range(warmup + steps):
@@ -150,15 +151,40 @@ def host_threads():
         return os.cpu_count() or 1
 
 
+def physical_cores():
+    """Physical cores of the host (hardware threads share a core), or None."""
+    try:
+        import psutil
+        return psutil.cpu_count(logical=False)
+    except ImportError:
+        pass
+    try:
+        cores, phys, core = set(), None, None
+        for line in Path('/proc/cpuinfo').read_text().splitlines():
+            if line.startswith('physical id'):
+                phys = line.split(':')[1].strip()
+            elif line.startswith('core id'):
+                core = line.split(':')[1].strip()
+                cores.add((phys, core))
+        return len(cores) or None
+    except OSError:
+        return None
+
+
+CPU_NOTE = ('the reference CPU path, CPU MuJoCo 2.3.7 FP64, is not installed here, so the FP64 C restatement '
+            'of the reference substep (oracle/) runs instead, one world per host thread at a time')
+
+
 def cpu_baseline(scene, seed, budget_s=12.0):
     threads = host_threads()
     worlds = 4 * threads
     probe = cpu_run(scene, worlds, 1, 0, seed, threads)
     steps = int(max(1, min(40, budget_s / max(probe, 1e-3))))
     secs = cpu_run(scene, worlds, steps, 0, seed, threads)
-    return dict(value=worlds * steps / secs, unit=UNIT, cores=threads, kind='port',
-                sample='%d worlds x %d control steps (25 substeps) of %s, FP32 C restatement on %d host threads'
-                       % (worlds, steps, scene.name, threads))
+    return dict(value=worlds * steps / secs, unit=UNIT, cores=threads, physical_cores=physical_cores(), kind='port',
+                precision='f64',
+                sample='%d worlds x %d control steps (25 substeps) of %s on %d host threads; %s'
+                       % (worlds, steps, scene.name, threads, CPU_NOTE))
 
 
 def reference_arm(args, scene):
@@ -169,15 +195,17 @@ def reference_arm(args, scene):
     worlds = 4 * threads
     secs = cpu_run(scene, worlds, args.steps, args.warmup, args.seed, threads)
     value = worlds * args.steps / secs
+    sample = '%d worlds per control step on %d host threads (%s physical cores); %s' % (
+        worlds, threads, physical_cores(), CPU_NOTE)
     line = dict(metric=METRIC, value=value, unit=UNIT, impl='reference', n_gpus=args.gpus, steps=args.steps,
                 warmup=args.warmup, ms_per_step=1e3 * secs / args.steps, higher_is_better=True, scaling='weak',
-                vs_baseline=None, dtype='f32', data='synthetic',
-                config=dict(workload=WORKLOADS[scene.name], worlds_per_gpu=args.worlds, substeps=scene.substeps),
+                vs_baseline=None, dtype='f64', data='synthetic (seeded %s states and actions)' % scene.name,
+                # the workload is the GPU arm's; each step of this arm is a bounded host sample of it
+                config=dict(workload=WORKLOADS[scene.name], worlds_per_gpu=args.worlds, substeps=scene.substeps,
+                            host_sample_worlds=worlds, host_threads=threads),
                 substeps_per_sec=value * scene.substeps,
-                cpu_baseline=dict(value=value, unit=UNIT, cores=threads, kind='port',
-                                  sample='%d worlds per step; reference CPU MuJoCo is not installed here, so the '
-                                         'FP32 C restatement of the reference substep runs on %d host threads'
-                                         % (worlds, threads)),
+                cpu_baseline=dict(value=value, unit=UNIT, cores=threads, physical_cores=physical_cores(),
+                                  kind='port', precision='f64', sample=sample),
                 e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
 

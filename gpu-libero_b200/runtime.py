@@ -26,6 +26,10 @@ from .scene import Scene, scene_a
 OVERFLOW_LIMITS = 0x200 | 0x400 | 0x20000
 # inspection outputs that a step never needs: allocated only for debug runtimes
 DEBUG_FIELDS = ('efc_J', 'efc_D', 'efc_aref', 'efc_type', 'efc_id', 'niter_trace', 'ls_trace')
+# scheduling data of a runtime's CTA slots, not world state: copying world rows
+# between runtimes must leave these out (`order` must stay a permutation of
+# the runtime's own worlds)
+SCHEDULE_FIELDS = ('order', 'work')
 
 
 def failure_report(overflow, error, limit=16):

@@ -43,7 +43,7 @@ torch = pytest.importorskip('torch')
 pytestmark = pytest.mark.gpu
 
 from gpu_libero_b200 import native, scene as scenes  # noqa: E402
-from gpu_libero_b200.runtime import Runtime  # noqa: E402
+from gpu_libero_b200.runtime import SCHEDULE_FIELDS, Runtime  # noqa: E402
 
 CONFIGS = {'b32': ('scene_b', 'fp32', 16384), 'b64': ('scene_b', 'fp64', 16384),
            'a32': ('scene_a', 'fp32', 4096), 'a64': ('scene_a', 'fp64', 8192)}
@@ -63,8 +63,9 @@ def rows(rt, idx):
 
 
 def load_rows(rt, src):
+    """World rows into another runtime (its CTA-slot scheduling stays its own)."""
     for k, t in rt.buffers.items():
-        if k in src:
+        if k in src and k not in SCHEDULE_FIELDS:
             t.copy_(torch.as_tensor(src[k]))
 
 
