@@ -35,9 +35,9 @@ UNIT = 'env control steps/s'
 # DRAM read + write bytes per world and control step (FP32), from one ncu
 # capture of control_step per scene (dram__bytes_read.sum + dram__bytes_write.sum
 # of one launch divided by its worlds; per-world state is independent, so the
-# traffic scales with the worlds of a launch): scene A captured at 2368 worlds,
-# scene B at 444 worlds
-TRAFFIC_BYTES_PER_WORLD = {'scene_a': 1032, 'scene_b': 9188}
+# traffic scales with the worlds of a launch): scene A captured at 1184 worlds,
+# scene B at 444 worlds (one wave each), after 25 warm-up control steps
+TRAFFIC_BYTES_PER_WORLD = {'scene_a': 1032, 'scene_b': 11269}
 # control-step stages the kernel stamps with clock64 (data.stage_cycles slots 1..15);
 # in worlds of several warps the FP64 OSC runs on the first warp beside collision
 # on the others, and 'osc_collision' holds that overlapped stage ('collision' is

@@ -11,13 +11,13 @@ oracle in three ways:
 
 1. frozen input, one substep: at 10 checkpoints the oracle and the CUDA kernel
    (a 32-world launch) each take the policy substep from the batch's own state.
-   qvel, ctrl, qfrc_actuator and qfrc_constraint agree within north_star's
-   bound (1e-4 in FP32, 1e-9 in FP64, relative to max(1, |value|)), and so do
-   Newton's qacc and the per-row efc_force in FP64.  In FP32 those two are the
-   Newton iterate itself, which two FP32 implementations reproduce to eps32
-   times the Hessian's conditioning (stiff contacts), not to rounding: they are
-   held to 1e-2, measured 2.2e-3 and 2.8e-4 at most (qvel = qvel + dt qacc
-   stays within 1e-5).  ncon and nefc are equal, and so are the Newton
+   qvel, ctrl and qfrc_actuator agree within north_star's bound (1e-4 in
+   FP32, 1e-9 in FP64, relative to max(1, |value|)), and so do Newton's qacc,
+   the per-row efc_force and qfrc_constraint = J'efc_force in FP64.  In FP32
+   those three are the Newton iterate itself, which two FP32 implementations
+   reproduce to eps32 times the Hessian's conditioning (stiff contacts), not
+   to rounding: they are held to 1e-2, measured 2.3e-3, 2.8e-4 and 1.0e-4 at
+   most (qvel = qvel + dt qacc stays within 1e-5).  ncon and nefc are equal, and so are the Newton
    iteration and line-search evaluation counts (FP64: always; FP32: the line
    search's bracket tests compare slopes at the FP32 tolerance floor, so a
    rounding difference may change its evaluation count in a small fraction of
@@ -132,7 +132,7 @@ def run(request, oracle_module):
 
 def test_frozen_substep(run):
     fp64 = run['precision'] == 'fp64'
-    bounds = {f: 1e-9 if fp64 else (1e-2 if f in ('qacc', 'efc_force') else 1e-4)
+    bounds = {f: 1e-9 if fp64 else (1e-2 if f in ('qacc', 'efc_force', 'qfrc_constraint') else 1e-4)
               for f in FIELDS + ('efc_force',)}
     worst, worst_mis, mismatched, samples, count_diff = {}, 0.0, 0, 0, 0
     for gpu, ref in run['frozen']:
