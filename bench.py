@@ -41,8 +41,10 @@ TRAFFIC_BYTES_PER_WORLD = {'scene_a': 1032, 'scene_b': 11269}
 # control-step stages the kernel stamps with clock64 (data.stage_cycles slots 1..15);
 # in worlds of several warps the FP64 OSC runs on the first warp beside collision
 # on the others, and 'osc_collision' holds that overlapped stage ('collision' is
-# then 0); one-warp worlds run them in turn, 'collision' then 'osc_collision'
-STAGES = ('kinematics', 'com_crb', 'mass_factor', 'collision', 'constraints', 'velocity', 'osc_collision', 'actuation',
+# then 0); likewise the rows' allocation beside actuation ('actuation_constraints',
+# with 'constraints' 0); one-warp worlds run each pair in turn
+STAGES = ('kinematics', 'com_crb', 'mass_factor', 'collision', 'constraints', 'velocity', 'osc_collision',
+          'actuation_constraints',
           'newton_init', 'linesearch', 'gradient', 'hessian', 'direction', 'euler', 'barrier_wait')
 WORKLOADS = {
     'scene_a': 'scene_a: Franka-like arm + gripper + plane + 3 free boxes, elliptic cones, 25 substeps/control step',

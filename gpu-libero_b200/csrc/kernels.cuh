@@ -516,8 +516,10 @@ template <class R> __device__ void solve_blocks(const R *H, const BlockRows &b, 
 
 // L L^T x = x over the kinematic-tree blocks (positions are dofs), factoring
 // first when `factor`; registers and shuffles when each lane owns at most one row
-template <class R, int T> __device__ void tree_solve(const Mdl<R> &M, R *L, R *x, R *colbuf, bool factor) {
-  const BlockRows b = TREE_ROWS(T);
+// (the world's warps [W0, W0 + NW) take the trees; by default all of them)
+template <class R, int T, int W0 = 0, int NW = T / 32>
+__device__ void tree_solve(const Mdl<R> &M, R *L, R *x, R *colbuf, bool factor) {
+  const BlockRows b = owned_rows(M.m.ntree, IF(tree_dofnum), IF(tree_dofadr), IF(tree_padr), LANE, (TID >> 5) - W0, NW);
   const int maxn = M.m.max_tree_dofs;
   if (b.rows <= 32 && maxn <= 16) {
     const int p = b.start[0] + b.a[0];
@@ -824,7 +826,11 @@ template <class R> __device__ void tree_segments(const Mdl<R> &M, Arena<R> &A, i
   __syncwarp();
 }
 
-template <class R, int T> __device__ void constraints(const Mdl<R> &M, Arena<R> &A) {
+template <class R, int T, int G0 = 0, int G = T> __device__ void actuation(const Mdl<R> &M, Arena<R> &A);
+
+// ACT: the world's other warps run the actuation stage while its first warp
+// allocates the rows (worlds of more than one warp)
+template <class R, int T, bool ACT = false> __device__ void constraints(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   const int cap = m.nefc_max, kmax = m.kmax_dof;
   const bool off = m.disable_flags & B200_DSBL_CONSTRAINT;
@@ -917,6 +923,8 @@ template <class R, int T> __device__ void constraints(const Mdl<R> &M, Arena<R> 
     __syncwarp();
     islands(M, A, coupled);
     tree_segments(M, A, A.iscal[13], ncon);
+  } else if constexpr (ACT) {
+    actuation<R, T, 32, T - 32>(M, A);
   }
   SYNC();
   const int nefc = A.iscal[1];
@@ -1524,9 +1532,10 @@ template <class R, int T, int G> __device__ void osc_control(const Mdl<R> &M, Ar
 }
 
 // ============================================================ actuation
-template <class R, int T> __device__ void actuation(const Mdl<R> &M, Arena<R> &A) {
+// The G threads [G0, G0 + G) of the world run it (whole warps).
+template <class R, int T, int G0, int G> __device__ void actuation(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
-  FOR(d, m.nv) {
+  for (int d = TID - G0; d < m.nv; d += G) {
     R f = 0;
     for (int u = 0; u < m.nu; ++u) {
       const int j = IF(actuator_trnid)[u];
@@ -1553,9 +1562,9 @@ template <class R, int T> __device__ void actuation(const Mdl<R> &M, Arena<R> &A
     A.qfrc_smooth[d] = A.qfrc_passive[d] - A.qfrc_bias[d] + f;
     A.qacc_smooth[d] = A.qfrc_smooth[d];
   }
-  SYNC();
-  tree_solve<R, T>(M, A.L, A.qacc_smooth, A.colbuf, false);
-  SYNC();
+  group_sync<T, G>();
+  tree_solve<R, T, G0 / 32, G / 32>(M, A.L, A.qacc_smooth, A.colbuf, false);
+  group_sync<T, G>();
 }
 
 // ============================================================ Newton
@@ -2305,6 +2314,19 @@ template <class R, int T> __device__ void position_velocity_stages(const Mdl<R> 
   STAGE((velocity<R, T>(M, A)), 6);
 }
 
+// Constraint rows and actuation: the two are independent; a world of several
+// warps runs actuation on its other warps while its first warp allocates the
+// rows (then all its threads fill them); a one-warp world runs them in turn.
+template <class R, int T> __device__ void constraints_and_actuation(const Mdl<R> &M, Arena<R> &A) {
+  if constexpr (T >= 64) {
+    constraints<R, T, true>(M, A);
+  } else {
+    constraints<R, T>(M, A);
+    mark<T>(A, 5);
+    actuation<R, T>(M, A);
+  }
+}
+
 // Collision and the FP64 OSC.  A world of several warps runs the OSC on its
 // first warp while its other warps run the broadphase and narrowphase (the
 // collision lists then start after the OSC's scratch in the union region); a
@@ -2367,8 +2389,7 @@ __global__ void __launch_bounds__(384, 1) control_step(const __grid_constant__ B
     if (act && (A.iscal[3] & B200_STATUS_BADSTATE)) act = false;
     position_velocity_stages<R, T>(M, A, act);
     STAGE((collide_and_control<R, T, CONVEX>(M, A, policy && s == 0)), 7);
-    STAGE((constraints<R, T>(M, A)), 5);
-    STAGE((actuation<R, T>(M, A)), 8);
+    STAGE((constraints_and_actuation<R, T>(M, A)), 8);
     newton_stages<R, T>(M, A, act);
     if (act && TID == 0) {
       const int it = A.iscal[4], nefc = A.iscal[1], evals = A.iscal[7] - A.iscal[9];
