@@ -537,7 +537,7 @@ __device__ int prim_sphere_sphere(PrimHits<R> &o, R margin, V3<R> p1, const R *m
   if (len < R(1e-15)) {
     n = cross(col(m1, 2), col(m2, 2));
     len = msqrt(dot(n, n));
-    n = len > R(0) ? n * (R(1) / len) : v3<R>(1, 0, 0);
+    n = len < R(1e-15) ? v3<R>(1, 0, 0) : n * (R(1) / len);  // mju_normalize3: +x below mjMINVAL
   } else
     n = n * (R(1) / len);
   o.dist[c] = dist;

@@ -2243,12 +2243,23 @@ template <class R, int T> __device__ __noinline__ void store_outputs(const B200M
   if ((dst = row_of<R>(d.qfrc_actuator, w, nv))) FOR(i, nv) dst[i] = A.qfrc_actuator[i];
   if ((dst = row_of<R>(d.qfrc_constraint, w, nv))) FOR(i, nv) dst[i] = A.qfrc_constraint[i];
   if ((dst = row_of<R>(d.qacc_smooth, w, nv))) FOR(i, nv) dst[i] = A.qacc_smooth[i];
+  if ((dst = row_of<R>(d.qfrc_smooth, w, nv))) FOR(i, nv) dst[i] = A.qfrc_smooth[i];
+  if ((dst = row_of<R>(d.qM, w, nv * nv))) {
+    const Mdl<R> M(m);
+    FOR(e, nv * nv) {  // the tree blocks expanded to dense dof order
+      const int i = e / nv, j = e % nv, t = IF(dof_treeid)[i], a = IF(tree_dofadr)[t], n = IF(tree_dofnum)[t];
+      dst[e] = IF(dof_treeid)[j] == t ? A.M[IF(tree_madr)[t] + (i - a) * n + (j - a)] : R(0);
+    }
+  }
   const int ncon = A.iscal[0], nefc = A.iscal[1];
   if ((dst = row_of<R>(d.con_dist, w, nc))) FOR(k, ncon) dst[k] = A.con[(size_t)A.con_order[k] * kCWidth + kCDist];
   if ((dst = row_of<R>(d.con_pos, w, nc * 3)))
     FOR(e, ncon * 3) dst[e] = A.con[(size_t)A.con_order[e / 3] * kCWidth + kCPos + e % 3];
   if ((dst = row_of<R>(d.con_frame, w, nc * 9)))
     FOR(e, ncon * 9) dst[e] = A.con[(size_t)A.con_order[e / 9] * kCWidth + kCFrame + e % 9];
+  if ((dst = row_of<R>(d.con_friction, w, nc * 5)))
+    FOR(e, ncon * 5) dst[e] = A.con[(size_t)A.con_order[e / 5] * kCWidth + kCFriction + e % 5];
+  if ((dst = row_of<R>(d.con_margin, w, nc))) FOR(k, ncon) dst[k] = A.con[(size_t)A.con_order[k] * kCWidth + kCMargin];
   if ((dst = row_of<R>(d.efc_force, w, m.nefc_max))) FOR(r, nefc) dst[r] = A.efc_force[r];
   if ((dst = row_of<R>(d.efc_D, w, m.nefc_max))) FOR(r, nefc) dst[r] = A.efc_D[r];
   if ((dst = row_of<R>(d.efc_aref, w, m.nefc_max))) FOR(r, nefc) dst[r] = A.efc_aref[r];
@@ -2270,6 +2281,7 @@ template <class R, int T> __device__ __noinline__ void store_outputs(const B200M
         if (A.con_order[k] == id) { id = k; break; }
     idst[r] = id;
   }
+  if ((idst = irow_of(d.con_dim, w, nc))) FOR(k, ncon) idst[k] = A.con_dim[A.con_order[k]];
   if ((idst = irow_of(d.con_geom, w, nc * 2)))
     FOR(e, ncon * 2) idst[e] = e & 1 ? A.con_g2[A.con_order[e >> 1]] : A.con_g1[A.con_order[e >> 1]];
   if (TID == 0) {
@@ -2451,6 +2463,7 @@ __global__ void __launch_bounds__(384, 1) forward_step(const __grid_constant__ B
   STAGE((actuation<R, T>(M, A)), 8);
   newton_stages<R, T>(M, A, act);
   if (!act) return;
+  if (TID == 0 && d.niter) irow_of(d.niter, w, 1)[0] = A.iscal[4];
   store_outputs<R, T>(m, d, A, w);
   store_state<R, T>(m, d, A, w, true);
 }

@@ -25,7 +25,8 @@ from .scene import Scene, scene_a
 # budget (it ends with its best face, as at its iteration limit)
 OVERFLOW_LIMITS = 0x200 | 0x400 | 0x20000
 # inspection outputs that a step never needs: allocated only for debug runtimes
-DEBUG_FIELDS = ('efc_J', 'efc_D', 'efc_aref', 'efc_type', 'efc_id', 'niter_trace', 'ls_trace')
+DEBUG_FIELDS = ('efc_J', 'efc_D', 'efc_aref', 'efc_type', 'efc_id', 'niter_trace', 'ls_trace', 'qM',
+                'qfrc_smooth', 'con_friction', 'con_margin', 'con_dim')
 # scheduling data of a runtime's CTA slots, not world state: copying world rows
 # between runtimes must leave these out (`order` must stay a permutation of
 # the runtime's own worlds)

@@ -19,9 +19,11 @@
  * the host evaluates it to allocate world-major [nworld, width] buffers.
  * Every output pointer may be NULL (not written).  Inspection outputs that a
  * step never needs (the dense constraint rows efc_J / efc_D / efc_aref /
- * efc_type / efc_id of the last substep, and the per-substep Newton and
- * line-search counts niter_trace / ls_trace of the last control step, first
- * 32 substeps) are allocated by the host only when it asks for them.
+ * efc_type / efc_id of the last substep, its dense mass matrix qM and smooth
+ * force qfrc_smooth, the contacts' friction / margin / dimension, and the
+ * per-substep Newton and line-search counts niter_trace / ls_trace of the
+ * last control step, first 32 substeps) are allocated by the host only when
+ * it asks for them.
  *
  * work / order: `work` is each world's solver work in its last control step
  * (sum over substeps of (Newton iterations + 1) x (rows + 32) + 4 contacts);
@@ -102,7 +104,8 @@
   X(qfrc_actuator, nv) X(qfrc_constraint, nv) X(qacc_smooth, nv) \
   X(con_dist, ncon_max) X(con_pos, ncon_max * 3) X(con_frame, ncon_max * 9) \
   X(efc_force, nefc_max) X(obs, nobs) \
-  X(efc_J, nefc_max * nv) X(efc_D, nefc_max) X(efc_aref, nefc_max)
+  X(efc_J, nefc_max * nv) X(efc_D, nefc_max) X(efc_aref, nefc_max) \
+  X(qM, nv * nv) X(qfrc_smooth, nv) X(con_friction, ncon_max * 5) X(con_margin, ncon_max)
 
 /* world-major int32 data: X(name, per-world width) */
 #define B200_DATA_INT(X) \
@@ -111,6 +114,6 @@
   X(integration_count, 1) X(efc_total, 1) X(con_total, 1) \
   X(newton_rows, 1) X(ls_rows, 1) X(efc_k, 1) X(efc_k2, 1) X(fact_blk, 1) \
   X(stage_cycles, 16) X(efc_type, nefc_max) X(efc_id, nefc_max) X(niter_trace, 32) X(ls_trace, 32) \
-  X(work, 1) X(order, 1)
+  X(work, 1) X(order, 1) X(con_dim, ncon_max)
 
 #endif

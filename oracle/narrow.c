@@ -27,7 +27,8 @@
 typedef struct { int count; real dist[2]; V3 pos[2], normal[2]; } PrimOut;
 
 /* MuJoCo _SphereSphere: depth along the centre line; coincident centres use
- * the cross product of the two z axes, then +x */
+ * the cross product of the two z axes, then +x when that is shorter than
+ * mjMINVAL (mju_normalize3's rule; collision_detect_primitive.cuh:276-283) */
 static int prim_sphere_sphere(PrimOut *o, real margin, V3 p1, const real *m1, real r1, V3 p2, const real *m2, real r2) {
   V3 dif = vsub(p1, p2);
   real cd2 = vdot(dif, dif), mind = margin + r1 + r2;
@@ -39,7 +40,7 @@ static int prim_sphere_sphere(PrimOut *o, real margin, V3 p1, const real *m1, re
   if (len < R(1e-15)) {
     n = vcross(mcol(m1, 2), mcol(m2, 2));
     len = rsqrt_(vdot(n, n));
-    n = len > 0 ? vscale(n, R(1) / len) : v3(1, 0, 0);
+    n = len < R(1e-15) ? v3(1, 0, 0) : vscale(n, R(1) / len);
   } else
     n = vscale(n, R(1) / len);
   o->dist[c] = dist;

@@ -1755,7 +1755,13 @@ static void publish_outputs(const B200Model *m, const B200Data *d, Work *k, int 
   if ((p = DR(qfrc_actuator, w, nv))) memcpy(p, k->qfrc_actuator, sizeof(real) * nv);
   if ((p = DR(qfrc_constraint, w, nv))) memcpy(p, k->qfrc_constraint, sizeof(real) * nv);
   if ((p = DR(qacc_smooth, w, nv))) memcpy(p, k->qacc_smooth, sizeof(real) * nv);
+  if ((p = DR(qfrc_smooth, w, nv))) memcpy(p, k->qfrc_smooth, sizeof(real) * nv);
+  if ((p = DR(qM, w, nv * nv)))
+    for (int i = 0; i < nv; ++i)
+      for (int j = 0; j < nv; ++j) p[i * nv + j] = mass_at(m, k->M, i, j);
   int nc = m->ncon_max, ne = m->nefc_max;
+  if ((p = DR(con_friction, w, nc * 5))) for (int c = 0; c < k->ncon; ++c) memcpy(p + 5 * c, k->con[c].friction, sizeof(real) * 5);
+  if ((p = DR(con_margin, w, nc))) for (int c = 0; c < k->ncon; ++c) p[c] = k->con[c].margin;
   if ((p = DR(con_dist, w, nc))) for (int c = 0; c < k->ncon; ++c) p[c] = k->con[c].dist;
   if ((p = DR(con_pos, w, nc * 3))) for (int c = 0; c < k->ncon; ++c) memcpy(p + 3 * c, k->con[c].pos, sizeof(real) * 3);
   if ((p = DR(con_frame, w, nc * 9))) for (int c = 0; c < k->ncon; ++c) memcpy(p + 9 * c, k->con[c].frame, sizeof(real) * 9);
@@ -1769,6 +1775,7 @@ static void publish_outputs(const B200Model *m, const B200Data *d, Work *k, int 
   if ((ip = DI(ncon, w, 1))) *ip = k->ncon;
   if ((ip = DI(nefc, w, 1))) *ip = k->nefc;
   if ((ip = DI(con_geom, w, nc * 2))) for (int c = 0; c < k->ncon; ++c) { ip[2 * c] = k->con[c].g1; ip[2 * c + 1] = k->con[c].g2; }
+  if ((ip = DI(con_dim, w, nc))) for (int c = 0; c < k->ncon; ++c) ip[c] = k->con[c].dim;
 }
 
 /* observation slab: arm+gripper qpos/qvel (current), end-effector pose and
@@ -1899,6 +1906,7 @@ int oracle_forward(const B200Model *m, const B200Data *d, int w0, int w1, int bo
     publish_obs(m, d, k, w, qpos, qvel);
     real *qa = DR(qacc, w, nv);
     if (qa) memcpy(qa, k->qacc, sizeof(real) * nv);
+    if (d->niter) *DI(niter, w, 1) = k->niter;
     k->ls_evals = 0;
   }
   free(k);

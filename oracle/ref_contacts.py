@@ -9,6 +9,12 @@ where the reference checkout exists and travels prebuilt; where it is absent,
 `collide(scene, xpos, xmat)` runs the reference's collision sequence
 (cuda_fp32/physics.py:95-100: broadphase, convex, planes, boxes) on given geom
 poses and returns its pooled contact list.
+
+The same target builds oracle/_ref/libref_native_{f64,f32}.so from
+ref_native.cu: the reference's native MuJoCo 2.3.7 sphere-sphere,
+sphere-capsule and capsule-capsule colliders (collision_detect_primitive.cuh)
+with its real_t as double and as float, for the families its FP32 engine
+lacks.  `RefNative.collide` runs them on given poses.
 """
 import ctypes as ct
 import os
@@ -19,6 +25,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 LIB = HERE / '_ref' / 'libref_contacts.so'
+NATIVE_LIBS = {'fp64': HERE / '_ref' / 'libref_native_f64.so', 'fp32': HERE / '_ref' / 'libref_native_f32.so'}
 P = ct.c_void_p
 
 
@@ -117,3 +124,47 @@ class RefCollision:
         res = {k: (a[:n] if k != 'overflow' else a) for k, a in arrays.items()}
         res.update(count=out.count, candidates=out.candidates, capacity=cap)
         return res
+
+
+def native_available():
+    return all(p.is_file() for p in NATIVE_LIBS.values())
+
+
+class RefNative:
+    """The reference's native sphere / capsule colliders on given geom poses,
+    with real_t of the given precision ('fp64' or 'fp32')."""
+
+    def __init__(self, precision='fp64'):
+        lib = self.lib = ct.CDLL(str(NATIVE_LIBS[precision]))
+        lib.refn_real_bits.restype = ct.c_int
+        lib.refn_max_hits.restype = ct.c_int
+        lib.refn_collide.restype = ct.c_int
+        lib.refn_collide.argtypes = [ct.c_int] * 3 + [P] * 8
+        self.bits = 64 if precision == 'fp64' else 32
+        if lib.refn_real_bits() != self.bits:
+            raise RuntimeError('%s has real_t of %d bits' % (NATIVE_LIBS[precision].name, lib.refn_real_bits()))
+        self.dtype = np.float64 if self.bits == 64 else np.float32
+        self.max_hits = lib.refn_max_hits()
+
+    def collide(self, scene, xpos, xmat, pairs, margin):
+        """Contacts of `pairs` [P, 2] (each pair's margin in `margin` [P]) for geom
+        poses xpos [W, ngeom*3], xmat [W, ngeom*9].  Returns count [W, P] (-1 for a
+        family these colliders do not cover) and hits [W, P, max_hits, 7]: dist,
+        pos[3], normal[3], in the library's precision."""
+        ng = scene.sizes['ngeom']
+        f = self.dtype
+        xp = np.ascontiguousarray(xpos, f).reshape(-1, ng * 3)
+        xm = np.ascontiguousarray(xmat, f).reshape(-1, ng * 9)
+        W = xp.shape[0]
+        types = np.ascontiguousarray(scene.ints['geom_type'], np.int32)
+        size = np.ascontiguousarray(scene.reals['geom_size'], f)
+        pr = np.ascontiguousarray(pairs, np.int32).reshape(-1, 2)
+        mg = np.ascontiguousarray(margin, f).reshape(-1)
+        count = np.zeros((W, len(pr)), np.int32)
+        hits = np.zeros((W, len(pr), self.max_hits, 7), f)
+        rc = self.lib.refn_collide(W, ng, len(pr), types.ctypes.data, size.ctypes.data, xp.ctypes.data,
+                                   xm.ctypes.data, pr.ctypes.data, mg.ctypes.data, count.ctypes.data,
+                                   hits.ctypes.data)
+        if rc:
+            raise RuntimeError('reference native colliders: CUDA error %d' % rc)
+        return count, hits
