@@ -59,6 +59,8 @@ template <class R, bool C> int prepare_rc(const B200Model *m, const Shape &sh) {
   const size_t smem = (size_t)sh.wpc * arena_for(m);
   return sh.T == 32 ? b200::configure_kernels<R, C, 32>(smem) : b200::configure_kernels<R, C, 128>(smem);
 }
+// the kernel variant with GJK / EPA: meshes, or box-box pairs on the convex path
+bool uses_convex(const B200Model *m) { return m->nmesh > 0 || m->boxbox_convex; }
 int launch_shape(const B200Model *m, Shape *sh) {
   const int limit = max_optin_smem();
   sh->wpc = worlds_per_cta(m, limit);
@@ -67,13 +69,13 @@ int launch_shape(const B200Model *m, Shape *sh) {
   const int per_sm = ((228 * 1024) / (sh->wpc * arena + 1024)) * sh->wpc;
   sh->T = per_sm <= 3 ? 128 : 32;
   if (sh->T * sh->wpc > 384) sh->wpc = 384 / sh->T;  // the kernels' launch bound
-  const bool convex = m->nmesh > 0;
+  const bool convex = uses_convex(m);
   if (m->real_bytes == 4) return convex ? prepare_rc<float, true>(m, *sh) : prepare_rc<float, false>(m, *sh);
   return convex ? prepare_rc<double, true>(m, *sh) : prepare_rc<double, false>(m, *sh);
 }
 // kernel instance by precision, mesh support and threads per world
 template <template <class, bool, int> class F, class... A> void dispatch(const B200Model *m, const Shape &sh, A... a) {
-  const bool c = m->nmesh > 0, t = sh.T == 128;
+  const bool c = uses_convex(m), t = sh.T == 128;
   if (m->real_bytes == 4) {
     if (c) t ? F<float, true, 128>::run(a...) : F<float, true, 32>::run(a...);
     else t ? F<float, false, 128>::run(a...) : F<float, false, 32>::run(a...);

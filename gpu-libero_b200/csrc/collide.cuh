@@ -1,5 +1,6 @@
-// Portions (sphere_box, capsule_box, box_box, clip_poly) restate MuJoCo Warp's
-// primitive contact geometry: Copyright 2025 The Newton Developers,
+// Portions (sphere_box, capsule_box, box_box, clip_poly, and the box manifold
+// box_manifold / clip_faces / largest_quad) restate MuJoCo Warp's contact
+// geometry: Copyright 2025 The Newton Developers,
 // SPDX-License-Identifier: Apache-2.0 (see NOTICE).
 // Per-pair collision for one world: broadphase filters and primitive
 // narrowphase.  One thread owns one candidate pair; contacts are appended to
@@ -673,7 +674,12 @@ template <class R> struct CShape {
   R margin;
 };
 
-template <class R> __device__ V3<R> cs_support(const CShape<R> &s, V3<R> d) {
+// The support point of a shape in direction d.  For a box, *corner receives
+// the support corner's index: bit k set for +size on local axis k (a zero
+// component takes the negative end), the labelling the box manifold reads
+// features from (mjwarp_convex_geometry.cuh convex_support); -1 otherwise.
+template <class R> __device__ V3<R> cs_support(const CShape<R> &s, V3<R> d, int *corner = nullptr) {
+  if (corner) *corner = -1;
   if (s.type == B200_GEOM_SPHERE) return s.pos + d * (s.size.x + R(0.5) * s.margin);
   const V3<R> l = rotT(s.rot, d);
   V3<R> r;
@@ -682,6 +688,7 @@ template <class R> __device__ V3<R> cs_support(const CShape<R> &s, V3<R> d) {
     r.z += (l.z > R(0) ? R(1) : l.z < R(0) ? R(-1) : R(0)) * s.size.y;
   } else if (s.type == B200_GEOM_BOX) {
     r = v3<R>(l.x > R(0) ? s.size.x : -s.size.x, l.y > R(0) ? s.size.y : -s.size.y, l.z > R(0) ? s.size.z : -s.size.z);
+    if (corner) *corner = int(l.x > R(0)) | int(l.y > R(0)) << 1 | int(l.z > R(0)) << 2;
   } else {
     int best = 0;
     R top = dot(ld3(s.vert), l);
@@ -699,7 +706,7 @@ template <class R> __device__ V3<R> cs_support(const CShape<R> &s, V3<R> d) {
 template <class R> struct Simplex {
   V3<R> w[4], a[4], b[4];
   R lam[4];
-  int n;
+  int n, ca[4], cb[4];  // box support corners of a and b (-1: not a box)
 };
 
 // Signed-volume distance sub-algorithm (Montanari, Petrinic and Barbieri,
@@ -828,7 +835,7 @@ template <class R> __device__ void simplex_reduce(Simplex<R> &s) {
     if (i < s.n && W.w[i] != R(0)) {
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        if (j == k) { t.w[j] = s.w[i]; t.a[j] = s.a[i]; t.b[j] = s.b[i]; t.lam[j] = W.w[i]; }
+        if (j == k) { t.w[j] = s.w[i]; t.a[j] = s.a[i]; t.b[j] = s.b[i]; t.lam[j] = W.w[i]; t.ca[j] = s.ca[i]; t.cb[j] = s.cb[i]; }
       ++k;
     }
   t.n = k;
@@ -852,7 +859,8 @@ template <class R> __device__ GjkOut<R> gjk(const CShape<R> &A, const CShape<R> 
   for (int it = 0; it < iterations; ++it) {
     if (norm < tol || mabs(prev - norm) < R(1e-15)) break;
     const V3<R> d = x * (R(1) / norm);
-    const V3<R> a = cs_support(A, -d), b = cs_support(B, d), w = a - b;
+    int ca, cb;
+    const V3<R> a = cs_support(A, -d, &ca), b = cs_support(B, d, &cb), w = a - b;
     if (dot(x, x - w) < R(0.5) * tol * tol) break;
     const R lower = dot(x, w);
     if (lower > R(0) && (cutoff == R(0) || lower >= cutoff * norm)) {
@@ -862,7 +870,7 @@ template <class R> __device__ GjkOut<R> gjk(const CShape<R> &A, const CShape<R> 
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i)
-      if (i == s.n) { s.w[i] = w; s.a[i] = a; s.b[i] = b; }
+      if (i == s.n) { s.w[i] = w; s.a[i] = a; s.b[i] = b; s.ca[i] = ca; s.cb[i] = cb; }
     s.n++;
     simplex_reduce(s);
     if (s.n < 1) break;
@@ -886,6 +894,7 @@ template <class R> __device__ GjkOut<R> gjk(const CShape<R> &A, const CShape<R> 
 constexpr int kEpaMaxV = 48, kEpaMaxF = 96;
 template <class R> struct Polytope {
   V3<R> w[kEpaMaxV], a[kEpaMaxV], b[kEpaMaxV];
+  int ca[kEpaMaxV], cb[kEpaMaxV];  // box support corners (-1: not a box)
   int nv, nf, face[kEpaMaxF][3];
   V3<R> n[kEpaMaxF];
   R d[kEpaMaxF];
@@ -925,7 +934,7 @@ template <class R> __device__ int epa_add_face(Polytope<R> &P, int i, int j, int
 template <class R> __device__ int epa_push(Polytope<R> &P, const CShape<R> &A, const CShape<R> &B, V3<R> d) {
   if (P.nv >= kEpaMaxV) return -1;
   const int v = P.nv++;
-  P.a[v] = cs_support(A, d); P.b[v] = cs_support(B, -d); P.w[v] = P.a[v] - P.b[v];
+  P.a[v] = cs_support(A, d, &P.ca[v]); P.b[v] = cs_support(B, -d, &P.cb[v]); P.w[v] = P.a[v] - P.b[v];
   return v;
 }
 
@@ -933,7 +942,7 @@ template <class R> __device__ bool epa_seed(Polytope<R> &P, const CShape<R> &A, 
   P.nf = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i)
-    if (i < s.n) { P.w[i] = s.w[i]; P.a[i] = s.a[i]; P.b[i] = s.b[i]; }
+    if (i < s.n) { P.w[i] = s.w[i]; P.a[i] = s.a[i]; P.b[i] = s.b[i]; P.ca[i] = s.ca[i]; P.cb[i] = s.cb[i]; }
   P.nv = s.n;
   for (int k = 0; P.nv < 2 && k < 6; ++k) {
     V3<R> ax = v3<R>(0, 0, 0);
@@ -983,19 +992,29 @@ template <class R> __device__ bool epa_seed(Polytope<R> &P, const CShape<R> &A, 
 // ok: a penetration depth was found; budget: the vertex or face pool filled
 // before EPA converged (it ends with its best face, as at its iteration
 // limit); horizon: the horizon edge list filled (the reference's EPA_HORIZON)
+// face_*: the support points and box corners of the final face's vertices
+// (the box manifold's input)
 template <class R> struct EpaOut {
   bool ok, budget, horizon;
   R depth;
   V3<R> x1, x2;
+  V3<R> face_a[3], face_b[3];
+  int face_ca[3], face_cb[3];
 };
 
+// discrete: two zero-margin boxes (polytopes).  EPA then stops when the
+// support distance is within 1e-7 of the face, or when the new support is a
+// corner pair the polytope already holds, which ends it on a face of the
+// Minkowski difference itself (mjwarp_convex_epa.cuh epa_expand).
 template <class R>
-__device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R> &s, R tol, int iterations) {
+__device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R> &s, R tol, int iterations,
+                         bool discrete = false) {
   EpaOut<R> o;
   o.ok = false;
   o.budget = o.horizon = false;
   Polytope<R> P;
   if (!epa_seed(P, A, B, s)) return o;
+  const R eps = discrete ? R(1e-7) : tol;
   int best = -1;
   for (int it = 0; it <= iterations; ++it) {
     best = -1;
@@ -1006,7 +1025,12 @@ __device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R
     const V3<R> n = P.n[best];
     const int v = epa_push(P, A, B, n);
     if (v < 0) { o.budget = true; break; }
-    if (dot(P.w[v], n) - P.d[best] < tol) { P.nv--; break; }
+    if (dot(P.w[v], n) - P.d[best] < eps) { P.nv--; break; }
+    if (discrete) {
+      bool repeated = false;
+      for (int q = 0; q < v; ++q) repeated |= P.ca[q] == P.ca[v] && P.cb[q] == P.cb[v];
+      if (repeated) { P.nv--; break; }
+    }
     int edges[3 * kEpaMaxF][2], ne = 0;
     for (int f = 0; f < P.nf; ++f) {
       if (!P.alive[f] || dot(P.n[f], P.w[v] - P.w[P.face[f][0]]) <= R(0)) continue;
@@ -1039,8 +1063,278 @@ __device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R
   o.x1 = P.a[i] * lu + P.a[j] * lv + P.a[l] * lw;
   o.x2 = P.b[i] * lu + P.b[j] * lv + P.b[l] * lw;
   o.depth = P.d[best];
+  const int fv[3] = {i, j, l};
+  for (int k = 0; k < 3; ++k) {
+    o.face_a[k] = P.a[fv[k]]; o.face_b[k] = P.b[fv[k]];
+    o.face_ca[k] = P.ca[fv[k]]; o.face_cb[k] = P.cb[fv[k]];
+  }
   o.ok = true;
   return o;
+}
+
+// ---------------------------------------------------------------- box manifold
+// Zero-margin box pairs reach the convex path (the reference routes box-box
+// there when no box pair has a margin, cuda_fp32/physics.py:89-90) and turn
+// EPA's single contact into a face manifold (mjwarp_box_manifold.cuh
+// box_multicontact): the corners of EPA's final face name a feature of each
+// box (a corner, an edge or a face); the features' face normals are paired
+// anti-parallel within 5.1 degrees (or a face normal with an edge
+// perpendicular to it within 5.1 degrees); the incident face (or edge) is
+// clipped against the side planes of the reference face; the clipped points
+// below the reference face are the contacts, at most four (the pair farthest
+// apart for an edge, the largest-area quadrilateral for more than four).
+template <class R> struct BoxManifold {
+  int count;
+  V3<R> one[4], two[4];
+  R dist[4];
+};
+template <class R> struct BoxFeature {
+  int dim, corner[3];
+  V3<R> pt[3];
+};
+template <class R> struct BoxNormals {
+  int count, face[3];
+  V3<R> n[3];
+};
+constexpr float kBoxAligned = 0.99605101346969604f, kBoxPerpendicular = 0.088782943785190582f;
+
+template <class R> __device__ BoxFeature<R> box_feature(const int *corner, const V3<R> *pt) {
+  BoxFeature<R> f;
+  for (int k = 0; k < 3; ++k) { f.corner[k] = corner[k]; f.pt[k] = pt[k]; }
+  if (f.corner[0] != f.corner[1]) {
+    f.dim = (f.corner[2] == f.corner[0] || f.corner[2] == f.corner[1]) ? 2 : 3;
+  } else {
+    f.corner[1] = f.corner[2];
+    f.pt[1] = f.pt[2];
+    f.dim = f.corner[0] != f.corner[2] ? 2 : 1;
+  }
+  return f;
+}
+template <class R> __device__ V3<R> box_axis(const CShape<R> &s, int face) {  // face 2k: +axis k, 2k+1: -axis k
+  V3<R> e = v3<R>(0, 0, 0);
+  e[face / 2] = face % 2 ? R(-1) : R(1);
+  return rot(s.rot, e);
+}
+// the face whose normal is within 5.1 degrees of direction d, if any
+template <class R> __device__ BoxNormals<R> box_normals_near(const CShape<R> &s, V3<R> d) {
+  BoxNormals<R> o;
+  o.count = 0;
+  const V3<R> l = normalize(rotT(s.rot, d));
+  for (int f = 0; f < 6; ++f)
+    if ((f % 2 ? -l[f / 2] : l[f / 2]) > R(kBoxAligned)) {
+      o.count = 1; o.face[0] = f; o.n[0] = box_axis(s, f);
+      return o;
+    }
+  return o;
+}
+// the face normals a feature lies on: the axes on which all its corners agree
+template <class R> __device__ BoxNormals<R> box_normals(const CShape<R> &s, const BoxFeature<R> &f, V3<R> d) {
+  BoxNormals<R> o;
+  o.count = 0;
+  if (f.dim == 1) {
+    o.count = 3;
+    for (int k = 0; k < 3; ++k) {
+      o.face[k] = 2 * k + ((f.corner[0] >> k) & 1 ? 0 : 1);
+      o.n[k] = box_axis(s, o.face[k]);
+    }
+    return o;
+  }
+  for (int k = 0; k < 3; ++k) {
+    bool all = true, none = true;
+    for (int i = 0; i < f.dim; ++i) {
+      const bool set = (f.corner[i] >> k) & 1;
+      all &= set; none &= !set;
+    }
+    if (all || none) {
+      o.face[o.count] = 2 * k + (all ? 0 : 1);
+      o.n[o.count] = box_axis(s, o.face[o.count]);
+      ++o.count;
+    }
+  }
+  if ((f.dim == 3 && o.count == 1) || (f.dim == 2 && o.count >= 1)) return o;
+  return box_normals_near(s, d);
+}
+// the box edges at a feature point: the edge itself for an edge, the three
+// edges leaving a corner; end[k] their far ends
+template <class R> __device__ BoxNormals<R> box_edges(const CShape<R> &s, const BoxFeature<R> &f, V3<R> *end) {
+  BoxNormals<R> o;
+  o.count = 0;
+  if (f.dim == 2) {
+    end[0] = f.pt[1];
+    o.n[0] = normalize(f.pt[1] - f.pt[0]);
+    o.count = 1;
+  } else if (f.dim == 1) {
+    V3<R> c;
+    for (int k = 0; k < 3; ++k) c[k] = (f.corner[0] >> k) & 1 ? s.size[k] : -s.size[k];
+    for (int k = 0; k < 3; ++k) {
+      V3<R> q = c;
+      q[k] = -q[k];
+      end[k] = rot(s.rot, q) + s.pos;
+      o.n[k] = normalize(end[k] - f.pt[0]);
+    }
+    o.count = 3;
+  }
+  return o;
+}
+// the four corners of face `face`, wound as the reference winds them
+template <class R> __device__ void box_face_corners(const CShape<R> &s, int face, V3<R> *v) {
+  constexpr unsigned char kWinding[6][4] = {{7, 3, 1, 5}, {2, 6, 4, 0}, {2, 3, 7, 6}, {4, 5, 1, 0}, {6, 7, 5, 4}, {3, 2, 0, 1}};
+  for (int i = 0; i < 4; ++i) {
+    V3<R> c;
+    for (int k = 0; k < 3; ++k) c[k] = (kWinding[face][i] >> k) & 1 ? s.size[k] : -s.size[k];
+    v[i] = rot(s.rot, c) + s.pos;
+  }
+}
+template <class R> __device__ R quad_area(V3<R> a, V3<R> b, V3<R> c, V3<R> d) {
+  const V3<R> n = cross(a - c, b - d);
+  return R(0.5) * msqrt(dot(n, n));
+}
+// four of n polygon vertices spanning the largest quadrilateral, by the
+// reference's rotating search (each vertex in turn as a, advancing d, then c,
+// then b while the area grows)
+template <class R> __device__ void largest_quad(const V3<R> *p, int n, int *q) {
+  int b = 1, c = 2, d = 3;
+  q[0] = 0; q[1] = b; q[2] = c; q[3] = d;
+  R area = quad_area(p[0], p[b], p[c], p[d]);
+  for (int a = 0; a < n; ++a) {
+    for (;;) {
+      R next = quad_area(p[a], p[b], p[c], p[(d + 1) % n]);
+      if (next <= area) break;
+      area = next; d = (d + 1) % n; q[0] = a; q[1] = b; q[2] = c; q[3] = d;
+      for (;;) {
+        next = quad_area(p[a], p[b], p[(c + 1) % n], p[d]);
+        if (next <= area) break;
+        area = next; c = (c + 1) % n; q[0] = a; q[1] = b; q[2] = c; q[3] = d;
+      }
+      for (;;) {
+        next = quad_area(p[a], p[(b + 1) % n], p[c], p[d]);
+        if (next <= area) break;
+        area = next; b = (b + 1) % n; q[0] = a; q[1] = b; q[2] = c; q[3] = d;
+      }
+    }
+    if (b == a) {
+      b = (b + 1) % n;
+      if (c == b) {
+        c = (c + 1) % n;
+        if (d == c) d = (d + 1) % n;
+      }
+    }
+  }
+}
+// clip polygon `inc` (n2 points) by the side planes of face `ref` (n1 >= 3
+// points, outward normal `normal`) and keep what lies below that face;
+// `dir` points from the incident shape's contact points to the reference's
+template <class R>
+__device__ BoxManifold<R> clip_faces(const V3<R> *ref, int n1, const V3<R> *inc, int n2, V3<R> normal, V3<R> dir) {
+  BoxManifold<R> o;
+  o.count = 0;
+  if (n1 < 3) return o;
+  V3<R> side[4], buf[2][8];
+  R plane[4];
+  for (int i = 0; i < n1; ++i) {
+    side[i] = cross(ref[(i + 1) % n1] - ref[i], (ref[i] + normal) - ref[i]);
+    plane[i] = dot(side[i], ref[i]);
+  }
+  int count = n2, cur = 0;
+  for (int i = 0; i < n2; ++i) buf[0][i] = inc[i];
+  for (int e = 0; e < n1; ++e) {
+    const V3<R> *in = buf[cur];
+    V3<R> *out = buf[cur ^ 1];
+    int m = 0;
+    for (int i = 0; i < count; ++i) {
+      const V3<R> p = in[i], q = in[(i + 1) % count];
+      const bool inp = dot(p - ref[e], side[e]) > R(-1e-10), inq = dot(q - ref[e], side[e]) > R(-1e-10);
+      if (!inp && !inq) continue;
+      if (inp && inq) { if (m < 8) out[m++] = q; continue; }
+      const R den = dot(side[e], q - p);
+      R t = mabs(den) < R(1e-10) ? R(1e30) : (plane[e] - dot(side[e], p)) / den;
+      if (t > R(-3e-7) && t < R(1) + R(3e-7)) {
+        t = mmin(R(1), mmax(R(0), t));
+        if (m < 8) out[m++] = p + (q - p) * t;
+      }
+      if (inq && m < 8) out[m++] = q;
+    }
+    cur ^= 1;
+    count = m;
+  }
+  V3<R> *poly = buf[cur];
+  int kept = 0;
+  for (int i = 0; i < count; ++i)
+    if (dot(poly[i] - ref[0], normal) <= R(0)) poly[kept++] = poly[i];
+  count = kept;
+  if (count < 1) return o;
+  int q[4] = {0, 1, 2, 3};
+  if (n2 == 2 && count > 2) {
+    R best = 0;
+    q[0] = 0; q[1] = 1;
+    for (int i = 0; i < count; ++i)
+      for (int j = i + 1; j < count; ++j) {
+        const V3<R> d = poly[j] - poly[i];
+        if (dot(d, d) > best) { best = dot(d, d); q[0] = i; q[1] = j; }
+      }
+    o.count = 2;
+  } else if (count > 4) {
+    largest_quad(poly, count, q);
+    o.count = 4;
+  } else
+    o.count = count;
+  for (int i = 0; i < o.count; ++i) {
+    const V3<R> v = poly[q[i]];
+    const R d = dot(v - ref[0], normal);
+    o.one[i] = v - dir * mabs(d);
+    o.two[i] = v;
+    o.dist[i] = d;
+  }
+  return o;
+}
+// EPA's final face -> the box-box contact manifold (count 0: keep EPA's contact)
+template <class R> __device__ BoxManifold<R> box_manifold(const CShape<R> &A, const CShape<R> &B, const EpaOut<R> &e) {
+  BoxManifold<R> none;
+  none.count = 0;
+  const BoxFeature<R> fa = box_feature<R>(e.face_ca, e.face_a), fb = box_feature<R>(e.face_cb, e.face_b);
+  const V3<R> dir = e.x2 - e.x1;
+  BoxNormals<R> na = box_normals(A, fa, -dir), nb = box_normals(B, fb, dir);
+  int i = 0, j = 0;
+  bool aligned = false, edge_a = false, edge_b = false;
+  for (int k = 0; k < na.count && !aligned; ++k)
+    for (int l = 0; l < nb.count; ++l)
+      if (dot(na.n[k], nb.n[l]) < -R(kBoxAligned)) { i = k; j = l; aligned = true; break; }
+  V3<R> end[3];
+  if (!aligned) {
+    if (fa.dim < 3 && nb.count && (fa.dim <= fb.dim || !na.count)) {
+      na = box_edges(A, fa, end);
+      for (int k = 0; k < nb.count && !aligned; ++k) {
+        if (dot(nb.n[k], dir) <= R(1e-15)) continue;
+        for (int l = 0; l < na.count; ++l)
+          if (mabs(dot(na.n[l], nb.n[k])) < R(kBoxPerpendicular)) { i = l; j = k; aligned = true; break; }
+      }
+      if (!aligned) return none;
+      edge_a = true;
+    } else if (fb.dim < 3) {
+      nb = box_edges(B, fb, end);
+      for (int k = 0; k < na.count && !aligned; ++k) {
+        if (dot(na.n[k], -dir) <= R(1e-15)) continue;
+        for (int l = 0; l < nb.count; ++l)
+          if (mabs(dot(nb.n[l], na.n[k])) < R(kBoxPerpendicular)) { i = l; j = k; aligned = true; break; }
+      }
+      if (!aligned) return none;
+      edge_b = true;
+    } else
+      return none;
+  }
+  V3<R> face_a[4], face_b[4];
+  int count_a = 4, count_b = 4;
+  if (edge_a) { face_a[0] = fa.pt[0]; face_a[1] = end[i]; count_a = 2; }
+  else box_face_corners(A, na.face[edge_b ? j : i], face_a);
+  if (edge_b) { face_b[0] = fb.pt[0]; face_b[1] = end[i]; count_b = 2; }
+  else box_face_corners(B, nb.face[j], face_b);
+  if (edge_a) {  // B's face is the reference face; contact points swap sides
+    BoxManifold<R> r = clip_faces(face_b, count_b, face_a, count_a, nb.n[j], -nb.n[j]);
+    for (int k = 0; k < r.count; ++k) { const V3<R> v = r.one[k]; r.one[k] = r.two[k]; r.two[k] = v; }
+    return r;
+  }
+  if (edge_b) return clip_faces(face_a, count_a, face_b, count_b, na.n[j], -na.n[j]);
+  return clip_faces(face_a, count_a, face_b, count_b, na.n[i], nb.n[j]);
 }
 
 template <class R>
@@ -1086,23 +1380,33 @@ __device__ __noinline__ void convex_pair(const Mdl<R> &M, Arena<R> &A, int pair,
       found = true;
     }
   }
+  // two zero-margin boxes: EPA ends on a face of the Minkowski difference and
+  // the contact becomes a face manifold
+  const bool boxes = S1.type == B200_GEOM_BOX && S2.type == B200_GEOM_BOX && p.margin == R(0);
+  BoxManifold<R> mf;
+  mf.count = 0;
   if (!found) {
     const GjkOut<R> r = gjk(S1, S2, tol, iters, p.gap);
     if (r.separated) return;
     if (r.dist > tol) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
     else {
-      const EpaOut<R> e = epa(S1, S2, r.s, tol, M.m.epa_iterations);
+      const EpaOut<R> e = epa(S1, S2, r.s, tol, M.m.epa_iterations, boxes);
       if (e.budget) atomicOr(&A.iscal[3], B200_WARN_EPA_BUDGET);
       if (e.horizon) atomicOr(&A.iscal[3], B200_OVERFLOW_EPA_HORIZON);
       if (!e.ok) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
-      else { dist = -e.depth; x1 = e.x1; x2 = e.x2; }
+      else {
+        dist = -e.depth; x1 = e.x1; x2 = e.x2;
+        if (boxes) mf = box_manifold(S1, S2, e);
+      }
     }
   }
   if (!(dist < p.gap)) return;
   const R distance = dist + p.margin;
+  if (mf.count < 1) { mf.count = 1; mf.one[0] = x1; mf.two[0] = x2; }
   V3<R> fr[3];
-  frame_from_normal(distance <= p.margin ? x1 - x2 : x2 - x1, fr);
-  emit(M, A, p, pair, 0, g1, g2, distance, (x1 + x2) * R(0.5) + origin, fr);
+  frame_from_normal(distance <= p.margin ? mf.one[0] - mf.two[0] : mf.two[0] - mf.one[0], fr);
+  for (int c = 0; c < mf.count; ++c)
+    emit(M, A, p, pair, c, g1, g2, mf.count > 1 ? mf.dist[c] : distance, (mf.one[c] + mf.two[c]) * R(0.5) + origin, fr);
 }
 
 // narrowphase family of a candidate pair (-1: filtered out or unsupported):
@@ -1113,6 +1417,7 @@ template <class R, bool CONVEX> __device__ int pair_family(const Mdl<R> &M, cons
   const int t1 = IF(geom_type)[g1], t2 = IF(geom_type)[g2];
   if (t2 == B200_GEOM_MESH) return CONVEX ? (t1 == B200_GEOM_PLANE ? 3 : 4) : -1;
   if (t1 == B200_GEOM_PLANE && t2 >= 2 && t2 <= 6) return 0;
+  if (t1 == B200_GEOM_BOX && t2 == B200_GEOM_BOX && M.m.boxbox_convex) return CONVEX ? 4 : -1;
   if (t2 == B200_GEOM_BOX && (t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE || t1 == B200_GEOM_BOX)) return 1;
   if ((t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE) && (t2 == B200_GEOM_SPHERE || t2 == B200_GEOM_CAPSULE))
     return 2;

@@ -404,6 +404,17 @@ class Scene:
                 # broadphase emits the lower geom type first (mjwarp_broadphase.cu:112-113)
                 pairs.append((j, i) if gtype[i] > gtype[j] else (i, j))
         self.pair_families = sorted({(int(gtype[a]), int(gtype[b])) for a, b in pairs})
+        # box-box pairs take the convex path (GJK/EPA and the box manifold)
+        # unless one of them has a margin (cuda_fp32/model.py:187-191,
+        # physics.py:89-90); the per-pair margin there is the larger geom margin
+        gmargin = np.array([g.margin for _, g in G], float)
+        boxbox = [(a, b) for a, b in pairs if gtype[a] == BOX and gtype[b] == BOX]
+        boxbox_convex = int(not any(max(gmargin[a], gmargin[b]) > 0 for a, b in boxbox))
+        # MJWarp's EPA budget: 16 when every convex pair is box-box, else the CCD iterations
+        convex_pairs = [(a, b) for a, b in pairs if gtype[b] == MESH and gtype[a] != PLANE] + \
+            (boxbox if boxbox_convex else [])
+        epa_default = 16 if convex_pairs and all(gtype[a] == BOX and gtype[b] == BOX for a, b in convex_pairs) \
+            else self.options.get('ccd_iterations', 50)
         # sites
         S = [(bi, s) for bi, b in enumerate(B) for s in b.sites]
         ns = len(S)
@@ -430,7 +441,8 @@ class Scene:
                           nlimited=int(limited.sum()), nfric=int(np.sum(fric > 0)),
                           nmesh=len(mesh_vertadr), nmeshvert=len(mesh_vert), nmeshpoly=len(polyvertadr),
                           nmeshpolyvert=len(polyvert), nmeshpolymap=len(polymap),
-                          ccd_iterations=opt.get('ccd_iterations', 50), epa_iterations=opt.get('epa_iterations', 32))
+                          ccd_iterations=opt.get('ccd_iterations', 50),
+                          epa_iterations=opt.get('epa_iterations', epa_default), boxbox_convex=boxbox_convex)
         ncon_max = cap['nconmax']
         cone = opt['cone']
         rows_per_contact = 3 if cone == 1 else 4
@@ -804,8 +816,9 @@ class _Site(dict):
         return self['name']
 
 
-def _panda(bodies, link_radius=0.06):
-    """Append a Franka-like arm (7 hinges + 2 finger slides) under the world."""
+def _panda(bodies, link_radius=0.06, box_margin=0.001):
+    """Append a Franka-like arm (7 hinges + 2 finger slides) under the world;
+    the finger pads are boxes with margin `box_margin`."""
     ARM, OBJ = 2, 1   # contype bits: arm geoms never collide with each other
     links = [  # (pos, quat, capsule half-length, capsule centre offset/axis quat)
         ((0, 0, 0.333), (1, 0, 0, 0)),
@@ -847,7 +860,7 @@ def _panda(bodies, link_radius=0.06):
         f.joints.append(Joint('finger_joint%d' % (1 if side > 0 else 2), SLIDE, (0, 1, 0), range=(lo, hi),
                               damping=100.0, armature=1.0, frictionloss=1.0))
         f.geoms.append(Geom('finger%d_pad' % (1 if side > 0 else 2), BOX, (0.01, 0.01, 0.025),
-                            (0, 0.012 * side, 0.028), contype=ARM, conaffinity=OBJ, margin=0.001, mass=0.1))
+                            (0, 0.012 * side, 0.028), contype=ARM, conaffinity=OBJ, margin=box_margin, mass=0.1))
         bodies.append(f)
     njoint = 9
     actuators = []
@@ -876,12 +889,16 @@ def _ee_xy(scene):
 
 
 def scene_a(seed=0, cone='elliptic', nconmax=32, njmax=None, iterations=50, ls_iterations=50,
-            tolerance=1e-8):
-    """BASELINE scene A: arm + gripper + plane + 3 free boxes (nq=30, nv=27)."""
+            tolerance=1e-8, box_margin=0.001):
+    """BASELINE scene A: arm + gripper + plane + 3 free boxes (nq=30, nv=27).
+
+    The boxes and finger pads carry a margin of `box_margin`; with 0, box-box
+    pairs take the convex path and its box manifold, as in a LIBERO scene whose
+    boxes have no margin."""
     rng = np.random.default_rng([seed, 0xA])
     bodies = [Body('world', -1)]
     bodies[0].geoms.append(Geom('floor', PLANE, (0, 0, 0.05), contype=1, conaffinity=3))
-    actuators, controller = _panda(bodies)
+    actuators, controller = _panda(bodies, box_margin=box_margin)
     objects = []
     for k in range(3):
         half = rng.uniform(0.02, 0.05, 3)
@@ -889,7 +906,7 @@ def scene_a(seed=0, cone='elliptic', nconmax=32, njmax=None, iterations=50, ls_i
         b = Body('box%d' % k, 0, (0.5, 0.0, half[2]))
         b.joints.append(Joint('box%d_free' % k, FREE))
         b.geoms.append(Geom('box%d_geom' % k, BOX, tuple(half), contype=1, conaffinity=3,
-                            friction=(1.0, 0.005, 0.0001), margin=0.001, mass=mass))
+                            friction=(1.0, 0.005, 0.0001), margin=box_margin, mass=mass))
         bodies.append(b)
         objects.append(dict(id=len(bodies) - 1, radius=float(np.linalg.norm(half[:2])), rbound=float(np.linalg.norm(half)),
                             rest_z=float(half[2]),
@@ -905,18 +922,19 @@ def scene_a(seed=0, cone='elliptic', nconmax=32, njmax=None, iterations=50, ls_i
 
 
 def scene_b(seed=0, cone='elliptic', nconmax=96, njmax=None, iterations=50, ls_iterations=50,
-            tolerance=1e-8, hull_points=32, epa_iterations=32, ccd_tolerance=1e-6):
+            tolerance=1e-8, hull_points=32, epa_iterations=32, ccd_tolerance=1e-6, box_margin=0.001):
     """BASELINE scene B: scene A's arm plus 12 dropped free objects (nq=93, nv=81).
 
     4 boxes (half-extents U[0.02,0.05]), 4 capsules (radius U[0.015,0.04],
     half-length U[0.02,0.05]), 2 spheres (radius U[0.02,0.05]) and 2 convex
     hulls of 32 random points on an ellipsoid with semi-axes U[0.02,0.06];
     masses U[0.05,0.3] kg, friction 1; dropped from z U[0.05,0.15] m with a
-    random orientation.  Boxes and hulls carry a 1 mm margin."""
+    random orientation.  Boxes (finger pads included) carry a margin of
+    `box_margin`, hulls a 1 mm margin."""
     rng = np.random.default_rng([seed, 0xB])
     bodies = [Body('world', -1)]
     bodies[0].geoms.append(Geom('floor', PLANE, (0, 0, 0.05), contype=1, conaffinity=3))
-    actuators, controller = _panda(bodies)
+    actuators, controller = _panda(bodies, box_margin=box_margin)
     objects = []
     kinds = [BOX] * 4 + [CAPSULE] * 4 + [SPHERE] * 2 + [MESH] * 2
     for k, kind in enumerate(kinds):
@@ -924,7 +942,7 @@ def scene_b(seed=0, cone='elliptic', nconmax=96, njmax=None, iterations=50, ls_i
         mesh, margin = None, 0.0
         if kind == BOX:
             size = tuple(rng.uniform(0.02, 0.05, 3))
-            radius, margin = float(np.linalg.norm(size)), 0.001
+            radius, margin = float(np.linalg.norm(size)), box_margin
         elif kind == CAPSULE:
             size = (rng.uniform(0.015, 0.04), rng.uniform(0.02, 0.05))
             radius = size[0] + size[1]

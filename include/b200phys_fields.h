@@ -31,6 +31,11 @@
  * kernel's CTA slots (slot i runs world order[i]).  b200phys_order_launch
  * refills it from `work`, so that worlds of similar work share a CTA.
  *
+ * boxbox_convex: box-box pairs take the convex path (GJK / EPA and the box
+ * manifold) instead of the SAT box collider; set when no box-box pair has a
+ * margin (the reference's has_boxbox_margin rule, cuda_fp32/model.py:187-191,
+ * physics.py:89-90).  Such a model runs the kernel variant with convex support.
+ *
  * task_body / task_lift_z: the synthetic scenes' task predicate.  Success is
  * the free body free_bodyid[task_body] (its centre of mass frame origin) above
  * task_lift_z; reward = 1 and done = 1 on success, else 0 (LIBERO's sparse
@@ -46,7 +51,7 @@
   X(iterations) X(ls_iterations) X(disable_flags) X(ee_site) X(real_bytes) \
   X(nvs) X(kmax_dof) X(max_tree_dofs) X(osc_uncouple) X(nfree) X(nobs) \
   X(nmesh) X(nmeshvert) X(nmeshpoly) X(nmeshpolyvert) X(nmeshpolymap) \
-  X(ccd_iterations) X(epa_iterations) X(nL) X(task_body)
+  X(ccd_iterations) X(epa_iterations) X(nL) X(task_body) X(boxbox_convex)
 
 /* real scalars of the model (stored as double, read as the kernel's real) */
 #define B200_MODEL_REAL_SCALARS(X) \

@@ -170,9 +170,12 @@ typedef struct {
   real margin; /* inflation: half the pair margin is added along the support direction */
 } CShape;
 
-/* support point of a shape in unit direction d (mjwarp_convex_geometry.cuh:17-68 contract) */
-static V3 cs_support(const CShape *s, V3 d) {
+/* support point of a shape in unit direction d (mjwarp_convex_geometry.cuh:17-68
+ * contract); for a box, *corner = the corner index, bit c set for +size on
+ * local axis c (a zero component takes the negative end), else -1 */
+static V3 cs_support_c(const CShape *s, V3 d, int *corner) {
   V3 p;
+  *corner = -1;
   if (s->type == B200_GEOM_SPHERE) return vadd(s->pos, vscale(d, s->size.v[0] + R(0.5) * s->margin));
   V3 l = mrotT(s->rot, d), r;
   if (s->type == B200_GEOM_CAPSULE) {
@@ -180,6 +183,7 @@ static V3 cs_support(const CShape *s, V3 d) {
     r.v[2] += (l.v[2] > 0 ? 1 : l.v[2] < 0 ? -1 : 0) * s->size.v[1];
   } else if (s->type == B200_GEOM_BOX) {
     for (int c = 0; c < 3; ++c) r.v[c] = (l.v[c] > 0 ? 1 : -1) * s->size.v[c];
+    *corner = (l.v[0] > 0) | (l.v[1] > 0) << 1 | (l.v[2] > 0) << 2;
   } else {
     int best = 0;
     real top = vdot(vload(s->vert), l);
@@ -193,8 +197,9 @@ static V3 cs_support(const CShape *s, V3 d) {
   if (s->margin > 0) p = vadd(p, vscale(d, R(0.5) * s->margin));
   return p;
 }
+static V3 cs_support(const CShape *s, V3 d) { int c; return cs_support_c(s, d, &c); }
 
-typedef struct { V3 w[4], a[4], b[4]; real lam[4]; int n; } Simplex;
+typedef struct { V3 w[4], a[4], b[4]; real lam[4]; int n, ca[4], cb[4]; } Simplex;
 
 /* Signed-volume distance sub-algorithm (Montanari, Petrinic and Barbieri,
  * ACM TOG 2017), the method of the reference's
@@ -313,7 +318,10 @@ static void simplex_reduce(Simplex *s) {
   Simplex t;
   int k = 0;
   for (int i = 0; i < s->n; ++i)
-    if (W.w[i] != 0) { t.w[k] = s->w[i]; t.a[k] = s->a[i]; t.b[k] = s->b[i]; t.lam[k] = W.w[i]; ++k; }
+    if (W.w[i] != 0) {
+      t.w[k] = s->w[i]; t.a[k] = s->a[i]; t.b[k] = s->b[i]; t.lam[k] = W.w[i]; t.ca[k] = s->ca[i]; t.cb[k] = s->cb[i];
+      ++k;
+    }
   t.n = k;
   *s = t;
 }
@@ -332,14 +340,15 @@ static GjkOut gjk(const CShape *A, const CShape *B, real tol, int iterations, re
   for (int it = 0; it < iterations; ++it) {
     if (norm < tol || rabs(prev - norm) < R(1e-15)) break;
     V3 d = vscale(x, R(1) / norm);
-    V3 a = cs_support(A, vneg(d)), b = cs_support(B, d), w = vsub(a, b);
+    int ca, cb;
+    V3 a = cs_support_c(A, vneg(d), &ca), b = cs_support_c(B, d, &cb), w = vsub(a, b);
     if (vdot(x, vsub(x, w)) < R(0.5) * tol * tol) break;
     real lower = vdot(x, w);
     if (lower > 0 && (cutoff == 0 || lower >= cutoff * norm)) {
       o.separated = 1; o.dist = R(1e30);
       return o;
     }
-    s->w[s->n] = w; s->a[s->n] = a; s->b[s->n] = b; s->n++;
+    s->w[s->n] = w; s->a[s->n] = a; s->b[s->n] = b; s->ca[s->n] = ca; s->cb[s->n] = cb; s->n++;
     simplex_reduce(s);
     if (s->n < 1) break;
     x = v3(0, 0, 0);
@@ -359,6 +368,7 @@ static GjkOut gjk(const CShape *A, const CShape *B, real tol, int iterations, re
 #define EPA_MAXF 96
 typedef struct {
   V3 w[EPA_MAXV], a[EPA_MAXV], b[EPA_MAXV];
+  int ca[EPA_MAXV], cb[EPA_MAXV]; /* box support corners (-1: not a box) */
   int nv, nf, face[EPA_MAXF][3];
   V3 n[EPA_MAXF];
   real d[EPA_MAXF];
@@ -397,7 +407,8 @@ static int epa_add_face(Polytope *P, int i, int j, int l) {
 static int epa_push(Polytope *P, const CShape *A, const CShape *B, V3 d) {
   if (P->nv >= EPA_MAXV) return -1;
   int v = P->nv++;
-  P->a[v] = cs_support(A, d); P->b[v] = cs_support(B, vneg(d)); P->w[v] = vsub(P->a[v], P->b[v]);
+  P->a[v] = cs_support_c(A, d, &P->ca[v]); P->b[v] = cs_support_c(B, vneg(d), &P->cb[v]);
+  P->w[v] = vsub(P->a[v], P->b[v]);
   return v;
 }
 
@@ -405,7 +416,9 @@ static int epa_push(Polytope *P, const CShape *A, const CShape *B, V3 d) {
  * shapes only touch (no volume around the origin) */
 static int epa_seed(Polytope *P, const CShape *A, const CShape *B, const Simplex *s) {
   P->nv = 0; P->nf = 0;
-  for (int i = 0; i < s->n; ++i) { P->w[i] = s->w[i]; P->a[i] = s->a[i]; P->b[i] = s->b[i]; }
+  for (int i = 0; i < s->n; ++i) {
+    P->w[i] = s->w[i]; P->a[i] = s->a[i]; P->b[i] = s->b[i]; P->ca[i] = s->ca[i]; P->cb[i] = s->cb[i];
+  }
   P->nv = s->n;
   static const real axes[6][3] = {{1, 0, 0}, {-1, 0, 0}, {0, 1, 0}, {0, -1, 0}, {0, 0, 1}, {0, 0, -1}};
   for (int k = 0; P->nv < 2 && k < 6; ++k) {
@@ -451,13 +464,24 @@ static int epa_seed(Polytope *P, const CShape *A, const CShape *B, const Simplex
   return 1;
 }
 
-typedef struct { int ok, budget, horizon; real depth; V3 x1, x2; } EpaOut; /* budget: a vertex/face pool filled; horizon: the edge list did */
+/* budget: a vertex/face pool filled; horizon: the edge list did; face_*: the
+ * final face's vertices (support points and box corners) */
+typedef struct {
+  int ok, budget, horizon;
+  real depth;
+  V3 x1, x2, face_a[3], face_b[3];
+  int face_ca[3], face_cb[3];
+} EpaOut;
 
-static EpaOut epa(const CShape *A, const CShape *B, const Simplex *s, real tol, int iterations) {
+/* discrete: two zero-margin boxes; EPA stops within 1e-7 or on a repeated
+ * corner pair (mjwarp_convex_epa.cuh epa_expand), on a face of the Minkowski
+ * difference itself */
+static EpaOut epa(const CShape *A, const CShape *B, const Simplex *s, real tol, int iterations, int discrete) {
   EpaOut o;
   memset(&o, 0, sizeof(o));
   Polytope P;
   if (!epa_seed(&P, A, B, s)) return o;
+  real eps = discrete ? R(1e-7) : tol;
   int best = -1;
   for (int it = 0; it <= iterations; ++it) {
     best = -1;
@@ -468,7 +492,12 @@ static EpaOut epa(const CShape *A, const CShape *B, const Simplex *s, real tol, 
     V3 n = P.n[best];
     int v = epa_push(&P, A, B, n);
     if (v < 0) { o.budget = 1; break; }
-    if (vdot(P.w[v], n) - P.d[best] < tol) { P.nv--; break; }
+    if (vdot(P.w[v], n) - P.d[best] < eps) { P.nv--; break; }
+    if (discrete) {
+      int repeated = 0;
+      for (int q = 0; q < v; ++q) repeated |= P.ca[q] == P.ca[v] && P.cb[q] == P.cb[v];
+      if (repeated) { P.nv--; break; }
+    }
     /* remove the faces that see the new vertex; keep their horizon */
     int edges[3 * EPA_MAXF][2], ne = 0;
     for (int f = 0; f < P.nf; ++f) {
@@ -502,8 +531,221 @@ static EpaOut epa(const CShape *A, const CShape *B, const Simplex *s, real tol, 
   o.x1 = vadd(vadd(vscale(P.a[i], lu), vscale(P.a[j], lv)), vscale(P.a[l], lw));
   o.x2 = vadd(vadd(vscale(P.b[i], lu), vscale(P.b[j], lv)), vscale(P.b[l], lw));
   o.depth = P.d[best];
+  int fv[3] = {i, j, l};
+  for (int q = 0; q < 3; ++q) {
+    o.face_a[q] = P.a[fv[q]]; o.face_b[q] = P.b[fv[q]]; o.face_ca[q] = P.ca[fv[q]]; o.face_cb[q] = P.cb[fv[q]];
+  }
   o.ok = 1;
   return o;
+}
+
+/* ---- box manifold (mjwarp_box_manifold.cuh box_multicontact): EPA's final
+ * face names a feature of each box by its corners; anti-parallel face normals
+ * (within 5.1 degrees), or a face normal and a perpendicular edge, pick the
+ * reference and incident faces; the incident polygon is clipped by the
+ * reference face's side planes, and the points below that face are the
+ * contacts (at most four) */
+#define BOX_ALIGNED R(0.99605101346969604)
+#define BOX_PERPENDICULAR R(0.088782943785190582)
+typedef struct { int count; V3 one[4], two[4]; real dist[4]; } BoxManifold;
+typedef struct { int dim, corner[3]; V3 pt[3]; } BoxFeature;
+typedef struct { int count, face[3]; V3 n[3]; } BoxNormals;
+
+static BoxFeature box_feature(const int *corner, const V3 *pt) {
+  BoxFeature f;
+  for (int q = 0; q < 3; ++q) { f.corner[q] = corner[q]; f.pt[q] = pt[q]; }
+  if (f.corner[0] != f.corner[1]) f.dim = (f.corner[2] == f.corner[0] || f.corner[2] == f.corner[1]) ? 2 : 3;
+  else { f.corner[1] = f.corner[2]; f.pt[1] = f.pt[2]; f.dim = f.corner[0] != f.corner[2] ? 2 : 1; }
+  return f;
+}
+static V3 box_axis(const CShape *s, int face) {
+  V3 e = v3(0, 0, 0);
+  e.v[face / 2] = face % 2 ? -1 : 1;
+  return mrot(s->rot, e);
+}
+static BoxNormals box_normals_near(const CShape *s, V3 d) {
+  BoxNormals o;
+  o.count = 0;
+  V3 l = vnormalize(mrotT(s->rot, d));
+  for (int f = 0; f < 6; ++f)
+    if ((f % 2 ? -l.v[f / 2] : l.v[f / 2]) > BOX_ALIGNED) { o.count = 1; o.face[0] = f; o.n[0] = box_axis(s, f); return o; }
+  return o;
+}
+static BoxNormals box_normals(const CShape *s, const BoxFeature *f, V3 d) {
+  BoxNormals o;
+  o.count = 0;
+  if (f->dim == 1) {
+    o.count = 3;
+    for (int c = 0; c < 3; ++c) { o.face[c] = 2 * c + ((f->corner[0] >> c) & 1 ? 0 : 1); o.n[c] = box_axis(s, o.face[c]); }
+    return o;
+  }
+  for (int c = 0; c < 3; ++c) {
+    int all = 1, none = 1;
+    for (int i = 0; i < f->dim; ++i) { int set = (f->corner[i] >> c) & 1; all &= set; none &= !set; }
+    if (all || none) { o.face[o.count] = 2 * c + (all ? 0 : 1); o.n[o.count] = box_axis(s, o.face[o.count]); ++o.count; }
+  }
+  if ((f->dim == 3 && o.count == 1) || (f->dim == 2 && o.count >= 1)) return o;
+  return box_normals_near(s, d);
+}
+static BoxNormals box_edges(const CShape *s, const BoxFeature *f, V3 *end) {
+  BoxNormals o;
+  o.count = 0;
+  if (f->dim == 2) { end[0] = f->pt[1]; o.n[0] = vnormalize(vsub(f->pt[1], f->pt[0])); o.count = 1; }
+  else if (f->dim == 1) {
+    V3 c;
+    for (int q = 0; q < 3; ++q) c.v[q] = (f->corner[0] >> q) & 1 ? s->size.v[q] : -s->size.v[q];
+    for (int q = 0; q < 3; ++q) {
+      V3 e = c;
+      e.v[q] = -e.v[q];
+      end[q] = vadd(mrot(s->rot, e), s->pos);
+      o.n[q] = vnormalize(vsub(end[q], f->pt[0]));
+    }
+    o.count = 3;
+  }
+  return o;
+}
+static void box_face_corners(const CShape *s, int face, V3 *v) {
+  static const unsigned char winding[6][4] = {{7, 3, 1, 5}, {2, 6, 4, 0}, {2, 3, 7, 6}, {4, 5, 1, 0}, {6, 7, 5, 4}, {3, 2, 0, 1}};
+  for (int i = 0; i < 4; ++i) {
+    V3 c;
+    for (int q = 0; q < 3; ++q) c.v[q] = (winding[face][i] >> q) & 1 ? s->size.v[q] : -s->size.v[q];
+    v[i] = vadd(mrot(s->rot, c), s->pos);
+  }
+}
+static real quad_area(V3 a, V3 b, V3 c, V3 d) {
+  V3 n = vcross(vsub(a, c), vsub(b, d));
+  return R(0.5) * rsqrt_(vdot(n, n));
+}
+static void largest_quad(const V3 *p, int n, int *q) {
+  int b = 1, c = 2, d = 3;
+  q[0] = 0; q[1] = b; q[2] = c; q[3] = d;
+  real area = quad_area(p[0], p[b], p[c], p[d]);
+  for (int a = 0; a < n; ++a) {
+    for (;;) {
+      real next = quad_area(p[a], p[b], p[c], p[(d + 1) % n]);
+      if (next <= area) break;
+      area = next; d = (d + 1) % n; q[0] = a; q[1] = b; q[2] = c; q[3] = d;
+      for (;;) {
+        next = quad_area(p[a], p[b], p[(c + 1) % n], p[d]);
+        if (next <= area) break;
+        area = next; c = (c + 1) % n; q[0] = a; q[1] = b; q[2] = c; q[3] = d;
+      }
+      for (;;) {
+        next = quad_area(p[a], p[(b + 1) % n], p[c], p[d]);
+        if (next <= area) break;
+        area = next; b = (b + 1) % n; q[0] = a; q[1] = b; q[2] = c; q[3] = d;
+      }
+    }
+    if (b == a) {
+      b = (b + 1) % n;
+      if (c == b) { c = (c + 1) % n; if (d == c) d = (d + 1) % n; }
+    }
+  }
+}
+static BoxManifold clip_faces(const V3 *ref, int n1, const V3 *inc, int n2, V3 normal, V3 dir) {
+  BoxManifold o;
+  o.count = 0;
+  if (n1 < 3) return o;
+  V3 side[4], buf[2][8];
+  real plane[4];
+  for (int i = 0; i < n1; ++i) {
+    side[i] = vcross(vsub(ref[(i + 1) % n1], ref[i]), vsub(vadd(ref[i], normal), ref[i]));
+    plane[i] = vdot(side[i], ref[i]);
+  }
+  int count = n2, cur = 0;
+  for (int i = 0; i < n2; ++i) buf[0][i] = inc[i];
+  for (int e = 0; e < n1; ++e) {
+    const V3 *in = buf[cur];
+    V3 *out = buf[cur ^ 1];
+    int m = 0;
+    for (int i = 0; i < count; ++i) {
+      V3 p = in[i], q = in[(i + 1) % count];
+      int inp = vdot(vsub(p, ref[e]), side[e]) > R(-1e-10), inq = vdot(vsub(q, ref[e]), side[e]) > R(-1e-10);
+      if (!inp && !inq) continue;
+      if (inp && inq) { if (m < 8) out[m++] = q; continue; }
+      real den = vdot(side[e], vsub(q, p));
+      real s = rabs(den) < R(1e-10) ? R(1e30) : (plane[e] - vdot(side[e], p)) / den;
+      if (s > R(-3e-7) && s < R(1) + R(3e-7)) {
+        s = s < 0 ? 0 : s > 1 ? 1 : s;
+        if (m < 8) out[m++] = vadd(p, vscale(vsub(q, p), s));
+      }
+      if (inq && m < 8) out[m++] = q;
+    }
+    cur ^= 1;
+    count = m;
+  }
+  V3 *poly = buf[cur];
+  int kept = 0;
+  for (int i = 0; i < count; ++i)
+    if (vdot(vsub(poly[i], ref[0]), normal) <= 0) poly[kept++] = poly[i];
+  count = kept;
+  if (count < 1) return o;
+  int q[4] = {0, 1, 2, 3};
+  if (n2 == 2 && count > 2) {
+    real best = 0;
+    q[0] = 0; q[1] = 1;
+    for (int i = 0; i < count; ++i)
+      for (int j = i + 1; j < count; ++j) {
+        V3 d = vsub(poly[j], poly[i]);
+        if (vdot(d, d) > best) { best = vdot(d, d); q[0] = i; q[1] = j; }
+      }
+    o.count = 2;
+  } else if (count > 4) { largest_quad(poly, count, q); o.count = 4; }
+  else o.count = count;
+  for (int i = 0; i < o.count; ++i) {
+    V3 v = poly[q[i]];
+    real d = vdot(vsub(v, ref[0]), normal);
+    o.one[i] = vsub(v, vscale(dir, rabs(d)));
+    o.two[i] = v;
+    o.dist[i] = d;
+  }
+  return o;
+}
+static BoxManifold box_manifold(const CShape *A, const CShape *B, const EpaOut *e) {
+  BoxManifold none;
+  none.count = 0;
+  BoxFeature fa = box_feature(e->face_ca, e->face_a), fb = box_feature(e->face_cb, e->face_b);
+  V3 dir = vsub(e->x2, e->x1);
+  BoxNormals na = box_normals(A, &fa, vneg(dir)), nb = box_normals(B, &fb, dir);
+  int i = 0, j = 0, aligned = 0, edge_a = 0, edge_b = 0;
+  for (int k = 0; k < na.count && !aligned; ++k)
+    for (int l = 0; l < nb.count; ++l)
+      if (vdot(na.n[k], nb.n[l]) < -BOX_ALIGNED) { i = k; j = l; aligned = 1; break; }
+  V3 end[3];
+  if (!aligned) {
+    if (fa.dim < 3 && nb.count && (fa.dim <= fb.dim || !na.count)) {
+      na = box_edges(A, &fa, end);
+      for (int k = 0; k < nb.count && !aligned; ++k) {
+        if (vdot(nb.n[k], dir) <= R(1e-15)) continue;
+        for (int l = 0; l < na.count; ++l)
+          if (rabs(vdot(na.n[l], nb.n[k])) < BOX_PERPENDICULAR) { i = l; j = k; aligned = 1; break; }
+      }
+      if (!aligned) return none;
+      edge_a = 1;
+    } else if (fb.dim < 3) {
+      nb = box_edges(B, &fb, end);
+      for (int k = 0; k < na.count && !aligned; ++k) {
+        if (vdot(na.n[k], vneg(dir)) <= R(1e-15)) continue;
+        for (int l = 0; l < nb.count; ++l)
+          if (rabs(vdot(nb.n[l], na.n[k])) < BOX_PERPENDICULAR) { i = l; j = k; aligned = 1; break; }
+      }
+      if (!aligned) return none;
+      edge_b = 1;
+    } else return none;
+  }
+  V3 face_a[4], face_b[4];
+  int count_a = 4, count_b = 4;
+  if (edge_a) { face_a[0] = fa.pt[0]; face_a[1] = end[i]; count_a = 2; }
+  else box_face_corners(A, na.face[edge_b ? j : i], face_a);
+  if (edge_b) { face_b[0] = fb.pt[0]; face_b[1] = end[i]; count_b = 2; }
+  else box_face_corners(B, nb.face[j], face_b);
+  if (edge_a) {
+    BoxManifold r = clip_faces(face_b, count_b, face_a, count_a, nb.n[j], vneg(nb.n[j]));
+    for (int k = 0; k < r.count; ++k) { V3 v = r.one[k]; r.one[k] = r.two[k]; r.two[k] = v; }
+    return r;
+  }
+  if (edge_b) return clip_faces(face_a, count_a, face_b, count_b, na.n[j], vneg(na.n[j]));
+  return clip_faces(face_a, count_a, face_b, count_b, na.n[i], nb.n[j]);
 }
 
 static CShape cs_make(const B200Model *m, const Work *k, int g, V3 origin, real margin) {
@@ -549,21 +791,32 @@ static void convex_collide(Work *k, const B200Model *m, int g1, int g2) {
       found = 1;
     }
   }
+  /* two zero-margin boxes: EPA ends on a face of the Minkowski difference and
+   * the contact becomes a face manifold (mjwarp_convex_collision.cuh:63-77) */
+  int boxes = A.type == B200_GEOM_BOX && B.type == B200_GEOM_BOX && p.margin == 0;
+  BoxManifold mf;
+  mf.count = 0;
   if (!found) {
     GjkOut r = gjk(&A, &B, tol, iters, cutoff);
     if (r.separated) return;
     if (r.dist > tol) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
     else {
-      EpaOut e = epa(&A, &B, &r.s, tol, m->epa_iterations);
+      EpaOut e = epa(&A, &B, &r.s, tol, m->epa_iterations, boxes);
       if (e.budget) k->overflow |= B200_WARN_EPA_BUDGET;
       if (e.horizon) k->overflow |= B200_OVERFLOW_EPA_HORIZON;
       if (!e.ok) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
-      else { dist = -e.depth; x1 = e.x1; x2 = e.x2; }
+      else {
+        dist = -e.depth; x1 = e.x1; x2 = e.x2;
+        if (boxes) mf = box_manifold(&A, &B, &e);
+      }
     }
   }
   if (!(dist < p.gap)) return;
   real distance = dist + p.margin;
+  if (mf.count < 1) { mf.count = 1; mf.one[0] = x1; mf.two[0] = x2; }
   real frame[9];
-  contact_frame(distance <= p.margin ? vsub(x1, x2) : vsub(x2, x1), frame);
-  publish(k, m, &p, g1, g2, distance, vadd(vscale(vadd(x1, x2), R(0.5)), origin), frame);
+  contact_frame(distance <= p.margin ? vsub(mf.one[0], mf.two[0]) : vsub(mf.two[0], mf.one[0]), frame);
+  for (int c = 0; c < mf.count; ++c)
+    publish(k, m, &p, g1, g2, mf.count > 1 ? mf.dist[c] : distance,
+            vadd(vscale(vadd(mf.one[c], mf.two[c]), R(0.5)), origin), frame);
 }

@@ -825,6 +825,8 @@ static void collision(const B200Model *m, Work *k) {
     int t1 = gt[g1], t2 = gt[g2];
     if (t1 == B200_GEOM_PLANE && t2 >= 2 && t2 <= 7) plane_collide(k, m, g1, g2);
     else if (t2 == B200_GEOM_MESH) convex_collide(k, m, g1, g2);
+    /* box-box on the convex path when no box pair has a margin (physics.py:89-90) */
+    else if (t1 == B200_GEOM_BOX && t2 == B200_GEOM_BOX && m->boxbox_convex) convex_collide(k, m, g1, g2);
     else if (t2 == B200_GEOM_BOX && (t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE || t1 == B200_GEOM_BOX))
       box_collide(k, m, g1, g2);
     else if ((t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE) && (t2 == B200_GEOM_SPHERE || t2 == B200_GEOM_CAPSULE))
@@ -2024,7 +2026,7 @@ int oracle_leaf_convex(int type1, const real *p1, const real *R1, const real *s1
     if (r.separated) return 0;
     if (r.dist > tol) { d = r.dist; x1 = r.x1; x2 = r.x2; }
     else {
-      EpaOut e = epa(&A, &B, &r.s, tol, epa_iterations);
+      EpaOut e = epa(&A, &B, &r.s, tol, epa_iterations, 0);
       if (e.budget || e.horizon) flags = 2;
       if (!e.ok) { d = r.dist; x1 = r.x1; x2 = r.x2; }
       else { d = -e.depth; x1 = e.x1; x2 = e.x2; }
