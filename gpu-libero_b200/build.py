@@ -5,9 +5,10 @@ with the repository snapshot.  Flags follow the reference FP32 build
 (libero/libero/gpu/cmake/MjwarpBox.cmake:15): FMA contraction on, IEEE
 division and square root, no flush-to-zero; never --use_fast_math.
 
-Translation units: csrc/abi.cu (C ABI, launch shape) and four instances of
-csrc/inst.cu (kernels for float / double, without / with mesh support), all
-compiled in parallel and linked into one shared library.
+Translation units: csrc/abi.cu (C ABI, launch shape) and six instances of
+csrc/inst.cu (kernels for float / double in the three convex modes of
+csrc/launch.h: no GJK / EPA, GJK / EPA for meshes, and with the zero-margin
+box-box path), all compiled in parallel and linked into one shared library.
 """
 import hashlib
 import os
@@ -26,7 +27,7 @@ NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
 FLAGS = ['-O3', '-std=c++17', '-gencode', 'arch=compute_100a,code=sm_100a', '-lineinfo',
          '--fmad=true', '--prec-div=true', '--prec-sqrt=true', '--ftz=false',
          '-Xcompiler', '-fPIC', '-I' + str(REPO / 'include'), '-I' + str(CSRC)]
-INSTANCES = [('float', 'false'), ('float', 'true'), ('double', 'false'), ('double', 'true')]
+INSTANCES = [(real, mode) for real in ('float', 'double') for mode in ('0', '1', '2')]
 
 
 def stale():

@@ -55,12 +55,13 @@ int worlds_per_cta(const B200Model *m, int limit) {
 struct Shape {
   int wpc, T;
 };
-template <class R, bool C> int prepare_rc(const B200Model *m, const Shape &sh) {
+template <class R, int C> int prepare_rc(const B200Model *m, const Shape &sh) {
   const size_t smem = (size_t)sh.wpc * arena_for(m);
   return sh.T == 32 ? b200::configure_kernels<R, C, 32>(smem) : b200::configure_kernels<R, C, 128>(smem);
 }
-// the kernel variant with GJK / EPA: meshes, or box-box pairs on the convex path
-bool uses_convex(const B200Model *m) { return m->nmesh > 0 || m->boxbox_convex; }
+// the kernel's convex mode: 2 box-box pairs on the convex path (with or
+// without meshes), 1 meshes, 0 neither
+int convex_mode(const B200Model *m) { return m->boxbox_convex ? 2 : m->nmesh > 0 ? 1 : 0; }
 int launch_shape(const B200Model *m, Shape *sh) {
   const int limit = max_optin_smem();
   sh->wpc = worlds_per_cta(m, limit);
@@ -69,20 +70,23 @@ int launch_shape(const B200Model *m, Shape *sh) {
   const int per_sm = ((228 * 1024) / (sh->wpc * arena + 1024)) * sh->wpc;
   sh->T = per_sm <= 3 ? 128 : 32;
   if (sh->T * sh->wpc > 384) sh->wpc = 384 / sh->T;  // the kernels' launch bound
-  const bool convex = uses_convex(m);
-  if (m->real_bytes == 4) return convex ? prepare_rc<float, true>(m, *sh) : prepare_rc<float, false>(m, *sh);
-  return convex ? prepare_rc<double, true>(m, *sh) : prepare_rc<double, false>(m, *sh);
+  const int c = convex_mode(m);
+  if (m->real_bytes == 4)
+    return c == 2 ? prepare_rc<float, 2>(m, *sh) : c ? prepare_rc<float, 1>(m, *sh) : prepare_rc<float, 0>(m, *sh);
+  return c == 2 ? prepare_rc<double, 2>(m, *sh) : c ? prepare_rc<double, 1>(m, *sh) : prepare_rc<double, 0>(m, *sh);
 }
-// kernel instance by precision, mesh support and threads per world
-template <template <class, bool, int> class F, class... A> void dispatch(const B200Model *m, const Shape &sh, A... a) {
-  const bool c = uses_convex(m), t = sh.T == 128;
-  if (m->real_bytes == 4) {
-    if (c) t ? F<float, true, 128>::run(a...) : F<float, true, 32>::run(a...);
-    else t ? F<float, false, 128>::run(a...) : F<float, false, 32>::run(a...);
-  } else {
-    if (c) t ? F<double, true, 128>::run(a...) : F<double, true, 32>::run(a...);
-    else t ? F<double, false, 128>::run(a...) : F<double, false, 32>::run(a...);
-  }
+// kernel instance by precision, convex mode and threads per world
+template <template <class, int, int> class F, class R, int C, class... A> void dispatch_t(bool t128, A... a) {
+  t128 ? F<R, C, 128>::run(a...) : F<R, C, 32>::run(a...);
+}
+template <template <class, int, int> class F, class R, class... A> void dispatch_c(int c, bool t128, A... a) {
+  if (c == 2) dispatch_t<F, R, 2>(t128, a...);
+  else if (c == 1) dispatch_t<F, R, 1>(t128, a...);
+  else dispatch_t<F, R, 0>(t128, a...);
+}
+template <template <class, int, int> class F, class... A> void dispatch(const B200Model *m, const Shape &sh, A... a) {
+  if (m->real_bytes == 4) dispatch_c<F, float>(convex_mode(m), sh.T == 128, a...);
+  else dispatch_c<F, double>(convex_mode(m), sh.T == 128, a...);
 }
 // Worlds sorted by their last control step's work into 256 buckets, heaviest
 // first (a counting sort in one CTA; worlds within a bucket land in arrival
@@ -114,10 +118,10 @@ __global__ void __launch_bounds__(1024) order_worlds(const int *work, int *order
   for (int i = t; i < n; i += blockDim.x) order[atomicAdd(&hist[bucket(i)], 1)] = i;
 }
 
-template <class R, bool C, int T> struct StepLaunch {
+template <class R, int C, int T> struct StepLaunch {
   template <class... A> static void run(A... a) { b200::launch_step<R, C, T>(a...); }
 };
-template <class R, bool C, int T> struct ForwardLaunch {
+template <class R, int C, int T> struct ForwardLaunch {
   template <class... A> static void run(A... a) { b200::launch_forward<R, C, T>(a...); }
 };
 }  // namespace

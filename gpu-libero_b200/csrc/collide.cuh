@@ -674,12 +674,7 @@ template <class R> struct CShape {
   R margin;
 };
 
-// The support point of a shape in direction d.  For a box, *corner receives
-// the support corner's index: bit k set for +size on local axis k (a zero
-// component takes the negative end), the labelling the box manifold reads
-// features from (mjwarp_convex_geometry.cuh convex_support); -1 otherwise.
-template <class R> __device__ V3<R> cs_support(const CShape<R> &s, V3<R> d, int *corner = nullptr) {
-  if (corner) *corner = -1;
+template <class R> __device__ V3<R> cs_support(const CShape<R> &s, V3<R> d) {
   if (s.type == B200_GEOM_SPHERE) return s.pos + d * (s.size.x + R(0.5) * s.margin);
   const V3<R> l = rotT(s.rot, d);
   V3<R> r;
@@ -688,7 +683,6 @@ template <class R> __device__ V3<R> cs_support(const CShape<R> &s, V3<R> d, int 
     r.z += (l.z > R(0) ? R(1) : l.z < R(0) ? R(-1) : R(0)) * s.size.y;
   } else if (s.type == B200_GEOM_BOX) {
     r = v3<R>(l.x > R(0) ? s.size.x : -s.size.x, l.y > R(0) ? s.size.y : -s.size.y, l.z > R(0) ? s.size.z : -s.size.z);
-    if (corner) *corner = int(l.x > R(0)) | int(l.y > R(0)) << 1 | int(l.z > R(0)) << 2;
   } else {
     int best = 0;
     R top = dot(ld3(s.vert), l);
@@ -702,12 +696,26 @@ template <class R> __device__ V3<R> cs_support(const CShape<R> &s, V3<R> d, int 
   if (s.margin > R(0)) p = p + d * (R(0.5) * s.margin);
   return p;
 }
+// A box's support point in direction d and its corner index: bit k set for
+// +size on local axis k (a zero component takes the negative end), the
+// labelling the box manifold reads features from
+// (mjwarp_convex_geometry.cuh convex_support).
+template <class R> __device__ V3<R> box_support(const CShape<R> &s, V3<R> d, int &corner) {
+  const V3<R> l = rotT(s.rot, d);
+  corner = int(l.x > R(0)) | int(l.y > R(0)) << 1 | int(l.z > R(0)) << 2;
+  const V3<R> r = v3<R>(l.x > R(0) ? s.size.x : -s.size.x, l.y > R(0) ? s.size.y : -s.size.y,
+                        l.z > R(0) ? s.size.z : -s.size.z);
+  return rot(s.rot, r) + s.pos;
+}
 
-template <class R> struct Simplex {
+template <class R> struct SimplexCore {
   V3<R> w[4], a[4], b[4];
   R lam[4];
-  int n, ca[4], cb[4];  // box support corners of a and b (-1: not a box)
+  int n;
 };
+// C: the box-box path, which also carries the support corners of a and b
+template <class R, bool C = false> struct Simplex : SimplexCore<R> {};
+template <class R> struct Simplex<R, true> : SimplexCore<R> { int ca[4], cb[4]; };
 
 // Signed-volume distance sub-algorithm (Montanari, Petrinic and Barbieri,
 // "Improving the GJK algorithm for faster and more reliable distance queries
@@ -822,45 +830,53 @@ template <class R> __device__ SvWeights<R> sv_tetrahedron(V3<R> a, V3<R> b, V3<R
 
 // Reduce the simplex to the vertices with nonzero weight (order kept), the
 // weights becoming the affine coordinates of the nearest point.
-template <class R> __device__ void simplex_reduce(Simplex<R> &s) {
+// C (corners): carry the box support corners (the box-box path only)
+template <class R, bool C> __device__ void simplex_reduce(Simplex<R, C> &s) {
   SvWeights<R> W;
   if (s.n == 4) W = sv_tetrahedron(s.w[0], s.w[1], s.w[2], s.w[3]);
   else if (s.n == 3) W = sv_triangle(s.w[0], s.w[1], s.w[2]);
   else if (s.n == 2) W = sv_segment(s.w[0], s.w[1]);
   else W = {{R(1), R(0), R(0), R(0)}};
-  Simplex<R> t;
+  Simplex<R, C> t;
   int k = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i)
     if (i < s.n && W.w[i] != R(0)) {
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        if (j == k) { t.w[j] = s.w[i]; t.a[j] = s.a[i]; t.b[j] = s.b[i]; t.lam[j] = W.w[i]; t.ca[j] = s.ca[i]; t.cb[j] = s.cb[i]; }
+        if (j == k) {
+          t.w[j] = s.w[i]; t.a[j] = s.a[i]; t.b[j] = s.b[i]; t.lam[j] = W.w[i];
+          if constexpr (C) { t.ca[j] = s.ca[i]; t.cb[j] = s.cb[i]; }
+        }
       ++k;
     }
   t.n = k;
   s = t;
 }
 
-template <class R> struct GjkOut {
+template <class R, bool C = false> struct GjkOut {
   bool separated;
   R dist;
   V3<R> x1, x2;
-  Simplex<R> s;
+  Simplex<R, C> s;
 };
 
-template <class R> __device__ GjkOut<R> gjk(const CShape<R> &A, const CShape<R> &B, R tol, int iterations, R cutoff) {
-  GjkOut<R> o;
+template <class R, bool C = false>
+__device__ GjkOut<R, C> gjk(const CShape<R> &A, const CShape<R> &B, R tol, int iterations, R cutoff) {
+  GjkOut<R, C> o;
   o.separated = false;
-  Simplex<R> &s = o.s;
+  Simplex<R, C> &s = o.s;
   s.n = 0;
   V3<R> x = A.pos - B.pos;
   R norm = msqrt(dot(x, x)), prev = -1;
   for (int it = 0; it < iterations; ++it) {
     if (norm < tol || mabs(prev - norm) < R(1e-15)) break;
     const V3<R> d = x * (R(1) / norm);
-    int ca, cb;
-    const V3<R> a = cs_support(A, -d, &ca), b = cs_support(B, d, &cb), w = a - b;
+    int ca = -1, cb = -1;
+    V3<R> a, b;
+    if constexpr (C) { a = box_support(A, -d, ca); b = box_support(B, d, cb); }
+    else { a = cs_support(A, -d); b = cs_support(B, d); }
+    const V3<R> w = a - b;
     if (dot(x, x - w) < R(0.5) * tol * tol) break;
     const R lower = dot(x, w);
     if (lower > R(0) && (cutoff == R(0) || lower >= cutoff * norm)) {
@@ -870,9 +886,12 @@ template <class R> __device__ GjkOut<R> gjk(const CShape<R> &A, const CShape<R> 
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i)
-      if (i == s.n) { s.w[i] = w; s.a[i] = a; s.b[i] = b; s.ca[i] = ca; s.cb[i] = cb; }
+      if (i == s.n) {
+        s.w[i] = w; s.a[i] = a; s.b[i] = b;
+        if constexpr (C) { s.ca[i] = ca; s.cb[i] = cb; }
+      }
     s.n++;
-    simplex_reduce(s);
+    simplex_reduce<R, C>(s);
     if (s.n < 1) break;
     x = v3<R>(0, 0, 0);
 #pragma unroll
@@ -892,18 +911,20 @@ template <class R> __device__ GjkOut<R> gjk(const CShape<R> &A, const CShape<R> 
 }
 
 constexpr int kEpaMaxV = 48, kEpaMaxF = 96;
-template <class R> struct Polytope {
+template <class R> struct PolytopeCore {
   V3<R> w[kEpaMaxV], a[kEpaMaxV], b[kEpaMaxV];
-  int ca[kEpaMaxV], cb[kEpaMaxV];  // box support corners (-1: not a box)
   int nv, nf, face[kEpaMaxF][3];
   V3<R> n[kEpaMaxF];
   R d[kEpaMaxF];
   bool alive[kEpaMaxF];
 };
+// C: the box-box path, which also keeps each vertex's box support corners
+template <class R, bool C = false> struct Polytope : PolytopeCore<R> {};
+template <class R> struct Polytope<R, true> : PolytopeCore<R> { int ca[kEpaMaxV], cb[kEpaMaxV]; };
 
 // Drop the dead faces, keeping the live ones in their order (the best-face
 // search breaks ties by the lower index, so the order is part of the result).
-template <class R> __device__ void epa_compact(Polytope<R> &P) {
+template <class R, bool C> __device__ void epa_compact(Polytope<R, C> &P) {
   int k = 0;
   for (int f = 0; f < P.nf; ++f) {
     if (!P.alive[f]) continue;
@@ -918,7 +939,7 @@ template <class R> __device__ void epa_compact(Polytope<R> &P) {
 
 // New face (i, j, l): its index, -1 for a degenerate triangle, -2 when the
 // face pool is full even after compaction.
-template <class R> __device__ int epa_add_face(Polytope<R> &P, int i, int j, int l) {
+template <class R, bool C> __device__ int epa_add_face(Polytope<R, C> &P, int i, int j, int l) {
   if (P.nf >= kEpaMaxF) epa_compact(P);
   if (P.nf >= kEpaMaxF) return -2;
   V3<R> n = cross(P.w[j] - P.w[i], P.w[l] - P.w[i]);
@@ -931,23 +952,29 @@ template <class R> __device__ int epa_add_face(Polytope<R> &P, int i, int j, int
   return f;
 }
 
-template <class R> __device__ int epa_push(Polytope<R> &P, const CShape<R> &A, const CShape<R> &B, V3<R> d) {
+template <class R, bool C> __device__ int epa_push(Polytope<R, C> &P, const CShape<R> &A, const CShape<R> &B, V3<R> d) {
   if (P.nv >= kEpaMaxV) return -1;
   const int v = P.nv++;
-  P.a[v] = cs_support(A, d, &P.ca[v]); P.b[v] = cs_support(B, -d, &P.cb[v]); P.w[v] = P.a[v] - P.b[v];
+  if constexpr (C) { P.a[v] = box_support(A, d, P.ca[v]); P.b[v] = box_support(B, -d, P.cb[v]); }
+  else { P.a[v] = cs_support(A, d); P.b[v] = cs_support(B, -d); }
+  P.w[v] = P.a[v] - P.b[v];
   return v;
 }
 
-template <class R> __device__ bool epa_seed(Polytope<R> &P, const CShape<R> &A, const CShape<R> &B, const Simplex<R> &s) {
+template <class R, bool C>
+__device__ bool epa_seed(Polytope<R, C> &P, const CShape<R> &A, const CShape<R> &B, const Simplex<R, C> &s) {
   P.nf = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i)
-    if (i < s.n) { P.w[i] = s.w[i]; P.a[i] = s.a[i]; P.b[i] = s.b[i]; P.ca[i] = s.ca[i]; P.cb[i] = s.cb[i]; }
+    if (i < s.n) {
+      P.w[i] = s.w[i]; P.a[i] = s.a[i]; P.b[i] = s.b[i];
+      if constexpr (C) { P.ca[i] = s.ca[i]; P.cb[i] = s.cb[i]; }
+    }
   P.nv = s.n;
   for (int k = 0; P.nv < 2 && k < 6; ++k) {
     V3<R> ax = v3<R>(0, 0, 0);
     ax[k / 2] = k % 2 ? R(-1) : R(1);
-    const int v = epa_push(P, A, B, ax);
+    const int v = epa_push<R, C>(P, A, B, ax);
     if (v == 0) continue;  // an empty simplex (coincident centres): the first vertex seeds
     const V3<R> e = P.w[v] - P.w[0];
     if (dot(e, e) < R(1e-20)) P.nv--;
@@ -961,18 +988,18 @@ template <class R> __device__ bool epa_seed(Polytope<R> &P, const CShape<R> &A, 
     V3<R> ax = v3<R>(0, 0, 0);
     ax[m] = 1;
     const V3<R> d = normalize(cross(e, ax));
-    int v = epa_push(P, A, B, d);
+    int v = epa_push<R, C>(P, A, B, d);
     V3<R> cr = cross(P.w[v] - P.w[0], e);
-    if (dot(cr, cr) < R(1e-20)) { P.nv--; v = epa_push(P, A, B, -d); cr = cross(P.w[v] - P.w[0], e); }
+    if (dot(cr, cr) < R(1e-20)) { P.nv--; v = epa_push<R, C>(P, A, B, -d); cr = cross(P.w[v] - P.w[0], e); }
     if (dot(cr, cr) < R(1e-20)) return false;
   }
   if (P.nv == 3) {
     const V3<R> n = normalize(cross(P.w[1] - P.w[0], P.w[2] - P.w[0]));
-    int v = epa_push(P, A, B, n);
+    int v = epa_push<R, C>(P, A, B, n);
     R h = dot(n, P.w[v] - P.w[0]);
     if (mabs(h) < R(1e-12) || dot(n, P.w[0]) > R(0)) {
       P.nv--;
-      v = epa_push(P, A, B, -n);
+      v = epa_push<R, C>(P, A, B, -n);
       h = dot(n, P.w[v] - P.w[0]);
     }
     if (mabs(h) < R(1e-12)) return false;
@@ -992,29 +1019,31 @@ template <class R> __device__ bool epa_seed(Polytope<R> &P, const CShape<R> &A, 
 // ok: a penetration depth was found; budget: the vertex or face pool filled
 // before EPA converged (it ends with its best face, as at its iteration
 // limit); horizon: the horizon edge list filled (the reference's EPA_HORIZON)
-// face_*: the support points and box corners of the final face's vertices
-// (the box manifold's input)
 template <class R> struct EpaOut {
   bool ok, budget, horizon;
   R depth;
   V3<R> x1, x2;
-  V3<R> face_a[3], face_b[3];
-  int face_ca[3], face_cb[3];
+};
+// the support points and box corners of EPA's final face (the box manifold's input)
+template <class R> struct EpaFace {
+  V3<R> a[3], b[3];
+  int ca[3], cb[3];
 };
 
-// discrete: two zero-margin boxes (polytopes).  EPA then stops when the
-// support distance is within 1e-7 of the face, or when the new support is a
-// corner pair the polytope already holds, which ends it on a face of the
-// Minkowski difference itself (mjwarp_convex_epa.cuh epa_expand).
-template <class R>
-__device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R> &s, R tol, int iterations,
-                         bool discrete = false) {
+// C: two zero-margin boxes (polytopes), with their support corners tracked.
+// EPA then stops when the support distance is within 1e-7 of the face, or
+// when the new support is a corner pair the polytope already holds, which
+// ends it on a face of the Minkowski difference itself
+// (mjwarp_convex_epa.cuh epa_expand), and reports that face in *face.
+template <class R, bool C = false>
+__device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R, C> &s, R tol, int iterations,
+                         EpaFace<R> *face = nullptr) {
   EpaOut<R> o;
   o.ok = false;
   o.budget = o.horizon = false;
-  Polytope<R> P;
-  if (!epa_seed(P, A, B, s)) return o;
-  const R eps = discrete ? R(1e-7) : tol;
+  Polytope<R, C> P;
+  if (!epa_seed<R, C>(P, A, B, s)) return o;
+  const R eps = C ? R(1e-7) : tol;
   int best = -1;
   for (int it = 0; it <= iterations; ++it) {
     best = -1;
@@ -1023,10 +1052,10 @@ __device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R
     if (best < 0) return o;
     if (it == iterations) break;
     const V3<R> n = P.n[best];
-    const int v = epa_push(P, A, B, n);
+    const int v = epa_push<R, C>(P, A, B, n);
     if (v < 0) { o.budget = true; break; }
     if (dot(P.w[v], n) - P.d[best] < eps) { P.nv--; break; }
-    if (discrete) {
+    if constexpr (C) {
       bool repeated = false;
       for (int q = 0; q < v; ++q) repeated |= P.ca[q] == P.ca[v] && P.cb[q] == P.cb[v];
       if (repeated) { P.nv--; break; }
@@ -1063,10 +1092,12 @@ __device__ EpaOut<R> epa(const CShape<R> &A, const CShape<R> &B, const Simplex<R
   o.x1 = P.a[i] * lu + P.a[j] * lv + P.a[l] * lw;
   o.x2 = P.b[i] * lu + P.b[j] * lv + P.b[l] * lw;
   o.depth = P.d[best];
-  const int fv[3] = {i, j, l};
-  for (int k = 0; k < 3; ++k) {
-    o.face_a[k] = P.a[fv[k]]; o.face_b[k] = P.b[fv[k]];
-    o.face_ca[k] = P.ca[fv[k]]; o.face_cb[k] = P.cb[fv[k]];
+  if constexpr (C) {
+    const int fv[3] = {i, j, l};
+    for (int k = 0; k < 3; ++k) {
+      face->a[k] = P.a[fv[k]]; face->b[k] = P.b[fv[k]];
+      face->ca[k] = P.ca[fv[k]]; face->cb[k] = P.cb[fv[k]];
+    }
   }
   o.ok = true;
   return o;
@@ -1288,10 +1319,11 @@ __device__ BoxManifold<R> clip_faces(const V3<R> *ref, int n1, const V3<R> *inc,
   return o;
 }
 // EPA's final face -> the box-box contact manifold (count 0: keep EPA's contact)
-template <class R> __device__ BoxManifold<R> box_manifold(const CShape<R> &A, const CShape<R> &B, const EpaOut<R> &e) {
+template <class R>
+__device__ BoxManifold<R> box_manifold(const CShape<R> &A, const CShape<R> &B, const EpaOut<R> &e, const EpaFace<R> &f) {
   BoxManifold<R> none;
   none.count = 0;
-  const BoxFeature<R> fa = box_feature<R>(e.face_ca, e.face_a), fb = box_feature<R>(e.face_cb, e.face_b);
+  const BoxFeature<R> fa = box_feature<R>(f.ca, f.a), fb = box_feature<R>(f.cb, f.b);
   const V3<R> dir = e.x2 - e.x1;
   BoxNormals<R> na = box_normals(A, fa, -dir), nb = box_normals(B, fb, dir);
   int i = 0, j = 0;
@@ -1380,24 +1412,50 @@ __device__ __noinline__ void convex_pair(const Mdl<R> &M, Arena<R> &A, int pair,
       found = true;
     }
   }
-  // two zero-margin boxes: EPA ends on a face of the Minkowski difference and
-  // the contact becomes a face manifold
-  const bool boxes = S1.type == B200_GEOM_BOX && S2.type == B200_GEOM_BOX && p.margin == R(0);
-  BoxManifold<R> mf;
-  mf.count = 0;
   if (!found) {
     const GjkOut<R> r = gjk(S1, S2, tol, iters, p.gap);
     if (r.separated) return;
     if (r.dist > tol) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
     else {
-      const EpaOut<R> e = epa(S1, S2, r.s, tol, M.m.epa_iterations, boxes);
+      const EpaOut<R> e = epa(S1, S2, r.s, tol, M.m.epa_iterations);
       if (e.budget) atomicOr(&A.iscal[3], B200_WARN_EPA_BUDGET);
       if (e.horizon) atomicOr(&A.iscal[3], B200_OVERFLOW_EPA_HORIZON);
       if (!e.ok) { dist = r.dist; x1 = r.x1; x2 = r.x2; }
-      else {
-        dist = -e.depth; x1 = e.x1; x2 = e.x2;
-        if (boxes) mf = box_manifold(S1, S2, e);
-      }
+      else { dist = -e.depth; x1 = e.x1; x2 = e.x2; }
+    }
+  }
+  if (!(dist < p.gap)) return;
+  const R distance = dist + p.margin;
+  V3<R> fr[3];
+  frame_from_normal(distance <= p.margin ? x1 - x2 : x2 - x1, fr);
+  emit(M, A, p, pair, 0, g1, g2, distance, (x1 + x2) * R(0.5) + origin, fr);
+}
+
+// Two zero-margin boxes on the convex path: GJK and EPA with the boxes'
+// support corners tracked, EPA ending on a face of the Minkowski difference,
+// and that face's manifold of up to four contacts
+// (mjwarp_convex_collision.cuh:63-77).  A separate function so that the
+// other convex pairs carry none of its state.
+template <class R>
+__device__ __noinline__ void convex_box_pair(const Mdl<R> &M, Arena<R> &A, int pair, int g1, int g2) {
+  const Material<R> p = material(M, g1, g2);
+  const V3<R> origin = ld3(A.gxpos + 3 * g1);
+  const CShape<R> S1 = cs_make(M, A, g1, origin, p.margin), S2 = cs_make(M, A, g2, origin, p.margin);
+  const R tol = R(M.m.ccd_tolerance);
+  const GjkOut<R, true> r = gjk<R, true>(S1, S2, tol, M.m.ccd_iterations, p.gap);
+  if (r.separated) return;
+  R dist = r.dist;
+  V3<R> x1 = r.x1, x2 = r.x2;
+  BoxManifold<R> mf;
+  mf.count = 0;
+  if (!(r.dist > tol)) {
+    EpaFace<R> face;
+    const EpaOut<R> e = epa<R, true>(S1, S2, r.s, tol, M.m.epa_iterations, &face);
+    if (e.budget) atomicOr(&A.iscal[3], B200_WARN_EPA_BUDGET);
+    if (e.horizon) atomicOr(&A.iscal[3], B200_OVERFLOW_EPA_HORIZON);
+    if (e.ok) {
+      dist = -e.depth; x1 = e.x1; x2 = e.x2;
+      mf = box_manifold(S1, S2, e, face);
     }
   }
   if (!(dist < p.gap)) return;
@@ -1411,27 +1469,36 @@ __device__ __noinline__ void convex_pair(const Mdl<R> &M, Arena<R> &A, int pair,
 
 // narrowphase family of a candidate pair (-1: filtered out or unsupported):
 // 0 plane-primitive, 1 box family, 2 sphere/capsule, 3 plane-mesh, 4 convex
-template <class R, bool CONVEX> __device__ int pair_family(const Mdl<R> &M, const Arena<R> &A, int pair) {
+template <class R, int CONVEX> __device__ int pair_family(const Mdl<R> &M, const Arena<R> &A, int pair) {
   const int g1 = IF(pair_geom)[2 * pair], g2 = IF(pair_geom)[2 * pair + 1];
   if (!candidate(M, A, g1, g2)) return -1;
   const int t1 = IF(geom_type)[g1], t2 = IF(geom_type)[g2];
   if (t2 == B200_GEOM_MESH) return CONVEX ? (t1 == B200_GEOM_PLANE ? 3 : 4) : -1;
   if (t1 == B200_GEOM_PLANE && t2 >= 2 && t2 <= 6) return 0;
-  if (t1 == B200_GEOM_BOX && t2 == B200_GEOM_BOX && M.m.boxbox_convex) return CONVEX ? 4 : -1;
+  if (t1 == B200_GEOM_BOX && t2 == B200_GEOM_BOX && M.m.boxbox_convex) return CONVEX == 2 ? 4 : -1;
   if (t2 == B200_GEOM_BOX && (t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE || t1 == B200_GEOM_BOX)) return 1;
   if ((t1 == B200_GEOM_SPHERE || t1 == B200_GEOM_CAPSULE) && (t2 == B200_GEOM_SPHERE || t2 == B200_GEOM_CAPSULE))
     return 2;
   return -1;
 }
 
-template <class R, bool CONVEX> __device__ void narrow_pair(const Mdl<R> &M, Arena<R> &A, int pair, int family) {
+template <class R, int CONVEX> __device__ void narrow_pair(const Mdl<R> &M, Arena<R> &A, int pair, int family) {
   const int g1 = IF(pair_geom)[2 * pair], g2 = IF(pair_geom)[2 * pair + 1];
   if (family == 0) plane_pair(M, A, pair, g1, g2);
   else if (family == 1) box_pair(M, A, pair, g1, g2);
   else if (family == 2) prim_pair(M, A, pair, g1, g2);
   else if constexpr (CONVEX) {
     if (family == 3) plane_mesh(M, A, material(M, g1, g2), pair, g1, g2);
-    else if (family == 4) convex_pair(M, A, pair, g1, g2);
+    else if (family == 4) {
+      if constexpr (CONVEX == 2) {
+        if (IF(geom_type)[g1] == B200_GEOM_BOX && IF(geom_type)[g2] == B200_GEOM_BOX &&
+            RF(geom_margin)[g1] + RF(geom_margin)[g2] == R(0)) {
+          convex_box_pair(M, A, pair, g1, g2);
+          return;
+        }
+      }
+      convex_pair(M, A, pair, g1, g2);
+    }
   }
 }
 

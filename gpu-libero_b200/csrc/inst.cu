@@ -1,5 +1,5 @@
-// Kernel instances of one precision (B200_INST_REAL) and mesh support
-// (B200_INST_CONVEX), for one and four warps per world.
+// Kernel instances of one precision (B200_INST_REAL) and convex mode
+// (B200_INST_CONVEX: 0, 1 or 2, see launch.h), for one and four warps per world.
 #include "kernels.cuh"
 
 namespace b200 {

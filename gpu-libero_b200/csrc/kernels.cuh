@@ -561,7 +561,7 @@ template <class R, int T> __device__ void mass_mul(const Mdl<R> &M, const R *Mb,
 // GJK/EPA pairs); models without meshes run the smaller variant.  The G
 // threads [G0, G0 + G) of the world run it; their pair lists start
 // list_offset bytes into the stage-scoped union region.
-template <class R, int T, bool CONVEX, int G0, int G>
+template <class R, int T, int CONVEX, int G0, int G>
 __device__ void collision(const Mdl<R> &M, Arena<R> &A, int list_offset) {
   const B200Model &m = M.m;
   const int gt = TID - G0;
@@ -2343,7 +2343,7 @@ template <class R, int T> __device__ void constraints_and_actuation(const Mdl<R>
 // first warp while its other warps run the broadphase and narrowphase (the
 // collision lists then start after the OSC's scratch in the union region); a
 // one-warp world runs them one after the other.
-template <class R, int T, bool CONVEX> __device__ void collide_and_control(const Mdl<R> &M, Arena<R> &A, bool policy) {
+template <class R, int T, int CONVEX> __device__ void collide_and_control(const Mdl<R> &M, Arena<R> &A, bool policy) {
   if constexpr (T >= 64) {
     if (TID < 32) osc_control<R, T, 32>(M, A, policy);
     else collision<R, T, CONVEX, 32, T - 32>(M, A, Arena<R>::kOscDoubles * (int)sizeof(double));
@@ -2364,7 +2364,7 @@ template <class R, int T> __device__ void newton_stages(const Mdl<R> &M, Arena<R
   if (act) mark<T>(A, 15);
 }
 
-template <class R, bool CONVEX, int T>
+template <class R, int CONVEX, int T>
 __global__ void __launch_bounds__(384, 1) control_step(const __grid_constant__ B200Model m, const __grid_constant__ B200Data d,
                                                      int substeps, int policy, int wpc, int arena) {
   static_assert(T % 32 == 0 && T / 32 <= Arena<R>::kColbufWarps, "per-warp scratch covers at most four warps");
@@ -2437,7 +2437,7 @@ __global__ void __launch_bounds__(384, 1) control_step(const __grid_constant__ B
   }
 }
 
-template <class R, bool CONVEX, int T>
+template <class R, int CONVEX, int T>
 __global__ void __launch_bounds__(384, 1) forward_step(const __grid_constant__ B200Model m, const __grid_constant__ B200Data d,
                                                      int bootstrap, const int *mask, int wpc, int arena) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -2471,17 +2471,17 @@ __global__ void __launch_bounds__(384, 1) forward_step(const __grid_constant__ B
 }  // namespace b200
 
 namespace b200 {
-template <class R, bool C, int T> int configure_kernels(size_t smem) {
+template <class R, int C, int T> int configure_kernels(size_t smem) {
   int rc = (int)cudaFuncSetAttribute(control_step<R, C, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (rc) return rc;
   return (int)cudaFuncSetAttribute(forward_step<R, C, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
-template <class R, bool C, int T>
+template <class R, int C, int T>
 void launch_step(const B200Model &m, const B200Data &d, int substeps, int policy, int wpc, int arena, int grid,
                  size_t smem, cudaStream_t s) {
   control_step<R, C, T><<<grid, T * wpc, smem, s>>>(m, d, substeps, policy, wpc, arena);
 }
-template <class R, bool C, int T>
+template <class R, int C, int T>
 void launch_forward(const B200Model &m, const B200Data &d, int bootstrap, const int *mask, int wpc, int arena,
                     int grid, size_t smem, cudaStream_t s) {
   forward_step<R, C, T><<<grid, T * wpc, smem, s>>>(m, d, bootstrap, mask, wpc, arena);
