@@ -141,7 +141,8 @@ template <class R> __device__ __forceinline__ R jdot(const Mdl<R> &M, const Aren
 }
 
 // ============================================================ position stage
-// forward kinematics, level by level (mjwarp_kinematics.cu:95-212 semantics)
+// forward kinematics (mjwarp_kinematics.cu:95-212 semantics): each body's
+// pose relative to its parent through its joints, composed down the tree
 template <class R, int T> __device__ void kinematics(const Mdl<R> &M, Arena<R> &A) {
   const B200Model &m = M.m;
   if (TID == 0) {
@@ -150,9 +151,85 @@ template <class R, int T> __device__ void kinematics(const Mdl<R> &M, Arena<R> &
   }
   SYNC();
   const int *order = IF(body_order), *lstart = IF(level_start);
-  // tree levels hold few bodies: the world's first warp walks them with warp
-  // barriers; the other warps wait once
-  if (WARP0) {
+  if (m.nbody <= 32) {
+    // one lane per body: each lane forms its body's transform relative to its
+    // parent (the joints' rotations in parallel), then the tree is composed
+    // by pointer jumping, ceil(log2 depth) rounds of shuffles instead of a
+    // walk down every level (the same products, grouped differently)
+    if (WARP0) {
+      const unsigned full = 0xffffffffu;
+      const int b = LANE;
+      V3<R> p = v3<R>(0, 0, 0);
+      Q4<R> q = {R(1), R(0), R(0), R(0)};
+      int anc = 0, parent = 0;
+      bool free_body = false;
+      if (b > 0 && b < m.nbody) {
+        const int first = IF(body_jntadr)[b], count = IF(body_jntnum)[b];
+        parent = anc = IF(body_parentid)[b];
+        if (count == 1 && IF(jnt_type)[first] == B200_JNT_FREE) {
+          const R *qp = A.qpos + IF(jnt_qposadr)[first];
+          p = v3<R>(qp[0], qp[1], qp[2]);
+          q = qnormalize(Q4<R>{qp[3], qp[4], qp[5], qp[6]});
+          anc = parent = 0;
+          free_body = true;
+          st3(A.anchor + 3 * first, p);
+          st3(A.axis + 3 * first, ld3(RF(jnt_axis) + 3 * first));
+        } else {
+          p = ld3(RF(body_pos) + 3 * b);
+          q = ldq(RF(body_quat) + 4 * b);
+          for (int j = first; j < first + count; ++j) {
+            const int kind = IF(jnt_type)[j], qa = IF(jnt_qposadr)[j];
+            const V3<R> lpos = ld3(RF(jnt_pos) + 3 * j), lax = ld3(RF(jnt_axis) + 3 * j);
+            const V3<R> anchor = qrot(lpos, q) + p, axis = qrot(lax, q);  // in the parent's frame
+            if (kind == B200_JNT_BALL) {
+              q = qmul(q, qnormalize(ldq(A.qpos + qa)));
+              p = anchor - qrot(lpos, q);
+            } else if (kind == B200_JNT_SLIDE) {
+              p = p + axis * (A.qpos[qa] - RF(qpos0)[qa]);
+            } else if (kind == B200_JNT_HINGE) {
+              const R angle = (A.qpos[qa] - RF(qpos0)[qa]) * R(0.5);
+              const R s = msin(angle), c = mcos(angle);
+              q = qmul(q, Q4<R>{c, lax.x * s, lax.y * s, lax.z * s});
+              p = anchor - qrot(lpos, q);
+            }
+            st3(A.anchor + 3 * j, anchor);
+            st3(A.axis + 3 * j, axis);
+          }
+          q = qnormalize(q);
+        }
+      }
+      for (int round = 0; round < 5; ++round) {
+        if (!__any_sync(full, anc != 0)) break;
+        const int a = anc;
+        const V3<R> pa = v3<R>(__shfl_sync(full, p.x, a), __shfl_sync(full, p.y, a), __shfl_sync(full, p.z, a));
+        const Q4<R> qa = {__shfl_sync(full, q.w, a), __shfl_sync(full, q.x, a), __shfl_sync(full, q.y, a),
+                          __shfl_sync(full, q.z, a)};
+        const int aa = __shfl_sync(full, anc, a);
+        if (a != 0) {
+          p = pa + qrot(p, qa);
+          q = qnormalize(qmul(qa, q));
+          anc = aa;
+        }
+      }
+      // the joints' anchors and axes: the parent's world transform applied
+      const V3<R> pp = v3<R>(__shfl_sync(full, p.x, parent), __shfl_sync(full, p.y, parent),
+                             __shfl_sync(full, p.z, parent));
+      const Q4<R> qp = {__shfl_sync(full, q.w, parent), __shfl_sync(full, q.x, parent),
+                        __shfl_sync(full, q.y, parent), __shfl_sync(full, q.z, parent)};
+      if (b > 0 && b < m.nbody) {
+        st3(A.xpos + 3 * b, p);
+        stq(A.xquat + 4 * b, q);
+        if (!free_body) {
+          const int first = IF(body_jntadr)[b], count = IF(body_jntnum)[b];
+          for (int j = first; j < first + count; ++j) {
+            st3(A.anchor + 3 * j, pp + qrot(ld3(A.anchor + 3 * j), qp));
+            st3(A.axis + 3 * j, qrot(ld3(A.axis + 3 * j), qp));
+          }
+        }
+      }
+      __syncwarp();
+    }
+  } else if (WARP0) {  // larger trees: the world's first warp walks the levels with warp barriers
     for (int level = 1; level < m.nlevel; ++level) {
       const int a = lstart[level], n = lstart[level + 1] - a;
       for (int k = LANE; k < n; k += 32) {
@@ -1066,9 +1143,77 @@ template <class R, int T> __device__ void velocity(const Mdl<R> &M, Arena<R> &A)
   }
   SYNC();
   const int *order = IF(body_order), *lstart = IF(level_start);
-  // tree levels hold few bodies: the world's first warp walks them with warp
-  // barriers; the other warps wait once
-  if (WARP0) {
+  if (m.nbody <= 32) {
+    // one lane per body, as in the kinematics: each body's own velocity
+    // increment, a pointer-jumping sum down the tree, then the bias
+    // accelerations from the parents' velocities and a second sum
+    if (WARP0) {
+      const unsigned full = 0xffffffffu;
+      const int b = LANE;
+      const bool body = b > 0 && b < m.nbody;
+      int parent = body ? IF(body_parentid)[b] : 0, anc = parent;
+      R lv[6] = {0, 0, 0, 0, 0, 0};
+      const int d0 = body ? IF(body_dofadr)[b] : 0, nd = body ? IF(body_dofnum)[b] : 0;
+      for (int i = 0; i < nd; ++i)
+        for (int c = 0; c < 6; ++c) lv[c] += A.cdof[6 * (d0 + i) + c] * A.qvel[d0 + i];
+      for (int round = 0; round < 5; ++round) {
+        if (!__any_sync(full, anc != 0)) break;
+        const int a = anc;
+        R add[6];
+        for (int c = 0; c < 6; ++c) add[c] = __shfl_sync(full, lv[c], a);
+        const int aa = __shfl_sync(full, anc, a);
+        if (a != 0) {
+          for (int c = 0; c < 6; ++c) lv[c] += add[c];
+          anc = aa;
+        }
+      }
+      R vel[6], la[6] = {0, 0, 0, 0, 0, 0};
+      for (int c = 0; c < 6; ++c) vel[c] = __shfl_sync(full, lv[c], parent);
+      if (parent == 0)
+        for (int c = 0; c < 6; ++c) vel[c] = 0;
+      if (body) {
+        int dof = d0;
+        const int j0 = IF(body_jntadr)[b], j1 = j0 + IF(body_jntnum)[b];
+        for (int j = j0; j < j1; ++j) {
+          const int type = IF(jnt_type)[j];
+          if (type == B200_JNT_FREE) {
+            for (int i = 0; i < 3; ++i) {
+              for (int c = 0; c < 6; ++c) vel[c] += A.cdof[6 * (dof + i) + c] * A.qvel[dof + i];
+              for (int c = 0; c < 6; ++c) A.cdof_dot[6 * (dof + i) + c] = 0;
+            }
+            dof += 3;
+          }
+          const int width = type == B200_JNT_FREE || type == B200_JNT_BALL ? 3 : 1;
+          for (int i = 0; i < width; ++i) {
+            R dd[6];
+            motion_cross(vel, A.cdof + 6 * (dof + i), dd);
+            for (int c = 0; c < 6; ++c) {
+              A.cdof_dot[6 * (dof + i) + c] = dd[c];
+              la[c] += dd[c] * A.qvel[dof + i];
+            }
+          }
+          for (int i = 0; i < width; ++i)
+            for (int c = 0; c < 6; ++c) vel[c] += A.cdof[6 * (dof + i) + c] * A.qvel[dof + i];
+          dof += width;
+        }
+      }
+      anc = parent;
+      for (int round = 0; round < 5; ++round) {
+        if (!__any_sync(full, anc != 0)) break;
+        const int a = anc;
+        R add[6];
+        for (int c = 0; c < 6; ++c) add[c] = __shfl_sync(full, la[c], a);
+        const int aa = __shfl_sync(full, anc, a);
+        if (a != 0) {
+          for (int c = 0; c < 6; ++c) la[c] += add[c];
+          anc = aa;
+        }
+      }
+      if (body)
+        for (int c = 0; c < 6; ++c) { A.cvel[6 * b + c] = lv[c]; A.cacc[6 * b + c] = A.cacc[c] + la[c]; }
+      __syncwarp();
+    }
+  } else if (WARP0) {  // larger trees: the world's first warp walks the levels with warp barriers
     for (int level = 1; level < m.nlevel; ++level) {
       const int a = lstart[level], n = lstart[level + 1] - a;
       for (int k = LANE; k < n; k += 32) {
