@@ -66,6 +66,9 @@ def parse():
     p.add_argument('--seed', type=int, default=0)
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-gather', action='store_true', help='skip the per-step observation all-gather (N > 1)')
+    p.add_argument('--model-rows', type=int, default=0,
+                   help='per-world parameter rows: K seeded rows of body masses (x U[0.8, 1.2]) and geom sliding '
+                        'frictions (x U[0.5, 1.5]); world w runs row w %% K (0: one shared model)')
     return p.parse_args()
 
 
@@ -123,12 +126,12 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU path
-def cpu_run(scene, worlds, steps, warmup, seed, threads, precision='fp64'):
+def cpu_run(scene, worlds, steps, warmup, seed, threads, precision='fp64', rows=None):
     """The reference's CPU path restated (C oracle port), threads over worlds.
     FP64 by default: the reference's own CPU path is FP64 CPU MuJoCo."""
     from gpu_libero_b200 import native
     Oracle = entry.load_oracle().Oracle
-    packed = native.PackedModel(scene, precision)
+    packed = native.PackedModel(scene, precision, rows=rows)
     host = native.alloc_numpy(packed, worlds)
     q, v = scene.initial_state(worlds, seed=seed)
     host['qpos'][:] = q
@@ -177,12 +180,12 @@ CPU_NOTE = ('the reference CPU path, CPU MuJoCo 2.3.7 FP64, is not installed her
             'of the reference substep (oracle/) runs instead, one world per host thread at a time')
 
 
-def cpu_baseline(scene, seed, budget_s=12.0):
+def cpu_baseline(scene, seed, rows=None, budget_s=12.0):
     threads = host_threads()
     worlds = 4 * threads
-    probe = cpu_run(scene, worlds, 1, 0, seed, threads)
+    probe = cpu_run(scene, worlds, 1, 0, seed, threads, rows=rows)
     steps = int(max(1, min(40, budget_s / max(probe, 1e-3))))
-    secs = cpu_run(scene, worlds, steps, 0, seed, threads)
+    secs = cpu_run(scene, worlds, steps, 0, seed, threads, rows=rows)
     return dict(value=worlds * steps / secs, unit=UNIT, cores=threads, physical_cores=physical_cores(), kind='port',
                 precision='f64',
                 sample='%d worlds x %d control steps (25 substeps) of %s on %d host threads; %s'
@@ -195,7 +198,8 @@ def reference_arm(args, scene):
         return
     threads = host_threads()
     worlds = 4 * threads
-    secs = cpu_run(scene, worlds, args.steps, args.warmup, args.seed, threads)
+    secs = cpu_run(scene, worlds, args.steps, args.warmup, args.seed, threads,
+                   rows=model_rows(scene, args.model_rows, args.seed))
     value = worlds * args.steps / secs
     sample = '%d worlds per control step on %d host threads (%s physical cores); %s' % (
         worlds, threads, physical_cores(), CPU_NOTE)
@@ -204,12 +208,25 @@ def reference_arm(args, scene):
                 vs_baseline=None, dtype='f64', data='synthetic (seeded %s states and actions)' % scene.name,
                 # the workload is the GPU arm's; each step of this arm is a bounded host sample of it
                 config=dict(workload=WORKLOADS[scene.name], worlds_per_gpu=args.worlds, substeps=scene.substeps,
-                            host_sample_worlds=worlds, host_threads=threads),
+                            host_sample_worlds=worlds, host_threads=threads, model_rows=args.model_rows or None),
                 substeps_per_sec=value * scene.substeps,
                 cpu_baseline=dict(value=value, unit=UNIT, cores=threads, physical_cores=physical_cores(),
                                   kind='port', precision='f64', sample=sample),
                 e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
+
+
+def model_rows(scene, k, seed):
+    """K seeded per-world parameter rows (mass and friction randomisation), or None."""
+    if k <= 0:
+        return None
+    rng = np.random.default_rng([seed, 0x5EED])
+    mass = np.asarray(scene.reals['body_mass'], np.float64)
+    friction = np.asarray(scene.reals['geom_friction'], np.float64).reshape(-1, 3)
+    rows_mass = mass[None] * rng.uniform(0.8, 1.2, (k, mass.size))
+    rows_friction = np.repeat(friction[None], k, axis=0)
+    rows_friction[:, :, 0] *= rng.uniform(0.5, 1.5, (k, friction.shape[0]))
+    return {'body_mass': rows_mass, 'geom_friction': rows_friction.reshape(k, -1)}
 
 
 # ---------------------------------------------------------------- GPU path
@@ -245,7 +262,8 @@ def main():
         dist.init_process_group('nccl', device_id=dev, timeout=timedelta(seconds=120))
     W = args.worlds
     offset = rank * W
-    rt = Runtime(scene, W, device=dev, precision=args.precision, world_offset=offset)
+    rows = model_rows(scene, args.model_rows, args.seed)
+    rt = Runtime(scene, W, device=dev, precision=args.precision, world_offset=offset, model_rows=rows)
     q, v = scene.initial_state(W, seed=args.seed, world_offset=offset)
     rt.set_state(np.concatenate([np.zeros((W, 1)), q, v], axis=1))
     rt.check()
@@ -332,7 +350,8 @@ def main():
     traffic = TRAFFIC_BYTES_PER_WORLD[args.scene] * W if args.precision == 'fp32' else None
 
     # e2e through the public API (pinned H2D actions, D2H observations)
-    env = B200BatchEnv(scene, W, device=dev, precision=args.precision, seed=args.seed, world_offset=offset)
+    env = B200BatchEnv(scene, W, device=dev, precision=args.precision, seed=args.seed, world_offset=offset,
+                       model_rows=rows)
     env.runtime.prepare_control_graph()
     host_actions = [scene.actions(W, k, seed=args.seed, world_offset=offset) for k in range(total)]
     for k in range(args.warmup):
@@ -354,7 +373,7 @@ def main():
 
     base = None
     if rank == 0 and world_size == 1 and not args.no_cpu_baseline:
-        base = cpu_baseline(scene, args.seed)
+        base = cpu_baseline(scene, args.seed, rows)
     if rank == 0:
         value = world_size * W * args.steps / elapsed_max
         line = dict(
@@ -364,6 +383,7 @@ def main():
             config=dict(workload=WORKLOADS[scene.name],
                         worlds_per_gpu=W, total_worlds=W * world_size, substeps=scene.substeps,
                         parallelism='world shards, one process per GPU', l2='flushed (256 MiB write) between steps',
+                        model_rows=args.model_rows or None,
                         obs_gather=('NCCL all-gather of the [W, %d] observation slab every step, side stream, '
                                     '%d bytes per step' % (scene.sizes['nobs'], gather.bytes_per_launch())
                                     if gather else None)),

@@ -19,7 +19,8 @@ constexpr size_t kSm100OptinSmem = 227 * 1024;
 bool model_ok(const B200Model *m) {
   return m && m->real && m->ints && (m->real_bytes == 4 || m->real_bytes == 8) && m->nv >= 1 && m->nv <= 128 &&
          m->nbody >= 2 && m->ncon_max >= 1 && m->nefc_max >= 1 && m->nefc_max <= 65535 && m->nvs >= m->nv && m->nsite > m->ee_site &&
-         m->nu >= 9 && m->ntree >= 1 && m->ntree <= 32 && m->kmax_dof >= m->max_tree_dofs;
+         m->nu >= 9 && m->ntree >= 1 && m->ntree <= 32 && m->kmax_dof >= m->max_tree_dofs &&
+         m->nvariant >= 0 && m->variant_stride >= 0;
 }
 bool data_ok(const B200Data *d) {
   return d && d->nworld >= 0 && d->qpos && d->qvel && d->qacc_warmstart && d->ctrl && d->time && d->goal_pos &&

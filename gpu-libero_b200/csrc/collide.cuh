@@ -28,8 +28,16 @@ template <class R> struct Mdl {
   const B200Model &m;
   const R *f;
   const int *i;
-  __device__ Mdl(const B200Model &m_) : m(m_), f((const R *)m_.real), i(m_.ints) {}
+  // row: the world's copy of the real arrays (per-world parameter rows)
+  __device__ Mdl(const B200Model &m_, int row = 0)
+      : m(m_), f((const R *)m_.real + (size_t)row * (size_t)m_.variant_stride), i(m_.ints) {}
 };
+// The parameter row of world w of a shard: the global world index modulo the
+// number of rows (mjwarp_constraint_build.cu:18-20, w % p.rows), so that a
+// world's parameters do not depend on how worlds are split over GPUs.
+__device__ inline int model_row(const B200Model &m, int world_offset, int w) {
+  return m.nvariant > 1 ? (int)(((long long)world_offset + w) % m.nvariant) : 0;
+}
 #define RF(name) (M.f + M.m.off_##name)
 #define IF(name) (M.i + M.m.off_##name)
 

@@ -2341,7 +2341,7 @@ __device__ __noinline__ void store_state(const B200Model &m, const B200Data &d, 
   // observation slab: arm+gripper qpos/qvel (current), end-effector pose and
   // free-body poses (last substep's kinematics, as MuJoCo publishes them)
   if (obs && (dst = row_of<R>(d.obs, w, m.nobs))) {
-    const Mdl<R> M(m);
+    const Mdl<R> M(m, model_row(m, d.world_offset, w));
     FOR(e, m.nobs) {
       R v = 0;
       if (e < 18) {
@@ -2390,7 +2390,7 @@ template <class R, int T> __device__ __noinline__ void store_outputs(const B200M
   if ((dst = row_of<R>(d.qacc_smooth, w, nv))) FOR(i, nv) dst[i] = A.qacc_smooth[i];
   if ((dst = row_of<R>(d.qfrc_smooth, w, nv))) FOR(i, nv) dst[i] = A.qfrc_smooth[i];
   if ((dst = row_of<R>(d.qM, w, nv * nv))) {
-    const Mdl<R> M(m);
+    const Mdl<R> M(m, model_row(m, d.world_offset, w));
     FOR(e, nv * nv) {  // the tree blocks expanded to dense dof order
       const int i = e / nv, j = e % nv, t = IF(dof_treeid)[i], a = IF(tree_dofadr)[t], n = IF(tree_dofnum)[t];
       dst[e] = IF(dof_treeid)[j] == t ? A.M[IF(tree_madr)[t] + (i - a) * n + (j - a)] : R(0);
@@ -2409,7 +2409,7 @@ template <class R, int T> __device__ __noinline__ void store_outputs(const B200M
   if ((dst = row_of<R>(d.efc_D, w, m.nefc_max))) FOR(r, nefc) dst[r] = A.efc_D[r];
   if ((dst = row_of<R>(d.efc_aref, w, m.nefc_max))) FOR(r, nefc) dst[r] = A.efc_aref[r];
   if ((dst = row_of<R>(d.efc_J, w, m.nefc_max * nv))) {
-    const Mdl<R> M(m);
+    const Mdl<R> M(m, model_row(m, d.world_offset, w));
     FOR(e, nefc * nv) {  // rows expanded to dense dof order
       const int r = e / nv, dof = e % nv, t0 = A.row_t[2 * r], t1 = A.row_t[2 * r + 1];
       const int n0 = t0 >= 0 ? IF(tree_dofnum)[t0] : 0, td = IF(dof_treeid)[dof], off = dof - IF(tree_dofadr)[td];
@@ -2529,7 +2529,7 @@ __global__ void __launch_bounds__(384, 1) control_step(const __grid_constant__ B
   Arena<R> &A = *reinterpret_cast<Arena<R> *>(wbase);
   if (slot < wpc && TID == 0) Arena<R>::layout(m, T, &A, wbase);
   __syncthreads();
-  const Mdl<R> M(m);
+  const Mdl<R> M(m, model_row(m, d.world_offset, w));
   if (act) {
     load_world<R, T>(m, d, A, w);
     if (TID == 0 && d.stage_cycles) {
@@ -2592,7 +2592,7 @@ __global__ void __launch_bounds__(384, 1) forward_step(const __grid_constant__ B
   Arena<R> &A = *reinterpret_cast<Arena<R> *>(wbase);
   if (slot < wpc && TID == 0) Arena<R>::layout(m, T, &A, wbase);
   __syncthreads();
-  const Mdl<R> M(m);
+  const Mdl<R> M(m, model_row(m, d.world_offset, w));
   if (act) load_world<R, T>(m, d, A, w);
   __syncthreads();
   position_velocity_stages<R, T>(M, A, act);

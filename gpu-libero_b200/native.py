@@ -76,15 +76,32 @@ def evaluate(expr, sizes):
     return int(eval(expr, {'__builtins__': {}}, dict(sizes)))
 
 
-class PackedModel:
-    """A scene's arrays packed into one real buffer and one int32 buffer."""
+# packed parameter rows larger than this are refused (the copies live in HBM
+# and are read through L2 by every world of their residue class)
+MAX_ROW_BYTES = 1 << 32
 
-    def __init__(self, scene, precision='fp32'):
+
+class PackedModel:
+    """A scene's arrays packed into one real buffer and one int32 buffer.
+
+    rows: per-world parameter rows, {real array name: array of P rows}, each
+    row the array's full length (a [P, ...] array is flattened per row).  World
+    w (global index) reads row w % P of each such array, the reference's
+    broadcast rule (cuda/dynamics/mjwarp_constraint_build.cu:18-20,
+    ``p.data + (w % p.rows) * width``).  The real buffer then holds
+    nvariant = lcm(P, ...) copies of every real array, variant_stride reals
+    apart; copy v carries row v % P of each array given, and the scene's own
+    values elsewhere.  Arrays derived from others (geom_aabb / geom_rbound from
+    geom sizes, body_invweight0 / dof_invweight0 from masses) are not
+    recomputed: give their rows too, or build the rows from compiled scenes
+    with scene.parameter_rows.  Int arrays and scalars are one per model."""
+
+    def __init__(self, scene, precision='fp32', rows=None):
         self.scene = scene
         self.dtype = np.float32 if precision in ('fp32', 'float32') else np.float64
         self.sizes = dict(scene.sizes)
         self.sizes['real_bytes'] = np.dtype(self.dtype).itemsize
-        ints, reals, self.offsets = [], [], {}
+        ints, reals, self.offsets, lengths = [], [], {}, {}
         at = 0
         for name, expr in LAYOUT.int_arrays:
             n = evaluate(expr, self.sizes)
@@ -103,8 +120,43 @@ class PackedModel:
                 raise ValueError('model real array %s has %d entries, expected %d' % (name, value.size, n))
             reals.append(value)
             self.offsets[name] = at
+            lengths[name] = n
             at += n
-        self.reals = np.ascontiguousarray(np.concatenate(reals + [np.zeros(1)]).astype(self.dtype))
+        base = np.concatenate(reals + [np.zeros(1)])
+        # one copy per parameter row, each starting on a 128-byte boundary
+        stride = -(-base.size // 32) * 32
+        table = {}
+        for name, value in (rows or {}).items():
+            if name not in lengths:
+                raise ValueError('parameter rows for %r: not a model real array' % (name,))
+            value = np.asarray(value, np.float64)
+            if value.ndim >= 1 and value.shape[0] >= 1:
+                value = value.reshape(value.shape[0], -1)
+            if value.ndim != 2 or value.shape[0] < 1 or value.shape[1] != lengths[name]:
+                raise ValueError('parameter rows for %s: expected [P >= 1, %d] values, got shape %s'
+                                 % (name, lengths[name], np.shape(value)))
+            if not np.all(np.isfinite(value)):
+                raise ValueError('parameter rows for %s hold non-finite values' % name)
+            table[name] = value
+        nvariant = 1
+        for value in table.values():
+            nvariant = int(np.lcm(nvariant, value.shape[0]))
+            if nvariant * stride * self.sizes['real_bytes'] > MAX_ROW_BYTES:
+                raise ValueError('parameter rows need %d model copies (the lcm of their row counts); '
+                                 'more than %d bytes' % (nvariant, MAX_ROW_BYTES))
+        packed = np.zeros((nvariant, stride))
+        packed[:, :base.size] = base
+        for name, value in table.items():
+            o = self.offsets[name]
+            packed[:, o:o + lengths[name]] = value[np.arange(nvariant) % value.shape[0]]
+        self.nvariant, self.variant_stride = nvariant, stride
+        self.sizes['nvariant'], self.sizes['variant_stride'] = nvariant, stride
+        self.reals = np.ascontiguousarray(packed.reshape(-1).astype(self.dtype))
+
+    def row_values(self, name, world):
+        """The values of real array `name` that global world `world` reads."""
+        o = self.offsets[name] + (world % self.nvariant) * self.variant_stride
+        return self.reals[o:o + evaluate(dict(LAYOUT.real_arrays)[name], self.sizes)]
 
     def struct(self, real_ptr, int_ptr):
         m = B200Model()

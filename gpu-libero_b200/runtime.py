@@ -46,7 +46,7 @@ class Runtime:
     """Owned device buffers plus the control-step graph of one world shard."""
 
     def __init__(self, scene, num_envs, *, device='cuda:0', precision='fp32', world_offset=0, library=None,
-                 debug=False, regroup=True):
+                 debug=False, regroup=True, model_rows=None):
         if not torch.cuda.is_available():
             raise RuntimeError('the b200 physics engine requires a CUDA device')
         self.device = torch.device(device)
@@ -54,7 +54,9 @@ class Runtime:
         self.n = int(num_envs)
         self.world_offset = int(world_offset)
         self.lib = library or native.Library()
-        self.packed = native.PackedModel(scene, precision)
+        # model_rows: per-world parameter rows (native.PackedModel); world
+        # world_offset + i of the whole batch reads row (world_offset + i) % P
+        self.packed = native.PackedModel(scene, precision, rows=model_rows)
         self.dtype = torch.float32 if self.packed.dtype == np.float32 else torch.float64
         with torch.cuda.device(self.device):
             self.model_real = torch.from_numpy(self.packed.reals).to(self.device)
@@ -223,7 +225,7 @@ class B200BatchEnv:
     physics_engine = 'b200'
 
     def __init__(self, scene=None, num_envs=8, *, init_states=None, seed=0, device='cuda:0', precision='fp32',
-                 physics_engine='b200', cuda_options=None, world_offset=0):
+                 physics_engine='b200', cuda_options=None, world_offset=0, model_rows=None):
         if physics_engine != 'b200':
             raise ValueError('B200BatchEnv serves physics_engine="b200"')
         if type(num_envs) is not int or num_envs < 1:
@@ -241,7 +243,8 @@ class B200BatchEnv:
         self.seed_value = seed
         self.world_offset = world_offset
         self._lock = RLock()
-        self.runtime = Runtime(self.scene, num_envs, device=device, precision=precision, world_offset=world_offset)
+        self.runtime = Runtime(self.scene, num_envs, device=device, precision=precision, world_offset=world_offset,
+                               model_rows=model_rows)
         self.nq, self.nv = self.scene.sizes['nq'], self.scene.sizes['nv']
         self._closed = self._failed = False
         self._integrations = np.zeros(num_envs, np.int64)

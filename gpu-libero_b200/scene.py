@@ -816,6 +816,40 @@ class _Site(dict):
         return self['name']
 
 
+def parameter_rows(scenes):
+    """Per-world parameter rows from compiled scenes of one topology.
+
+    Returns {real array name: [len(scenes), length]} for every real array
+    that differs between the scenes; with native.PackedModel(scenes[0],
+    rows=...) world w then runs scenes[w % len(scenes)]'s arrays, derived ones
+    included (inertias, AABBs, invweights).  The scenes must agree on sizes,
+    int arrays, scalars and options, except meaninertia, which stays the first
+    scene's (one value per model: the reference's Newton leaves take
+    m.stat.meaninertia as one scalar, host/runtime/newton/mjwarp_linesearch.py:79)."""
+    scenes = list(scenes)
+    if not scenes:
+        raise ValueError('parameter_rows needs at least one scene')
+    first = scenes[0]
+    for k, other in enumerate(scenes[1:], 1):
+        if other.sizes != first.sizes:
+            raise ValueError('scene %d has other sizes than scene 0' % k)
+        for name, value in first.ints.items():
+            if not np.array_equal(np.asarray(value), np.asarray(other.ints[name])):
+                raise ValueError('scene %d differs from scene 0 in int array %s (topology)' % (k, name))
+        for name, value in first.scalars.items():
+            if name != 'meaninertia' and value != other.scalars[name]:
+                raise ValueError('scene %d differs from scene 0 in scalar %s' % (k, name))
+        for name in set(first.options) | set(other.options):
+            if first.options.get(name) != other.options.get(name):
+                raise ValueError('scene %d differs from scene 0 in scalar option %s' % (k, name))
+    rows = {}
+    for name in first.reals:
+        stack = np.stack([np.asarray(sc.reals[name], np.float64).reshape(-1) for sc in scenes])
+        if np.any(stack != stack[0]):
+            rows[name] = stack
+    return rows
+
+
 def _panda(bodies, link_radius=0.06, box_margin=0.001):
     """Append a Franka-like arm (7 hinges + 2 finger slides) under the world;
     the finger pads are boxes with margin `box_margin`."""

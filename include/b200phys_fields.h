@@ -36,6 +36,15 @@
  * margin (the reference's has_boxbox_margin rule, cuda_fp32/model.py:187-191,
  * physics.py:89-90).  Such a model runs the kernel variant with convex support.
  *
+ * nvariant / variant_stride: per-world model parameter rows.  The real
+ * buffer holds max(nvariant, 1) copies of every real array, variant_stride
+ * reals apart (offsets off_* are within one copy); world w of a shard reads
+ * copy (world_offset + w) % nvariant, the reference's broadcast rule
+ * parameter(p, w) = p.data + (w % p.rows) * width
+ * (cuda/dynamics/mjwarp_constraint_build.cu:18-20).  The int arrays (the
+ * topology) and the real scalars (timestep, gravity, impratio, tolerances,
+ * meaninertia) are one per model.  nvariant 0 or 1 is one shared model.
+ *
  * task_body / task_lift_z: the synthetic scenes' task predicate.  Success is
  * the free body free_bodyid[task_body] (its centre of mass frame origin) above
  * task_lift_z; reward = 1 and done = 1 on success, else 0 (LIBERO's sparse
@@ -51,7 +60,8 @@
   X(iterations) X(ls_iterations) X(disable_flags) X(ee_site) X(real_bytes) \
   X(nvs) X(kmax_dof) X(max_tree_dofs) X(osc_uncouple) X(nfree) X(nobs) \
   X(nmesh) X(nmeshvert) X(nmeshpoly) X(nmeshpolyvert) X(nmeshpolymap) \
-  X(ccd_iterations) X(epa_iterations) X(nL) X(task_body) X(boxbox_convex)
+  X(ccd_iterations) X(epa_iterations) X(nL) X(task_body) X(boxbox_convex) \
+  X(nvariant) X(variant_stride)
 
 /* real scalars of the model (stored as double, read as the kernel's real) */
 #define B200_MODEL_REAL_SCALARS(X) \

@@ -1835,16 +1835,28 @@ static void step1(const B200Model *m, Work *k, const real *qpos, const real *qve
 
 static int check_model(const B200Model *m) {
   return m && m->real_bytes == (int)sizeof(real) && m->nbody <= MAXB && m->nv <= MAXV && m->ngeom <= MAXG &&
-         m->nsite <= 8 && m->nu <= 16;
+         m->nsite <= 8 && m->nu <= 16 && m->nvariant >= 0 && m->variant_stride >= 0;
+}
+
+/* The model as world w of the shard sees it: the real arrays of its parameter
+ * row, (world_offset + w) % nvariant (mjwarp_constraint_build.cu:18-20). */
+static B200Model world_model(const B200Model *base, const B200Data *d, int w) {
+  B200Model m = *base;
+  if (base->nvariant > 1) {
+    long long row = ((long long)d->world_offset + w) % base->nvariant;
+    m.real = (const real *)base->real + (size_t)row * (size_t)base->variant_stride;
+  }
+  return m;
 }
 
 /* Advance worlds [w0, w1) by `substeps` substeps (reference control graph). */
-int oracle_step(const B200Model *m, const B200Data *d, int w0, int w1, int substeps, int policy) {
-  if (!check_model(m)) return 1;
+int oracle_step(const B200Model *base, const B200Data *d, int w0, int w1, int substeps, int policy) {
+  if (!check_model(base)) return 1;
   Work *k = (Work *)calloc(1, sizeof(Work));
   if (!k) return 2;
-  int nq = m->nq, nv = m->nv, nu = m->nu;
+  int nq = base->nq, nv = base->nv, nu = base->nu;
   for (int w = w0; w < w1; ++w) {
+    const B200Model mw = world_model(base, d, w), *m = &mw;
     real *qpos = DR(qpos, w, nq), *qvel = DR(qvel, w, nv), *warm = DR(qacc_warmstart, w, nv);
     int *overflow = DI(overflow, w, 1), *error = DI(error, w, 1);
     if (bad_state(m, qpos, qvel)) *overflow |= B200_STATUS_BADSTATE;
@@ -1883,12 +1895,13 @@ int oracle_step(const B200Model *m, const B200Data *d, int w0, int w1, int subst
 }
 
 /* Forward only (reference Physics.forward): no integration. */
-int oracle_forward(const B200Model *m, const B200Data *d, int w0, int w1, int bootstrap) {
-  if (!check_model(m)) return 1;
+int oracle_forward(const B200Model *base, const B200Data *d, int w0, int w1, int bootstrap) {
+  if (!check_model(base)) return 1;
   Work *k = (Work *)calloc(1, sizeof(Work));
   if (!k) return 2;
-  int nq = m->nq, nv = m->nv, nu = m->nu;
+  int nq = base->nq, nv = base->nv, nu = base->nu;
   for (int w = w0; w < w1; ++w) {
+    const B200Model mw = world_model(base, d, w), *m = &mw;
     real *qpos = DR(qpos, w, nq), *qvel = DR(qvel, w, nv), *warm = DR(qacc_warmstart, w, nv);
     if (bad_state(m, qpos, qvel)) *DI(overflow, w, 1) |= B200_STATUS_BADSTATE;
     step1(m, k, qpos, qvel);
