@@ -63,6 +63,7 @@ template <class R> struct Arena {
                // [11] islands [12] largest island [13] single-dof rows [14] refactor Newton H
                // [15] sum of row widths k_r [16..19] OSC factor flags [20..22] pinv flags
                // [23] sum of k_r^2 [24] factored block work (n^3 + 6 n^2)
+               // [25] GJK / EPA pairs past the broadphase this substep
   R *red;    // reduction scratch: up to 9 values per warp of the world
   long long *prof;  // [0] last stamp, [1..15] per-stage cycle sums (stage profiling only)
   int ubytes;       // size of the stage-scoped union region (H, OSC and kinematics scratch)

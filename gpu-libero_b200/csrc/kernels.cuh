@@ -610,16 +610,9 @@ __device__ void tree_solve(const Mdl<R> &M, R *L, R *x, R *colbuf, bool factor) 
 }
 
 // lower triangles of the dense tree blocks of M into packed blocks at tree_padr
+// (tree_lsrc: each packed entry's index in the dense blocks, from the host)
 template <class R, int T> __device__ void pack_tree_blocks(const Mdl<R> &M, const R *Mb, R *P) {
-  FOR(e, M.m.nL) {
-    int t = 0;
-    while (t + 1 < M.m.ntree && IF(tree_padr)[t + 1] <= e) ++t;
-    const int loc = e - IF(tree_padr)[t], n = IF(tree_dofnum)[t];
-    int a = (int)((msqrt(8.0f * loc + 1.0f) - 1.0f) * 0.5f);
-    while (tri(a, 0) > loc) --a;
-    while (tri(a + 1, 0) <= loc) ++a;
-    P[e] = Mb[IF(tree_madr)[t] + a * n + (loc - tri(a, 0))];
-  }
+  FOR(e, M.m.nL) P[e] = Mb[IF(tree_lsrc)[e]];
 }
 
 // y = M x with the dense tree blocks (one thread per dof)
@@ -650,7 +643,7 @@ __device__ void collision(const Mdl<R> &M, Arena<R> &A, int list_offset) {
   int *fam = (int *)((unsigned char *)A.H + list_offset), *cnt = fam + m.npair, *fill = cnt + kFam,
       *list = fill + kFam;
   const bool grouped = list_offset + (2 * m.npair + 2 * kFam) * (int)sizeof(int) <= A.ubytes;
-  if (gt == 0) A.iscal[8] = 0;
+  if (gt == 0) A.iscal[8] = A.iscal[25] = 0;
   if (grouped && gt < 2 * kFam) cnt[gt] = 0;
   group_sync<T, G>();
   if (!(m.disable_flags & (B200_DSBL_CONSTRAINT | B200_DSBL_CONTACT))) {
@@ -661,6 +654,7 @@ __device__ void collision(const Mdl<R> &M, Arena<R> &A, int list_offset) {
         if (f >= 0) atomicAdd(&cnt[f], 1);
       }
       group_sync<T, G>();
+      if (gt == 0) A.iscal[25] = cnt[4];  // GJK / EPA pairs, for the world's work estimate
       int off[kFam], total = 0;
       for (int f = 0; f < kFam; ++f) { off[f] = total; total += cnt[f]; }
       for (int p = gt; p < m.npair; p += G) {
@@ -1005,54 +999,72 @@ template <class R, int T, bool ACT = false> __device__ void constraints(const Md
   }
   SYNC();
   const int nefc = A.iscal[1];
-  // Jacobian rows over the rows' tree segments, one (row, slot) per thread
-  FOR(w, nefc * kmax) {
-    const int r = w / kmax, k = w % kmax, type = A.efc_type[r];
-    const int t0 = A.row_t[2 * r], t1 = A.row_t[2 * r + 1];
-    const int n0 = t0 >= 0 ? IF(tree_dofnum)[t0] : 0, n1 = t1 >= 0 ? IF(tree_dofnum)[t1] : 0;
+  // Jacobian rows over the rows' tree segments.  The single-dof rows (friction,
+  // limits: rows [0, nsingle)) take one (row, slot) per thread; the contacts
+  // one (contact, slot) per thread, which forms the contact point's Jacobian at
+  // the slot's dof once and projects it on every row of the contact.
+  const int nsingle = A.iscal[13], ncon = A.iscal[0];
+  FOR(w, nsingle * kmax) {
+    const int r = w / kmax, k = w % kmax, t0 = A.row_t[2 * r];
     R v = 0;
-    if (k < n0 + n1) {
-      const int d = k < n0 ? IF(tree_dofadr)[t0] + k : IF(tree_dofadr)[t1] + k - n0;
-      if (type == 1) v = R(d == A.efc_id[r]);
-      else if (type == 3) {
+    if (t0 >= 0 && k < IF(tree_dofnum)[t0]) {
+      const int d = IF(tree_dofadr)[t0] + k;
+      if (A.efc_type[r] == 1) v = R(d == A.efc_id[r]);
+      else {
         const int j = A.efc_id[r];
         if (d == IF(jnt_dofadr)[j]) {
           const R *range = RF(jnt_range) + 2 * j;
           const R q = A.qpos[IF(jnt_qposadr)[j]];
           v = R((q - range[0]) < (range[1] - q)) * R(2) - R(1);
         }
-      } else {
-        const int c = A.efc_id[r], comp = r - A.con_adr[c];
-        const R *cr = A.con + (size_t)c * kCWidth;
-        const int b1 = IF(geom_bodyid)[A.con_g1[c]], b2 = IF(geom_bodyid)[A.con_g2[c]];
-        const bool in1 = dof_ancestor(M, b1, d), in2 = dof_ancestor(M, b2, d);
-        if (in1 || in2) {
-          const V3<R> point = ld3(cr + kCPos);
-          const R *mo = A.cdof + 6 * d;
-          const V3<R> ang = v3<R>(mo[0], mo[1], mo[2]), lin = v3<R>(mo[3], mo[4], mo[5]);
-          V3<R> l = v3<R>(0, 0, 0), a = v3<R>(0, 0, 0);
-          if (in2) {
-            l = lin + cross(ang, point - ld3(A.com + 3 * IF(body_rootid)[b2]));
-            a = ang;
-          }
-          if (in1) {
-            l = l - (lin + cross(ang, point - ld3(A.com + 3 * IF(body_rootid)[b1])));
-            a = a - ang;
-          }
-          const int dim = A.con_dim[c];
-          if (elliptic) v = dot(comp < 3 ? l : a, ld3(cr + kCFrame + 3 * (comp % 3)));
-          else {
-            v = dot(l, ld3(cr + kCFrame));
-            if (dim > 1) {
-              const int dir = comp / 2 + 1;
-              const R fr = cr[kCFriction + dir - 1] * (R(1) - R(2) * R(comp & 1));
-              v += dot(dir < 3 ? l : a, ld3(cr + kCFrame + 3 * (dir % 3))) * fr;
-            }
-          }
-        }
       }
     }
     A.J[(size_t)r * kmax + k] = v;
+  }
+  FOR(w, ncon * kmax) {
+    const int c = w / kmax, k = w % kmax, r0 = A.con_adr[c];
+    if (r0 < 0) continue;
+    const int dim = A.con_dim[c], count = elliptic || dim == 1 ? dim : 2 * (dim - 1);
+    const int t0 = A.row_t[2 * r0], t1 = A.row_t[2 * r0 + 1];
+    const int n0 = t0 >= 0 ? IF(tree_dofnum)[t0] : 0, n1 = t1 >= 0 ? IF(tree_dofnum)[t1] : 0;
+    const R *cr = A.con + (size_t)c * kCWidth;
+    V3<R> l = v3<R>(0, 0, 0), a = v3<R>(0, 0, 0);
+    bool hit = false;
+    if (k < n0 + n1) {
+      const int d = k < n0 ? IF(tree_dofadr)[t0] + k : IF(tree_dofadr)[t1] + k - n0;
+      const int b1 = IF(geom_bodyid)[A.con_g1[c]], b2 = IF(geom_bodyid)[A.con_g2[c]];
+      const bool in1 = dof_ancestor(M, b1, d), in2 = dof_ancestor(M, b2, d);
+      hit = in1 || in2;
+      if (hit) {
+        const V3<R> point = ld3(cr + kCPos);
+        const R *mo = A.cdof + 6 * d;
+        const V3<R> ang = v3<R>(mo[0], mo[1], mo[2]), lin = v3<R>(mo[3], mo[4], mo[5]);
+        if (in2) {
+          l = lin + cross(ang, point - ld3(A.com + 3 * IF(body_rootid)[b2]));
+          a = ang;
+        }
+        if (in1) {
+          l = l - (lin + cross(ang, point - ld3(A.com + 3 * IF(body_rootid)[b1])));
+          a = a - ang;
+        }
+      }
+    }
+    R *Jc = A.J + (size_t)r0 * kmax + k;
+    for (int comp = 0; comp < count; ++comp) {
+      R v = 0;
+      if (hit) {
+        if (elliptic) v = dot(comp < 3 ? l : a, ld3(cr + kCFrame + 3 * (comp % 3)));
+        else {
+          v = dot(l, ld3(cr + kCFrame));
+          if (dim > 1) {
+            const int dir = comp / 2 + 1;
+            const R fr = cr[kCFriction + dir - 1] * (R(1) - R(2) * R(comp & 1));
+            v += dot(dir < 3 ? l : a, ld3(cr + kCFrame + 3 * (dir % 3))) * fr;
+          }
+        }
+      }
+      Jc[(size_t)comp * kmax] = v;
+    }
   }
   SYNC();
   // row parameters (impedance, D, aref); sum of row widths for the FLOP counters
@@ -2563,7 +2575,9 @@ __global__ void __launch_bounds__(384, 1) control_step(const __grid_constant__ B
       A.iscal[24] = 0;
       if (s < 32 && d.niter_trace) irow_of(d.niter_trace, w, 32)[s] = it;
       if (s < 32 && d.ls_trace) irow_of(d.ls_trace, w, 32)[s] = evals;
-      work += (it + 1) * (nefc + 32) + 4 * A.iscal[0];
+      // a GJK / EPA pair stalls its world's collision stage about as long as
+      // 1500 work units of Newton rows do: worlds with such pairs share CTAs
+      work += (it + 1) * (nefc + 32) + 4 * A.iscal[0] + 1500 * A.iscal[25];
     }
     if (act && s == substeps - 1) store_outputs<R, T>(m, d, A, w);
     STAGE((euler<R, T>(M, A)), 14);

@@ -280,6 +280,10 @@ class Scene:
         tri_sizes = tree_dofnum * (tree_dofnum + 1) // 2   # packed lower-triangular factor blocks
         tree_padr = np.r_[0, np.cumsum(tri_sizes)[:-1]].astype(np.int32)
         nL = int(np.sum(tri_sizes))
+        # source of each packed lower-triangle entry in the dense tree blocks
+        tree_lsrc = np.concatenate([tree_madr[t] + np.array([a * n + j for a in range(n) for j in range(a + 1)],
+                                                            np.int64)
+                                    for t, n in enumerate(tree_dofnum)]).astype(np.int32)
         # subtree intervals (depth-first order => contiguous)
         subtree_end = np.arange(nb, dtype=np.int32) + 1
         for bi in range(nb - 1, 0, -1):
@@ -474,6 +478,7 @@ class Scene:
             dof_jntid=np.array([d['jnt'] for d in dofs], np.int32),
             dof_parentid=dof_parent, dof_treeid=dof_tree,
             tree_dofadr=tree_dofadr, tree_dofnum=tree_dofnum, tree_madr=tree_madr, tree_padr=tree_padr,
+            tree_lsrc=tree_lsrc,
             geom_type=gtype, geom_bodyid=gbody,
             geom_condim=np.array([g.condim for _, g in G], np.int32),
             geom_priority=np.zeros(ng, np.int32),

@@ -26,7 +26,8 @@
  * it asks for them.
  *
  * work / order: `work` is each world's solver work in its last control step
- * (sum over substeps of (Newton iterations + 1) x (rows + 32) + 4 contacts);
+ * (sum over substeps of (Newton iterations + 1) x (rows + 32) + 4 contacts
+ * + 1500 x GJK / EPA pairs past the broadphase);
  * `order`, when given, is the permutation that assigns worlds to the step
  * kernel's CTA slots (slot i runs world order[i]).  b200phys_order_launch
  * refills it from `work`, so that worlds of similar work share a CTA.
@@ -77,7 +78,7 @@
   X(jnt_type, njnt) X(jnt_qposadr, njnt) X(jnt_dofadr, njnt) \
   X(jnt_bodyid, njnt) X(jnt_limited, njnt) \
   X(dof_bodyid, nv) X(dof_jntid, nv) X(dof_parentid, nv) X(dof_treeid, nv) \
-  X(tree_dofadr, ntree) X(tree_dofnum, ntree) X(tree_madr, ntree) X(tree_padr, ntree) \
+  X(tree_dofadr, ntree) X(tree_dofnum, ntree) X(tree_madr, ntree) X(tree_padr, ntree) X(tree_lsrc, nL) \
   X(geom_type, ngeom) X(geom_bodyid, ngeom) X(geom_condim, ngeom) \
   X(geom_priority, ngeom) X(site_bodyid, nsite) X(pair_geom, npair * 2) \
   X(limited_jnt, nlimited) X(fric_dof, nfric) \
