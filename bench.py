@@ -37,7 +37,7 @@ UNIT = 'env control steps/s'
 # of one launch divided by its worlds; per-world state is independent, so the
 # traffic scales with the worlds of a launch): scene A captured at 1184 worlds,
 # scene B at 444 worlds (one wave each), after 25 warm-up control steps
-TRAFFIC_BYTES_PER_WORLD = {'scene_a': 1213, 'scene_b': 10888}
+TRAFFIC_BYTES_PER_WORLD = {'scene_a': 1247, 'scene_b': 11377}
 # control-step stages the kernel stamps with clock64 (data.stage_cycles slots 1..15);
 # in worlds of several warps the FP64 OSC runs on the first warp beside collision
 # on the others, and 'osc_collision' holds that overlapped stage ('collision' is
